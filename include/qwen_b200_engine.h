@@ -1,0 +1,90 @@
+/*
+ * Device-resident full-model engine (28 decoder layers + embedding + final RMSNorm + tied fp16 LM head
+ * + greedy argmax) on one B200, built from the same kernels as the drop-in per-layer ABI.
+ *
+ * The reference has no engine: its caller (verification/real_host_top_backend.py:208-351) re-quantizes
+ * and re-sends every layer's weights to the host .so on every call, rounds hidden states to bf16
+ * between layers (:260, :334) and finishes with the Hugging Face final norm and LM head (:138-146).
+ * This engine keeps the weights, the KV cache and the activations in HBM, applies the same bf16
+ * rounding between layers, and exposes the prefill / decode-step pair that RealHostTopBackend
+ * implements, with token ids in and next-token ids out. All functions return 0 on success, 1 for an
+ * invalid argument, 30 for a CUDA failure (see qwen_b200_last_error()), 31 if no device is usable.
+ *
+ * Numerics: decode uses the reference's decode operators (double RMSNorm, exact RoPE, expf softmax and
+ * SiLU); prefill uses the reference's prefill approximations (approx_sqrt/approx_sincos/approx_exp),
+ * exactly as RealHostTopBackend mixes the two .so paths. The attention residual is dropped, as in the
+ * reference's quantized layer (hls/decode_only/qwen_decode_attention_kernel.cpp:215).
+ */
+#ifndef QWEN_B200_ENGINE_H
+#define QWEN_B200_ENGINE_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct qwen_engine qwen_engine;
+
+/* Create an engine on CUDA device `device` with weight codes of `wbits` (4: packed int4, the reference
+ * format; 8: int8), room for `max_seqs` concurrent sequences of up to `max_len` tokens each. */
+int qwen_engine_create(int device, int wbits, int max_seqs, int max_len, qwen_engine** out);
+void qwen_engine_destroy(qwen_engine* e);
+
+/* Fill every parameter with the deterministic seeded generator (weights N(0, weight_sigma) quantized per
+ * output channel, biases N(0, 0.02), norm weights N(1, 0.02), fp16 embedding N(0, 0.02)). */
+int qwen_engine_init_synthetic(qwen_engine* e, uint64_t seed, float weight_sigma);
+/* Load one layer from DDR images in the layout of `wbits` (hls/common/llm_memory_layout.h:84-128). */
+int qwen_engine_load_layer(qwen_engine* e, int layer, const uint8_t* weight_ddr, const float* scale_ddr);
+/* Load the fp16 [151936][1536] embedding / LM head (as uint16 bits) and the final norm weight [1536]. */
+int qwen_engine_load_embedding(qwen_engine* e, const uint16_t* embed_f16, const float* final_norm);
+
+/* Prefill `n` tokens into sequence slot `slot` (which must be empty); writes the greedy next token. */
+int qwen_engine_prefill(qwen_engine* e, int slot, const int32_t* tokens, int n, int32_t* next_token);
+/* One greedy decode step for `n` sequences: tokens[i] is appended to slots[i]; next_tokens[i] receives
+ * the argmax. Host buffers; the call returns after the next tokens are on the host. */
+int qwen_engine_decode(qwen_engine* e, const int32_t* slots, const int32_t* tokens, int n, int32_t* next_tokens);
+
+/* Write / read `n_tokens` KV rows of one layer of a slot in the reference's flat token-major layout
+ * ([t][kv_head][128] fp32). write_kv also sets the slot length to n_tokens when layer == 27. */
+int qwen_engine_write_kv(qwen_engine* e, int slot, int layer, const float* k, const float* v, int n_tokens);
+int qwen_engine_read_kv(qwen_engine* e, int slot, int layer, float* k, float* v, int n_tokens);
+int qwen_engine_set_seq_len(qwen_engine* e, int slot, int len);
+int qwen_engine_seq_len(qwen_engine* e, int slot);
+int qwen_engine_reset(qwen_engine* e, int slot);
+
+/* Options: "graphs" (capture decode steps in CUDA graphs, default 1), "pdl" (programmatic dependent
+ * launch, default 1), "dump_hidden" (keep every layer's output of the last call, default 0),
+ * "logits" (keep the last call's logits, default 0). */
+int qwen_engine_set_option(qwen_engine* e, const char* name, long long value);
+/* Per-layer outputs of the last prefill/decode call: [28][rows][1536] floats (rows = tokens of that call). */
+int qwen_engine_read_hidden(qwen_engine* e, float* out, long long n_floats);
+/* Logits of the last call: [rows][151936] floats. */
+int qwen_engine_read_logits(qwen_engine* e, float* out, long long n_floats);
+
+/* Device-resident timing loop: `warmup` + `steps` greedy decode steps of the `n` sequences in `slots`,
+ * each step feeding its argmax back as the next input on the device (no host round trip); the `steps`
+ * are timed with CUDA events on the engine's stream. Writes the mean milliseconds per step. */
+int qwen_engine_bench_decode(qwen_engine* e, const int32_t* slots, const int32_t* first_tokens, int n, int steps,
+                             int warmup, float* ms_per_step);
+/* One decode step with device-resident token buffers on the engine's stream, without a host round trip:
+ * d_tokens[i] (device int32) is appended to slots[i]; d_next[i] (device int32) receives the argmax. The
+ * call returns once the step is enqueued; positions advance on the host bookkeeping immediately. */
+int qwen_engine_decode_device(qwen_engine* e, const int32_t* slots, const int32_t* d_tokens, int n,
+                              int32_t* d_next);
+/* Copy one layer's parameters back out in the DDR-image layout of the engine's width. */
+int qwen_engine_read_layer(qwen_engine* e, int layer, uint8_t* weight_ddr, float* scale_ddr);
+/* Time each decode kernel kind in isolation with CUDA events on the engine's stream (layers rotated so
+ * that weights come from HBM, not L2) for `n` tokens at history `past`; ms_out[6] receives the mean
+ * per-launch milliseconds of {qkv, attention, o, gate_up, down, lm_head}. */
+int qwen_engine_profile_kernels(qwen_engine* e, int n, int past, int iters, float* ms_out);
+/* The engine's CUDA stream (cudaStream_t) for callers that record their own events. */
+void* qwen_engine_stream(qwen_engine* e);
+/* Number of kernels one decode step of `n` sequences launches. */
+int qwen_engine_kernels_per_decode_step(qwen_engine* e, int n);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* QWEN_B200_ENGINE_H */

@@ -1,0 +1,215 @@
+// Drop-in C-ABI of the reference's libqwen_decode_stub.so (hls/decode_only/qwen_decode_host_wrapper.h:9-113),
+// running on the GPU through libqwen_b200.so. Argument meaning, validation order and status codes follow
+// the reference:
+//   - qwen_decode_attention_kernel null / negative-history check -> 1 (qwen_decode_attention_kernel.cpp:187-193)
+//   - qwen_decode_mlp_kernel null check -> 1 (qwen_decode_mlp_kernel.cpp:98-102)
+//   - top wrapper: invalid layer or history -> 10, any null port -> 11 (qwen_decode_top_wrapper.cpp:31-38)
+// The `_w8` entry points take the same arguments with one int8 code per weight (the W8 track; the DDR
+// layout keeps the reference's field order with 1-byte weights). They have no counterpart in the
+// reference.
+#include <cstddef>
+#include <cstdint>
+
+#include "../../include/qwen_decode_host_wrapper.h"
+#include "runtime.h"
+
+namespace {
+
+constexpr int kLayers = 28;
+
+qb::LayerPtrs make_layer(const float* input_ln, const float* post_ln, const uint8_t* qw, const uint8_t* kw,
+                         const uint8_t* vw, const uint8_t* ow, const uint8_t* gw, const uint8_t* uw,
+                         const uint8_t* dw, const float* qb, const float* kb, const float* vb, const float* qs,
+                         const float* ks, const float* vs, const float* os, const float* gs, const float* us,
+                         const float* ds) {
+  qb::LayerPtrs L;
+  L.q_w = qw;
+  L.k_w = kw;
+  L.v_w = vw;
+  L.o_w = ow;
+  L.gate_w = gw;
+  L.up_w = uw;
+  L.down_w = dw;
+  L.input_ln = input_ln;
+  L.post_ln = post_ln;
+  L.q_b = qb;
+  L.k_b = kb;
+  L.v_b = vb;
+  L.q_s = qs;
+  L.k_s = ks;
+  L.v_s = vs;
+  L.o_s = os;
+  L.gate_s = gs;
+  L.up_s = us;
+  L.down_s = ds;
+  return L;
+}
+
+bool attention_args_ok(const float* x, int past, const float* ln, const uint8_t* qw, const uint8_t* kw,
+                       const uint8_t* vw, const uint8_t* ow, const float* qb, const float* kb, const float* vb,
+                       const float* qs, const float* ks, const float* vs, const float* os, const float* kc,
+                       const float* vc, const float* out) {
+  return !(x == nullptr || out == nullptr || past < 0 || ln == nullptr || qw == nullptr || kw == nullptr ||
+           vw == nullptr || ow == nullptr || qb == nullptr || kb == nullptr || vb == nullptr || qs == nullptr ||
+           ks == nullptr || vs == nullptr || os == nullptr || kc == nullptr || vc == nullptr);
+}
+
+bool mlp_args_ok(const float* a, const float* ln, const uint8_t* gw, const uint8_t* uw, const uint8_t* dw,
+                 const float* gs, const float* us, const float* ds, const float* out) {
+  return !(a == nullptr || out == nullptr || ln == nullptr || gw == nullptr || uw == nullptr || dw == nullptr ||
+           gs == nullptr || us == nullptr || ds == nullptr);
+}
+
+int attention_forward(int wbits, const float* x, int past, const float* ln, const uint8_t* qw, const uint8_t* kw,
+                      const uint8_t* vw, const uint8_t* ow, const float* qb, const float* kb, const float* vb,
+                      const float* qs, const float* ks, const float* vs, const float* os, float* kc, float* vc,
+                      float* out) {
+  if (!attention_args_ok(x, past, ln, qw, kw, vw, ow, qb, kb, vb, qs, ks, vs, os, kc, vc, out)) return 1;
+  const qb::LayerPtrs L = make_layer(ln, nullptr, qw, kw, vw, ow, nullptr, nullptr, nullptr, qb, kb, vb, qs, ks, vs,
+                                     os, nullptr, nullptr, nullptr);
+  return qb::run_decode(wbits, L, true, false, x, past, kc, vc, out, nullptr);
+}
+
+int mlp_forward(int wbits, const float* a, const float* ln, const uint8_t* gw, const uint8_t* uw, const uint8_t* dw,
+                const float* gs, const float* us, const float* ds, float* out) {
+  if (!mlp_args_ok(a, ln, gw, uw, dw, gs, us, ds, out)) return 1;
+  const qb::LayerPtrs L = make_layer(nullptr, ln, nullptr, nullptr, nullptr, nullptr, gw, uw, dw, nullptr, nullptr,
+                                     nullptr, nullptr, nullptr, nullptr, nullptr, gs, us, ds);
+  return qb::run_decode(wbits, L, false, true, a, 0, nullptr, nullptr, nullptr, out);
+}
+
+int layer_forward(int wbits, const float* x, int past, const float* in_ln, const float* post_ln, const uint8_t* qw,
+                  const uint8_t* kw, const uint8_t* vw, const uint8_t* ow, const uint8_t* gw, const uint8_t* uw,
+                  const uint8_t* dw, const float* qb, const float* kb, const float* vb, const float* qs,
+                  const float* ks, const float* vs, const float* os, const float* gs, const float* us,
+                  const float* ds, float* kc, float* vc, float* out) {
+  // qwen_decode_host_wrapper.cpp:157-218: attention into a temporary, then the MLP into `out`. The MLP's
+  // null check runs after the attention half has written the KV row, as in the reference.
+  if (!attention_args_ok(x, past, in_ln, qw, kw, vw, ow, qb, kb, vb, qs, ks, vs, os, kc, vc, out)) return 1;
+  const qb::LayerPtrs L =
+      make_layer(in_ln, post_ln, qw, kw, vw, ow, gw, uw, dw, qb, kb, vb, qs, ks, vs, os, gs, us, ds);
+  if (!mlp_args_ok(x, post_ln, gw, uw, dw, gs, us, ds, out)) {
+    float scratch[1536];
+    const int st = qb::run_decode(wbits, L, true, false, x, past, kc, vc, scratch, nullptr);
+    return st ? st : 1;
+  }
+  return qb::run_decode(wbits, L, true, true, x, past, kc, vc, nullptr, out);
+}
+
+int top_forward(int wbits, int layer_id, int past, uint64_t in_addr, uint64_t out_addr, uint64_t w_base,
+                uint64_t s_base, uint64_t k_base, uint64_t v_base, const uint8_t* weight_ddr, const float* scale_ddr,
+                float* kv_cache_ddr, float* activation_ddr, uint8_t* weight_sram, float* kv_sram, int32_t* psum_sram,
+                float* softmax_sram, float* control_sram) {
+  if (layer_id < 0 || layer_id >= kLayers || past < 0) return 10;
+  if (weight_ddr == nullptr || scale_ddr == nullptr || kv_cache_ddr == nullptr || activation_ddr == nullptr ||
+      weight_sram == nullptr || kv_sram == nullptr || psum_sram == nullptr || softmax_sram == nullptr ||
+      control_sram == nullptr) {
+    return 11;
+  }
+  // address decode (qwen_decode_top_wrapper.cpp:40-75): floats at base + byte_offset / 4
+  const qb::LayerPtrs L = qb::layer_ptrs_from_ddr(weight_ddr, w_base, scale_ddr, s_base, wbits);
+  const float* x = activation_ddr + in_addr / 4;
+  float* out = activation_ddr + out_addr / 4;
+  float* kc = kv_cache_ddr + k_base / 4;
+  float* vc = kv_cache_ddr + v_base / 4;
+  return qb::run_decode(wbits, L, true, true, x, past, kc, vc, nullptr, out);
+}
+
+}  // namespace
+
+extern "C" {
+
+int qwen_decode_stub_forward(const float* input_token, int past_seq_len, float* output_token) {
+  // qwen_decode_host_wrapper.cpp:12-71: fixed all-zero int4 weights, unit scales and norm weights, zero
+  // biases, a zeroed history of past_seq_len tokens; gate/up reuse q, down reuses o.
+  if (input_token == nullptr || output_token == nullptr || past_seq_len < 0) return 1;
+  const qb::LayerPtrs& Z = qb::zero_layer_device();
+  if (Z.q_w == nullptr) return 31;
+  qb::LayerPtrs L = Z;
+  L.post_ln = Z.input_ln;
+  L.gate_w = Z.q_w;
+  L.up_w = Z.q_w;
+  L.down_w = Z.o_w;
+  float* kv = new float[(size_t)(past_seq_len + 1) * 256 * 2]();
+  const int st = qb::run_decode(4, L, true, true, input_token, past_seq_len, kv,
+                                kv + (size_t)(past_seq_len + 1) * 256, nullptr, output_token);
+  delete[] kv;
+  return st;
+}
+
+int qwen_decode_attention_smoke_forward(const float* input_token, int past_seq_len,
+                                        const float* input_layernorm_weight, const uint8_t* q_packed_weights,
+                                        const uint8_t* k_packed_weights, const uint8_t* v_packed_weights,
+                                        const uint8_t* o_packed_weights, const float* q_bias, const float* k_bias,
+                                        const float* v_bias, const float* q_scales, const float* k_scales,
+                                        const float* v_scales, const float* o_scales, float* k_cache, float* v_cache,
+                                        float* output_token) {
+  return attention_forward(4, input_token, past_seq_len, input_layernorm_weight, q_packed_weights, k_packed_weights,
+                           v_packed_weights, o_packed_weights, q_bias, k_bias, v_bias, q_scales, k_scales, v_scales,
+                           o_scales, k_cache, v_cache, output_token);
+}
+
+int qwen_decode_mlp_smoke_forward(const float* attention_residual_token, const float* post_attention_layernorm_weight,
+                                  const uint8_t* gate_packed_weights, const uint8_t* up_packed_weights,
+                                  const uint8_t* down_packed_weights, const float* gate_scales,
+                                  const float* up_scales, const float* down_scales, float* output_token) {
+  return mlp_forward(4, attention_residual_token, post_attention_layernorm_weight, gate_packed_weights,
+                     up_packed_weights, down_packed_weights, gate_scales, up_scales, down_scales, output_token);
+}
+
+int qwen_decode_layer_smoke_forward(const float* input_token, int past_seq_len, const float* input_layernorm_weight,
+                                    const float* post_attention_layernorm_weight, const uint8_t* q_packed_weights,
+                                    const uint8_t* k_packed_weights, const uint8_t* v_packed_weights,
+                                    const uint8_t* o_packed_weights, const uint8_t* gate_packed_weights,
+                                    const uint8_t* up_packed_weights, const uint8_t* down_packed_weights,
+                                    const float* q_bias, const float* k_bias, const float* v_bias,
+                                    const float* q_scales, const float* k_scales, const float* v_scales,
+                                    const float* o_scales, const float* gate_scales, const float* up_scales,
+                                    const float* down_scales, float* k_cache, float* v_cache, float* output_token) {
+  return layer_forward(4, input_token, past_seq_len, input_layernorm_weight, post_attention_layernorm_weight,
+                       q_packed_weights, k_packed_weights, v_packed_weights, o_packed_weights, gate_packed_weights,
+                       up_packed_weights, down_packed_weights, q_bias, k_bias, v_bias, q_scales, k_scales, v_scales,
+                       o_scales, gate_scales, up_scales, down_scales, k_cache, v_cache, output_token);
+}
+
+int qwen_decode_top_smoke_forward(int layer_id, int past_seq_len, uint64_t input_token_addr,
+                                  uint64_t output_token_addr, uint64_t layer_weights_base_addr,
+                                  uint64_t layer_scales_base_addr, uint64_t k_cache_base_addr,
+                                  uint64_t v_cache_base_addr, const uint8_t* weight_ddr, const float* scale_ddr,
+                                  float* kv_cache_ddr, float* activation_ddr, uint8_t* weight_sram, float* kv_sram,
+                                  int32_t* partial_sum_sram, float* softmax_sram, float* control_sram) {
+  return top_forward(4, layer_id, past_seq_len, input_token_addr, output_token_addr, layer_weights_base_addr,
+                     layer_scales_base_addr, k_cache_base_addr, v_cache_base_addr, weight_ddr, scale_ddr,
+                     kv_cache_ddr, activation_ddr, weight_sram, kv_sram, partial_sum_sram, softmax_sram,
+                     control_sram);
+}
+
+int qwen_decode_layer_smoke_forward_w8(const float* input_token, int past_seq_len,
+                                       const float* input_layernorm_weight,
+                                       const float* post_attention_layernorm_weight, const uint8_t* q_weights,
+                                       const uint8_t* k_weights, const uint8_t* v_weights, const uint8_t* o_weights,
+                                       const uint8_t* gate_weights, const uint8_t* up_weights,
+                                       const uint8_t* down_weights, const float* q_bias, const float* k_bias,
+                                       const float* v_bias, const float* q_scales, const float* k_scales,
+                                       const float* v_scales, const float* o_scales, const float* gate_scales,
+                                       const float* up_scales, const float* down_scales, float* k_cache,
+                                       float* v_cache, float* output_token) {
+  return layer_forward(8, input_token, past_seq_len, input_layernorm_weight, post_attention_layernorm_weight,
+                       q_weights, k_weights, v_weights, o_weights, gate_weights, up_weights, down_weights, q_bias,
+                       k_bias, v_bias, q_scales, k_scales, v_scales, o_scales, gate_scales, up_scales, down_scales,
+                       k_cache, v_cache, output_token);
+}
+
+int qwen_decode_top_smoke_forward_w8(int layer_id, int past_seq_len, uint64_t input_token_addr,
+                                     uint64_t output_token_addr, uint64_t layer_weights_base_addr,
+                                     uint64_t layer_scales_base_addr, uint64_t k_cache_base_addr,
+                                     uint64_t v_cache_base_addr, const uint8_t* weight_ddr, const float* scale_ddr,
+                                     float* kv_cache_ddr, float* activation_ddr, uint8_t* weight_sram, float* kv_sram,
+                                     int32_t* partial_sum_sram, float* softmax_sram, float* control_sram) {
+  return top_forward(8, layer_id, past_seq_len, input_token_addr, output_token_addr, layer_weights_base_addr,
+                     layer_scales_base_addr, k_cache_base_addr, v_cache_base_addr, weight_ddr, scale_ddr,
+                     kv_cache_ddr, activation_ddr, weight_sram, kv_sram, partial_sum_sram, softmax_sram,
+                     control_sram);
+}
+
+}  // extern "C"

@@ -1,0 +1,698 @@
+// Device-resident Qwen2.5-1.5B engine: weights, paged KV cache and activations stay in HBM; a decode step
+// is one CUDA-graph launch of 5 kernels per layer plus the LM head (programmatic dependent launch lets
+// each kernel's CTAs be scheduled while the previous one drains).
+//
+// Per-layer flow matches the reference's top wrappers (hls/decode_only/qwen_decode_top_wrapper.cpp:79-112,
+// hls/prefill_only/qwen_prefill_top_core.cpp:158-182) followed by the caller's bf16 rounding
+// (verification/real_host_top_backend.py:260, 334); the final norm / LM head / argmax stand in for the
+// caller's Hugging Face modules (:138-146) as defined in oracle/qwen_oracle.c (`oracle_lm_head_argmax`).
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cmath>
+#include <cstring>
+#include <map>
+#include <string>
+#include <vector>
+
+#include "../../include/qwen_b200_engine.h"
+#include "qwen_kernels.cuh"
+#include "runtime.h"
+
+namespace qb {
+namespace {
+
+__global__ void embed_gather_kernel(const uint16_t* __restrict__ embed, const int* __restrict__ tokens, int n,
+                                    float* __restrict__ x) {
+  const int t = blockIdx.x;
+  if (t >= n) return;
+  const __half* row = reinterpret_cast<const __half*>(embed) + (size_t)tokens[t] * kHidden;
+  for (int d = threadIdx.x; d < kHidden; d += blockDim.x) x[(size_t)t * kHidden + d] = __half2float(row[d]);
+}
+
+// flat [n][256] K and V of one layer <-> paged rows of one slot
+__global__ void kv_scatter_kernel(const float* __restrict__ kf, const float* __restrict__ vf, int n, KvView kv,
+                                  int slot, int to_pages) {
+  const int t = blockIdx.x;
+  if (t >= n) return;
+  float* kd = kv_row(kv, slot, t, 0);
+  float* vd = kv_row(kv, slot, t, 1);
+  for (int d = threadIdx.x; d < kKvWidth; d += blockDim.x) {
+    if (to_pages) {
+      kd[d] = kf[(size_t)t * kKvWidth + d];
+      vd[d] = vf[(size_t)t * kKvWidth + d];
+    } else {
+      const_cast<float*>(kf)[(size_t)t * kKvWidth + d] = kd[d];
+      const_cast<float*>(vf)[(size_t)t * kKvWidth + d] = vd[d];
+    }
+  }
+}
+
+__global__ void advance_pos_kernel(int* __restrict__ pos, int n) {
+  griddep_wait();
+  if ((int)threadIdx.x < n) pos[threadIdx.x] += 1;
+}
+
+// end of a device-resident decode step: next input token = argmax, position + 1
+__global__ void advance_kernel(int* __restrict__ tokens, const int* __restrict__ next, int* __restrict__ pos, int n) {
+  griddep_wait();
+  const int t = threadIdx.x;
+  if (t < n) {
+    tokens[t] = next[t];
+    pos[t] += 1;
+  }
+}
+
+#define E_TRY(expr)                                                                                 \
+  do {                                                                                              \
+    cudaError_t _e = (expr);                                                                        \
+    if (_e != cudaSuccess) {                                                                        \
+      set_error("%s failed: %s (%s:%d)", #expr, cudaGetErrorString(_e), __FILE__, __LINE__);        \
+      return kStatusCuda;                                                                           \
+    }                                                                                               \
+  } while (0)
+
+template <typename T>
+cudaError_t dalloc(T** p, size_t count) {
+  return cudaMalloc(reinterpret_cast<void**>(p), count * sizeof(T));
+}
+
+}  // namespace
+}  // namespace qb
+
+using namespace qb;
+
+struct qwen_engine {
+  int device = 0, wbits = 8, max_seqs = 1, max_len = 1, max_pages = 1;
+  cudaStream_t stream = nullptr;
+  // parameters
+  uint8_t* wimg = nullptr;
+  float* simg = nullptr;
+  uint64_t layer_bytes = 0;
+  LayerDev layers[kLayers];
+  uint16_t* embed = nullptr;
+  float* final_norm = nullptr;
+  // KV pages
+  float* kv_pool = nullptr;
+  int n_pages = 0;
+  int* d_page_table = nullptr;
+  std::vector<int> page_table;   // [max_seqs][max_pages], -1 = unassigned
+  std::vector<int> free_pages;
+  std::vector<int> seq_len;
+  // decode state (up to kGemvMaxTokens tokens per group)
+  int *d_tokens = nullptr, *d_pos = nullptr, *d_seq = nullptr, *d_next = nullptr;
+  int* h_io = nullptr;  // pinned: [4 tokens][4 pos][4 seq][4 next]
+  float *x = nullptr, *q = nullptr, *ctx = nullptr, *a = nullptr, *h = nullptr, *y0 = nullptr, *y1 = nullptr;
+  float* attn_part = nullptr;
+  unsigned* attn_cnt = nullptr;
+  float* lm_part = nullptr;
+  unsigned* lm_cnt = nullptr;
+  float* dump = nullptr;
+  float* logits = nullptr;
+  int last_rows = 0;
+  // rope tables
+  float *rope_dec_cos = nullptr, *rope_dec_sin = nullptr, *rope_pre_cos = nullptr, *rope_pre_sin = nullptr;
+  int rope_dec_len = 0, rope_pre_len = 0;
+  // prefill buffers
+  int pre_cap = 0;
+  float *p_x = nullptr, *p_xn = nullptr, *p_q = nullptr, *p_ctx = nullptr, *p_a = nullptr, *p_h = nullptr,
+        *p_k = nullptr, *p_v = nullptr;
+  int* p_tokens = nullptr;
+  // options
+  bool use_graphs = true, use_pdl = true, dump_hidden = false, keep_logits = false;
+  std::map<long long, cudaGraphExec_t> graphs;
+  std::vector<int> dev_slots;  // slots whose positions are current in d_pos / d_seq (decode_device path)
+};
+
+namespace {
+
+int ensure_rope_dec(qwen_engine* e, int need) {
+  if (need <= e->rope_dec_len) return 0;
+  int len = std::max(1024, e->rope_dec_len);
+  while (len < need) len *= 2;
+  std::vector<float> c((size_t)len * 64), s((size_t)len * 64);
+  for (int pos = 0; pos < len; ++pos)
+    for (int pair = 0; pair < 64; ++pair) {
+      const double angle = (double)pos * std::pow((double)kRopeTheta, -2.0 * (double)pair / (double)kHeadDim);
+      c[(size_t)pos * 64 + pair] = (float)std::cos(angle);
+      s[(size_t)pos * 64 + pair] = (float)std::sin(angle);
+    }
+  cudaFree(e->rope_dec_cos);
+  cudaFree(e->rope_dec_sin);
+  E_TRY(dalloc(&e->rope_dec_cos, (size_t)len * 64));
+  E_TRY(dalloc(&e->rope_dec_sin, (size_t)len * 64));
+  E_TRY(cudaMemcpy(e->rope_dec_cos, c.data(), c.size() * 4, cudaMemcpyHostToDevice));
+  E_TRY(cudaMemcpy(e->rope_dec_sin, s.data(), s.size() * 4, cudaMemcpyHostToDevice));
+  e->rope_dec_len = len;
+  return 0;
+}
+
+int ensure_rope_pre(qwen_engine* e, int need) {
+  if (need <= e->rope_pre_len) return 0;
+  int len = std::max(128, e->rope_pre_len);
+  while (len < need) len *= 2;
+  cudaFree(e->rope_pre_cos);
+  cudaFree(e->rope_pre_sin);
+  E_TRY(dalloc(&e->rope_pre_cos, (size_t)len * 64));
+  E_TRY(dalloc(&e->rope_pre_sin, (size_t)len * 64));
+  E_TRY(launch_prefill_rope_table(len, e->rope_pre_cos, e->rope_pre_sin, e->stream));
+  e->rope_pre_len = len;
+  return 0;
+}
+
+KvView paged_view(qwen_engine* e, int layer) {
+  KvView kv;
+  kv.k = e->kv_pool;
+  kv.v = nullptr;
+  kv.page_table = e->d_page_table;
+  kv.layer = layer;
+  kv.max_pages = e->max_pages;
+  return kv;
+}
+
+// make sure slot has pages for positions [0, len)
+int ensure_pages(qwen_engine* e, int slot, int len) {
+  const int need = (len + kPage - 1) / kPage;
+  if (need > e->max_pages) {
+    set_error("sequence length %d exceeds the engine's max_len %d", len, e->max_len);
+    return kStatusInvalid;
+  }
+  bool changed = false;
+  for (int p = 0; p < need; ++p) {
+    int& entry = e->page_table[(size_t)slot * e->max_pages + p];
+    if (entry < 0) {
+      if (e->free_pages.empty()) {
+        set_error("KV page pool exhausted");
+        return kStatusInvalid;
+      }
+      entry = e->free_pages.back();
+      e->free_pages.pop_back();
+      changed = true;
+    }
+  }
+  if (changed) {
+    E_TRY(cudaMemcpyAsync(e->d_page_table + (size_t)slot * e->max_pages,
+                          e->page_table.data() + (size_t)slot * e->max_pages, (size_t)e->max_pages * 4,
+                          cudaMemcpyHostToDevice, e->stream));
+  }
+  return 0;
+}
+
+int ensure_prefill_buffers(qwen_engine* e, int n) {
+  if (n <= e->pre_cap) return 0;
+  int cap = std::max(128, e->pre_cap);
+  while (cap < n) cap *= 2;
+  float** bufs[] = {&e->p_x, &e->p_xn, &e->p_q, &e->p_ctx, &e->p_a};
+  for (float** b : bufs) {
+    cudaFree(*b);
+    E_TRY(dalloc(b, (size_t)cap * kHidden));
+  }
+  cudaFree(e->p_h);
+  E_TRY(dalloc(&e->p_h, (size_t)cap * kInter));
+  cudaFree(e->p_k);
+  cudaFree(e->p_v);
+  E_TRY(dalloc(&e->p_k, (size_t)cap * kKvWidth));
+  E_TRY(dalloc(&e->p_v, (size_t)cap * kKvWidth));
+  cudaFree(e->p_tokens);
+  E_TRY(dalloc(&e->p_tokens, (size_t)cap));
+  e->pre_cap = cap;
+  return 0;
+}
+
+// Enqueue one decode step for nt tokens whose ids/positions/slots are already in d_tokens/d_pos/d_seq.
+// max_len bounds the attention grid (positions + 1 of every token must be <= max_len).
+int enqueue_decode(qwen_engine* e, int nt, int max_len, bool advance) {
+  const bool pdl = e->use_pdl;
+  DecodeTokens tok{e->d_pos, e->d_seq, nt};
+  float* xin = nullptr;
+  for (int l = 0; l < kLayers; ++l) {
+    const LayerDev& L = e->layers[l];
+    XSource src{xin, e->embed, e->d_tokens};
+    KvView kv = paged_view(e, l);
+    E_TRY(launch_decode_qkv(e->wbits, L, src, tok, e->rope_dec_cos, e->rope_dec_sin, e->q, kv, e->stream,
+                            pdl && l > 0));
+    E_TRY(launch_decode_attention(e->q, kv, tok, max_len, e->ctx, e->attn_part, e->attn_cnt, e->stream, pdl));
+    E_TRY(launch_decode_o(e->wbits, L, e->ctx, nt, e->a, e->stream, pdl));
+    E_TRY(launch_decode_gateup(e->wbits, L, e->a, nt, e->h, e->stream, pdl));
+    float* yout = (l & 1) ? e->y1 : e->y0;
+    E_TRY(launch_decode_down(e->wbits, L, e->h, e->a, nt, yout, true, e->stream, pdl));
+    if (e->dump_hidden) {
+      E_TRY(cudaMemcpyAsync(e->dump + (size_t)l * nt * kHidden, yout, (size_t)nt * kHidden * 4,
+                            cudaMemcpyDeviceToDevice, e->stream));
+    }
+    xin = yout;
+  }
+  E_TRY(launch_lm_head_argmax(e->embed, e->final_norm, xin, nt, e->keep_logits ? e->logits : nullptr, e->lm_part,
+                              e->lm_cnt, e->d_next, e->stream, pdl && !e->dump_hidden));
+  if (advance) {
+    E_TRY(launch_k(advance_kernel, dim3(1), dim3(32), 0, e->stream, pdl, e->d_tokens, (const int*)e->d_next,
+                   e->d_pos, nt));
+  }
+  return 0;
+}
+
+int run_decode_step(qwen_engine* e, int nt, int max_len, bool advance) {
+  const int chunks = (max_len + 63) / 64;
+  const int bucket = ((chunks + 7) / 8) * 8;  // re-capture every 512 positions
+  const int grid_len = bucket * 64;
+  if (!e->use_graphs || e->dump_hidden || e->keep_logits) return enqueue_decode(e, nt, grid_len, advance);
+  const long long key = ((long long)nt << 40) | ((long long)advance << 39) | bucket;
+  auto it = e->graphs.find(key);
+  if (it == e->graphs.end()) {
+    // one eager pass first (same positions: it writes exactly what the graph will rewrite), so every
+    // kernel's one-time attribute setup happens outside stream capture
+    if (int st = enqueue_decode(e, nt, grid_len, false)) return st;
+    cudaGraph_t g;
+    E_TRY(cudaStreamBeginCapture(e->stream, cudaStreamCaptureModeThreadLocal));
+    const int st = enqueue_decode(e, nt, grid_len, advance);
+    cudaError_t ce = cudaStreamEndCapture(e->stream, &g);
+    if (st) return st;
+    E_TRY(ce);
+    cudaGraphExec_t exec;
+    E_TRY(cudaGraphInstantiate(&exec, g, 0));
+    cudaGraphDestroy(g);
+    it = e->graphs.emplace(key, exec).first;
+  }
+  E_TRY(cudaGraphLaunch(it->second, e->stream));
+  return 0;
+}
+
+}  // namespace
+
+extern "C" {
+
+int qwen_engine_create(int device, int wbits, int max_seqs, int max_len, qwen_engine** out) {
+  if (!out || (wbits != 4 && wbits != 8) || max_seqs <= 0 || max_len <= 0 || max_len > kMaxSeq) return kStatusInvalid;
+  int n = 0;
+  if (cudaGetDeviceCount(&n) != cudaSuccess || device < 0 || device >= n) {
+    set_error("CUDA device %d is not available", device);
+    return kStatusNoDevice;
+  }
+  qwen_engine* e = new qwen_engine();
+  e->device = device;
+  e->wbits = wbits;
+  e->max_seqs = max_seqs;
+  e->max_len = max_len;
+  e->max_pages = (max_len + kPage - 1) / kPage;
+  E_TRY(cudaSetDevice(device));
+  E_TRY(cudaStreamCreateWithFlags(&e->stream, cudaStreamNonBlocking));
+  const LayerLayout lay = layer_layout(wbits);
+  e->layer_bytes = (lay.total + 255) / 256 * 256;
+  E_TRY(dalloc(&e->wimg, e->layer_bytes * kLayers));
+  E_TRY(dalloc(&e->simg, e->layer_bytes / 4 * kLayers));
+  for (int l = 0; l < kLayers; ++l)
+    e->layers[l] = layer_dev_from_ddr(e->wimg + e->layer_bytes * l, e->simg + e->layer_bytes / 4 * l, wbits);
+  E_TRY(dalloc(&e->embed, (size_t)kVocab * kHidden));
+  E_TRY(dalloc(&e->final_norm, (size_t)kHidden));
+  e->n_pages = max_seqs * e->max_pages;
+  E_TRY(dalloc(&e->kv_pool, (size_t)e->n_pages * kPageFloats));
+  E_TRY(dalloc(&e->d_page_table, (size_t)max_seqs * e->max_pages));
+  e->page_table.assign((size_t)max_seqs * e->max_pages, -1);
+  E_TRY(cudaMemcpy(e->d_page_table, e->page_table.data(), e->page_table.size() * 4, cudaMemcpyHostToDevice));
+  for (int p = e->n_pages - 1; p >= 0; --p) e->free_pages.push_back(p);
+  e->seq_len.assign(max_seqs, 0);
+  const int T = kGemvMaxTokens;
+  E_TRY(dalloc(&e->d_tokens, T));
+  E_TRY(dalloc(&e->d_pos, T));
+  E_TRY(dalloc(&e->d_seq, T));
+  E_TRY(dalloc(&e->d_next, T));
+  E_TRY(cudaMallocHost(&e->h_io, 16 * sizeof(int)));
+  E_TRY(dalloc(&e->x, (size_t)T * kHidden));
+  E_TRY(dalloc(&e->q, (size_t)T * kHidden));
+  E_TRY(dalloc(&e->ctx, (size_t)T * kHidden));
+  E_TRY(dalloc(&e->a, (size_t)T * kHidden));
+  E_TRY(dalloc(&e->y0, (size_t)T * kHidden));
+  E_TRY(dalloc(&e->y1, (size_t)T * kHidden));
+  E_TRY(dalloc(&e->h, (size_t)T * kInter));
+  E_TRY(dalloc(&e->attn_part, attn_partial_floats(T, max_len + 512 + 64)));
+  E_TRY(dalloc(&e->attn_cnt, (size_t)T * kKvHeads));
+  E_TRY(cudaMemset(e->attn_cnt, 0, (size_t)T * kKvHeads * 4));
+  E_TRY(dalloc(&e->lm_part, (size_t)lm_head_partial_floats()));
+  E_TRY(dalloc(&e->lm_cnt, 1));
+  E_TRY(cudaMemset(e->lm_cnt, 0, 4));
+  E_TRY(dalloc(&e->dump, (size_t)kLayers * std::max(T, 1) * kHidden));
+  E_TRY(dalloc(&e->logits, (size_t)T * kVocab));
+  if (int st = ensure_rope_dec(e, max_len + 1)) return st;
+  *out = e;
+  return 0;
+}
+
+void qwen_engine_destroy(qwen_engine* e) {
+  if (!e) return;
+  cudaSetDevice(e->device);
+  for (auto& kv : e->graphs) cudaGraphExecDestroy(kv.second);
+  void* ptrs[] = {e->wimg, e->simg, e->embed, e->final_norm, e->kv_pool, e->d_page_table, e->d_tokens, e->d_pos,
+                  e->d_seq, e->d_next, e->x, e->q, e->ctx, e->a, e->y0, e->y1, e->h, e->attn_part, e->attn_cnt,
+                  e->lm_part, e->lm_cnt, e->dump, e->logits, e->rope_dec_cos, e->rope_dec_sin, e->rope_pre_cos,
+                  e->rope_pre_sin, e->p_x, e->p_xn, e->p_q, e->p_ctx, e->p_a, e->p_h, e->p_k, e->p_v, e->p_tokens};
+  for (void* p : ptrs) cudaFree(p);
+  if (e->h_io) cudaFreeHost(e->h_io);
+  if (e->stream) cudaStreamDestroy(e->stream);
+  delete e;
+}
+
+int qwen_engine_init_synthetic(qwen_engine* e, uint64_t seed, float weight_sigma) {
+  if (!e) return kStatusInvalid;
+  E_TRY(cudaSetDevice(e->device));
+  for (int l = 0; l < kLayers; ++l)
+    E_TRY(launch_synth_layer(seed, l, e->wbits, weight_sigma, e->wimg + e->layer_bytes * l,
+                             e->simg + e->layer_bytes / 4 * l, e->stream));
+  E_TRY(launch_synth_embedding(seed, e->embed, e->stream));
+  E_TRY(launch_synth_fill(seed, (1ull << 20) + 1, kHidden, 1.0f, 0.02f, e->final_norm, e->stream));
+  E_TRY(cudaStreamSynchronize(e->stream));
+  return 0;
+}
+
+int qwen_engine_load_layer(qwen_engine* e, int layer, const uint8_t* weight_ddr, const float* scale_ddr) {
+  if (!e || layer < 0 || layer >= kLayers || !weight_ddr || !scale_ddr) return kStatusInvalid;
+  E_TRY(cudaSetDevice(e->device));
+  const LayerLayout lay = layer_layout(e->wbits);
+  E_TRY(cudaMemcpy(e->wimg + e->layer_bytes * layer, weight_ddr, lay.total, cudaMemcpyDefault));
+  E_TRY(cudaMemcpy(e->simg + e->layer_bytes / 4 * layer, scale_ddr, lay.total / 4 * 4, cudaMemcpyDefault));
+  return 0;
+}
+
+int qwen_engine_load_embedding(qwen_engine* e, const uint16_t* embed_f16, const float* final_norm) {
+  if (!e || !embed_f16 || !final_norm) return kStatusInvalid;
+  E_TRY(cudaSetDevice(e->device));
+  E_TRY(cudaMemcpy(e->embed, embed_f16, (size_t)kVocab * kHidden * 2, cudaMemcpyDefault));
+  E_TRY(cudaMemcpy(e->final_norm, final_norm, (size_t)kHidden * 4, cudaMemcpyDefault));
+  return 0;
+}
+
+int qwen_engine_set_option(qwen_engine* e, const char* name, long long value) {
+  if (!e || !name) return kStatusInvalid;
+  const std::string n(name);
+  if (n == "graphs") e->use_graphs = value != 0;
+  else if (n == "pdl") {
+    e->use_pdl = value != 0;
+    for (auto& kv : e->graphs) cudaGraphExecDestroy(kv.second);
+    e->graphs.clear();
+  } else if (n == "dump_hidden") e->dump_hidden = value != 0;
+  else if (n == "logits") e->keep_logits = value != 0;
+  else return kStatusInvalid;
+  return 0;
+}
+
+int qwen_engine_prefill(qwen_engine* e, int slot, const int32_t* tokens, int n, int32_t* next_token) {
+  if (!e || slot < 0 || slot >= e->max_seqs || !tokens || n <= 0 || n > e->max_len) return kStatusInvalid;
+  if (e->seq_len[slot] != 0) {
+    set_error("prefill into a non-empty slot %d (reset it first)", slot);
+    return kStatusInvalid;
+  }
+  for (int i = 0; i < n; ++i)
+    if (tokens[i] < 0 || tokens[i] >= kVocab) return kStatusInvalid;
+  E_TRY(cudaSetDevice(e->device));
+  if (int st = ensure_prefill_buffers(e, n)) return st;
+  if (int st = ensure_rope_pre(e, n)) return st;
+  if (int st = ensure_pages(e, slot, n)) return st;
+  cudaStream_t s = e->stream;
+  E_TRY(cudaMemcpyAsync(e->p_tokens, tokens, (size_t)n * 4, cudaMemcpyHostToDevice, s));
+  embed_gather_kernel<<<n, 256, 0, s>>>(e->embed, e->p_tokens, n, e->p_x);
+  E_TRY(cudaGetLastError());
+  for (int l = 0; l < kLayers; ++l) {
+    const LayerDev& L = e->layers[l];
+    E_TRY(launch_prefill_rmsnorm(e->p_x, L.input_ln, n, e->p_xn, s));
+    E_TRY(launch_prefill_qkv(e->wbits, L, e->p_xn, n, e->rope_pre_cos, e->rope_pre_sin, e->p_q, e->p_k, e->p_v, s));
+    E_TRY(launch_prefill_attention(e->p_q, e->p_k, e->p_v, n, e->p_ctx, s));
+    E_TRY(launch_prefill_o(e->wbits, L, e->p_ctx, n, e->p_a, s));
+    kv_scatter_kernel<<<n, 256, 0, s>>>(e->p_k, e->p_v, n, paged_view(e, l), slot, 1);
+    E_TRY(cudaGetLastError());
+    E_TRY(launch_prefill_rmsnorm(e->p_a, L.post_ln, n, e->p_xn, s));
+    E_TRY(launch_prefill_gateup(e->wbits, L, e->p_xn, n, e->p_h, s));
+    E_TRY(launch_prefill_down(e->wbits, L, e->p_h, e->p_a, n, e->p_x, true, s));
+    if (e->dump_hidden) {
+      // prefill keeps each layer's output row of the last prompt token
+      E_TRY(cudaMemcpyAsync(e->dump + (size_t)l * kHidden, e->p_x + (size_t)(n - 1) * kHidden, kHidden * 4,
+                            cudaMemcpyDeviceToDevice, s));
+    }
+  }
+  E_TRY(launch_lm_head_argmax(e->embed, e->final_norm, e->p_x + (size_t)(n - 1) * kHidden, 1,
+                              e->keep_logits ? e->logits : nullptr, e->lm_part, e->lm_cnt, e->d_next, s, false));
+  E_TRY(cudaMemcpyAsync(e->h_io + 12, e->d_next, 4, cudaMemcpyDeviceToHost, s));
+  E_TRY(cudaStreamSynchronize(s));
+  e->seq_len[slot] = n;
+  e->last_rows = 1;
+  if (next_token) *next_token = e->h_io[12];
+  return 0;
+}
+
+int qwen_engine_decode(qwen_engine* e, const int32_t* slots, const int32_t* tokens, int n, int32_t* next_tokens) {
+  if (!e || !slots || !tokens || n <= 0) return kStatusInvalid;
+  E_TRY(cudaSetDevice(e->device));
+  for (int base = 0; base < n; base += kGemvMaxTokens) {
+    const int nt = std::min(kGemvMaxTokens, n - base);
+    int max_len = 0;
+    for (int i = 0; i < nt; ++i) {
+      const int slot = slots[base + i];
+      if (slot < 0 || slot >= e->max_seqs || tokens[base + i] < 0 || tokens[base + i] >= kVocab) return kStatusInvalid;
+      for (int j = 0; j < i; ++j)
+        if (slots[base + j] == slot) return kStatusInvalid;
+      const int pos = e->seq_len[slot];
+      if (int st = ensure_pages(e, slot, pos + 1)) return st;
+      e->h_io[i] = tokens[base + i];
+      e->h_io[4 + i] = pos;
+      e->h_io[8 + i] = slot;
+      max_len = std::max(max_len, pos + 1);
+    }
+    if (int st = ensure_rope_dec(e, max_len)) return st;
+    e->dev_slots.clear();
+    E_TRY(cudaMemcpyAsync(e->d_tokens, e->h_io, nt * 4, cudaMemcpyHostToDevice, e->stream));
+    E_TRY(cudaMemcpyAsync(e->d_pos, e->h_io + 4, nt * 4, cudaMemcpyHostToDevice, e->stream));
+    E_TRY(cudaMemcpyAsync(e->d_seq, e->h_io + 8, nt * 4, cudaMemcpyHostToDevice, e->stream));
+    if (int st = run_decode_step(e, nt, max_len, false)) return st;
+    E_TRY(cudaMemcpyAsync(e->h_io + 12, e->d_next, nt * 4, cudaMemcpyDeviceToHost, e->stream));
+    E_TRY(cudaStreamSynchronize(e->stream));
+    for (int i = 0; i < nt; ++i) {
+      next_tokens[base + i] = e->h_io[12 + i];
+      e->seq_len[slots[base + i]] += 1;
+    }
+    e->last_rows = nt;
+  }
+  return 0;
+}
+
+int qwen_engine_bench_decode(qwen_engine* e, const int32_t* slots, const int32_t* first_tokens, int n, int steps,
+                             int warmup, float* ms_per_step) {
+  if (!e || !slots || !first_tokens || n <= 0 || n > kGemvMaxTokens || steps <= 0 || warmup < 0) return kStatusInvalid;
+  E_TRY(cudaSetDevice(e->device));
+  int max_end = 0;
+  for (int i = 0; i < n; ++i) {
+    const int slot = slots[i];
+    if (slot < 0 || slot >= e->max_seqs) return kStatusInvalid;
+    const int end = e->seq_len[slot] + warmup + steps;
+    if (int st = ensure_pages(e, slot, end)) return st;
+    e->h_io[i] = first_tokens[i];
+    e->h_io[4 + i] = e->seq_len[slot];
+    e->h_io[8 + i] = slot;
+    max_end = std::max(max_end, end);
+  }
+  if (int st = ensure_rope_dec(e, max_end)) return st;
+  e->dev_slots.clear();
+  E_TRY(cudaMemcpyAsync(e->d_tokens, e->h_io, n * 4, cudaMemcpyHostToDevice, e->stream));
+  E_TRY(cudaMemcpyAsync(e->d_pos, e->h_io + 4, n * 4, cudaMemcpyHostToDevice, e->stream));
+  E_TRY(cudaMemcpyAsync(e->d_seq, e->h_io + 8, n * 4, cudaMemcpyHostToDevice, e->stream));
+  // the attention grid must cover every position reached in the run: one graph for the whole run
+  for (int i = 0; i < warmup; ++i)
+    if (int st = run_decode_step(e, n, max_end, true)) return st;
+  cudaEvent_t t0, t1;
+  E_TRY(cudaEventCreate(&t0));
+  E_TRY(cudaEventCreate(&t1));
+  E_TRY(cudaStreamSynchronize(e->stream));
+  E_TRY(cudaEventRecord(t0, e->stream));
+  for (int i = 0; i < steps; ++i)
+    if (int st = run_decode_step(e, n, max_end, true)) return st;
+  E_TRY(cudaEventRecord(t1, e->stream));
+  E_TRY(cudaEventSynchronize(t1));
+  float ms = 0.f;
+  E_TRY(cudaEventElapsedTime(&ms, t0, t1));
+  cudaEventDestroy(t0);
+  cudaEventDestroy(t1);
+  for (int i = 0; i < n; ++i) e->seq_len[slots[i]] += warmup + steps;
+  if (ms_per_step) *ms_per_step = ms / steps;
+  return 0;
+}
+
+int qwen_engine_write_kv(qwen_engine* e, int slot, int layer, const float* k, const float* v, int n_tokens) {
+  if (!e || slot < 0 || slot >= e->max_seqs || layer < 0 || layer >= kLayers || !k || !v || n_tokens <= 0)
+    return kStatusInvalid;
+  E_TRY(cudaSetDevice(e->device));
+  if (int st = ensure_prefill_buffers(e, n_tokens)) return st;
+  if (int st = ensure_pages(e, slot, n_tokens)) return st;
+  E_TRY(cudaMemcpyAsync(e->p_k, k, (size_t)n_tokens * kKvWidth * 4, cudaMemcpyDefault, e->stream));
+  E_TRY(cudaMemcpyAsync(e->p_v, v, (size_t)n_tokens * kKvWidth * 4, cudaMemcpyDefault, e->stream));
+  kv_scatter_kernel<<<n_tokens, 256, 0, e->stream>>>(e->p_k, e->p_v, n_tokens, paged_view(e, layer), slot, 1);
+  E_TRY(cudaGetLastError());
+  E_TRY(cudaStreamSynchronize(e->stream));
+  if (layer == kLayers - 1) e->seq_len[slot] = n_tokens;
+  e->dev_slots.clear();
+  return 0;
+}
+
+int qwen_engine_read_kv(qwen_engine* e, int slot, int layer, float* k, float* v, int n_tokens) {
+  if (!e || slot < 0 || slot >= e->max_seqs || layer < 0 || layer >= kLayers || !k || !v || n_tokens <= 0 ||
+      n_tokens > e->seq_len[slot])
+    return kStatusInvalid;
+  E_TRY(cudaSetDevice(e->device));
+  if (int st = ensure_prefill_buffers(e, n_tokens)) return st;
+  kv_scatter_kernel<<<n_tokens, 256, 0, e->stream>>>(e->p_k, e->p_v, n_tokens, paged_view(e, layer), slot, 0);
+  E_TRY(cudaGetLastError());
+  E_TRY(cudaMemcpyAsync(k, e->p_k, (size_t)n_tokens * kKvWidth * 4, cudaMemcpyDefault, e->stream));
+  E_TRY(cudaMemcpyAsync(v, e->p_v, (size_t)n_tokens * kKvWidth * 4, cudaMemcpyDefault, e->stream));
+  E_TRY(cudaStreamSynchronize(e->stream));
+  return 0;
+}
+
+int qwen_engine_set_seq_len(qwen_engine* e, int slot, int len) {
+  if (!e || slot < 0 || slot >= e->max_seqs || len < 0 || len > e->max_len) return kStatusInvalid;
+  if (int st = ensure_pages(e, slot, len)) return st;
+  e->seq_len[slot] = len;
+  e->dev_slots.clear();
+  return 0;
+}
+
+int qwen_engine_seq_len(qwen_engine* e, int slot) {
+  if (!e || slot < 0 || slot >= e->max_seqs) return -1;
+  return e->seq_len[slot];
+}
+
+int qwen_engine_reset(qwen_engine* e, int slot) {
+  if (!e || slot < 0 || slot >= e->max_seqs) return kStatusInvalid;
+  for (int p = 0; p < e->max_pages; ++p) {
+    int& entry = e->page_table[(size_t)slot * e->max_pages + p];
+    if (entry >= 0) e->free_pages.push_back(entry);
+    entry = -1;
+  }
+  E_TRY(cudaSetDevice(e->device));
+  E_TRY(cudaMemcpy(e->d_page_table + (size_t)slot * e->max_pages, e->page_table.data() + (size_t)slot * e->max_pages,
+                   (size_t)e->max_pages * 4, cudaMemcpyHostToDevice));
+  e->seq_len[slot] = 0;
+  e->dev_slots.clear();
+  return 0;
+}
+
+int qwen_engine_read_hidden(qwen_engine* e, float* out, long long n_floats) {
+  if (!e || !out) return kStatusInvalid;
+  const long long have = (long long)kLayers * e->last_rows * kHidden;
+  if (n_floats < have) return kStatusInvalid;
+  E_TRY(cudaMemcpy(out, e->dump, (size_t)have * 4, cudaMemcpyDeviceToHost));
+  return 0;
+}
+
+int qwen_engine_read_logits(qwen_engine* e, float* out, long long n_floats) {
+  if (!e || !out) return kStatusInvalid;
+  const long long have = (long long)e->last_rows * kVocab;
+  if (n_floats < have) return kStatusInvalid;
+  E_TRY(cudaMemcpy(out, e->logits, (size_t)have * 4, cudaMemcpyDeviceToHost));
+  return 0;
+}
+
+int qwen_engine_decode_device(qwen_engine* e, const int32_t* slots, const int32_t* d_tokens, int n,
+                              int32_t* d_next) {
+  if (!e || !slots || !d_tokens || !d_next || n <= 0 || n > kGemvMaxTokens) return kStatusInvalid;
+  E_TRY(cudaSetDevice(e->device));
+  int max_len = 0;
+  const std::vector<int> want(slots, slots + n);
+  for (int i = 0; i < n; ++i) {
+    const int slot = slots[i];
+    if (slot < 0 || slot >= e->max_seqs) return kStatusInvalid;
+    const int pos = e->seq_len[slot];
+    if (int st = ensure_pages(e, slot, pos + 1)) return st;
+    max_len = std::max(max_len, pos + 1);
+  }
+  if (int st = ensure_rope_dec(e, max_len)) return st;
+  if (want != e->dev_slots) {
+    // (re)upload positions and slots; steady-state calls keep them on the device and advance them there
+    E_TRY(cudaStreamSynchronize(e->stream));
+    for (int i = 0; i < n; ++i) {
+      e->h_io[4 + i] = e->seq_len[slots[i]];
+      e->h_io[8 + i] = slots[i];
+    }
+    E_TRY(cudaMemcpyAsync(e->d_pos, e->h_io + 4, n * 4, cudaMemcpyHostToDevice, e->stream));
+    E_TRY(cudaMemcpyAsync(e->d_seq, e->h_io + 8, n * 4, cudaMemcpyHostToDevice, e->stream));
+    E_TRY(cudaStreamSynchronize(e->stream));
+    e->dev_slots = want;
+  }
+  E_TRY(cudaMemcpyAsync(e->d_tokens, d_tokens, n * 4, cudaMemcpyDeviceToDevice, e->stream));
+  if (int st = run_decode_step(e, n, max_len, false)) return st;
+  E_TRY(cudaMemcpyAsync(d_next, e->d_next, n * 4, cudaMemcpyDeviceToDevice, e->stream));
+  advance_pos_kernel<<<1, 32, 0, e->stream>>>(e->d_pos, n);
+  E_TRY(cudaGetLastError());
+  for (int i = 0; i < n; ++i) e->seq_len[slots[i]] += 1;
+  e->last_rows = n;
+  return 0;
+}
+
+int qwen_engine_read_layer(qwen_engine* e, int layer, uint8_t* weight_ddr, float* scale_ddr) {
+  if (!e || layer < 0 || layer >= kLayers || !weight_ddr || !scale_ddr) return kStatusInvalid;
+  E_TRY(cudaSetDevice(e->device));
+  const LayerLayout lay = layer_layout(e->wbits);
+  E_TRY(cudaMemcpy(weight_ddr, e->wimg + e->layer_bytes * layer, lay.total, cudaMemcpyDeviceToHost));
+  E_TRY(cudaMemcpy(scale_ddr, e->simg + e->layer_bytes / 4 * layer, lay.total / 4 * 4, cudaMemcpyDeviceToHost));
+  return 0;
+}
+
+int qwen_engine_profile_kernels(qwen_engine* e, int n, int past, int iters, float* ms_out) {
+  if (!e || n <= 0 || n > kGemvMaxTokens || past < 0 || past + 1 > e->max_len || iters <= 0 || !ms_out)
+    return kStatusInvalid;
+  E_TRY(cudaSetDevice(e->device));
+  // scratch sequences: slots 0..n-1 hold `past` tokens (contents are whatever the pool holds)
+  for (int i = 0; i < n; ++i) {
+    if (int st = ensure_pages(e, i, past + 1)) return st;
+    e->h_io[i] = 1000 + i;
+    e->h_io[4 + i] = past;
+    e->h_io[8 + i] = i;
+  }
+  if (int st = ensure_rope_dec(e, past + 1)) return st;
+  e->dev_slots.clear();
+  E_TRY(cudaMemcpyAsync(e->d_tokens, e->h_io, n * 4, cudaMemcpyHostToDevice, e->stream));
+  E_TRY(cudaMemcpyAsync(e->d_pos, e->h_io + 4, n * 4, cudaMemcpyHostToDevice, e->stream));
+  E_TRY(cudaMemcpyAsync(e->d_seq, e->h_io + 8, n * 4, cudaMemcpyHostToDevice, e->stream));
+  E_TRY(cudaMemsetAsync(e->y0, 0, (size_t)n * kHidden * 4, e->stream));
+  E_TRY(cudaMemsetAsync(e->ctx, 0, (size_t)n * kHidden * 4, e->stream));
+  E_TRY(cudaMemsetAsync(e->a, 0, (size_t)n * kHidden * 4, e->stream));
+  E_TRY(cudaMemsetAsync(e->h, 0, (size_t)n * kInter * 4, e->stream));
+  DecodeTokens tok{e->d_pos, e->d_seq, n};
+  cudaEvent_t t0, t1;
+  E_TRY(cudaEventCreate(&t0));
+  E_TRY(cudaEventCreate(&t1));
+  for (int kind = 0; kind < 6; ++kind) {
+    auto launch = [&](int l) -> cudaError_t {
+      const LayerDev& L = e->layers[l];
+      KvView kv = paged_view(e, l);
+      switch (kind) {
+        case 0: return launch_decode_qkv(e->wbits, L, XSource{e->y0, e->embed, e->d_tokens}, tok, e->rope_dec_cos,
+                                         e->rope_dec_sin, e->q, kv, e->stream, false);
+        case 1: return launch_decode_attention(e->q, kv, tok, past + 1, e->ctx, e->attn_part, e->attn_cnt, e->stream,
+                                               false);
+        case 2: return launch_decode_o(e->wbits, L, e->ctx, n, e->a, e->stream, false);
+        case 3: return launch_decode_gateup(e->wbits, L, e->a, n, e->h, e->stream, false);
+        case 4: return launch_decode_down(e->wbits, L, e->h, e->a, n, e->y1, true, e->stream, false);
+        default: return launch_lm_head_argmax(e->embed, e->final_norm, e->y0, n, nullptr, e->lm_part, e->lm_cnt,
+                                              e->d_next, e->stream, false);
+      }
+    };
+    for (int w = 0; w < 3; ++w) E_TRY(launch(w % kLayers));
+    E_TRY(cudaEventRecord(t0, e->stream));
+    for (int i = 0; i < iters; ++i) E_TRY(launch(i % kLayers));
+    E_TRY(cudaEventRecord(t1, e->stream));
+    E_TRY(cudaEventSynchronize(t1));
+    float ms = 0.f;
+    E_TRY(cudaEventElapsedTime(&ms, t0, t1));
+    ms_out[kind] = ms / iters;
+  }
+  cudaEventDestroy(t0);
+  cudaEventDestroy(t1);
+  return 0;
+}
+
+void* qwen_engine_stream(qwen_engine* e) { return e ? (void*)e->stream : nullptr; }
+
+int qwen_engine_kernels_per_decode_step(qwen_engine* e, int n) {
+  (void)e;
+  const int groups = (n + kGemvMaxTokens - 1) / kGemvMaxTokens;
+  return groups * (kLayers * 5 + 1);
+}
+
+}  // extern "C"

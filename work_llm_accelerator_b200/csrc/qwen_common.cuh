@@ -1,0 +1,256 @@
+// Shared constants, the reference's DDR layout, and the device-side restatement of the reference's
+// elementwise operators with identical IEEE rounding.
+//
+// Model constants: hls/common/qwen2_model_config.h:7-52. Layout: hls/common/llm_memory_layout.h:55-149.
+// Approximate operators: hls/prefill_only/qwen_prefill_attention_kernel.cpp:47-143 (host variant, not the
+// __SYNTHESIS__ one). Every float operation in those operators is written with an explicit _rn intrinsic so
+// nvcc cannot fuse a multiply and an add into an FMA: the reference's x86-64 -O2 build never fuses, and a
+// fused operation rounds once where the reference rounds twice.
+#pragma once
+
+#include <cstdint>
+#include <cstddef>
+
+#ifdef __CUDACC__
+#define QB_HD __host__ __device__ __forceinline__
+#else
+#define QB_HD inline
+#endif
+
+namespace qb {
+
+constexpr int kHidden = 1536;
+constexpr int kInter = 8960;
+constexpr int kLayers = 28;
+constexpr int kHeads = 12;
+constexpr int kKvHeads = 2;
+constexpr int kHeadDim = 128;
+constexpr int kKvWidth = kKvHeads * kHeadDim;  // 256
+constexpr int kGroups = kHeads / kKvHeads;     // 6 query heads share one KV head
+constexpr int kQkvRows = kHidden + 2 * kKvWidth;  // 2048: q | k | v rows, contiguous in the layout
+constexpr int kVocab = 151936;
+constexpr int kMaxSeq = 32768;
+constexpr float kEps = 1.0e-6f;
+constexpr float kRopeTheta = 1000000.0f;
+
+// Reference status codes (qwen_decode_top_wrapper.cpp:11-12, qwen_prefill_top_core.h:7-9).
+constexpr int kStatusOk = 0;
+constexpr int kStatusInvalid = 1;
+constexpr int kStatusCapacity = 2;
+constexpr int kStatusDecodeDescriptor = 10;
+constexpr int kStatusDecodePort = 11;
+constexpr int kStatusPrefillDescriptor = 20;
+constexpr int kStatusPrefillPort = 21;
+constexpr int kStatusPrefillWindow = 22;
+// Codes that exist only in this implementation (the reference runs on the host and cannot fail this way).
+constexpr int kStatusCuda = 30;      // a CUDA call failed; the message is in qwen_b200_last_error()
+constexpr int kStatusNoDevice = 31;  // no CUDA device / extension unusable
+
+// ------------------------------------------------------------------------------------------------
+// Layer parameter layout. wbits = 4 is the reference layout (two nibbles per byte); wbits = 8 keeps
+// the same field order with one byte per weight (the W8 track).
+// ------------------------------------------------------------------------------------------------
+struct LayerLayout {
+  uint64_t input_ln, q_w, k_w, v_w, o_w, post_ln, gate_w, up_w, down_w;
+  uint64_t q_b, k_b, v_b;
+  uint64_t q_s, k_s, v_s, o_s, gate_s, up_s, down_s;
+  uint64_t total;
+};
+
+QB_HD uint64_t weight_bytes(uint64_t out_dim, uint64_t in_dim, int wbits) { return out_dim * in_dim * wbits / 8; }
+
+QB_HD LayerLayout layer_layout(int wbits) {
+  LayerLayout l{};
+  uint64_t off = 0;
+  l.input_ln = off; off += kHidden * 4;
+  l.q_w = off; off += weight_bytes(kHidden, kHidden, wbits);
+  l.k_w = off; off += weight_bytes(kKvWidth, kHidden, wbits);
+  l.v_w = off; off += weight_bytes(kKvWidth, kHidden, wbits);
+  l.o_w = off; off += weight_bytes(kHidden, kHidden, wbits);
+  l.post_ln = off; off += kHidden * 4;
+  l.gate_w = off; off += weight_bytes(kInter, kHidden, wbits);
+  l.up_w = off; off += weight_bytes(kInter, kHidden, wbits);
+  l.down_w = off; off += weight_bytes(kHidden, kInter, wbits);
+  l.q_b = off; off += kHidden * 4;
+  l.k_b = off; off += kKvWidth * 4;
+  l.v_b = off; off += kKvWidth * 4;
+  l.q_s = off; off += kHidden * 4;
+  l.k_s = off; off += kKvWidth * 4;
+  l.v_s = off; off += kKvWidth * 4;
+  l.o_s = off; off += kHidden * 4;
+  l.gate_s = off; off += kInter * 4;
+  l.up_s = off; off += kInter * 4;
+  l.down_s = off; off += kHidden * 4;
+  l.total = off;
+  return l;
+}
+
+// Device view of one layer's parameters (all device pointers).
+struct LayerDev {
+  const uint8_t* qkv_w;   // [2048 rows][1536] codes: q | k | v contiguous
+  const uint8_t* o_w;     // [1536][1536]
+  const uint8_t* gu_w;    // [2 * 8960][1536]: gate | up contiguous
+  const uint8_t* down_w;  // [1536][8960]
+  const float* input_ln;  // [1536]
+  const float* post_ln;   // [1536]
+  const float* qkv_b;     // [2048]
+  const float* qkv_s;     // [2048]
+  const float* o_s;       // [1536]
+  const float* gu_s;      // [2 * 8960]
+  const float* down_s;    // [1536]
+};
+
+QB_HD LayerDev layer_dev_from_ddr(const uint8_t* weight_base, const float* scale_base, int wbits) {
+  const LayerLayout l = layer_layout(wbits);
+  LayerDev d;
+  d.qkv_w = weight_base + l.q_w;
+  d.o_w = weight_base + l.o_w;
+  d.gu_w = weight_base + l.gate_w;
+  d.down_w = weight_base + l.down_w;
+  d.input_ln = scale_base + l.input_ln / 4;
+  d.post_ln = scale_base + l.post_ln / 4;
+  d.qkv_b = scale_base + l.q_b / 4;
+  d.qkv_s = scale_base + l.q_s / 4;
+  d.o_s = scale_base + l.o_s / 4;
+  d.gu_s = scale_base + l.gate_s / 4;
+  d.down_s = scale_base + l.down_s / 4;
+  return d;
+}
+
+// ------------------------------------------------------------------------------------------------
+// KV cache view: flat (the reference's token-major [t][kv_head][128] fp32, separate K and V bases)
+// or paged (page table per sequence; a page holds kPage tokens of every layer's K and V).
+// ------------------------------------------------------------------------------------------------
+constexpr int kPage = 64;
+
+struct KvView {
+  float* k;                // flat: K base of this sequence/layer. paged: pool base
+  float* v;                // flat: V base. paged: unused
+  const int* page_table;   // nullptr => flat
+  int layer;               // paged only
+  int max_pages;           // paged only: row length of the page table
+};
+
+// Floats per page: [layer][K|V][kPage][256].
+constexpr uint64_t kPageFloats = (uint64_t)kLayers * 2ull * kPage * kKvWidth;
+
+QB_HD float* kv_row(const KvView& kv, int seq, int token, int which /*0=K,1=V*/) {
+  if (kv.page_table == nullptr) {
+    return (which ? kv.v : kv.k) + (uint64_t)token * kKvWidth;
+  }
+  const int page = kv.page_table[seq * kv.max_pages + token / kPage];
+  return kv.k + (uint64_t)page * kPageFloats + ((uint64_t)kv.layer * 2 + which) * kPage * kKvWidth +
+         (uint64_t)(token % kPage) * kKvWidth;
+}
+
+// ------------------------------------------------------------------------------------------------
+// Deterministic synthetic parameters (bit-identical to the oracle's generator): SplitMix64 finalizer
+// and a 12-term Irwin-Hall sum of 16-bit uniforms.
+// ------------------------------------------------------------------------------------------------
+QB_HD uint64_t mix64(uint64_t x) {
+  x ^= x >> 30;
+  x *= 0xBF58476D1CE4E5B9ull;
+  x ^= x >> 27;
+  x *= 0x94D049BB133111EBull;
+  x ^= x >> 31;
+  return x;
+}
+
+QB_HD uint64_t synth_key(uint64_t seed, uint64_t stream) { return mix64(seed ^ mix64(stream + 0x9E3779B97F4A7C15ull)); }
+
+#ifdef __CUDACC__
+__device__ __forceinline__ float synth_normal_dev(uint64_t key, uint64_t index, float mean, float sigma) {
+  long long sum = 0;
+#pragma unroll
+  for (uint64_t j = 0; j < 3; ++j) {
+    const uint64_t h = mix64(key + index * 3ull + j);
+    sum += (long long)(h & 0xFFFF) + (long long)((h >> 16) & 0xFFFF) + (long long)((h >> 32) & 0xFFFF) +
+           (long long)((h >> 48) & 0xFFFF);
+  }
+  const float z = __fmul_rn(__ll2float_rn(2 * sum - 12 * 65535), 1.0f / 131072.0f);
+  return __fadd_rn(__fmul_rn(z, sigma), mean);
+}
+
+// ------------------------------------------------------------------------------------------------
+// Prefill approximations, bit-identical to the reference host code.
+// ------------------------------------------------------------------------------------------------
+constexpr float kPi = 3.14159265358979323846f;
+constexpr float kTwoPi = 6.28318530717958647692f;
+constexpr float kHalfPi = 1.57079632679489661923f;
+constexpr float kAttentionScaling = 0.08838834764831845f;  // qwen_prefill_attention_kernel.cpp:28
+constexpr float kRopeFreqStep = 0.8058421877614801f;      // qwen_prefill_attention_kernel.cpp:29
+
+// qwen_prefill_attention_kernel.cpp:47-57
+__device__ __forceinline__ float approx_sqrt(float value) {
+  if (value <= 0.0f) return 0.0f;
+  float guess = value > 1.0f ? value : 1.0f;
+#pragma unroll
+  for (int i = 0; i < 6; ++i) guess = __fmul_rn(0.5f, __fadd_rn(guess, __fdiv_rn(value, guess)));
+  return guess;
+}
+
+// qwen_prefill_attention_kernel.cpp:59-85
+__device__ __forceinline__ void approx_sincos(float angle, float* s, float* c) {
+  float r = angle;
+  while (r > kPi) r = __fsub_rn(r, kTwoPi);
+  while (r < -kPi) r = __fadd_rn(r, kTwoPi);
+  float cos_sign = 1.0f;
+  if (r > kHalfPi) {
+    r = __fsub_rn(kPi, r);
+    cos_sign = -1.0f;
+  } else if (r < -kHalfPi) {
+    r = __fsub_rn(-kPi, r);
+    cos_sign = -1.0f;
+  }
+  const float c6 = -1.0f / 5040.0f, c4 = 1.0f / 120.0f, c2 = -1.0f / 6.0f;
+  const float d6 = -1.0f / 720.0f, d4 = 1.0f / 24.0f;
+  const float x2 = __fmul_rn(r, r);
+  float t = __fmul_rn(x2, c6);
+  t = __fadd_rn(c4, t);
+  t = __fmul_rn(x2, t);
+  t = __fadd_rn(c2, t);
+  t = __fmul_rn(x2, t);
+  t = __fadd_rn(1.0f, t);
+  *s = __fmul_rn(r, t);
+  float u = __fmul_rn(x2, d6);
+  u = __fadd_rn(d4, u);
+  u = __fmul_rn(x2, u);
+  u = __fadd_rn(-0.5f, u);
+  u = __fmul_rn(x2, u);
+  *c = __fmul_rn(cos_sign, __fadd_rn(1.0f, u));
+}
+
+// qwen_prefill_attention_kernel.cpp:87-110. Below -1 the argument is halved until it is >= -1 and
+// the degree-6 Taylor value is squared back; above -1 there is no range reduction (so large positive
+// arguments are far from exp, exactly as in the reference).
+__device__ __forceinline__ float approx_exp(float value) {
+  if (value <= -16.0f) return 0.0f;
+  int half_steps = 0;
+  float scaled = value;
+  while (scaled < -1.0f) {
+    scaled = __fmul_rn(scaled, 0.5f);
+    ++half_steps;
+  }
+  float term = 1.0f, series = 1.0f;
+#pragma unroll
+  for (int degree = 1; degree <= 6; ++degree) {
+    term = __fmul_rn(term, __fdiv_rn(scaled, (float)degree));
+    series = __fadd_rn(series, term);
+  }
+  for (int i = 0; i < half_steps; ++i) series = __fmul_rn(series, series);
+  return series > 0.0f ? series : 0.0f;
+}
+
+// Round-to-nearest-even to bf16, kept in fp32 (verification/reference_wrapper_backend.py:40-46).
+__device__ __forceinline__ float round_bf16(float x) {
+  uint32_t b = __float_as_uint(x);
+  b += 0x7FFFu + ((b >> 16) & 1u);
+  return __uint_as_float(b & 0xFFFF0000u);
+}
+
+// Programmatic dependent launch: wait for the preceding kernel's writes / let the next kernel start.
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void griddep_launch() { asm volatile("griddepcontrol.launch_dependents;" :::); }
+#endif  // __CUDACC__
+
+}  // namespace qb
