@@ -1,0 +1,29 @@
+/*
+ * Device-pointer operator API of libqwen_b200.so: single hot-path kernels on buffers the caller already
+ * holds in GPU memory, enqueued on the caller's stream (no host staging, no synchronisation).
+ * Status codes: 0 ok, 1 invalid argument (message in qwen_b200_last_error()), 30 CUDA failure.
+ */
+#ifndef QWEN_B200_OPS_H
+#define QWEN_B200_OPS_H
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Decode attention context for one token: 12 query heads over 2 KV heads, head_dim 128 (replaces the
+ * reference's decode_attention_context, hls/decode_only/qwen_decode_attention_kernel.cpp:113-162).
+ *   q        [1536] fp32, the token's post-RoPE query (device memory)
+ *   k_cache  [seq_len][256] fp32 token-major keys (device memory), the token's own row included
+ *   v_cache  [seq_len][256] fp32 token-major values (device memory)
+ *   context  [1536] fp32 output (device memory)
+ *   stream   cudaStream_t (NULL = legacy default stream)
+ * The split-history scratch is allocated by the library on a device's first call and grown when a
+ * longer history arrives; calls on one device share it, so calls that overlap on the GPU race. */
+int qwen_b200_decode_attention(const float* q, const float* k_cache, const float* v_cache, int seq_len,
+                               float* context, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* QWEN_B200_OPS_H */

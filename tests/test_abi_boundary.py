@@ -19,6 +19,7 @@ HEADERS = {
     "qwen_prefill_host_wrapper.h": "LIB_PREFILL",
     "qwen_b200_engine.h": "LIB_CORE",
     "qwen_b200_runtime.h": "LIB_CORE",
+    "qwen_b200_ops.h": "LIB_CORE",
 }
 
 

@@ -1,0 +1,90 @@
+// Device-pointer operator API (include/qwen_b200_ops.h): hot-path kernels on caller-owned GPU buffers.
+#include <cuda_runtime.h>
+
+#include <mutex>
+
+#include "../../include/qwen_b200_ops.h"
+#include "qwen_kernels.cuh"
+#include "runtime.h"
+
+namespace qb {
+namespace {
+
+constexpr int kMaxDevices = 64;
+
+struct OpScratch {
+  float* part = nullptr;
+  size_t part_floats = 0;
+  unsigned* counters = nullptr;  // 2 (one per KV head), zeroed at allocation
+  int* tok = nullptr;            // [pos, seq]
+};
+
+std::mutex g_ops_mu;
+OpScratch g_ops[kMaxDevices];
+
+bool device_accessible(const void* p) {
+  cudaPointerAttributes a;
+  if (cudaPointerGetAttributes(&a, p) != cudaSuccess) {
+    cudaGetLastError();
+    return false;
+  }
+  return a.type == cudaMemoryTypeDevice || a.type == cudaMemoryTypeManaged;
+}
+
+__global__ void set_token_kernel(int* tok, int pos) {
+  tok[0] = pos;
+  tok[1] = 0;
+}
+
+}  // namespace
+}  // namespace qb
+
+extern "C" int qwen_b200_decode_attention(const float* q, const float* k_cache, const float* v_cache, int seq_len,
+                                          float* context, void* stream) {
+  using namespace qb;
+  if (!q || !k_cache || !v_cache || !context || seq_len <= 0 || seq_len > kMaxSeq) {
+    set_error("qwen_b200_decode_attention: null buffer or seq_len %d outside 1..%d", seq_len, kMaxSeq);
+    return kStatusInvalid;
+  }
+  if (!device_accessible(q) || !device_accessible(k_cache) || !device_accessible(v_cache) ||
+      !device_accessible(context)) {
+    set_error("qwen_b200_decode_attention: every buffer must be device (or managed) memory");
+    return kStatusInvalid;
+  }
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) {
+    set_error("qwen_b200_decode_attention: no current CUDA device");
+    return kStatusNoDevice;
+  }
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  std::lock_guard<std::mutex> lock(g_ops_mu);
+  OpScratch& o = g_ops[dev];
+  const size_t need = attn_partial_floats(1, seq_len);
+  cudaError_t e = cudaSuccess;
+  if (o.counters == nullptr) {
+    if ((e = cudaMalloc(&o.counters, 2 * sizeof(unsigned))) == cudaSuccess &&
+        (e = cudaMalloc(&o.tok, 2 * sizeof(int))) == cudaSuccess) {
+      e = cudaMemset(o.counters, 0, 2 * sizeof(unsigned));
+    }
+  }
+  if (e == cudaSuccess && o.part_floats < need) {
+    if (o.part) cudaFree(o.part);
+    o.part = nullptr;
+    o.part_floats = 0;
+    if ((e = cudaMalloc(&o.part, need * sizeof(float))) == cudaSuccess) o.part_floats = need;
+  }
+  if (e == cudaSuccess) {
+    set_token_kernel<<<1, 1, 0, s>>>(o.tok, seq_len - 1);
+    e = cudaGetLastError();
+  }
+  if (e == cudaSuccess) {
+    DecodeTokens tok{o.tok, o.tok + 1, 1};
+    KvView kv{const_cast<float*>(k_cache), const_cast<float*>(v_cache), nullptr, 0, 0};
+    e = launch_decode_attention(q, kv, tok, seq_len, context, o.part, o.counters, s, false);
+  }
+  if (e != cudaSuccess) {
+    set_error("qwen_b200_decode_attention: %s", cudaGetErrorString(e));
+    return kStatusCuda;
+  }
+  return 0;
+}

@@ -63,6 +63,9 @@ def core_lib() -> ctypes.CDLL:
         lib.qwen_b200_set_prefill_seq_capacity.argtypes = [ctypes.c_int]
         lib.qwen_b200_set_prefill_seq_capacity.restype = ctypes.c_int
         _configure_engine(lib)
+        lib.qwen_b200_decode_attention.argtypes = [ctypes.c_void_p] * 3 + [ctypes.c_int, ctypes.c_void_p,
+                                                                            ctypes.c_void_p]
+        lib.qwen_b200_decode_attention.restype = ctypes.c_int
         _core = lib
     return _core
 
@@ -335,3 +338,11 @@ class EngineBackend:
         ids = np.asarray(input_ids, dtype=np.int64).reshape(-1)
         self.engine.decode([cache], ids[-1:].astype(np.int32))
         return DecodeResult(logits=self.engine.read_logits(1), cache=cache)
+
+
+def decode_attention(q_ptr: int, k_ptr: int, v_ptr: int, seq_len: int, ctx_ptr: int, stream: int = 0) -> None:
+    """Device-pointer decode attention (include/qwen_b200_ops.h): raw device addresses in, enqueued on
+    `stream`."""
+    st = core_lib().qwen_b200_decode_attention(q_ptr, k_ptr, v_ptr, seq_len, ctx_ptr, stream or None)
+    if st != 0:
+        raise EngineError(f"qwen_b200_decode_attention failed with status {st}: {last_error()}")
