@@ -22,6 +22,18 @@ extern "C" {
 int qwen_b200_decode_attention(const float* q, const float* k_cache, const float* v_cache, int seq_len,
                                float* context, void* stream);
 
+/* Same computation and arguments as qwen_b200_decode_attention, for callers that cannot allocate device
+ * memory at the point where they run attention -- e.g. a serving runtime that reserves all GPU memory in
+ * its own pool at start-up, or a latency-critical loop where cudaMalloc/cudaFree would synchronise the
+ * device. No counterpart in the reference (its host library has no device memory at all). It allocates
+ * nothing: its scratch is a fixed array compiled into the library (about 0.8 MB, held on every GPU that
+ * loads the library until the process exits), so seq_len is limited to 8192 (status 1 above it). The
+ * first call on a device looks up that array's address and should come before any stream capture. All
+ * calls on a device share the array (each call clears the parts that must start at zero), so calls that
+ * overlap on the GPU race. */
+int qwen_b200_decode_attention_noalloc(const float* q, const float* k_cache, const float* v_cache, int seq_len,
+                                       float* context, void* stream);
+
 #ifdef __cplusplus
 }
 #endif
