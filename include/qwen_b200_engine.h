@@ -55,7 +55,7 @@ int qwen_engine_reset(qwen_engine* e, int slot);
 
 /* Options: "graphs" (capture decode steps in CUDA graphs, default 1), "pdl" (programmatic dependent
  * launch, default 1), "dump_hidden" (keep every layer's output of the last call, default 0),
- * "logits" (keep the last call's logits, default 0). */
+ * "logits" (keep the last call's logits, default 0), "prefetch" (stream the next kernels' weights into L2, default 1). */
 int qwen_engine_set_option(qwen_engine* e, const char* name, long long value);
 /* Per-layer outputs of the last prefill/decode call: [28][rows][1536] floats (rows = tokens of that call). */
 int qwen_engine_read_hidden(qwen_engine* e, float* out, long long n_floats);

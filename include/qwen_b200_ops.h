@@ -34,6 +34,20 @@ int qwen_b200_decode_attention(const float* q, const float* k_cache, const float
 int qwen_b200_decode_attention_noalloc(const float* q, const float* k_cache, const float* v_cache, int seq_len,
                                        float* context, void* stream);
 
+/* Integer core of the W8 projections on the int8 tensor cores, exposed so that its exactness can be
+ * checked: the fp32 activations x[t] (t < n_tokens <= 4, length k) are written as step[t] * X with
+ * step[t] = max|x[t]| / 8355710 (fp32 division; 1.0 for an all-zero row) and X = rint(x / step) split into
+ * balanced int8 digits X = d0 + 256 d1 + 65536 d2, each in [-128, 127]; then
+ *   acc[r][4 d + t] = sum_i codes[r][i] * d_d(t, i)     (int32, exact)
+ * for every row r, and 0 in the columns of absent tokens. The W8 projections compute
+ * y = scale[r] * step[t] * (acc0 + 256 acc1 + 65536 acc2) from the same sums, in place of the reference's
+ * fp32 dot product (hls/decode_only/qwen_decode_attention_kernel.cpp:62-98).
+ *   codes  [rows][k] int8 weight codes (device memory, 16-byte aligned), rows % 128 == 0, k % 128 == 0
+ *   x      [n_tokens][k] fp32 (device memory)
+ *   acc    [rows][12] int32 output (device memory);  step  [n_tokens] fp32 output (device memory) */
+int qwen_b200_w8_digit_products(const signed char* codes, int rows, int k, const float* x, int n_tokens, int* acc,
+                                float* step, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

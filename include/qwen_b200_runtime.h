@@ -18,6 +18,9 @@ const char* qwen_b200_last_error(void);
 int qwen_b200_prefill_seq_capacity(void);
 /* Set the prefill capacity (1..32768); returns 0, or 1 for an out-of-range value. */
 int qwen_b200_set_prefill_seq_capacity(int capacity);
+/* Error flag of the streaming kernels on the current device: 0 = none, 1 = a pipeline wait gave up after
+ * its bounded timeout (the kernel ended early instead of hanging). reset != 0 clears it. */
+unsigned qwen_b200_kernel_error(int reset);
 /* Number of visible CUDA devices (0 when the driver or device is absent). */
 int qwen_b200_device_count(void);
 

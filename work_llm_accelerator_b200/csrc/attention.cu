@@ -3,10 +3,11 @@
 // Decode (hls/decode_only/qwen_decode_attention_kernel.cpp:113-162): the reference makes two passes over
 // the whole history (max, then expf(s - max)). Here the history is split into 64-token chunks, one CTA
 // per (token, KV head, chunk) handling the 6 query heads that share the KV head, so each K/V row is read
-// once for all six. Each chunk keeps its own max; the last CTA of a (token, KV head) to finish merges the
-// chunks in chunk order (rescaling by expf(m_c - M)), so the result equals the two-pass value up to
-// rounding and is deterministic. Scores q.k are summed serially over the 128 dims with separately
-// rounded multiply and add, exactly as the reference does.
+// once for all six. The chunk's K and V rows are staged in shared memory with all loads in flight at
+// once (history rows before the grid-dependency wait, the new row after it). Each chunk keeps its own
+// max; the last CTA of a (token, KV head) to finish merges the chunks in chunk order (rescaling by
+// expf(m_c - M)), so the result equals the two-pass value up to rounding and is deterministic; a history
+// of one chunk writes the context directly.
 //
 // Prefill (hls/prefill_only/qwen_prefill_attention_kernel.cpp:204-289): approx_exp(a) * approx_exp(b) is
 // not approx_exp(a + b), so online rescaling would change results; the kernel keeps the reference's two
@@ -18,120 +19,215 @@
 namespace qb {
 namespace {
 
-constexpr int kChunk = 64;            // decode keys per CTA
+constexpr int kChunk = 64;                 // decode keys per CTA
 constexpr int kPartStride = 2 + kHeadDim;  // m, l, acc[128]
+constexpr int kAttnThreads = 128;
+constexpr int kRow = kHeadDim + 4;         // padded smem row (16-byte aligned, conflict-free float4 reads)
 
-__global__ void __launch_bounds__(64) decode_attn_kernel(const float* __restrict__ q, KvView kv, DecodeTokens tok,
-                                                         int max_chunks, float* __restrict__ ctx,
-                                                         float* __restrict__ part, unsigned* __restrict__ counters) {
+struct DecodeAttnSmem {
+  float ks[kChunk][kRow];
+  float vs[kChunk][kHeadDim];
+  float qs[kGroups][kRow];
+  float es[kChunk][8];  // per key: the six heads' scores, then weights (padded to 8)
+  float ms[kGroups], ls[kGroups];
+  bool last;
+};
+
+__device__ __forceinline__ void cp_async16(void* smem_dst, const void* gmem_src) {
+  const unsigned d = (unsigned)__cvta_generic_to_shared(smem_dst);
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(d), "l"(gmem_src) : "memory");
+}
+
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+
+__device__ __forceinline__ void prefetch_l2(const void* p, unsigned bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
+}
+
+// Hint: stream `bytes` of the next kernels' weights into L2 while this latency-bound kernel runs; the
+// region is split evenly over the grid's CTAs.
+__device__ __forceinline__ void prefetch_region(const uint8_t* pf, size_t bytes, unsigned cta, unsigned ctas) {
+  if (pf == nullptr || bytes == 0) return;
+  const size_t per = ((bytes + ctas - 1) / ctas + 15) & ~size_t(15);
+  const size_t b0 = (size_t)cta * per;
+  const size_t b1 = min(bytes, b0 + per);
+  for (size_t off = b0 + (size_t)threadIdx.x * 16384; off < b1; off += (size_t)blockDim.x * 16384)
+    prefetch_l2(pf + off, (unsigned)min((size_t)16384, b1 - off));
+}
+
+__global__ void __launch_bounds__(kAttnThreads) decode_attn_kernel(const float* __restrict__ q, KvView kv,
+                                                                   DecodeTokens tok, int max_chunks,
+                                                                   float* __restrict__ ctx, float* __restrict__ part,
+                                                                   unsigned* __restrict__ counters,
+                                                                   const uint8_t* pf, size_t pf_bytes) {
+  extern __shared__ float4 smem4[];
+  DecodeAttnSmem& sm = *reinterpret_cast<DecodeAttnSmem*>(smem4);
   const int c = blockIdx.x, g = blockIdx.y, t = blockIdx.z;
-  const int tid = threadIdx.x;
-  __shared__ float qs[kGroups][kHeadDim];
-  __shared__ float es[kGroups][kChunk];
-  __shared__ float ms[kGroups], ls[kGroups];
-  __shared__ bool last;
+  const int tid = threadIdx.x, warp = tid / 32, lane = tid % 32;
+  prefetch_region(pf, pf_bytes, (blockIdx.z * gridDim.y + blockIdx.y) * gridDim.x + blockIdx.x,
+                  gridDim.x * gridDim.y * gridDim.z);
 
-  griddep_wait();
+  // Positions and history rows were written before the preceding kernel started, so they are read
+  // before the grid-dependency wait; only the new row and the query depend on that kernel.
   const int L = tok.pos[t] + 1;
   const int nchunks = (L + kChunk - 1) / kChunk;
   if (c >= nchunks) return;
   const int seq = tok.seq[t];
-  const float scaling = (float)(1.0 / 1.4142135623730951 / 8.0);  // float(1/sqrt(128)), :119
-
-  for (int i = tid; i < kGroups * kHeadDim; i += 64)
-    qs[i / kHeadDim][i % kHeadDim] = q[(size_t)t * kHidden + g * kGroups * kHeadDim + i];
+  const int k0 = c * kChunk;
+  const int n = min(kChunk, L - k0);
+  const int pos = L - 1;
+  // A chunk is exactly one KV page (kChunk == kPage): rows are 256 floats apart from the chunk's first row,
+  // in the paged and in the flat layout, so one page-table lookup serves the whole chunk.
+  static_assert(kChunk == kPage, "a decode chunk must map onto one KV page");
+  const float* kbase = kv_row(kv, seq, k0, 0) + g * kHeadDim;
+  const float* vbase = kv_row(kv, seq, k0, 1) + g * kHeadDim;
+  const int nhist = min(n, pos - k0);  // rows of this chunk that precede the new token
+  // every row of the chunk in flight at once: asynchronous global->shared copies, one wait
+  for (int i = tid; i < nhist * 32; i += kAttnThreads) {
+    const int r = i >> 5, f = i & 31;
+    cp_async16(&sm.ks[r][4 * f], kbase + (size_t)r * kKvWidth + 4 * f);
+    cp_async16(&sm.vs[r][4 * f], vbase + (size_t)r * kKvWidth + 4 * f);
+  }
+  griddep_wait();
+  if (pos < k0 + kChunk && tid < 32) {
+    const int r = pos - k0;
+    cp_async16(&sm.ks[r][4 * tid], kbase + (size_t)r * kKvWidth + 4 * tid);
+    cp_async16(&sm.vs[r][4 * tid], vbase + (size_t)r * kKvWidth + 4 * tid);
+  }
+  for (int i = tid; i < kGroups * 32; i += kAttnThreads) {
+    const int h = i >> 5, f = i & 31;
+    cp_async16(&sm.qs[h][4 * f], q + (size_t)t * kHidden + (g * kGroups + h) * kHeadDim + 4 * f);
+  }
+  cp_async_wait_all();
   __syncthreads();
+  griddep_launch();
 
-  // scores: one key per thread, six serial dot products
-  const int j = c * kChunk + tid;
-  float sc[kGroups];
-  if (j < L) {
-    const float4* kr = reinterpret_cast<const float4*>(kv_row(kv, seq, j, 0) + g * kHeadDim);
+  // scores: thread = (key, three of the six heads); K read once per key pair (broadcast)
+  const float scaling = kAttentionScaling;  // == float(1 / sqrt(128)), qwen_decode_attention_kernel.cpp:119
+  {
+    const int key = tid >> 1, h0 = (tid & 1) * 3;
+    float s0 = 0.f, s1 = 0.f, s2 = 0.f;
+#pragma unroll 8
+    for (int f = 0; f < 32; ++f) {
+      const float4 kk = *reinterpret_cast<const float4*>(&sm.ks[key][4 * f]);
+      const float4 a = *reinterpret_cast<const float4*>(&sm.qs[h0][4 * f]);
+      const float4 b = *reinterpret_cast<const float4*>(&sm.qs[h0 + 1][4 * f]);
+      const float4 d = *reinterpret_cast<const float4*>(&sm.qs[h0 + 2][4 * f]);
+      s0 = fmaf(a.x, kk.x, fmaf(a.y, kk.y, fmaf(a.z, kk.z, fmaf(a.w, kk.w, s0))));
+      s1 = fmaf(b.x, kk.x, fmaf(b.y, kk.y, fmaf(b.z, kk.z, fmaf(b.w, kk.w, s1))));
+      s2 = fmaf(d.x, kk.x, fmaf(d.y, kk.y, fmaf(d.z, kk.z, fmaf(d.w, kk.w, s2))));
+    }
+    const bool ok = key < n;
+    sm.es[key][h0] = ok ? s0 * scaling : -INFINITY;
+    sm.es[key][h0 + 1] = ok ? s1 * scaling : -INFINITY;
+    sm.es[key][h0 + 2] = ok ? s2 * scaling : -INFINITY;
+  }
+  __syncthreads();
+  // softmax statistics of this chunk: warp w < 3 handles heads 2w, 2w+1 over the 64 keys
+  if (warp < 3) {
 #pragma unroll
-    for (int h = 0; h < kGroups; ++h) sc[h] = 0.0f;
-#pragma unroll 4
-    for (int d4 = 0; d4 < kHeadDim / 4; ++d4) {
-      const float4 kk = kr[d4];
+    for (int j = 0; j < 2; ++j) {
+      const int h = 2 * warp + j;
+      const float a = sm.es[lane][h], b = sm.es[lane + 32][h];
+      float m = fmaxf(a, b);
 #pragma unroll
-      for (int h = 0; h < kGroups; ++h) {
-        sc[h] = __fadd_rn(sc[h], __fmul_rn(qs[h][4 * d4 + 0], kk.x));
-        sc[h] = __fadd_rn(sc[h], __fmul_rn(qs[h][4 * d4 + 1], kk.y));
-        sc[h] = __fadd_rn(sc[h], __fmul_rn(qs[h][4 * d4 + 2], kk.z));
-        sc[h] = __fadd_rn(sc[h], __fmul_rn(qs[h][4 * d4 + 3], kk.w));
+      for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+      m = fmaxf(m, -1.0e30f);  // the reference's initial max
+      const float ea = lane < n ? expf(a - m) : 0.f;
+      const float eb = lane + 32 < n ? expf(b - m) : 0.f;
+      sm.es[lane][h] = ea;
+      sm.es[lane + 32][h] = eb;
+      float l = ea + eb;
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) l += __shfl_xor_sync(0xffffffffu, l, o);
+      if (lane == 0) {
+        sm.ms[h] = m;
+        sm.ls[h] = l;
       }
     }
-#pragma unroll
-    for (int h = 0; h < kGroups; ++h) es[h][tid] = __fmul_rn(sc[h], scaling);
-  } else {
-#pragma unroll
-    for (int h = 0; h < kGroups; ++h) es[h][tid] = -INFINITY;
   }
   __syncthreads();
-  const int n = min(kChunk, L - c * kChunk);
-  if (tid < kGroups) {
-    float m = -1.0e30f;
-    for (int i = 0; i < n; ++i) m = m < es[tid][i] ? es[tid][i] : m;
-    ms[tid] = m;
-  }
-  __syncthreads();
+  // P.V: thread = one of the 128 dims, six heads
+  float acc[kGroups];
 #pragma unroll
-  for (int h = 0; h < kGroups; ++h) es[h][tid] = tid < n ? expf(es[h][tid] - ms[h]) : 0.0f;
-  __syncthreads();
-  if (tid < kGroups) {
-    float l = 0.0f;
-    for (int i = 0; i < n; ++i) l += es[tid][i];
-    ls[tid] = l;
+  for (int h = 0; h < kGroups; ++h) acc[h] = 0.f;
+#pragma unroll 4
+  for (int key = 0; key < n; ++key) {
+    const float vv = sm.vs[key][tid];
+    const float4 e03 = *reinterpret_cast<const float4*>(&sm.es[key][0]);
+    const float2 e45 = *reinterpret_cast<const float2*>(&sm.es[key][4]);
+    acc[0] = fmaf(e03.x, vv, acc[0]);
+    acc[1] = fmaf(e03.y, vv, acc[1]);
+    acc[2] = fmaf(e03.z, vv, acc[2]);
+    acc[3] = fmaf(e03.w, vv, acc[3]);
+    acc[4] = fmaf(e45.x, vv, acc[4]);
+    acc[5] = fmaf(e45.y, vv, acc[5]);
   }
-  // P.V: thread owns dims 2*tid, 2*tid+1 for all six heads
-  float acc[kGroups][2];
-#pragma unroll
-  for (int h = 0; h < kGroups; ++h) acc[h][0] = acc[h][1] = 0.0f;
-  for (int i = 0; i < n; ++i) {
-    const float2 vv = *reinterpret_cast<const float2*>(kv_row(kv, seq, c * kChunk + i, 1) + g * kHeadDim + 2 * tid);
+  float* out_base = ctx + (size_t)t * kHidden + g * kGroups * kHeadDim + tid;
+  if (nchunks == 1) {
 #pragma unroll
     for (int h = 0; h < kGroups; ++h) {
-      acc[h][0] = fmaf(es[h][i], vv.x, acc[h][0]);
-      acc[h][1] = fmaf(es[h][i], vv.y, acc[h][1]);
+      const float inv = sm.ls[h] > 0.0f ? 1.0f / sm.ls[h] : 0.0f;
+      out_base[h * kHeadDim] = acc[h] * inv;
     }
+    return;
   }
-  __syncthreads();
   float* my = part + (((size_t)t * kKvHeads + g) * max_chunks + c) * kGroups * kPartStride;
 #pragma unroll
-  for (int h = 0; h < kGroups; ++h) {
-    my[h * kPartStride + 2 + 2 * tid] = acc[h][0];
-    my[h * kPartStride + 3 + 2 * tid] = acc[h][1];
-    if (tid == 0) {
-      my[h * kPartStride + 0] = ms[h];
-      my[h * kPartStride + 1] = ls[h];
-    }
+  for (int h = 0; h < kGroups; ++h) my[h * kPartStride + 2 + tid] = acc[h];
+  if (tid < kGroups) {
+    my[tid * kPartStride + 0] = sm.ms[tid];
+    my[tid * kPartStride + 1] = sm.ls[tid];
   }
   __threadfence();
   __syncthreads();
   if (tid == 0) {
     const unsigned prev = atomicAdd(&counters[t * kKvHeads + g], 1u);
-    last = (prev == (unsigned)nchunks - 1u);
+    sm.last = (prev == (unsigned)nchunks - 1u);
   }
   __syncthreads();
-  if (!last) return;
+  if (!sm.last) return;
   __threadfence();
-  // merge the chunks of this (token, KV head) in chunk order
+  // Merge this (token, KV head)'s chunks in chunk order (deterministic). The per-chunk statistics go
+  // through shared memory (reusing the score buffer: up to kChunk chunks per pass), so every thread's
+  // accumulator loads are independent and stay in flight together.
   const float* base = part + ((size_t)t * kKvHeads + g) * max_chunks * kGroups * kPartStride;
+  float o[kGroups], Lsum[kGroups], M[kGroups];
 #pragma unroll
   for (int h = 0; h < kGroups; ++h) {
-    float M = -INFINITY;
-    for (int cc = 0; cc < nchunks; ++cc) M = fmaxf(M, __ldcg(&base[(cc * kGroups + h) * kPartStride]));
-    float Lsum = 0.0f, o0 = 0.0f, o1 = 0.0f;
-    for (int cc = 0; cc < nchunks; ++cc) {
-      const float* pc = base + (cc * kGroups + h) * kPartStride;
-      const float w = expf(__ldcg(&pc[0]) - M);
-      Lsum = fmaf(__ldcg(&pc[1]), w, Lsum);
-      o0 = fmaf(__ldcg(&pc[2 + 2 * tid]), w, o0);
-      o1 = fmaf(__ldcg(&pc[3 + 2 * tid]), w, o1);
+    o[h] = 0.f;
+    Lsum[h] = 0.f;
+    M[h] = -INFINITY;
+  }
+  for (int cc = 0; cc < nchunks; ++cc) {  // global max per head (the m values are tiny and cached)
+#pragma unroll
+    for (int h = 0; h < kGroups; ++h) M[h] = fmaxf(M[h], __ldcg(&base[(cc * kGroups + h) * kPartStride]));
+  }
+  for (int c0 = 0; c0 < nchunks; c0 += kChunk) {
+    const int cn = min(kChunk, nchunks - c0);
+    __syncthreads();
+    for (int i = tid; i < cn * kGroups; i += kAttnThreads) {
+      const int cc = i / kGroups, h = i % kGroups;
+      const float* pc = base + ((c0 + cc) * kGroups + h) * kPartStride;
+      const float w = expf(__ldcg(&pc[0]) - M[h]);
+      sm.es[cc][h] = w;
+      sm.vs[cc][h] = __ldcg(&pc[1]) * w;
     }
-    const float inv = Lsum > 0.0f ? 1.0f / Lsum : 0.0f;
-    float* out = ctx + (size_t)t * kHidden + (g * kGroups + h) * kHeadDim + 2 * tid;
-    out[0] = o0 * inv;
-    out[1] = o1 * inv;
+    __syncthreads();
+#pragma unroll 4
+    for (int cc = 0; cc < cn; ++cc) {
+      const float* pc = base + (size_t)(c0 + cc) * kGroups * kPartStride + 2 + tid;
+#pragma unroll
+      for (int h = 0; h < kGroups; ++h) {
+        o[h] = fmaf(__ldcg(&pc[h * kPartStride]), sm.es[cc][h], o[h]);
+        Lsum[h] += sm.vs[cc][h];
+      }
+    }
+  }
+#pragma unroll
+  for (int h = 0; h < kGroups; ++h) {
+    const float inv = Lsum[h] > 0.0f ? 1.0f / Lsum[h] : 0.0f;
+    out_base[h * kHeadDim] = o[h] * inv;
   }
   if (tid == 0) counters[t * kKvHeads + g] = 0u;
 }
@@ -257,10 +353,18 @@ size_t attn_partial_floats(int nt, int max_len) {
 }
 
 cudaError_t launch_decode_attention(const float* q, KvView kv, DecodeTokens tok, int max_len, float* ctx,
-                                    float* scratch, unsigned* counters, cudaStream_t s, bool pdl) {
+                                    float* scratch, unsigned* counters, cudaStream_t s, bool pdl,
+                                    const void* prefetch, size_t prefetch_bytes) {
   const int max_chunks = (max_len + kChunk - 1) / kChunk;
-  return launch_k(decode_attn_kernel, dim3(max_chunks, kKvHeads, tok.nt), dim3(64), 0, s, pdl, q, kv, tok,
-                  max_chunks, ctx, scratch, counters);
+  const size_t smem = sizeof(DecodeAttnSmem);
+  static bool attr_set = false;
+  if (!attr_set) {
+    cudaError_t e = cudaFuncSetAttribute(decode_attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+    attr_set = true;
+  }
+  return launch_k(decode_attn_kernel, dim3(max_chunks, kKvHeads, tok.nt), dim3(kAttnThreads), smem, s, pdl, q, kv,
+                  tok, max_chunks, ctx, scratch, counters, static_cast<const uint8_t*>(prefetch), prefetch_bytes);
 }
 
 cudaError_t launch_prefill_attention(const float* q, const float* k_cache, const float* v_cache, int S, float* ctx,

@@ -3,34 +3,31 @@
 // Reference computation (`project_tiled`, hls/decode_only/qwen_decode_attention_kernel.cpp:62-98 and
 // hls/decode_only/qwen_decode_mlp_kernel.cpp:44-77): y[o] = bias[o] + sum_i x[i] * (code(o,i) * scale[o]),
 // accumulated serially in fp32. Here the per-channel scale is applied once in the epilogue,
-// y[o] = bias[o] + scale[o] * sum_i x[i] * code(o,i), and the sum is split across lanes and warps
-// (fp32 FMA). The reorder changes results by rounding only (relative ~1e-7).
+// y[o] = bias[o] + scale[o] * sum_i x[i] * code(o,i), and the sum is split across lanes (fp32 FMA). The
+// reorder changes results by rounding only (relative ~1e-7).
 //
-// Layout of the work: a warp owns R weight rows ("row group") and walks them in 16-byte chunks, lane l
-// taking chunks l, l+32, ... (128-bit, L1-bypassing loads; the next chunk is loaded before the current
-// one is consumed). KSPLIT warps may share one row group, each taking a contiguous slice of chunks, and
-// reduce through shared memory. Activations for all NT tokens are staged once per CTA in shared memory,
-// swizzled so that the per-lane float4 reads of a chunk are bank-conflict free; RMSNorm (decode form:
-// double-precision sum of squares, hls/decode_only/qwen_decode_attention_kernel.cpp:13-27) and the
-// embedding gather are fused into that staging step. Integer codes become floats with the 2^23
-// magic-number trick (byte permute + one FADD), exact for int8 and int4.
+// Structure (one persistent CTA per SM): a producer warp streams the weight rows of 8-row work units into
+// a ring of shared-memory stages with cp.async.bulk copies completing on mbarriers, starting before the
+// kernel waits for its predecessor (weights do not depend on it), so HBM is busy from the first cycle.
+// Eight consumer warps take one row each: lane l multiplies 16-byte chunks l, l+32, ... of its row slice
+// with the activations (staged once per CTA in shared memory, swizzled for conflict-free float4 reads;
+// RMSNorm in the decode form -- double sum of squares, hls/decode_only/qwen_decode_attention_kernel.cpp:13-27
+// -- and the embedding gather are fused into that staging), then reduces with warp shuffles. Row results
+// meet in shared memory for the pairwise epilogues (RoPE pairs p/p+64, SiLU(gate) * up). Integer codes
+// become floats with the 2^23 magic-number trick (byte permute + one FADD), exact for int8 and int4.
 #include <cuda_fp16.h>
 
 #include "qwen_kernels.cuh"
+#include "sm100_async.cuh"
 
 namespace qb {
 namespace {
 
-constexpr int kThreads = 256;
-constexpr int kWarps = kThreads / 32;
-
-__device__ __forceinline__ uint4 ldg_stream(const void* p) {
-  uint4 r;
-  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
-               : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
-               : "l"(p));
-  return r;
-}
+constexpr int kRows = 8;                   // rows per work unit = consumer warps
+constexpr int kConsumers = kRows * 32;     // consumer threads
+constexpr int kThreads = kConsumers + 32;  // + one producer warp
+constexpr int kBarConsumers = 1;           // named barrier id among consumer warps
+constexpr int kSmemTarget = 110 * 1024;    // stay below half an SM so the next kernel's CTA fits beside
 
 // float4 index swizzle inside one token's activation row in shared memory.
 __device__ __forceinline__ int swz(int f) { return f ^ ((f >> 3) & 7); }
@@ -45,8 +42,8 @@ __device__ __forceinline__ float byte_magic(uint32_t w, int k) {
 }
 
 // Multiply-accumulate one 16-byte chunk of one row into acc[t] (and acc_hi[t] for high int4 nibbles,
-// which carry a factor 16 removed after the reduction). xs points at this chunk's float4s for token 0;
-// tokens are `tstride` float4 apart.
+// which carry a factor 16 removed after the reduction). f0 is the chunk's first float4 index in the
+// activation row; tokens are `tstride` float4 apart.
 template <int WBITS, int NT>
 __device__ __forceinline__ void chunk_fma(const uint4 w, const float4* xs, int f0, int tstride, float (&acc)[NT],
                                           float (&acc_hi)[NT]) {
@@ -121,16 +118,22 @@ enum XMode { kXPlain = 0, kXNorm = 1, kXEmbedNorm = 2 };
 struct GemvArgs {
   const uint8_t* w;   // row-major codes (rows * K * WBITS / 8 bytes)
   int K;              // input length (1536 or 8960)
-  int ngroups;        // row groups
+  int nunits;         // 8-row work units
   int nt;             // tokens actually present (<= NT)
   const float* x;     // [nt][K] (kXPlain, kXNorm)
   const uint16_t* embed;
   const int* tokens;
   const float* norm_w;
+  const uint8_t* pf;  // optional L2 prefetch hint (next kernels' weights)
+  size_t pf_bytes;
+  int kb_bytes;       // bytes of one row per stage (a column block)
+  int nkb;            // column blocks per row
+  int nstages;        // ring depth
 };
 
 // Stage the activations of nt tokens into shared memory (swizzled), applying the decode RMSNorm when
 // asked: out = float((double)x * inv * (double)w), inv = 1 / sqrt(sum(double x^2) / 1536 + eps).
+// Run by the consumer warps only.
 template <int NT, int MODE>
 __device__ __forceinline__ void stage_x(const GemvArgs& a, float4* xs, double* red) {
   const int K4 = a.K / 4;
@@ -140,7 +143,7 @@ __device__ __forceinline__ void stage_x(const GemvArgs& a, float4* xs, double* r
   for (int t = 0; t < NT; ++t) {
     ss[t] = 0.0;
     if (t < a.nt) {
-      for (int i = tid; i < K4; i += kThreads) {
+      for (int i = tid; i < K4; i += kConsumers) {
         float4 v;
         if constexpr (MODE == kXEmbedNorm) {
           const uint2 h = *reinterpret_cast<const uint2*>(a.embed + (size_t)a.tokens[t] * kHidden + i * 4);
@@ -156,7 +159,7 @@ __device__ __forceinline__ void stage_x(const GemvArgs& a, float4* xs, double* r
         }
       }
     } else {
-      for (int i = tid; i < K4; i += kThreads) xs[t * K4 + swz(i)] = make_float4(0.f, 0.f, 0.f, 0.f);
+      for (int i = tid; i < K4; i += kConsumers) xs[t * K4 + swz(i)] = make_float4(0.f, 0.f, 0.f, 0.f);
     }
   }
   if constexpr (MODE != kXPlain) {
@@ -164,16 +167,16 @@ __device__ __forceinline__ void stage_x(const GemvArgs& a, float4* xs, double* r
 #pragma unroll
     for (int t = 0; t < NT; ++t) {
       const double v = warp_sum_d(ss[t]);
-      if (lane == 0) red[t * kWarps + warp] = v;
+      if (lane == 0) red[t * kRows + warp] = v;
     }
-    __syncthreads();
+    named_sync(kBarConsumers, kConsumers);
 #pragma unroll
     for (int t = 0; t < NT; ++t) {
       double tot = 0.0;
-      for (int w = 0; w < kWarps; ++w) tot += red[t * kWarps + w];
+      for (int w = 0; w < kRows; ++w) tot += red[t * kRows + w];
       const double inv = 1.0 / sqrt(tot / (double)kHidden + (double)kEps);
       if (t < a.nt) {
-        for (int i = tid; i < K4; i += kThreads) {
+        for (int i = tid; i < K4; i += kConsumers) {
           float4 v = xs[t * K4 + swz(i)];
           const float4 w = reinterpret_cast<const float4*>(a.norm_w)[i];
           v.x = (float)((double)v.x * inv * (double)w.x);
@@ -187,110 +190,134 @@ __device__ __forceinline__ void stage_x(const GemvArgs& a, float4* xs, double* r
   }
 }
 
-template <int WBITS, int NT, int R, int KSPLIT, int MODE, class Epi>
-__global__ void __launch_bounds__(kThreads) gemv_kernel(GemvArgs a, Epi epi) {
-  extern __shared__ float4 smem[];
-  float4* xs = smem;
-  float* red = reinterpret_cast<float*>(xs + (size_t)NT * (a.K / 4));
-  __shared__ double nred[NT * kWarps];
+template <int WBITS, int NT, int MODE, class Epi>
+__global__ void __launch_bounds__(kThreads, 1) gemv_kernel(GemvArgs a, Epi epi) {
+  extern __shared__ __align__(128) unsigned char smem[];
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem);
+  uint64_t* empty = full + a.nstages;
+  float4* xs = reinterpret_cast<float4*>(smem + 256);
+  const int K4 = a.K / 4;
+  uint8_t* stages = reinterpret_cast<uint8_t*>(xs + (size_t)NT * K4);
+  float* red = reinterpret_cast<float*>(stages + (size_t)a.nstages * kRows * a.kb_bytes);
+  __shared__ double nred[NT * kRows];
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const size_t row_bytes = (size_t)a.K * WBITS / 8;
 
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < a.nstages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], kRows);
+    }
+    mbar_fence_init();
+  }
+  __syncthreads();
+
+  if (warp == kRows) {
+    // ---- producer warp: weights are independent of the preceding kernel, so no grid-dependency wait.
+    if (a.pf != nullptr && a.pf_bytes != 0) {
+      const size_t per = ((a.pf_bytes + gridDim.x - 1) / gridDim.x + 15) & ~size_t(15);
+      const size_t b0 = (size_t)blockIdx.x * per, b1 = min(a.pf_bytes, b0 + per);
+      for (size_t off = b0 + (size_t)lane * 32768; off < b1; off += 32 * 32768)
+        prefetch_l2(a.pf + off, (unsigned)min((size_t)32768, b1 - off));
+    }
+    if (lane == 0) {
+      int s = 0;
+      unsigned ph = 0;
+      const unsigned stage_tx = (unsigned)(kRows * a.kb_bytes);
+      bool ok = true;
+      for (int u = blockIdx.x; u < a.nunits && ok; u += gridDim.x) {
+        for (int kb = 0; kb < a.nkb; ++kb) {
+          if (!(ok = mbar_wait(&empty[s], ph ^ 1))) break;
+          mbar_arrive_expect_tx(&full[s], stage_tx);
+          uint8_t* dst = stages + (size_t)s * kRows * a.kb_bytes;
+#pragma unroll
+          for (int r = 0; r < kRows; ++r)
+            bulk_g2s(dst + (size_t)r * a.kb_bytes, a.w + (size_t)epi.row(u, r) * row_bytes + (size_t)kb * a.kb_bytes,
+                     (unsigned)a.kb_bytes, &full[s]);
+          if (++s == a.nstages) {
+            s = 0;
+            ph ^= 1;
+          }
+        }
+      }
+      // every stage released by the consumers => no copy is still in flight when the CTA exits
+      for (int i = 0; i < a.nstages && ok; ++i) {
+        ok = mbar_wait(&empty[s], ph ^ 1);
+        if (++s == a.nstages) {
+          s = 0;
+          ph ^= 1;
+        }
+      }
+    }
+    return;
+  }
+
+  // ---- consumer warps
   griddep_wait();
   stage_x<NT, MODE>(a, xs, nred);
-  __syncthreads();
-  griddep_launch();
+  named_sync(kBarConsumers, kConsumers);
+  if (threadIdx.x == 0) griddep_launch();
 
-  constexpr int kGroupsPerCta = kWarps / KSPLIT;
-  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
-  const int gslot = warp / KSPLIT, part = warp % KSPLIT;
-  const int K4 = a.K / 4;
-  const size_t row_bytes = (size_t)a.K * WBITS / 8;
-  const int nchunks = (int)(row_bytes / 16);
-  const int cpp = (nchunks + KSPLIT - 1) / KSPLIT;
-  const int c0 = part * cpp;
-  const int c1 = min(nchunks, c0 + cpp);
+  const int kb_chunks = a.kb_bytes / 16;
   constexpr int kF4PerChunk = WBITS == 8 ? 4 : (WBITS == 4 ? 8 : 2);
-
-  for (int gbase = blockIdx.x * kGroupsPerCta; gbase < a.ngroups; gbase += gridDim.x * kGroupsPerCta) {
-    const int g = gbase + gslot;
-    float acc[R][NT], acch[R][NT];
+  int s = 0;
+  unsigned ph = 0;
+  int slot = 0;
+  bool dead = false;  // a bounded wait gave up: keep the barrier schedule, skip the work
+  for (int u = blockIdx.x; u < a.nunits; u += gridDim.x) {
+    const int row = epi.row(u, warp);
+    const typename Epi::Pre pre = epi.preload(row, lane);
+    float acc[NT], acch[NT];
 #pragma unroll
-    for (int r = 0; r < R; ++r)
-#pragma unroll
-      for (int t = 0; t < NT; ++t) acc[r][t] = acch[r][t] = 0.0f;
-
-    if (g < a.ngroups) {
-      const uint8_t* rowp[R];
-#pragma unroll
-      for (int r = 0; r < R; ++r) rowp[r] = a.w + (size_t)epi.row(g, r) * row_bytes;
-      int c = c0 + lane;
-      uint4 cur[R];
-      if (c < c1) {
-#pragma unroll
-        for (int r = 0; r < R; ++r) cur[r] = ldg_stream(rowp[r] + (size_t)c * 16);
+    for (int t = 0; t < NT; ++t) acc[t] = acch[t] = 0.0f;
+    for (int kb = 0; kb < a.nkb; ++kb) {
+      if (!dead && !mbar_wait(&full[s], ph)) dead = true;
+      if (!dead) {
+        const uint4* srow = reinterpret_cast<const uint4*>(stages + ((size_t)s * kRows + warp) * a.kb_bytes);
+        const int fbase = kb * kb_chunks * kF4PerChunk;
+        for (int c = lane; c < kb_chunks; c += 32)
+          chunk_fma<WBITS, NT>(srow[c], xs, fbase + c * kF4PerChunk, K4, acc, acch);
       }
-      for (; c < c1; c += 32) {
-        uint4 nxt[R];
-        const int cn = c + 32;
-        if (cn < c1) {
-#pragma unroll
-          for (int r = 0; r < R; ++r) nxt[r] = ldg_stream(rowp[r] + (size_t)cn * 16);
-        }
-#pragma unroll
-        for (int r = 0; r < R; ++r) chunk_fma<WBITS, NT>(cur[r], xs, c * kF4PerChunk, K4, acc[r], acch[r]);
-#pragma unroll
-        for (int r = 0; r < R; ++r) cur[r] = nxt[r];
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[s]);
+      if (++s == a.nstages) {
+        s = 0;
+        ph ^= 1;
       }
     }
-
-    float v[R][NT];
+    float v[NT];
 #pragma unroll
-    for (int r = 0; r < R; ++r)
-#pragma unroll
-      for (int t = 0; t < NT; ++t) {
-        const float s = WBITS == 4 ? fmaf(acch[r][t], 0.0625f, acc[r][t]) : acc[r][t];
-        v[r][t] = warp_sum(s);
-      }
-
-    if constexpr (KSPLIT == 1) {
-      if (g < a.ngroups && lane == 0) epi.finish(g, v, a.nt);
-    } else {
-      float* slot = red + ((size_t)gslot * KSPLIT + part) * (R * NT);
-      if (lane == 0) {
-#pragma unroll
-        for (int r = 0; r < R; ++r)
-#pragma unroll
-          for (int t = 0; t < NT; ++t) slot[r * NT + t] = v[r][t];
-      }
-      __syncthreads();
-      if (part == 0 && lane == 0 && g < a.ngroups) {
-        const float* base = red + (size_t)gslot * KSPLIT * (R * NT);
-#pragma unroll
-        for (int r = 0; r < R; ++r)
-#pragma unroll
-          for (int t = 0; t < NT; ++t) {
-            float s = 0.0f;
-            for (int p = 0; p < KSPLIT; ++p) s += base[p * R * NT + r * NT + t];
-            v[r][t] = s;
-          }
-        epi.finish(g, v, a.nt);
-      }
-      __syncthreads();
+    for (int t = 0; t < NT; ++t) v[t] = warp_sum(WBITS == 4 ? fmaf(acch[t], 0.0625f, acc[t]) : acc[t]);
+    float* rs = red + (size_t)slot * kRows * NT;
+    epi.row_done(u, warp, lane, row, pre, v, rs, a.nt);
+    if (Epi::kPairs) {
+      named_sync(kBarConsumers, kConsumers);
+      epi.pair_done(u, warp, lane, row, rs, a.nt);
     }
+    slot ^= 1;
   }
   epi.cta_end(a.nt);
 }
 
 // ------------------------------------------------------------------------------------------------
-// epilogues
+// epilogues: row(u, w) maps work unit u and consumer warp w to a weight row; row_done() runs in every
+// consumer warp (lanes < nt, one token each) once its row is reduced; pair_done() runs after all eight
+// rows of the unit are in shared memory (Epi::kPairs).
 // ------------------------------------------------------------------------------------------------
+struct NoPre {};
+
 struct EpiBase {
-  __device__ void cta_end(int) {}
+  __device__ void cta_end(int) const {}
 };
 
 // q | k | v rows with bias; RoPE on q and k heads (rotate-half pairs p, p+64); K and V rows go to the
-// cache at the token's position (qwen_decode_attention_kernel.cpp:100-111, 202-213). Row group g = one
-// (head, pair) with rows {h*128 + p, h*128 + p + 64}.
+// cache at the token's position (qwen_decode_attention_kernel.cpp:100-111, 202-213). Unit u = 4 pairs of
+// one head: warp w holds row h*128 + p0 + (w >> 1) + 64 * (w & 1).
 struct EpiQkv : EpiBase {
+  static constexpr bool kPairs = true;
+  struct Pre {
+    float bias, scale;
+  };
   const float* bias;
   const float* scale;
   const float* cosv;  // [pos][64]
@@ -298,178 +325,189 @@ struct EpiQkv : EpiBase {
   float* q_out;
   KvView kv;
   DecodeTokens tok;
-  __device__ int row(int g, int r) const { return (g >> 6) * kHeadDim + (g & 63) + r * 64; }
+  __device__ int row(int u, int w) const { return (u >> 4) * kHeadDim + (u & 15) * 4 + (w >> 1) + (w & 1) * 64; }
+  __device__ Pre preload(int r, int lane) const { return lane < kGemvMaxTokens ? Pre{bias[r], scale[r]} : Pre{0.f, 0.f}; }
   template <int NT>
-  __device__ void finish(int g, const float (&v)[2][NT], int nt) const {
-    const int h = g >> 6, p = g & 63;
-    const int re = h * kHeadDim + p, ro = re + 64;
+  __device__ void row_done(int, int w, int lane, int, const Pre& p, const float (&v)[NT], float* rs, int nt) const {
 #pragma unroll
-    for (int t = 0; t < NT; ++t) {
-      if (t >= nt) break;
-      float ye = bias[re] + scale[re] * v[0][t];
-      float yo = bias[ro] + scale[ro] * v[1][t];
-      const int pos = tok.pos[t];
-      if (h < kHeads + kKvHeads) {
-        const float c = cosv[(size_t)pos * 64 + p], s = sinv[(size_t)pos * 64 + p];
-        const float ne = __fsub_rn(__fmul_rn(ye, c), __fmul_rn(yo, s));
-        const float no = __fadd_rn(__fmul_rn(yo, c), __fmul_rn(ye, s));
-        ye = ne;
-        yo = no;
-      }
-      if (h < kHeads) {
-        q_out[(size_t)t * kHidden + re] = ye;
-        q_out[(size_t)t * kHidden + ro] = yo;
-      } else {
-        const int which = h < kHeads + kKvHeads ? 0 : 1;
-        float* dst = kv_row(kv, tok.seq[t], pos, which);
-        const int base = re - kHidden - which * kKvWidth;
-        dst[base] = ye;
-        dst[base + 64] = yo;
-      }
-    }
+    for (int t = 0; t < NT; ++t)
+      if (lane == t && t < nt) rs[w * NT + t] = p.bias + p.scale * v[t];
   }
+  __device__ void pair_done(int u, int w, int lane, int r, const float* rs, int nt) const {
+    if (lane >= nt) return;
+    constexpr int NTS = kGemvMaxTokens;
+    (void)NTS;
+    const int t = lane;
+    const int h = r / kHeadDim;
+    const int ntok = nt;
+    (void)ntok;
+    const float mine = rs[w * stride_ + t];
+    const float other = rs[(w ^ 1) * stride_ + t];
+    float y = mine;
+    const int pos = tok.pos[t];
+    if (h < kHeads + kKvHeads) {
+      const int p = r % kHeadDim - (w & 1) * 64;
+      const float c = cosv[(size_t)pos * 64 + p], s = sinv[(size_t)pos * 64 + p];
+      y = (w & 1) == 0 ? __fsub_rn(__fmul_rn(mine, c), __fmul_rn(other, s))
+                       : __fadd_rn(__fmul_rn(mine, c), __fmul_rn(other, s));
+    }
+    if (h < kHeads) {
+      q_out[(size_t)t * kHidden + r] = y;
+    } else {
+      const int which = h < kHeads + kKvHeads ? 0 : 1;
+      kv_row(kv, tok.seq[t], pos, which)[r - kHidden - which * kKvWidth] = y;
+    }
+    (void)u;
+  }
+  int stride_;  // tokens per row in the shared row buffer (= NT of the instantiation)
 };
 
 // y = scale * acc (o_proj: no bias, no residual, qwen_decode_attention_kernel.cpp:215).
-template <int R>
 struct EpiScale : EpiBase {
+  static constexpr bool kPairs = false;
+  struct Pre {
+    float scale;
+  };
   const float* scale;
   float* out;
   int n;  // output row length
-  __device__ int row(int g, int r) const { return g * R + r; }
+  __device__ int row(int u, int w) const { return u * kRows + w; }
+  __device__ Pre preload(int r, int lane) const { return lane < kGemvMaxTokens ? Pre{scale[r]} : Pre{0.f}; }
   template <int NT>
-  __device__ void finish(int g, const float (&v)[R][NT], int nt) const {
+  __device__ void row_done(int, int, int lane, int r, const Pre& p, const float (&v)[NT], float*, int nt) const {
 #pragma unroll
-    for (int r = 0; r < R; ++r) {
-      const int o = g * R + r;
-#pragma unroll
-      for (int t = 0; t < NT; ++t)
-        if (t < nt) out[(size_t)t * n + o] = scale[o] * v[r][t];
-    }
+    for (int t = 0; t < NT; ++t)
+      if (lane == t && t < nt) out[(size_t)t * n + r] = p.scale * v[t];
   }
+  __device__ void pair_done(int, int, int, int, const float*, int) const {}
 };
 
 // h[j] = silu(gate[j]) * up[j] with silu(v) = v / (1 + expf(-v)) (qwen_decode_mlp_kernel.cpp:79-81,
-// 113-115). Row group g covers j = 2g, 2g+1: rows {j, 8960 + j, j + 1, 8960 + j + 1}.
+// 113-115). Unit u covers j = 4u .. 4u+3: warp w holds gate row (w even) or up row (w odd) of j = 4u + w/2.
 struct EpiGateUp : EpiBase {
+  static constexpr bool kPairs = true;
+  struct Pre {
+    float scale;
+  };
   const float* scale;  // gate | up scales
   float* h;
-  __device__ int row(int g, int r) const { return 2 * g + (r >> 1) + (r & 1) * kInter; }
+  int stride_;
+  __device__ int row(int u, int w) const { return 4 * u + (w >> 1) + (w & 1) * kInter; }
+  __device__ Pre preload(int r, int lane) const { return lane < kGemvMaxTokens ? Pre{scale[r]} : Pre{0.f}; }
   template <int NT>
-  __device__ void finish(int g, const float (&v)[4][NT], int nt) const {
+  __device__ void row_done(int, int w, int lane, int, const Pre& p, const float (&v)[NT], float* rs, int nt) const {
 #pragma unroll
-    for (int jj = 0; jj < 2; ++jj) {
-      const int j = 2 * g + jj;
-#pragma unroll
-      for (int t = 0; t < NT; ++t) {
-        if (t >= nt) break;
-        const float gv = scale[j] * v[2 * jj][t];
-        const float uv = scale[kInter + j] * v[2 * jj + 1][t];
-        const float silu = __fdiv_rn(gv, __fadd_rn(1.0f, expf(-gv)));
-        h[(size_t)t * kInter + j] = __fmul_rn(silu, uv);
-      }
-    }
+    for (int t = 0; t < NT; ++t)
+      if (lane == t && t < nt) rs[w * NT + t] = p.scale * v[t];
+  }
+  __device__ void pair_done(int u, int w, int lane, int, const float* rs, int nt) const {
+    if ((w & 1) || lane >= nt) return;
+    const int t = lane;
+    const float gv = rs[w * stride_ + t];
+    const float uv = rs[(w + 1) * stride_ + t];
+    const float silu = __fdiv_rn(gv, __fadd_rn(1.0f, expf(-gv)));
+    h[(size_t)t * kInter + 4 * u + (w >> 1)] = __fmul_rn(silu, uv);
   }
 };
 
 // out = a + scale * acc (qwen_decode_mlp_kernel.cpp:116-119), optionally rounded to bf16 for the next
 // layer (the caller's rounding, verification/real_host_top_backend.py:334).
-template <int R>
 struct EpiDown : EpiBase {
+  static constexpr bool kPairs = false;
+  struct Pre {
+    float scale, resid[kGemvMaxTokens];
+  };
   const float* scale;
   const float* a;
   float* out;
   bool round_out;
-  __device__ int row(int g, int r) const { return g * R + r; }
+  int nt_;
+  __device__ int row(int u, int w) const { return u * kRows + w; }
+  __device__ Pre preload(int r, int lane) const {
+    Pre p{};
+    if (lane < nt_) {
+      p.scale = scale[r];
+      p.resid[0] = a[(size_t)lane * kHidden + r];
+    }
+    return p;
+  }
   template <int NT>
-  __device__ void finish(int g, const float (&v)[R][NT], int nt) const {
+  __device__ void row_done(int, int, int lane, int r, const Pre& p, const float (&v)[NT], float*, int nt) const {
 #pragma unroll
-    for (int r = 0; r < R; ++r) {
-      const int o = g * R + r;
-#pragma unroll
-      for (int t = 0; t < NT; ++t) {
-        if (t >= nt) break;
-        float y = __fadd_rn(a[(size_t)t * kHidden + o], scale[o] * v[r][t]);
+    for (int t = 0; t < NT; ++t) {
+      if (lane == t && t < nt) {
+        float y = __fadd_rn(p.resid[0], p.scale * v[t]);
         if (round_out) y = round_bf16(y);
-        out[(size_t)t * kHidden + o] = y;
+        out[(size_t)t * kHidden + r] = y;
       }
     }
   }
+  __device__ void pair_done(int, int, int, int, const float*, int) const {}
 };
 
-// Greedy LM head: logits[v] = E[v] . y, argmax with the lowest index winning ties. Each warp keeps its
-// best per token; the CTA reduces them into `partial`, and the last CTA to finish reduces all CTAs.
-template <int R, int NT>
+// Greedy LM head: logits[v] = E[v] . y, argmax with the lowest index winning ties. Lane t of each warp keeps
+// token t's best over the warp's rows; the CTA reduces them into `partial`, and the last CTA to finish
+// reduces all CTAs.
 struct EpiLm {
+  static constexpr bool kPairs = false;
+  struct Pre {};
   float* logits;  // optional
-  float* partial; // [gridDim][NT][2]
+  float* partial; // [gridDim][kGemvMaxTokens][2]
   unsigned* counter;
   int* next_token;
-  // per-lane-0 running best (lives in registers of the calling thread)
-  mutable float best_v[NT];
-  mutable int best_i[NT];
-  __device__ int row(int g, int r) const { return g * R + r; }
-  __device__ void init() const {
+  mutable float best_v;
+  mutable int best_i;
+  __device__ int row(int u, int w) const { return u * kRows + w; }
+  __device__ Pre preload(int, int) const { return Pre{}; }
+  template <int NT>
+  __device__ void row_done(int, int, int lane, int r, const Pre&, const float (&v)[NT], float*, int nt) const {
 #pragma unroll
     for (int t = 0; t < NT; ++t) {
-      best_v[t] = -INFINITY;
-      best_i[t] = 0x7fffffff;
-    }
-  }
-  template <int NT2>
-  __device__ void finish(int g, const float (&v)[R][NT2], int nt) const {
-#pragma unroll
-    for (int r = 0; r < R; ++r) {
-      const int o = g * R + r;
-#pragma unroll
-      for (int t = 0; t < NT; ++t) {
-        if (t >= nt) break;
-        if (logits) logits[(size_t)t * kVocab + o] = v[r][t];
-        if (v[r][t] > best_v[t] || (v[r][t] == best_v[t] && o < best_i[t])) {
-          best_v[t] = v[r][t];
-          best_i[t] = o;
+      if (lane == t && t < nt) {
+        if (logits) logits[(size_t)t * kVocab + r] = v[t];
+        if (v[t] > best_v || (v[t] == best_v && r < best_i)) {
+          best_v = v[t];
+          best_i = r;
         }
       }
     }
   }
+  __device__ void pair_done(int, int, int, int, const float*, int) const {}
   __device__ void cta_end(int nt) const {
-    __shared__ float sv[kWarps][NT];
-    __shared__ int si[kWarps][NT];
+    __shared__ float sv[kRows][kGemvMaxTokens];
+    __shared__ int si[kRows][kGemvMaxTokens];
     __shared__ bool last;
     const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
-    if (lane == 0) {
-#pragma unroll
-      for (int t = 0; t < NT; ++t) {
-        sv[warp][t] = best_v[t];
-        si[warp][t] = best_i[t];
-      }
+    if (lane < kGemvMaxTokens) {
+      sv[warp][lane] = best_v;
+      si[warp][lane] = best_i;
     }
-    __syncthreads();
+    named_sync(kBarConsumers, kConsumers);
     if (threadIdx.x == 0) {
       for (int t = 0; t < nt; ++t) {
         float bv = -INFINITY;
         int bi = 0x7fffffff;
-        for (int w = 0; w < kWarps; ++w)
+        for (int w = 0; w < kRows; ++w)
           if (sv[w][t] > bv || (sv[w][t] == bv && si[w][t] < bi)) {
             bv = sv[w][t];
             bi = si[w][t];
           }
-        partial[((size_t)blockIdx.x * NT + t) * 2] = bv;
-        partial[((size_t)blockIdx.x * NT + t) * 2 + 1] = __int_as_float(bi);
+        partial[((size_t)blockIdx.x * kGemvMaxTokens + t) * 2] = bv;
+        partial[((size_t)blockIdx.x * kGemvMaxTokens + t) * 2 + 1] = __int_as_float(bi);
       }
       __threadfence();
       const unsigned prev = atomicAdd(counter, 1u);
       last = (prev == gridDim.x - 1);
     }
-    __syncthreads();
+    named_sync(kBarConsumers, kConsumers);
     if (last && threadIdx.x == 0) {
       __threadfence();
       for (int t = 0; t < nt; ++t) {
         float bv = -INFINITY;
         int bi = 0x7fffffff;
         for (unsigned b = 0; b < gridDim.x; ++b) {
-          const float pv = __ldcg(&partial[((size_t)b * NT + t) * 2]);
-          const int pi = __float_as_int(__ldcg(&partial[((size_t)b * NT + t) * 2 + 1]));
+          const float pv = __ldcg(&partial[((size_t)b * kGemvMaxTokens + t) * 2]);
+          const int pi = __float_as_int(__ldcg(&partial[((size_t)b * kGemvMaxTokens + t) * 2 + 1]));
           if (pv > bv || (pv == bv && pi < bi)) {
             bv = pv;
             bi = pi;
@@ -482,17 +520,6 @@ struct EpiLm {
   }
 };
 
-template <int WBITS, int NT, int R, int KSPLIT, int MODE, class Epi>
-cudaError_t run_gemv(const GemvArgs& a, const Epi& epi, int grid, cudaStream_t s, bool pdl) {
-  const size_t smem = (size_t)NT * a.K * sizeof(float) + (KSPLIT > 1 ? (size_t)kWarps * R * NT * sizeof(float) : 0);
-  auto kern = gemv_kernel<WBITS, NT, R, KSPLIT, MODE, Epi>;
-  if (smem > 48 * 1024) {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    if (e != cudaSuccess) return e;
-  }
-  return launch_k(kern, dim3(grid), dim3(kThreads), smem, s, pdl, a, epi);
-}
-
 int num_sms() {
   static int n = 0;
   if (n == 0) {
@@ -504,38 +531,68 @@ int num_sms() {
   return n;
 }
 
-int grid_for(int ngroups, int groups_per_cta, int max_ctas) {
-  const int need = (ngroups + groups_per_cta - 1) / groups_per_cta;
-  return need < max_ctas ? need : max_ctas;
+// Stage geometry: a row is split into column blocks of at most 4 KB so that a stage (8 rows) stays small;
+// ring depth fills the shared-memory target (at least 2 stages).
+void plan_stages(GemvArgs& a, int wbits, int nt_alloc) {
+  const int row_bytes = a.K * wbits / 8;
+  int nkb = 1;
+  while (row_bytes / nkb > 4096 || (row_bytes % nkb) != 0 || ((row_bytes / nkb) % 16) != 0) ++nkb;
+  a.nkb = nkb;
+  a.kb_bytes = row_bytes / nkb;
+  const int x_bytes = nt_alloc * a.K * 4;
+  const int stage = kRows * a.kb_bytes;
+  int ns = (kSmemTarget - 256 - x_bytes - 2 * kRows * nt_alloc * 4) / stage;
+  if (ns < 2) ns = 2;
+  if (ns > 8) ns = 8;
+  a.nstages = ns;
 }
 
-// Dispatch on (wbits, nt) to compiled instances.
-template <int R, int KSPLIT, int MODE, class Epi, int NT>
-cudaError_t dispatch_wbits(int wbits, const GemvArgs& a, const Epi& e, int grid, cudaStream_t s, bool pdl) {
-  if (wbits == 8) return run_gemv<8, NT, R, KSPLIT, MODE>(a, e, grid, s, pdl);
-  if (wbits == 4) return run_gemv<4, NT, R, KSPLIT, MODE>(a, e, grid, s, pdl);
+template <int WBITS, int NT, int MODE, class Epi>
+cudaError_t run_gemv(GemvArgs a, const Epi& epi, cudaStream_t s, bool pdl) {
+  plan_stages(a, WBITS, NT);
+  const size_t smem = 256 + (size_t)NT * a.K * 4 + (size_t)a.nstages * kRows * a.kb_bytes + 2 * kRows * NT * 4;
+  auto kern = gemv_kernel<WBITS, NT, MODE, Epi>;
+  static size_t attr_bytes = 0;  // per instantiation: raise the dynamic shared-memory limit when needed
+  if (smem > attr_bytes) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+    attr_bytes = smem;
+  }
+  const int grid = a.nunits < num_sms() ? a.nunits : num_sms();
+  return launch_k(kern, dim3(grid), dim3(kThreads), smem, s, pdl, a, epi);
+}
+
+template <int MODE, class Epi, int NT>
+cudaError_t dispatch_wbits(int wbits, const GemvArgs& a, Epi e, cudaStream_t s, bool pdl) {
+  if (wbits == 8) return run_gemv<8, NT, MODE>(a, e, s, pdl);
+  if (wbits == 4) return run_gemv<4, NT, MODE>(a, e, s, pdl);
   return cudaErrorInvalidValue;
 }
 
-template <int R, int KSPLIT, int MODE, class Epi>
-cudaError_t dispatch(int wbits, const GemvArgs& a, const Epi& e, int grid, cudaStream_t s, bool pdl) {
+template <int MODE, class Epi>
+cudaError_t dispatch(int wbits, const GemvArgs& a, Epi e, cudaStream_t s, bool pdl) {
   switch (a.nt) {
-    case 1: return dispatch_wbits<R, KSPLIT, MODE, Epi, 1>(wbits, a, e, grid, s, pdl);
-    case 2: return dispatch_wbits<R, KSPLIT, MODE, Epi, 2>(wbits, a, e, grid, s, pdl);
+    case 1: return dispatch_wbits<MODE, Epi, 1>(wbits, a, e, s, pdl);
+    case 2: return dispatch_wbits<MODE, Epi, 2>(wbits, a, e, s, pdl);
     case 3:
-    case 4: return dispatch_wbits<R, KSPLIT, MODE, Epi, 4>(wbits, a, e, grid, s, pdl);
+    case 4: return dispatch_wbits<MODE, Epi, 4>(wbits, a, e, s, pdl);
     default: return cudaErrorInvalidValue;
   }
 }
 
+int nt_alloc(int nt) { return nt <= 2 ? nt : 4; }
+
 }  // namespace
 
 cudaError_t launch_decode_qkv(int wbits, const LayerDev& L, XSource src, DecodeTokens tok, const float* rope_cos,
-                              const float* rope_sin, float* q_out, KvView kv, cudaStream_t s, bool pdl) {
+                              const float* rope_sin, float* q_out, KvView kv, cudaStream_t s, bool pdl,
+                              const void* pf, size_t pf_bytes) {
   GemvArgs a{};
+  a.pf = static_cast<const uint8_t*>(pf);
+  a.pf_bytes = pf_bytes;
   a.w = L.qkv_w;
   a.K = kHidden;
-  a.ngroups = kQkvRows / 2;  // (head, pair) groups
+  a.nunits = kQkvRows / kRows;
   a.nt = tok.nt;
   a.x = src.x;
   a.embed = src.embed;
@@ -549,149 +606,103 @@ cudaError_t launch_decode_qkv(int wbits, const LayerDev& L, XSource src, DecodeT
   e.q_out = q_out;
   e.kv = kv;
   e.tok = tok;
-  const int grid = grid_for(a.ngroups, kWarps, 4 * num_sms());
-  if (src.x == nullptr) return dispatch<2, 1, kXEmbedNorm>(wbits, a, e, grid, s, pdl);
-  return dispatch<2, 1, kXNorm>(wbits, a, e, grid, s, pdl);
+  e.stride_ = nt_alloc(tok.nt);
+  if (src.x == nullptr) return dispatch<kXEmbedNorm>(wbits, a, e, s, pdl);
+  return dispatch<kXNorm>(wbits, a, e, s, pdl);
 }
 
 cudaError_t launch_decode_o(int wbits, const LayerDev& L, const float* ctx, int nt, float* out, cudaStream_t s,
-                            bool pdl) {
+                            bool pdl, const void* pf, size_t pf_bytes) {
   GemvArgs a{};
+  a.pf = static_cast<const uint8_t*>(pf);
+  a.pf_bytes = pf_bytes;
   a.w = L.o_w;
   a.K = kHidden;
-  a.ngroups = kHidden / 2;
+  a.nunits = kHidden / kRows;
   a.nt = nt;
   a.x = ctx;
-  EpiScale<2> e;
+  EpiScale e;
   e.scale = L.o_s;
   e.out = out;
   e.n = kHidden;
-  const int grid = grid_for(a.ngroups, kWarps / 2, 4 * num_sms());
-  return dispatch<2, 2, kXPlain>(wbits, a, e, grid, s, pdl);
+  return dispatch<kXPlain>(wbits, a, e, s, pdl);
 }
 
 cudaError_t launch_decode_gateup(int wbits, const LayerDev& L, const float* x, int nt, float* h, cudaStream_t s,
-                                 bool pdl) {
+                                 bool pdl, const void* pf, size_t pf_bytes) {
   GemvArgs a{};
+  a.pf = static_cast<const uint8_t*>(pf);
+  a.pf_bytes = pf_bytes;
   a.w = L.gu_w;
   a.K = kHidden;
-  a.ngroups = kInter / 2;
+  a.nunits = 2 * kInter / kRows;
   a.nt = nt;
   a.x = x;
   a.norm_w = L.post_ln;
   EpiGateUp e;
   e.scale = L.gu_s;
   e.h = h;
-  const int grid = grid_for(a.ngroups, kWarps, 4 * num_sms());
-  return dispatch<4, 1, kXNorm>(wbits, a, e, grid, s, pdl);
+  e.stride_ = nt_alloc(nt);
+  return dispatch<kXNorm>(wbits, a, e, s, pdl);
 }
 
 cudaError_t launch_decode_down(int wbits, const LayerDev& L, const float* h, const float* a_res, int nt, float* out,
-                               bool round_out, cudaStream_t s, bool pdl) {
+                               bool round_out, cudaStream_t s, bool pdl, const void* pf, size_t pf_bytes) {
   GemvArgs a{};
+  a.pf = static_cast<const uint8_t*>(pf);
+  a.pf_bytes = pf_bytes;
   a.w = L.down_w;
   a.K = kInter;
-  a.ngroups = kHidden / 4;
+  a.nunits = kHidden / kRows;
   a.nt = nt;
   a.x = h;
-  EpiDown<4> e;
+  EpiDown e;
   e.scale = L.down_s;
   e.a = a_res;
   e.out = out;
   e.round_out = round_out;
-  const int grid = grid_for(a.ngroups, 1, 4 * num_sms());
-  return dispatch<4, 8, kXPlain>(wbits, a, e, grid, s, pdl);
+  e.nt_ = nt;
+  return dispatch<kXPlain>(wbits, a, e, s, pdl);
 }
 
 namespace {
-constexpr int kLmR = 4;
-constexpr int kLmGrid = 4 * 148;
 template <int NT>
-__global__ void __launch_bounds__(kThreads) lm_head_kernel(GemvArgs a, EpiLm<kLmR, NT> epi) {
-  epi.init();
-  // Reuse the generic body through a thin wrapper: identical to gemv_kernel<16, NT, kLmR, 1, kXNorm>.
-  extern __shared__ float4 smem[];
-  float4* xs = smem;
-  __shared__ double nred[NT * kWarps];
-  griddep_wait();
-  stage_x<NT, kXNorm>(a, xs, nred);
-  __syncthreads();
-  griddep_launch();
-  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
-  const int K4 = a.K / 4;
-  const size_t row_bytes = (size_t)a.K * 2;
-  const int nchunks = (int)(row_bytes / 16);
-  for (int gbase = blockIdx.x * kWarps; gbase < a.ngroups; gbase += gridDim.x * kWarps) {
-    const int g = gbase + warp;
-    float acc[kLmR][NT], acch[kLmR][NT];
-#pragma unroll
-    for (int r = 0; r < kLmR; ++r)
-#pragma unroll
-      for (int t = 0; t < NT; ++t) acc[r][t] = acch[r][t] = 0.0f;
-    if (g < a.ngroups) {
-      const uint8_t* rowp[kLmR];
-#pragma unroll
-      for (int r = 0; r < kLmR; ++r) rowp[r] = a.w + (size_t)(g * kLmR + r) * row_bytes;
-      int c = lane;
-      uint4 cur[kLmR];
-#pragma unroll
-      for (int r = 0; r < kLmR; ++r) cur[r] = ldg_stream(rowp[r] + (size_t)c * 16);
-      for (; c < nchunks; c += 32) {
-        uint4 nxt[kLmR];
-        if (c + 32 < nchunks) {
-#pragma unroll
-          for (int r = 0; r < kLmR; ++r) nxt[r] = ldg_stream(rowp[r] + (size_t)(c + 32) * 16);
-        }
-#pragma unroll
-        for (int r = 0; r < kLmR; ++r) chunk_fma<16, NT>(cur[r], xs, c * 2, K4, acc[r], acch[r]);
-#pragma unroll
-        for (int r = 0; r < kLmR; ++r) cur[r] = nxt[r];
-      }
-    }
-    float v[kLmR][NT];
-#pragma unroll
-    for (int r = 0; r < kLmR; ++r)
-#pragma unroll
-      for (int t = 0; t < NT; ++t) v[r][t] = warp_sum(acc[r][t]);
-    if (g < a.ngroups && lane == 0) epi.finish(g, v, a.nt);
-  }
-  epi.cta_end(a.nt);
-}
-
-template <int NT>
-cudaError_t run_lm(const GemvArgs& a, const EpiLm<kLmR, NT>& e, cudaStream_t s, bool pdl) {
-  const size_t smem = (size_t)NT * a.K * sizeof(float);
-  return launch_k(lm_head_kernel<NT>, dim3(kLmGrid), dim3(kThreads), smem, s, pdl, a, e);
+cudaError_t run_lm(const GemvArgs& a, EpiLm e, cudaStream_t s, bool pdl) {
+  e.best_v = -INFINITY;
+  e.best_i = 0x7fffffff;
+  return run_gemv<16, NT, kXNorm>(a, e, s, pdl);
 }
 }  // namespace
 
-int lm_head_partial_floats() { return kLmGrid * kGemvMaxTokens * 2; }
+int lm_head_partial_floats() { return 1024 * kGemvMaxTokens * 2; }
 
 cudaError_t launch_lm_head_argmax(const uint16_t* embed, const float* norm_w, const float* x, int nt, float* logits,
                                   float* partial, unsigned* counter, int* next_token, cudaStream_t s, bool pdl) {
   GemvArgs a{};
   a.w = reinterpret_cast<const uint8_t*>(embed);
   a.K = kHidden;
-  a.ngroups = kVocab / kLmR;
+  a.nunits = kVocab / kRows;
   a.nt = nt;
   a.x = x;
   a.norm_w = norm_w;
+  EpiLm e{logits, partial, counter, next_token, -INFINITY, 0x7fffffff};
   switch (nt) {
-    case 1: {
-      EpiLm<kLmR, 1> e{logits, partial, counter, next_token};
-      return run_lm<1>(a, e, s, pdl);
-    }
-    case 2: {
-      EpiLm<kLmR, 2> e{logits, partial, counter, next_token};
-      return run_lm<2>(a, e, s, pdl);
-    }
+    case 1: return run_lm<1>(a, e, s, pdl);
+    case 2: return run_lm<2>(a, e, s, pdl);
     case 3:
-    case 4: {
-      EpiLm<kLmR, 4> e{logits, partial, counter, next_token};
-      return run_lm<4>(a, e, s, pdl);
-    }
+    case 4: return run_lm<4>(a, e, s, pdl);
     default: return cudaErrorInvalidValue;
   }
+}
+
+unsigned gemv_kernel_error(bool reset) {
+  unsigned v = 0;
+  if (cudaMemcpyFromSymbol(&v, g_kernel_error, sizeof(v)) != cudaSuccess) return 0xFFFFFFFFu;
+  if (reset && v) {
+    const unsigned z = 0;
+    cudaMemcpyToSymbol(g_kernel_error, &z, sizeof(z));
+  }
+  return v;
 }
 
 }  // namespace qb

@@ -17,6 +17,7 @@
 #include <vector>
 
 #include "../../include/qwen_b200_engine.h"
+#include "qgemm.h"
 #include "qwen_kernels.cuh"
 #include "runtime.h"
 
@@ -120,9 +121,13 @@ struct qwen_engine {
         *p_k = nullptr, *p_v = nullptr;
   int* p_tokens = nullptr;
   // options
-  bool use_graphs = true, use_pdl = true, dump_hidden = false, keep_logits = false;
+  bool use_graphs = true, use_pdl = true, dump_hidden = false, keep_logits = false, prefetch = true;
   std::map<long long, cudaGraphExec_t> graphs;
   std::vector<int> dev_slots;  // slots whose positions are current in d_pos / d_seq (decode_device path)
+  // int8 tensor-core projections (wbits == 8)
+  bool use_qgemm = true;
+  QgemmLayerMaps maps[kLayers];
+  QgemmScratch qsc{nullptr, nullptr};
 };
 
 namespace {
@@ -226,17 +231,42 @@ int enqueue_decode(qwen_engine* e, int nt, int max_len, bool advance) {
   const bool pdl = e->use_pdl;
   DecodeTokens tok{e->d_pos, e->d_seq, nt};
   float* xin = nullptr;
+  const uint64_t wb = (uint64_t)e->wbits;
+  const size_t o_bytes = (size_t)kHidden * kHidden * wb / 8;
+  const size_t gu_bytes = (size_t)2 * kInter * kHidden * wb / 8;
+  const size_t down_bytes = (size_t)kInter * kHidden * wb / 8;
+  const size_t qkv_bytes = (size_t)kQkvRows * kHidden * wb / 8;
+  const size_t lm_head_prefetch = (size_t)32 << 20;
   for (int l = 0; l < kLayers; ++l) {
     const LayerDev& L = e->layers[l];
     XSource src{xin, e->embed, e->d_tokens};
     KvView kv = paged_view(e, l);
-    E_TRY(launch_decode_qkv(e->wbits, L, src, tok, e->rope_dec_cos, e->rope_dec_sin, e->q, kv, e->stream,
-                            pdl && l > 0));
-    E_TRY(launch_decode_attention(e->q, kv, tok, max_len, e->ctx, e->attn_part, e->attn_cnt, e->stream, pdl));
-    E_TRY(launch_decode_o(e->wbits, L, e->ctx, nt, e->a, e->stream, pdl));
-    E_TRY(launch_decode_gateup(e->wbits, L, e->a, nt, e->h, e->stream, pdl));
+    // Each kernel streams the next kernels' weights into L2 while it runs (the weights are independent
+    // of the activations), so HBM stays busy through the latency-bound kernels and launch gaps.
+    const bool last = l + 1 == kLayers;
+    const void* next_qkv = last ? (const void*)e->embed : (const void*)e->layers[l + 1].qkv_w;
+    const size_t next_qkv_bytes = last ? lm_head_prefetch : qkv_bytes;
     float* yout = (l & 1) ? e->y1 : e->y0;
-    E_TRY(launch_decode_down(e->wbits, L, e->h, e->a, nt, yout, true, e->stream, pdl));
+    if (e->wbits == 8 && e->use_qgemm) {
+      // int8 tensor cores; each kernel's TMA producer starts streaming its weights before it waits
+      const QgemmLayerMaps& M = e->maps[l];
+      E_TRY(qgemm_qkv(M, L, src, tok, e->rope_dec_cos, e->rope_dec_sin, e->q, kv, e->qsc, e->stream, pdl && l > 0));
+      E_TRY(launch_decode_attention(e->q, kv, tok, max_len, e->ctx, e->attn_part, e->attn_cnt, e->stream, pdl,
+                                    e->prefetch ? L.gu_w : nullptr, gu_bytes));
+      E_TRY(qgemm_o(M, L, e->ctx, nt, e->a, e->qsc, e->stream, pdl));
+      E_TRY(qgemm_gateup(M, L, e->a, nt, e->h, e->qsc, e->stream, pdl));
+      E_TRY(qgemm_down(M, L, e->h, e->a, nt, yout, true, e->qsc, e->stream, pdl));
+    } else {
+      E_TRY(launch_decode_qkv(e->wbits, L, src, tok, e->rope_dec_cos, e->rope_dec_sin, e->q, kv, e->stream,
+                              pdl && l > 0, e->prefetch ? L.o_w : nullptr, o_bytes));
+      E_TRY(launch_decode_attention(e->q, kv, tok, max_len, e->ctx, e->attn_part, e->attn_cnt, e->stream, pdl,
+                                    e->prefetch ? L.gu_w : nullptr, gu_bytes));
+      E_TRY(launch_decode_o(e->wbits, L, e->ctx, nt, e->a, e->stream, pdl, e->prefetch ? L.down_w : nullptr,
+                            down_bytes));
+      E_TRY(launch_decode_gateup(e->wbits, L, e->a, nt, e->h, e->stream, pdl, e->prefetch ? next_qkv : nullptr,
+                                 next_qkv_bytes));
+      E_TRY(launch_decode_down(e->wbits, L, e->h, e->a, nt, yout, true, e->stream, pdl));
+    }
     if (e->dump_hidden) {
       E_TRY(cudaMemcpyAsync(e->dump + (size_t)l * nt * kHidden, yout, (size_t)nt * kHidden * 4,
                             cudaMemcpyDeviceToDevice, e->stream));
@@ -303,6 +333,17 @@ int qwen_engine_create(int device, int wbits, int max_seqs, int max_len, qwen_en
   E_TRY(dalloc(&e->simg, e->layer_bytes / 4 * kLayers));
   for (int l = 0; l < kLayers; ++l)
     e->layers[l] = layer_dev_from_ddr(e->wimg + e->layer_bytes * l, e->simg + e->layer_bytes / 4 * l, wbits);
+  if (wbits == 8) {
+    for (int l = 0; l < kLayers; ++l)
+      if (!qgemm_make_layer_maps(&e->maps[l], e->layers[l])) {
+        set_error("cuTensorMapEncodeTiled failed for layer %d", l);
+        return kStatusCuda;
+      }
+    E_TRY(dalloc(&e->qsc.acc, qgemm_acc_ints()));
+    E_TRY(dalloc(&e->qsc.cnt, qgemm_counter_count()));
+    E_TRY(cudaMemset(e->qsc.acc, 0, qgemm_acc_ints() * 4));
+    E_TRY(cudaMemset(e->qsc.cnt, 0, qgemm_counter_count() * 4));
+  }
   E_TRY(dalloc(&e->embed, (size_t)kVocab * kHidden));
   E_TRY(dalloc(&e->final_norm, (size_t)kHidden));
   e->n_pages = max_seqs * e->max_pages;
@@ -345,7 +386,8 @@ void qwen_engine_destroy(qwen_engine* e) {
   void* ptrs[] = {e->wimg, e->simg, e->embed, e->final_norm, e->kv_pool, e->d_page_table, e->d_tokens, e->d_pos,
                   e->d_seq, e->d_next, e->x, e->q, e->ctx, e->a, e->y0, e->y1, e->h, e->attn_part, e->attn_cnt,
                   e->lm_part, e->lm_cnt, e->dump, e->logits, e->rope_dec_cos, e->rope_dec_sin, e->rope_pre_cos,
-                  e->rope_pre_sin, e->p_x, e->p_xn, e->p_q, e->p_ctx, e->p_a, e->p_h, e->p_k, e->p_v, e->p_tokens};
+                  e->rope_pre_sin, e->p_x, e->p_xn, e->p_q, e->p_ctx, e->p_a, e->p_h, e->p_k, e->p_v, e->p_tokens,
+                  e->qsc.acc, e->qsc.cnt};
   for (void* p : ptrs) cudaFree(p);
   if (e->h_io) cudaFreeHost(e->h_io);
   if (e->stream) cudaStreamDestroy(e->stream);
@@ -387,6 +429,14 @@ int qwen_engine_set_option(qwen_engine* e, const char* name, long long value) {
   if (n == "graphs") e->use_graphs = value != 0;
   else if (n == "pdl") {
     e->use_pdl = value != 0;
+    for (auto& kv : e->graphs) cudaGraphExecDestroy(kv.second);
+    e->graphs.clear();
+  } else if (n == "prefetch") {
+    e->prefetch = value != 0;
+    for (auto& kv : e->graphs) cudaGraphExecDestroy(kv.second);
+    e->graphs.clear();
+  } else if (n == "qgemm") {
+    e->use_qgemm = value != 0;
     for (auto& kv : e->graphs) cudaGraphExecDestroy(kv.second);
     e->graphs.clear();
   } else if (n == "dump_hidden") e->dump_hidden = value != 0;
@@ -661,6 +711,16 @@ int qwen_engine_profile_kernels(qwen_engine* e, int n, int past, int iters, floa
     auto launch = [&](int l) -> cudaError_t {
       const LayerDev& L = e->layers[l];
       KvView kv = paged_view(e, l);
+      if (e->wbits == 8 && e->use_qgemm && kind != 1 && kind != 5) {
+        const QgemmLayerMaps& M = e->maps[l];
+        switch (kind) {
+          case 0: return qgemm_qkv(M, L, XSource{e->y0, e->embed, e->d_tokens}, tok, e->rope_dec_cos, e->rope_dec_sin,
+                                   e->q, kv, e->qsc, e->stream, false);
+          case 2: return qgemm_o(M, L, e->ctx, n, e->a, e->qsc, e->stream, false);
+          case 3: return qgemm_gateup(M, L, e->a, n, e->h, e->qsc, e->stream, false);
+          default: return qgemm_down(M, L, e->h, e->a, n, e->y1, true, e->qsc, e->stream, false);
+        }
+      }
       switch (kind) {
         case 0: return launch_decode_qkv(e->wbits, L, XSource{e->y0, e->embed, e->d_tokens}, tok, e->rope_dec_cos,
                                          e->rope_dec_sin, e->q, kv, e->stream, false);

@@ -4,6 +4,7 @@
 #include <mutex>
 
 #include "../../include/qwen_b200_ops.h"
+#include "qgemm.h"
 #include "qwen_kernels.cuh"
 #include "runtime.h"
 
@@ -17,6 +18,7 @@ struct OpScratch {
   size_t part_floats = 0;
   unsigned* counters = nullptr;  // 2 (one per KV head), zeroed at allocation
   int* tok = nullptr;            // [pos, seq]
+  QgemmScratch qsc{nullptr, nullptr};
 };
 
 std::mutex g_ops_mu;
@@ -84,6 +86,56 @@ extern "C" int qwen_b200_decode_attention(const float* q, const float* k_cache, 
   }
   if (e != cudaSuccess) {
     set_error("qwen_b200_decode_attention: %s", cudaGetErrorString(e));
+    return kStatusCuda;
+  }
+  return 0;
+}
+
+extern "C" int qwen_b200_w8_digit_products(const signed char* codes, int rows, int k, const float* x, int n_tokens,
+                                           int* acc, float* step, void* stream) {
+  using namespace qb;
+  if (!codes || !x || !acc || !step || rows <= 0 || rows % 128 || k <= 0 || k % 128 || n_tokens < 1 ||
+      n_tokens > 4 || (reinterpret_cast<uintptr_t>(codes) & 15)) {
+    set_error("qwen_b200_w8_digit_products: rows %d / k %d must be positive multiples of 128, n_tokens %d in 1..4, "
+              "codes 16-byte aligned",
+              rows, k, n_tokens);
+    return kStatusInvalid;
+  }
+  if (!device_accessible(codes) || !device_accessible(x) || !device_accessible(acc) || !device_accessible(step)) {
+    set_error("qwen_b200_w8_digit_products: every buffer must be device (or managed) memory");
+    return kStatusInvalid;
+  }
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) {
+    set_error("qwen_b200_w8_digit_products: no current CUDA device");
+    return kStatusNoDevice;
+  }
+  std::lock_guard<std::mutex> lock(g_ops_mu);
+  OpScratch& o = g_ops[dev];
+  cudaError_t e = cudaSuccess;
+  if (o.qsc.acc == nullptr) {
+    if ((e = cudaMalloc(&o.qsc.acc, qgemm_acc_ints() * sizeof(int))) == cudaSuccess &&
+        (e = cudaMalloc(&o.qsc.cnt, qgemm_counter_count() * sizeof(unsigned))) == cudaSuccess &&
+        (e = cudaMemset(o.qsc.acc, 0, qgemm_acc_ints() * sizeof(int))) == cudaSuccess)
+      e = cudaMemset(o.qsc.cnt, 0, qgemm_counter_count() * sizeof(unsigned));
+    if (e != cudaSuccess) {
+      cudaFree(o.qsc.acc);
+      cudaFree(o.qsc.cnt);
+      o.qsc = QgemmScratch{nullptr, nullptr};
+    }
+  }
+  QgemmMap map;
+  if (e == cudaSuccess && !qgemm_make_map(&map, reinterpret_cast<const uint8_t*>(codes), rows, k, 128)) {
+    set_error("qwen_b200_w8_digit_products: cuTensorMapEncodeTiled failed");
+    return kStatusCuda;
+  }
+  if (e == cudaSuccess) e = qgemm_raw(map, rows, k, x, n_tokens, acc, step, o.qsc, static_cast<cudaStream_t>(stream));
+  if (e == cudaErrorInvalidValue) {
+    set_error("qwen_b200_w8_digit_products: k %d needs more shared memory than one CTA has", k);
+    return kStatusInvalid;
+  }
+  if (e != cudaSuccess) {
+    set_error("qwen_b200_w8_digit_products: %s", cudaGetErrorString(e));
     return kStatusCuda;
   }
   return 0;

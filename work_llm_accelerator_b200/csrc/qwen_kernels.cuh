@@ -29,27 +29,35 @@ struct XSource {
 };
 
 // --- decode (batch 1..4), CUDA-core GEMV kernels --------------------------------------------------
+// `pf`/`pf_bytes` optionally name weights of following kernels to stream into L2 before the kernel
+// waits for its predecessor (programmatic dependent launch).
 // q_out [nt][1536]; K and V rows written at each token's position through `kv`.
 cudaError_t launch_decode_qkv(int wbits, const LayerDev& L, XSource src, DecodeTokens tok, const float* rope_cos,
-                              const float* rope_sin, float* q_out, KvView kv, cudaStream_t s, bool pdl);
+                              const float* rope_sin, float* q_out, KvView kv, cudaStream_t s, bool pdl,
+                              const void* pf = nullptr, size_t pf_bytes = 0);
 // out [nt][1536] = o_proj(ctx)
 cudaError_t launch_decode_o(int wbits, const LayerDev& L, const float* ctx, int nt, float* out, cudaStream_t s,
-                            bool pdl);
+                            bool pdl, const void* pf = nullptr, size_t pf_bytes = 0);
 // h [nt][8960] = silu(gate(norm(a))) * up(norm(a))
 cudaError_t launch_decode_gateup(int wbits, const LayerDev& L, const float* a, int nt, float* h, cudaStream_t s,
-                                 bool pdl);
+                                 bool pdl, const void* pf = nullptr, size_t pf_bytes = 0);
 // out [nt][1536] = a + down(h), optionally rounded to bf16 (RNE) for the next layer
 cudaError_t launch_decode_down(int wbits, const LayerDev& L, const float* h, const float* a, int nt, float* out,
-                               bool round_out, cudaStream_t s, bool pdl);
+                               bool round_out, cudaStream_t s, bool pdl, const void* pf = nullptr,
+                               size_t pf_bytes = 0);
 // next_token[t] = argmax_v (E[v] . rmsnorm(x[t]) ); logits optional [nt][vocab]
 cudaError_t launch_lm_head_argmax(const uint16_t* embed, const float* norm_w, const float* x, int nt, float* logits,
                                   float* partial, unsigned* counter, int* next_token, cudaStream_t s, bool pdl);
 int lm_head_partial_floats();  // size of the `partial` scratch in floats
+// Error flag of the streaming GEMV kernels (1 = a bounded mbarrier wait gave up); optionally cleared.
+unsigned gemv_kernel_error(bool reset);
 
 // --- decode attention (flash-decoding over 64-token chunks; combine by the last chunk CTA) -------
 // ctx [nt][1536]. scratch: attn_partial_floats(nt, max_len) floats; counters: nt * 2 uints (zeroed once).
+// `prefetch`/`prefetch_bytes` optionally name weights of the following kernels to stream into L2 meanwhile.
 cudaError_t launch_decode_attention(const float* q, KvView kv, DecodeTokens tok, int max_len, float* ctx,
-                                    float* scratch, unsigned* counters, cudaStream_t s, bool pdl);
+                                    float* scratch, unsigned* counters, cudaStream_t s, bool pdl,
+                                    const void* prefetch = nullptr, size_t prefetch_bytes = 0);
 size_t attn_partial_floats(int nt, int max_len);
 
 // --- prefill -------------------------------------------------------------------------------------

@@ -18,6 +18,7 @@
 #include <string>
 #include <vector>
 
+#include "qgemm.h"
 #include "qwen_kernels.cuh"
 #include "runtime.h"
 
@@ -55,6 +56,8 @@ struct Ctx {
   std::vector<float> host_cos, host_sin;
   bool counters_zeroed = false;
   size_t counters_bytes = 0;
+  // int8 tensor-core projections (wbits 8): split-K scratch
+  QgemmScratch qsc{nullptr, nullptr};
   // zero-weight layer for the stub entry points
   Buf zw, zs;
   LayerPtrs zero{};
@@ -216,6 +219,21 @@ LayerPtrs layer_ptrs_from_ddr(const uint8_t* weight_ddr, uint64_t wb, const floa
   return p;
 }
 
+// W8 layers run their projections on the int8 tensor cores: TMA descriptors of the staged image.
+int ensure_qgemm(Ctx& c, const LayerDev& D, QgemmLayerMaps* maps) {
+  if (c.qsc.acc == nullptr) {
+    QB_TRY(cudaMalloc(&c.qsc.acc, qgemm_acc_ints() * 4));
+    QB_TRY(cudaMalloc(&c.qsc.cnt, qgemm_counter_count() * 4));
+    QB_TRY(cudaMemset(c.qsc.acc, 0, qgemm_acc_ints() * 4));
+    QB_TRY(cudaMemset(c.qsc.cnt, 0, qgemm_counter_count() * 4));
+  }
+  if (!qgemm_make_layer_maps(maps, D)) {
+    set_error("cuTensorMapEncodeTiled failed");
+    return kStatusCuda;
+  }
+  return 0;
+}
+
 int run_decode(int wbits, const LayerPtrs& L, bool attention, bool mlp, const float* x, int past, float* k_cache,
                float* v_cache, float* attn_out, float* out) {
   std::lock_guard<std::mutex> lock(g_mu);
@@ -223,6 +241,11 @@ int run_decode(int wbits, const LayerPtrs& L, bool attention, bool mlp, const fl
   if (int st = init_ctx(c)) return st;
   LayerDev D;
   if (int st = stage_layer(c, wbits, L, attention, mlp, &D)) return st;
+  QgemmLayerMaps maps;
+  const bool tc = wbits == 8;
+  if (tc) {
+    if (int st = ensure_qgemm(c, D, &maps)) return st;
+  }
   const size_t H = (size_t)kHidden * 4;
   QB_TRY(ensure(c.x, H));
   QB_TRY(ensure(c.a, H));
@@ -256,11 +279,20 @@ int run_decode(int wbits, const LayerPtrs& L, bool attention, bool mlp, const fl
     DecodeTokens tok{(const int*)c.dpos.p, (const int*)c.dseq.p, 1};
     KvView kv{(float*)c.kc.p, (float*)c.vc.p, nullptr, 0, 0};
     XSource src{(const float*)c.x.p, nullptr, nullptr};
-    QB_TRY(launch_decode_qkv(wbits, D, src, tok, (const float*)c.rope_dec_cos.p, (const float*)c.rope_dec_sin.p,
-                             (float*)c.q.p, kv, c.stream, false));
+    if (tc) {
+      QB_TRY(qgemm_qkv(maps, D, src, tok, (const float*)c.rope_dec_cos.p, (const float*)c.rope_dec_sin.p,
+                       (float*)c.q.p, kv, c.qsc, c.stream, false));
+    } else {
+      QB_TRY(launch_decode_qkv(wbits, D, src, tok, (const float*)c.rope_dec_cos.p, (const float*)c.rope_dec_sin.p,
+                               (float*)c.q.p, kv, c.stream, false));
+    }
     QB_TRY(launch_decode_attention((const float*)c.q.p, kv, tok, len, (float*)c.ctx.p, (float*)c.attn_part.p,
                                    (unsigned*)c.counters.p, c.stream, false));
-    QB_TRY(launch_decode_o(wbits, D, (const float*)c.ctx.p, 1, (float*)c.a.p, c.stream, false));
+    if (tc) {
+      QB_TRY(qgemm_o(maps, D, (const float*)c.ctx.p, 1, (float*)c.a.p, c.qsc, c.stream, false));
+    } else {
+      QB_TRY(launch_decode_o(wbits, D, (const float*)c.ctx.p, 1, (float*)c.a.p, c.stream, false));
+    }
     a_dev = (float*)c.a.p;
     const size_t row = (size_t)past * kKvWidth;
     QB_TRY(cudaMemcpyAsync(k_cache + row, (float*)c.kc.p + row, kKvWidth * 4, cudaMemcpyDefault, c.stream));
@@ -269,8 +301,13 @@ int run_decode(int wbits, const LayerPtrs& L, bool attention, bool mlp, const fl
   }
   if (mlp) {
     QB_TRY(ensure(c.h, (size_t)kInter * 4));
-    QB_TRY(launch_decode_gateup(wbits, D, a_dev, 1, (float*)c.h.p, c.stream, false));
-    QB_TRY(launch_decode_down(wbits, D, (const float*)c.h.p, a_dev, 1, (float*)c.out.p, false, c.stream, false));
+    if (tc) {
+      QB_TRY(qgemm_gateup(maps, D, a_dev, 1, (float*)c.h.p, c.qsc, c.stream, false));
+      QB_TRY(qgemm_down(maps, D, (const float*)c.h.p, a_dev, 1, (float*)c.out.p, false, c.qsc, c.stream, false));
+    } else {
+      QB_TRY(launch_decode_gateup(wbits, D, a_dev, 1, (float*)c.h.p, c.stream, false));
+      QB_TRY(launch_decode_down(wbits, D, (const float*)c.h.p, a_dev, 1, (float*)c.out.p, false, c.stream, false));
+    }
     QB_TRY(cudaMemcpyAsync(out, c.out.p, H, cudaMemcpyDefault, c.stream));
   }
   QB_TRY(cudaStreamSynchronize(c.stream));
@@ -357,6 +394,10 @@ int qwen_b200_set_prefill_seq_capacity(int capacity) {
   qb::prefill_seq_capacity();
   qb::g_prefill_capacity = capacity;
   return 0;
+}
+
+unsigned qwen_b200_kernel_error(int reset) {
+  return qb::gemv_kernel_error(reset != 0) | qb::qgemm_kernel_error(reset != 0);
 }
 
 int qwen_b200_device_count(void) {

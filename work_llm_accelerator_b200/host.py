@@ -66,6 +66,11 @@ def core_lib() -> ctypes.CDLL:
         lib.qwen_b200_decode_attention.argtypes = [ctypes.c_void_p] * 3 + [ctypes.c_int, ctypes.c_void_p,
                                                                             ctypes.c_void_p]
         lib.qwen_b200_decode_attention.restype = ctypes.c_int
+        lib.qwen_b200_w8_digit_products.argtypes = [ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_void_p,
+                                                    ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p]
+        lib.qwen_b200_w8_digit_products.restype = ctypes.c_int
+        lib.qwen_b200_kernel_error.argtypes = [ctypes.c_int]
+        lib.qwen_b200_kernel_error.restype = ctypes.c_uint
         _core = lib
     return _core
 
@@ -346,3 +351,18 @@ def decode_attention(q_ptr: int, k_ptr: int, v_ptr: int, seq_len: int, ctx_ptr: 
     st = core_lib().qwen_b200_decode_attention(q_ptr, k_ptr, v_ptr, seq_len, ctx_ptr, stream or None)
     if st != 0:
         raise EngineError(f"qwen_b200_decode_attention failed with status {st}: {last_error()}")
+
+
+def w8_digit_products(codes_ptr: int, rows: int, k: int, x_ptr: int, n_tokens: int, acc_ptr: int, step_ptr: int,
+                      stream: int = 0) -> None:
+    """Integer core of the W8 tensor-core projections (include/qwen_b200_ops.h): acc[r][4d+t] = sum_i
+    codes[r][i] * digit_d(x[t])[i] and the per-token steps, on device buffers."""
+    st = core_lib().qwen_b200_w8_digit_products(codes_ptr, rows, k, x_ptr, n_tokens, acc_ptr, step_ptr,
+                                                 stream or None)
+    if st != 0:
+        raise EngineError(f"qwen_b200_w8_digit_products failed with status {st}: {last_error()}")
+
+
+def kernel_error(reset: bool = False) -> int:
+    """Error flag of the streaming kernels on the current device (1 = a bounded pipeline wait gave up)."""
+    return int(core_lib().qwen_b200_kernel_error(1 if reset else 0))

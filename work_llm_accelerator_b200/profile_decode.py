@@ -1,0 +1,57 @@
+"""Small, self-contained decode workloads for kernel profiling (one GPU, synthetic weights).
+
+    python -m work_llm_accelerator_b200.profile_decode kernels --wbits 8 --iters 2
+        times each decode kernel of one layer in isolation (engine profile_kernels) and prints the
+        per-kernel microseconds: a capture of a single kernel (`ncu -k regex:<name> -c 1`) stays small.
+    python -m work_llm_accelerator_b200.profile_decode steps --wbits 8 --prompt 512 --steps 3
+        prefills one sequence and runs full 28-layer decode steps (CUDA graphs by default): the launch
+        list of a whole step.
+
+Both hold about 2.2 GB (W8) of weights on the device plus a 1024-position KV pool.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+
+import numpy as np
+
+from . import host
+
+
+def main(argv=None) -> int:
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("mode", choices=["kernels", "steps"])
+    ap.add_argument("--wbits", type=int, default=8, choices=[4, 8])
+    ap.add_argument("--seed", type=int, default=7)
+    ap.add_argument("--iters", type=int, default=2, help="kernels: launches of each kernel")
+    ap.add_argument("--past", type=int, default=512, help="kernels: history length of the attention launch")
+    ap.add_argument("--prompt", type=int, default=512, help="steps: prompt length")
+    ap.add_argument("--steps", type=int, default=3, help="steps: decode steps")
+    ap.add_argument("--graphs", type=int, default=1, help="steps: 1 = CUDA graphs, 0 = eager launches")
+    ap.add_argument("--option", action="append", default=[], metavar="NAME=VALUE",
+                    help="engine option (e.g. qgemm=0, prefetch=0, pdl=0)")
+    a = ap.parse_args(argv)
+
+    eng = host.Engine(0, a.wbits, max_seqs=1, max_len=1024)
+    try:
+        eng.init_synthetic(a.seed)
+        for opt in a.option:
+            name, value = opt.split("=", 1)
+            eng.set_option(name, int(value))
+        if a.mode == "kernels":
+            us = eng.profile_kernels(1, a.past, iters=a.iters)
+            print(json.dumps({k: round(v * 1000.0, 3) for k, v in us.items()}))
+        else:
+            eng.set_option("graphs", a.graphs)
+            prompt = np.random.default_rng(1).integers(0, 151936, a.prompt).astype(np.int32)
+            tok = eng.prefill(0, prompt)
+            ms = eng.bench_decode([0], [tok], a.steps, 1)
+            print(json.dumps({"ms_per_step": ms}))
+    finally:
+        eng.close()
+    return 0
+
+
+if __name__ == "__main__":
+    raise SystemExit(main())
