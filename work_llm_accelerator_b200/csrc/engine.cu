@@ -17,6 +17,7 @@
 #include <vector>
 
 #include "../../include/qwen_b200_engine.h"
+#include "decode_stack.h"
 #include "qgemm.h"
 #include "qwen_kernels.cuh"
 #include "runtime.h"
@@ -128,6 +129,17 @@ struct qwen_engine {
   bool use_qgemm = true;
   QgemmLayerMaps maps[kLayers];
   QgemmScratch qsc{nullptr, nullptr};
+  // persistent whole-step kernel (wbits == 8): tiled weights, schedule, synchronisation words
+  bool use_stack = true;
+  bool tiles_dirty = true;
+  uint8_t* wtiles = nullptr;
+  LayerDev* d_layers = nullptr;
+  stack::SyncWords* sync = nullptr;
+  int* stack_acc = nullptr;
+  uint32_t* d_item_off = nullptr;
+  stack::Item* d_items = nullptr;
+  int stack_ctas = 0;
+  int attn_max_chunks = 0;
 };
 
 namespace {
@@ -225,6 +237,23 @@ int ensure_prefill_buffers(qwen_engine* e, int n) {
   return 0;
 }
 
+// Rebuild the tiled copy of the int8 weights after they changed (outside any stream capture).
+int ensure_tiles(qwen_engine* e) {
+  if (e->wbits != 8 || !e->tiles_dirty) return 0;
+  cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+  E_TRY(cudaStreamIsCapturing(e->stream, &cap));
+  if (cap != cudaStreamCaptureStatusNone) {
+    set_error("weights changed during stream capture");
+    return kStatusCuda;
+  }
+  for (int l = 0; l < kLayers; ++l)
+    E_TRY(stack::launch_tile_layer(e->layers[l], e->wtiles + (size_t)l * stack::kLayerTileBytes, e->stream));
+  e->tiles_dirty = false;
+  return 0;
+}
+
+bool stack_enabled(const qwen_engine* e) { return e->wbits == 8 && e->use_stack && e->wtiles != nullptr; }
+
 // Enqueue one decode step for nt tokens whose ids/positions/slots are already in d_tokens/d_pos/d_seq.
 // max_len bounds the attention grid (positions + 1 of every token must be <= max_len).
 int enqueue_decode(qwen_engine* e, int nt, int max_len, bool advance) {
@@ -237,7 +266,38 @@ int enqueue_decode(qwen_engine* e, int nt, int max_len, bool advance) {
   const size_t down_bytes = (size_t)kInter * kHidden * wb / 8;
   const size_t qkv_bytes = (size_t)kQkvRows * kHidden * wb / 8;
   const size_t lm_head_prefetch = (size_t)32 << 20;
-  for (int l = 0; l < kLayers; ++l) {
+  if (stack_enabled(e)) {
+    if (int st = ensure_tiles(e)) return st;
+    stack::Args a{};
+    a.wtiles = e->wtiles;
+    a.layers = e->d_layers;
+    a.embed = e->embed;
+    a.tokens = e->d_tokens;
+    a.pos = e->d_pos;
+    a.seq = e->d_seq;
+    a.nt = nt;
+    a.rope_cos = e->rope_dec_cos;
+    a.rope_sin = e->rope_dec_sin;
+    a.kv_pool = e->kv_pool;
+    a.page_table = e->d_page_table;
+    a.max_pages = e->max_pages;
+    a.y0 = e->y0;
+    a.y1 = e->y1;
+    a.q = e->q;
+    a.ctx = e->ctx;
+    a.a = e->a;
+    a.h = e->h;
+    a.dump = e->dump_hidden ? e->dump : nullptr;
+    a.attn_part = e->attn_part;
+    a.attn_max_chunks = e->attn_max_chunks;
+    a.acc = e->stack_acc;
+    a.sync = e->sync;
+    a.item_off = e->d_item_off;
+    a.items = e->d_items;
+    E_TRY(stack::launch_decode_stack(a, e->stack_ctas, e->stream));
+    xin = ((kLayers - 1) & 1) ? e->y1 : e->y0;
+  }
+  for (int l = 0; l < kLayers && !stack_enabled(e); ++l) {
     const LayerDev& L = e->layers[l];
     XSource src{xin, e->embed, e->d_tokens};
     KvView kv = paged_view(e, l);
@@ -274,7 +334,7 @@ int enqueue_decode(qwen_engine* e, int nt, int max_len, bool advance) {
     xin = yout;
   }
   E_TRY(launch_lm_head_argmax(e->embed, e->final_norm, xin, nt, e->keep_logits ? e->logits : nullptr, e->lm_part,
-                              e->lm_cnt, e->d_next, e->stream, pdl && !e->dump_hidden));
+                              e->lm_cnt, e->d_next, e->stream, pdl && !e->dump_hidden && !stack_enabled(e)));
   if (advance) {
     E_TRY(launch_k(advance_kernel, dim3(1), dim3(32), 0, e->stream, pdl, e->d_tokens, (const int*)e->d_next,
                    e->d_pos, nt));
@@ -283,6 +343,7 @@ int enqueue_decode(qwen_engine* e, int nt, int max_len, bool advance) {
 }
 
 int run_decode_step(qwen_engine* e, int nt, int max_len, bool advance) {
+  if (int st = ensure_tiles(e)) return st;
   const int chunks = (max_len + 63) / 64;
   const int bucket = ((chunks + 7) / 8) * 8;  // re-capture every 512 positions
   const int grid_len = bucket * 64;
@@ -343,6 +404,25 @@ int qwen_engine_create(int device, int wbits, int max_seqs, int max_len, qwen_en
     E_TRY(dalloc(&e->qsc.cnt, qgemm_counter_count()));
     E_TRY(cudaMemset(e->qsc.acc, 0, qgemm_acc_ints() * 4));
     E_TRY(cudaMemset(e->qsc.cnt, 0, qgemm_counter_count() * 4));
+    int sms = 0;
+    E_TRY(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device));
+    int coop = 0;
+    E_TRY(cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, device));
+    if (coop && stack::decode_stack_smem() <= (size_t)227 * 1024) {
+      const stack::Schedule sc = stack::build_schedule(sms);
+      e->stack_ctas = sms;
+      E_TRY(dalloc(&e->wtiles, (size_t)kLayers * stack::kLayerTileBytes));
+      E_TRY(dalloc(&e->d_layers, (size_t)kLayers));
+      E_TRY(cudaMemcpy(e->d_layers, e->layers, sizeof(LayerDev) * kLayers, cudaMemcpyHostToDevice));
+      E_TRY(cudaMalloc(&e->sync, sizeof(stack::SyncWords)));
+      E_TRY(cudaMemset(e->sync, 0, sizeof(stack::SyncWords)));
+      E_TRY(dalloc(&e->stack_acc, (size_t)stack::kAccTiles * 128 * 12));
+      E_TRY(cudaMemset(e->stack_acc, 0, (size_t)stack::kAccTiles * 128 * 12 * 4));
+      E_TRY(dalloc(&e->d_item_off, sc.off.size()));
+      E_TRY(cudaMemcpy(e->d_item_off, sc.off.data(), sc.off.size() * 4, cudaMemcpyHostToDevice));
+      E_TRY(dalloc(&e->d_items, sc.items.size()));
+      E_TRY(cudaMemcpy(e->d_items, sc.items.data(), sc.items.size() * sizeof(stack::Item), cudaMemcpyHostToDevice));
+    }
   }
   E_TRY(dalloc(&e->embed, (size_t)kVocab * kHidden));
   E_TRY(dalloc(&e->final_norm, (size_t)kHidden));
@@ -367,6 +447,7 @@ int qwen_engine_create(int device, int wbits, int max_seqs, int max_len, qwen_en
   E_TRY(dalloc(&e->y1, (size_t)T * kHidden));
   E_TRY(dalloc(&e->h, (size_t)T * kInter));
   E_TRY(dalloc(&e->attn_part, attn_partial_floats(T, max_len + 512 + 64)));
+  e->attn_max_chunks = (max_len + 512 + 64 + 63) / 64;
   E_TRY(dalloc(&e->attn_cnt, (size_t)T * kKvHeads));
   E_TRY(cudaMemset(e->attn_cnt, 0, (size_t)T * kKvHeads * 4));
   E_TRY(dalloc(&e->lm_part, (size_t)lm_head_partial_floats()));
@@ -387,7 +468,8 @@ void qwen_engine_destroy(qwen_engine* e) {
                   e->d_seq, e->d_next, e->x, e->q, e->ctx, e->a, e->y0, e->y1, e->h, e->attn_part, e->attn_cnt,
                   e->lm_part, e->lm_cnt, e->dump, e->logits, e->rope_dec_cos, e->rope_dec_sin, e->rope_pre_cos,
                   e->rope_pre_sin, e->p_x, e->p_xn, e->p_q, e->p_ctx, e->p_a, e->p_h, e->p_k, e->p_v, e->p_tokens,
-                  e->qsc.acc, e->qsc.cnt};
+                  e->qsc.acc, e->qsc.cnt, e->wtiles, e->d_layers, e->sync, e->stack_acc, e->d_item_off,
+                  e->d_items};
   for (void* p : ptrs) cudaFree(p);
   if (e->h_io) cudaFreeHost(e->h_io);
   if (e->stream) cudaStreamDestroy(e->stream);
@@ -402,6 +484,8 @@ int qwen_engine_init_synthetic(qwen_engine* e, uint64_t seed, float weight_sigma
                              e->simg + e->layer_bytes / 4 * l, e->stream));
   E_TRY(launch_synth_embedding(seed, e->embed, e->stream));
   E_TRY(launch_synth_fill(seed, (1ull << 20) + 1, kHidden, 1.0f, 0.02f, e->final_norm, e->stream));
+  e->tiles_dirty = true;
+  if (int st = ensure_tiles(e)) return st;
   E_TRY(cudaStreamSynchronize(e->stream));
   return 0;
 }
@@ -412,6 +496,7 @@ int qwen_engine_load_layer(qwen_engine* e, int layer, const uint8_t* weight_ddr,
   const LayerLayout lay = layer_layout(e->wbits);
   E_TRY(cudaMemcpy(e->wimg + e->layer_bytes * layer, weight_ddr, lay.total, cudaMemcpyDefault));
   E_TRY(cudaMemcpy(e->simg + e->layer_bytes / 4 * layer, scale_ddr, lay.total / 4 * 4, cudaMemcpyDefault));
+  e->tiles_dirty = true;
   return 0;
 }
 
@@ -433,6 +518,10 @@ int qwen_engine_set_option(qwen_engine* e, const char* name, long long value) {
     e->graphs.clear();
   } else if (n == "prefetch") {
     e->prefetch = value != 0;
+    for (auto& kv : e->graphs) cudaGraphExecDestroy(kv.second);
+    e->graphs.clear();
+  } else if (n == "stack") {
+    e->use_stack = value != 0;
     for (auto& kv : e->graphs) cudaGraphExecDestroy(kv.second);
     e->graphs.clear();
   } else if (n == "qgemm") {
@@ -750,8 +839,8 @@ int qwen_engine_profile_kernels(qwen_engine* e, int n, int past, int iters, floa
 void* qwen_engine_stream(qwen_engine* e) { return e ? (void*)e->stream : nullptr; }
 
 int qwen_engine_kernels_per_decode_step(qwen_engine* e, int n) {
-  (void)e;
   const int groups = (n + kGemvMaxTokens - 1) / kGemvMaxTokens;
+  if (e && stack_enabled(e)) return groups * 2;
   return groups * (kLayers * 5 + 1);
 }
 

@@ -25,69 +25,34 @@
 
 #include "qwen_kernels.cuh"
 #include "qgemm.h"
-#include "sm100_async.cuh"
+#include "umma_sm100.cuh"
 
 namespace qb {
 namespace {
 
-constexpr int kTileM = 128;
-constexpr int kTileN = 16;       // activation-digit rows (3 digits x up to 4 tokens, padded)
-constexpr int kKBlock = 128;     // bytes of K per stage (one 128-byte swizzle atom)
+using umma::kDigitRange;
+using umma::kKBlock;
+using umma::kTileM;
+using umma::kTileN;
+using umma::fence_after;
+using umma::fence_before;
+using umma::mma_commit;
+using umma::mma_i8;
+using umma::sw128_desc;
+using umma::tmem_ld16;
+
 constexpr int kStages = 4;
 constexpr int kThreads = 192;    // 6 warps
 constexpr int kEpiThreads = 128; // warps 2..5
 constexpr int kBarEpi = 1;       // named barrier among the epilogue warps
 constexpr int kTmemCols = 32;
-constexpr float kDigitRange = 8355710.0f;  // |X| <= 127 * 65793 after rounding
 
-// ---------------------------------------------------------------------------------------------------
-// PTX wrappers
-// ---------------------------------------------------------------------------------------------------
 __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int c0, int c1, uint64_t* bar) {
   asm volatile(
       "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], "
       "[%4];" ::"r"(smem_u32(dst)),
       "l"(map), "r"(c0), "r"(c1), "r"(smem_u32(bar))
       : "memory");
-}
-
-__device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
-  uint64_t d = 0;
-  d |= (uint64_t)((saddr & 0x3FFFFu) >> 4);  // start address (16-byte units)
-  d |= (uint64_t)1 << 16;                    // leading byte offset (unused for swizzled K-major)
-  d |= (uint64_t)(1024 >> 4) << 32;          // stride byte offset: 8 rows x 128 bytes
-  d |= (uint64_t)1 << 46;                    // descriptor version (sm_100)
-  d |= (uint64_t)2 << 61;                    // 128-byte swizzle
-  return d;
-}
-
-// kind::i8, D = s32, A = B = signed int8, both K-major, M = 128, N = 16
-constexpr uint32_t kIdesc = (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(kTileN >> 3) << 17) |
-                            ((uint32_t)(kTileM >> 4) << 24);
-
-__device__ __forceinline__ void mma_i8(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t accumulate) {
-  asm volatile(
-      "{\n.reg .pred p;\nsetp.ne.b32 p, %4, 0;\ntcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n}" ::"r"(
-          d_tmem),
-      "l"(a), "l"(b), "r"(kIdesc), "r"(accumulate)
-      : "memory");
-}
-
-__device__ __forceinline__ void mma_commit(uint64_t* bar) {
-  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
-               : "memory");
-}
-
-__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
-__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
-
-__device__ __forceinline__ void tmem_ld16(uint32_t taddr, int (&v)[16]) {
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
-      : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]), "=r"(v[8]),
-        "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15])
-      : "r"(taddr));
-  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
 
 // ---------------------------------------------------------------------------------------------------
@@ -182,10 +147,8 @@ __device__ void build_digits(const QArgs& a, Smem& sm, uint8_t* bsm, int kb0, in
           if (MODE != kQPlain) v = (float)((double)v * inv * (double)a.norm_w[k]);
         }
         const int X = (int)rintf(__fdiv_rn(v, step));
-        const int d0 = ((X + 128) & 255) - 128;
-        const int r1 = (X - d0) >> 8;
-        const int d1 = ((r1 + 128) & 255) - 128;
-        const int d2 = (r1 - d1) >> 8;
+        int d0, d1, d2;
+        umma::split_digits(X, d0, d1, d2);
         w0[e >> 2] |= (uint32_t)(d0 & 255) << (8 * (e & 3));
         w1[e >> 2] |= (uint32_t)(d1 & 255) << (8 * (e & 3));
         w2[e >> 2] |= (uint32_t)(d2 & 255) << (8 * (e & 3));
@@ -235,14 +198,11 @@ __global__ void __launch_bounds__(kThreads, 1) qgemm_kernel(const __grid_constan
     mbar_fence_init();
   }
   if (warp == 1) {
-    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&sm.tmem_base)),
-                 "r"(kTmemCols)
-                 : "memory");
-    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    umma::tmem_alloc(&sm.tmem_base, kTmemCols);
   }
-  tc_fence_before();
+  fence_before();
   __syncthreads();
-  tc_fence_after();
+  fence_after();
   const uint32_t tmem = sm.tmem_base;
 
   if (warp == 0) {
@@ -280,12 +240,12 @@ __global__ void __launch_bounds__(kThreads, 1) qgemm_kernel(const __grid_constan
     // ---- MMA issuer
     if (lane == 0) {
       bool ok = mbar_wait(&sm.b_ready, 0);
-      tc_fence_after();
+      fence_after();
       int s = 0;
       unsigned ph = 0;
       for (int kb = kb0; kb < kb1; ++kb) {
         if (ok) ok = mbar_wait(&sm.full[s], ph);
-        tc_fence_after();
+        fence_after();
         if (ok) {
           const uint32_t abase = smem_u32(sm.a[s]);
           const uint32_t bbase = smem_u32(bsm + (size_t)(kb - kb0) * 2048);
@@ -305,11 +265,11 @@ __global__ void __launch_bounds__(kThreads, 1) qgemm_kernel(const __grid_constan
     // ---- activation digits, then the epilogue
     griddep_wait();
     build_digits<MODE>(a, sm, bsm, kb0, kb1);
-    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // generic writes -> tensor-core reads
+    umma::fence_async_smem();  // generic writes -> tensor-core reads
     mbar_arrive(&sm.b_ready);
     if (threadIdx.x == 64) griddep_launch();
     const bool ok = mbar_wait(&sm.acc_ready, 0);
-    tc_fence_after();
+    fence_after();
     const int quarter = warp & 3;          // TMEM lanes this warp may read
     const int r = quarter * 32 + lane;     // tile row
     int v[16];
@@ -356,11 +316,11 @@ __global__ void __launch_bounds__(kThreads, 1) qgemm_kernel(const __grid_constan
       }
     }
   }
-  tc_fence_before();
+  fence_before();
   __syncthreads();
   if (warp == 1) {
-    tc_fence_after();
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols) : "memory");
+    fence_after();
+    umma::tmem_dealloc(tmem, kTmemCols);
   }
 }
 

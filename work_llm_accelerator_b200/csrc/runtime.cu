@@ -18,6 +18,7 @@
 #include <string>
 #include <vector>
 
+#include "decode_stack.h"
 #include "qgemm.h"
 #include "qwen_kernels.cuh"
 #include "runtime.h"
@@ -397,7 +398,8 @@ int qwen_b200_set_prefill_seq_capacity(int capacity) {
 }
 
 unsigned qwen_b200_kernel_error(int reset) {
-  return qb::gemv_kernel_error(reset != 0) | qb::qgemm_kernel_error(reset != 0);
+  return qb::gemv_kernel_error(reset != 0) | qb::qgemm_kernel_error(reset != 0) |
+         qb::stack::decode_stack_kernel_error(reset != 0);
 }
 
 int qwen_b200_device_count(void) {
