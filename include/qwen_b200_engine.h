@@ -55,10 +55,18 @@ int qwen_engine_reset(qwen_engine* e, int slot);
 
 /* Options: "graphs" (capture decode steps in CUDA graphs, default 1), "pdl" (programmatic dependent
  * launch, default 1), "dump_hidden" (keep every layer's output of the last call, default 0),
- * "logits" (keep the last call's logits, default 0), "prefetch" (stream the next kernels' weights into L2, default 1). */
+ * "logits" (keep the last call's logits, default 0), "prefetch" (stream the next kernels' weights into L2,
+ * default 1), "stack" (W8: the whole decode step as one persistent kernel, default 1; 0 = five tensor-core
+ * kernels per layer), "qgemm" (W8 separate-kernel path on the int8 tensor cores, default 1; 0 = CUDA-core
+ * GEMV), "trace" (record a per-CTA, per-layer timeline of the persistent kernel, default 0). */
 int qwen_engine_set_option(qwen_engine* e, const char* name, long long value);
 /* Per-layer outputs of the last prefill/decode call: [28][rows][1536] floats (rows = tokens of that call). */
 int qwen_engine_read_hidden(qwen_engine* e, float* out, long long n_floats);
+/* Timeline of the last persistent-kernel decode step (option "trace"): [ctas][28][slots] global-timer
+ * nanoseconds, 0 where a CTA had no work. Slot i (stage i: 0 q|k|v, 1 attention, 2 o_proj, 3 gate|up,
+ * 4 down) = inputs ready, 5 + i = digits built, 10 + i = epilogues done; 16 + s / 20 + s (projection s:
+ * 0 q|k|v, 1 o, 2 gate|up, 3 down) = first weight unit issued / last MMA committed. */
+int qwen_engine_read_trace(qwen_engine* e, unsigned long long* out, long long n, int* ctas, int* slots);
 /* Logits of the last call: [rows][151936] floats. */
 int qwen_engine_read_logits(qwen_engine* e, float* out, long long n_floats);
 

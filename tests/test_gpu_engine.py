@@ -196,3 +196,37 @@ def test_batched_decode_matches_single(host):
         assert batched == single
     finally:
         eng.close()
+
+
+def _decode_trace(host, seed, prompt, steps, max_len=256, **options):
+    eng = host.Engine(0, 8, max_seqs=1, max_len=max_len)
+    try:
+        eng.init_synthetic(seed)
+        for name, value in options.items():
+            eng.set_option(name, value)
+        eng.set_option("dump_hidden", 1)
+        toks = [eng.prefill(0, prompt)]
+        hidden = []
+        for _ in range(steps):
+            toks.append(int(eng.decode([0], [toks[-1]])[0]))
+            hidden.append(eng.read_hidden(1).copy())
+        return toks, hidden
+    finally:
+        eng.close()
+
+
+@pytest.mark.parametrize("prompt_len", [5, 130])
+def test_persistent_step_kernel_matches_separate_kernels(host, prompt_len):
+    """The single-launch decode step (decode_stack.cu: all 28 layers in one persistent kernel) and the
+    five-launches-per-layer tensor-core path do the same arithmetic in the same order: every layer's
+    hidden state and every token are bit-identical. 130 prompt tokens give three 64-key attention chunks
+    (cross-CTA chunk merge); 5 give one."""
+    rng = np.random.default_rng(prompt_len)
+    prompt = [int(t) for t in rng.integers(0, qo.VOCAB, prompt_len)]
+    host.kernel_error(reset=True)
+    toks_s, hid_s = _decode_trace(host, 21, prompt, 4, max_len=512, stack=1)
+    assert host.kernel_error(reset=True) == 0
+    toks_k, hid_k = _decode_trace(host, 21, prompt, 4, max_len=512, stack=0)
+    assert toks_s == toks_k
+    for step, (a, b) in enumerate(zip(hid_s, hid_k)):
+        assert np.array_equal(a, b), (step, rel_l2(a, b))

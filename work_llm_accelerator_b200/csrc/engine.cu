@@ -140,6 +140,7 @@ struct qwen_engine {
   stack::Item* d_items = nullptr;
   int stack_ctas = 0;
   int attn_max_chunks = 0;
+  unsigned long long* trace = nullptr;  // optional timeline of the persistent kernel
 };
 
 namespace {
@@ -294,6 +295,7 @@ int enqueue_decode(qwen_engine* e, int nt, int max_len, bool advance) {
     a.sync = e->sync;
     a.item_off = e->d_item_off;
     a.items = e->d_items;
+    a.trace = e->trace;
     E_TRY(stack::launch_decode_stack(a, e->stack_ctas, e->stream));
     xin = ((kLayers - 1) & 1) ? e->y1 : e->y0;
   }
@@ -471,6 +473,7 @@ void qwen_engine_destroy(qwen_engine* e) {
                   e->qsc.acc, e->qsc.cnt, e->wtiles, e->d_layers, e->sync, e->stack_acc, e->d_item_off,
                   e->d_items};
   for (void* p : ptrs) cudaFree(p);
+  cudaFree(e->trace);
   if (e->h_io) cudaFreeHost(e->h_io);
   if (e->stream) cudaStreamDestroy(e->stream);
   delete e;
@@ -518,6 +521,17 @@ int qwen_engine_set_option(qwen_engine* e, const char* name, long long value) {
     e->graphs.clear();
   } else if (n == "prefetch") {
     e->prefetch = value != 0;
+    for (auto& kv : e->graphs) cudaGraphExecDestroy(kv.second);
+    e->graphs.clear();
+  } else if (n == "trace") {
+    if (value != 0 && e->trace == nullptr && e->stack_ctas > 0) {
+      const size_t n_stamps = (size_t)e->stack_ctas * kLayers * stack::kTraceSlots;
+      E_TRY(cudaMalloc(&e->trace, n_stamps * 8));
+      E_TRY(cudaMemset(e->trace, 0, n_stamps * 8));
+    } else if (value == 0 && e->trace != nullptr) {
+      E_TRY(cudaFree(e->trace));
+      e->trace = nullptr;
+    }
     for (auto& kv : e->graphs) cudaGraphExecDestroy(kv.second);
     e->graphs.clear();
   } else if (n == "stack") {
@@ -716,6 +730,16 @@ int qwen_engine_read_hidden(qwen_engine* e, float* out, long long n_floats) {
   const long long have = (long long)kLayers * e->last_rows * kHidden;
   if (n_floats < have) return kStatusInvalid;
   E_TRY(cudaMemcpy(out, e->dump, (size_t)have * 4, cudaMemcpyDeviceToHost));
+  return 0;
+}
+
+int qwen_engine_read_trace(qwen_engine* e, unsigned long long* out, long long n, int* ctas, int* slots) {
+  if (!e || !out || !ctas || !slots) return kStatusInvalid;
+  *ctas = e->stack_ctas;
+  *slots = stack::kTraceSlots;
+  const long long have = (long long)e->stack_ctas * kLayers * stack::kTraceSlots;
+  if (e->trace == nullptr || n < have) return kStatusInvalid;
+  E_TRY(cudaMemcpy(out, e->trace, (size_t)have * 8, cudaMemcpyDeviceToHost));
   return 0;
 }
 

@@ -103,11 +103,15 @@ __device__ void build_digits(const QArgs& a, Smem& sm, uint8_t* bsm, int kb0, in
     if (t >= a.nt) break;
     double inv = 1.0;
     if (MODE != kQPlain) {
+      // thread tid sums elements 512 j + 4 tid + e (j < K / 512, e < 4) in that order: the same partial
+      // sums as the persistent decode kernel, so both paths produce bit-identical results
       double ss = 0.0;
-      for (int k = tid; k < a.K; k += kEpiThreads) {
-        const double v = load_x(a, MODE, t, k);
-        ss += v * v;
-      }
+      for (int j = 0; j < a.K / 512; ++j)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const double v = load_x(a, MODE, t, 512 * j + 4 * tid + e);
+          ss += v * v;
+        }
 #pragma unroll
       for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
       if (lane == 0) sm.red[warp][t] = ss;
@@ -344,7 +348,7 @@ struct QEpiQkv {
     const int row = tile * kTileM + r;
     const float b = bias[row], s = scale[row];
 #pragma unroll
-    for (int t = 0; t < 4; ++t) ys[r][t] = b + s * yv[t];
+    for (int t = 0; t < 4; ++t) ys[r][t] = __fmaf_rn(s, yv[t], b);
     named_sync(kBarEpi, kEpiThreads);
     const int h = tile;
     for (int t = 0; t < nt; ++t) {

@@ -162,6 +162,9 @@ def _configure_engine(lib: ctypes.CDLL) -> None:
     lib.qwen_engine_set_option.argtypes = [vp, ctypes.c_char_p, ctypes.c_longlong]
     lib.qwen_engine_read_hidden.argtypes = [vp, _F, ctypes.c_longlong]
     lib.qwen_engine_read_logits.argtypes = [vp, _F, ctypes.c_longlong]
+    lib.qwen_engine_read_trace.argtypes = [vp, np.ctypeslib.ndpointer(np.uint64, flags="C_CONTIGUOUS"),
+                                           ctypes.c_longlong, ctypes.POINTER(ctypes.c_int),
+                                           ctypes.POINTER(ctypes.c_int)]
     lib.qwen_engine_bench_decode.argtypes = [vp, _I32, _I32, i, i, i, ctypes.POINTER(ctypes.c_float)]
     lib.qwen_engine_decode_device.argtypes = [vp, _I32, vp, i, vp]
     lib.qwen_engine_read_layer.argtypes = [vp, i, _B, _F]
@@ -174,7 +177,7 @@ def _configure_engine(lib: ctypes.CDLL) -> None:
               "qwen_engine_set_seq_len", "qwen_engine_seq_len", "qwen_engine_reset", "qwen_engine_set_option",
               "qwen_engine_read_hidden", "qwen_engine_read_logits", "qwen_engine_bench_decode",
               "qwen_engine_kernels_per_decode_step", "qwen_engine_decode_device", "qwen_engine_read_layer",
-              "qwen_engine_profile_kernels"):
+              "qwen_engine_profile_kernels", "qwen_engine_read_trace"):
         getattr(lib, n).restype = i
 
 
@@ -262,6 +265,14 @@ class Engine:
 
     def reset(self, slot: int) -> None:
         _check(self.lib.qwen_engine_reset(self.handle, slot), "reset")
+
+    def read_trace(self, ctas: int = 148) -> np.ndarray:
+        """Timeline of the last persistent-kernel step: [ctas][28][slots] global-timer ns (option "trace")."""
+        c, sl = ctypes.c_int(), ctypes.c_int()
+        out = np.zeros(ctas * 28 * 32, np.uint64)
+        _check(self.lib.qwen_engine_read_trace(self.handle, out, out.size, ctypes.byref(c), ctypes.byref(sl)),
+               "read_trace")
+        return out[:c.value * 28 * sl.value].reshape(c.value, 28, sl.value)
 
     def read_hidden(self, rows: int) -> np.ndarray:
         out = np.zeros(LAYERS * rows * HIDDEN, np.float32)
