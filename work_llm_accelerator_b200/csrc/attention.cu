@@ -211,7 +211,7 @@ __global__ void __launch_bounds__(kAttnThreads) decode_attn_kernel(const float* 
       const float* pc = base + ((c0 + cc) * kGroups + h) * kPartStride;
       const float w = expf(__ldcg(&pc[0]) - M[h]);
       sm.es[cc][h] = w;
-      sm.vs[cc][h] = __ldcg(&pc[1]) * w;
+      sm.vs[cc][h] = __fmul_rn(__ldcg(&pc[1]), w);
     }
     __syncthreads();
 #pragma unroll 4
@@ -220,7 +220,7 @@ __global__ void __launch_bounds__(kAttnThreads) decode_attn_kernel(const float* 
 #pragma unroll
       for (int h = 0; h < kGroups; ++h) {
         o[h] = fmaf(__ldcg(&pc[h * kPartStride]), sm.es[cc][h], o[h]);
-        Lsum[h] += sm.vs[cc][h];
+        Lsum[h] = __fadd_rn(Lsum[h], sm.vs[cc][h]);
       }
     }
   }

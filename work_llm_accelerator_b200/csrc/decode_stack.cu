@@ -39,7 +39,7 @@ namespace {
 
 using namespace umma;
 
-constexpr int kRing = 9;           // weight stages per CTA
+constexpr int kRing = 9;           // weight stages per CTA (shared memory); Args::ring uses 2..kRing of them
 constexpr int kThreads = 192;
 constexpr int kWorkers = 128;
 constexpr int kBarW = 1;           // named barrier of the worker warps
@@ -91,17 +91,35 @@ __device__ __forceinline__ unsigned ld_relaxed(const unsigned* p) {
   return v;
 }
 
+// Completion signals: the workers' writes are ordered before one thread's release operation by a CTA
+// barrier, so a single gpu-scope release (instead of a fence in every thread) publishes all of them; the
+// waiting side acquires with one thread and releases its workers with a barrier.
+__device__ __forceinline__ void red_release(unsigned* p, unsigned v) {
+  asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+__device__ __forceinline__ unsigned atom_add_acq_rel(unsigned* p, unsigned v) {
+  unsigned old;
+  asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
+  return old;
+}
+
 __device__ __forceinline__ void give_up(unsigned* abort_flag) {
   atomicExch(&g_kernel_error, kErrMbarTimeout);
   atomicExch(abort_flag, 1u);
 }
 
 // Spin until *p >= target; false after the time limit or once another CTA has aborted.
+__device__ __forceinline__ void fence_acquire() { asm volatile("fence.acq_rel.gpu;" ::: "memory"); }
+
 __device__ bool wait_count(const unsigned* p, unsigned target, unsigned* abort_flag) {
   if (ld_acquire(p) >= target) return true;
   const long long t0 = clock64();
   while (true) {
-    if (ld_acquire(p) >= target) return true;
+    if (ld_relaxed(p) >= target) {
+      fence_acquire();
+      return true;
+    }
     if (ld_relaxed(abort_flag)) return false;
     if (clock64() - t0 > kSpinLimit) {
       give_up(abort_flag);
@@ -128,10 +146,7 @@ __device__ bool mwait(uint64_t* bar, unsigned parity, unsigned* abort_flag) {
 
 // All workers continue once *p >= target (one thread spins; the barrier releases the rest).
 __device__ __forceinline__ void workers_wait(const unsigned* p, unsigned target, unsigned* abort_flag, int tid) {
-  if (tid == 0) {
-    wait_count(p, target, abort_flag);
-    __threadfence();
-  }
+  if (tid == 0) wait_count(p, target, abort_flag);
   named_sync(kBarW, kWorkers);
 }
 
@@ -154,10 +169,14 @@ __device__ __forceinline__ void cp_async16(void* smem_dst, const void* gmem_src)
 
 __device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
 
+__device__ __forceinline__ int ring_depth(const Args& a) { return a.ring < 2 ? 2 : a.ring > kRing ? kRing : a.ring; }
+
 // ---------------------------------------------------------------------------------------------------
 // producer and MMA issuer
 // ---------------------------------------------------------------------------------------------------
-__device__ void producer(const Args& a, uint8_t* ring, Ctrl& cs, uint32_t i0, uint32_t i1, unsigned* abort_flag) {
+__device__ void producer(const Args& a, uint8_t* ring_smem, Ctrl& cs, uint32_t i0, uint32_t i1,
+                         unsigned* abort_flag) {
+  const int ring = ring_depth(a);
   int s = 0;
   unsigned ph = 0, issued = 0, last_ph = 0;
   bool ok = true;
@@ -174,10 +193,10 @@ __device__ void producer(const Args& a, uint8_t* ring, Ctrl& cs, uint32_t i0, ui
           stamp(a, l, kTraceIssue + cur);
         }
         mbar_arrive_expect_tx(&cs.full[s], kUnitBytes);
-        bulk_g2s(ring + (size_t)s * kUnitBytes, src + (size_t)kb * kUnitBytes, kUnitBytes, &cs.full[s]);
+        bulk_g2s(ring_smem + (size_t)s * kUnitBytes, src + (size_t)kb * kUnitBytes, kUnitBytes, &cs.full[s]);
         issued |= 1u << s;
         last_ph = (last_ph & ~(1u << s)) | (ph << s);
-        if (++s == kRing) {
+        if (++s == ring) {
           s = 0;
           ph ^= 1;
         }
@@ -189,8 +208,9 @@ __device__ void producer(const Args& a, uint8_t* ring, Ctrl& cs, uint32_t i0, ui
     if ((issued >> r) & 1) mbar_wait(&cs.full[r], (last_ph >> r) & 1);
 }
 
-__device__ void mma_issuer(const Args& a, uint8_t* ring, uint8_t* digits, Ctrl& cs, uint32_t tmem, uint32_t i0,
+__device__ void mma_issuer(const Args& a, uint8_t* ring_smem, uint8_t* digits, Ctrl& cs, uint32_t tmem, uint32_t i0,
                            uint32_t i1, unsigned* abort_flag) {
+  const int ring = ring_depth(a);
   int s = 0;
   unsigned ph = 0, item_no = 0, inst = 0;
   bool ok = true;
@@ -215,14 +235,14 @@ __device__ void mma_issuer(const Args& a, uint8_t* ring, uint8_t* digits, Ctrl& 
         ok = ok && mwait(&cs.full[s], ph, abort_flag);
         fence_after();
         if (ok) {
-          const uint32_t abase = smem_u32(ring + (size_t)s * kUnitBytes);
+          const uint32_t abase = smem_u32(ring_smem + (size_t)s * kUnitBytes);
           const uint32_t bbase = dbase + (uint32_t)(it.dslot + kb - it.kb0) * kDigitBlockBytes;
 #pragma unroll
           for (int j = 0; j < kKBlock / 32; ++j)
             mma_i8(d, sw128_desc(abase + 32 * j), sw128_desc(bbase + 32 * j), (kb > it.kb0 || j > 0) ? 1u : 0u);
         }
         mma_commit(&cs.empty[s]);
-        if (++s == kRing) {
+        if (++s == ring) {
           s = 0;
           ph ^= 1;
         }
@@ -256,8 +276,14 @@ __device__ __forceinline__ void put_digits(uint8_t* blk, int t, int kk, const fl
 // Digits of a whole 1536-wide row per token: x (or the embedding rows of the tokens when x is null),
 // optionally RMS-normalised with norm_w (double accumulation, as the decode reference). Thread tid owns
 // elements 512 j + 4 tid .. +3, j < 3.
-__device__ void build_full(const Args& a, Ctrl& cs, uint8_t* dbuf, const float* x, const float* norm_w, int tid,
-                           float (&step)[4]) {
+__device__ __forceinline__ void load_norm(const float* norm_w, int tid, float4 (&wv)[3]) {
+#pragma unroll
+  for (int j = 0; j < 3; ++j) wv[j] = __ldg(reinterpret_cast<const float4*>(norm_w + 512 * j + 4 * tid));
+}
+
+// wv: the norm weights of this thread's elements (loaded before the wait for x), used when norm is true.
+__device__ void build_full(const Args& a, Ctrl& cs, uint8_t* dbuf, const float* x, bool norm, const float4 (&wv)[3],
+                           int tid, float (&step)[4]) {
   const int warp = tid >> 5, lane = tid & 31;
   for (int t = 0; t < a.nt; ++t) {
     float v[3][4];
@@ -283,7 +309,7 @@ __device__ void build_full(const Args& a, Ctrl& cs, uint8_t* dbuf, const float* 
         v[j][3] = __high2float(h1);
       }
     }
-    if (norm_w != nullptr) {
+    if (norm) {
       double ss = 0.0;
 #pragma unroll
       for (int j = 0; j < 3; ++j)
@@ -297,7 +323,7 @@ __device__ void build_full(const Args& a, Ctrl& cs, uint8_t* dbuf, const float* 
       const double inv = 1.0 / sqrt(tot / (double)kHidden + (double)kEps);
 #pragma unroll
       for (int j = 0; j < 3; ++j) {
-        const float4 w = __ldg(reinterpret_cast<const float4*>(norm_w + 512 * j + 4 * tid));
+        const float4 w = wv[j];
         v[j][0] = (float)((double)v[j][0] * inv * (double)w.x);
         v[j][1] = (float)((double)v[j][1] * inv * (double)w.y);
         v[j][2] = (float)((double)v[j][2] * inv * (double)w.z);
@@ -327,7 +353,7 @@ __device__ void build_full(const Args& a, Ctrl& cs, uint8_t* dbuf, const float* 
 // max|h| gathered by the gate|up epilogues.
 __device__ void build_down(const Args& a, uint8_t* dbuf, int l, uint32_t b0, uint32_t b1, int tid, float (&step)[4]) {
   for (int t = 0; t < a.nt; ++t) {
-    const float mx = __uint_as_float(__ldcg(&a.sync->hmax[l][t]));
+    const float mx = __uint_as_float(__ldcg(&a.sync->hmax[l].pad[t]));
     const float st = mx > 0.0f ? mx / kDigitRange : 1.0f;
     step[t] = st;
     for (uint32_t i = b0; i < b1; ++i) {
@@ -350,13 +376,74 @@ struct WorkerCtx {
   int tid, quarter, lane, r;
   unsigned item_no;
   uint32_t tmem;
+  int pos[4], seq[4];     // per token, constant for the launch
+  float* kvrow[4];        // this step's KV row of layer 0 (K), per token; other layers/V at fixed offsets
 };
+
+// Per-item constants, loaded before the accumulator is ready so that no dependent global load is left on
+// the path from the MMA to the completion signal.
+struct EpiConst {
+  float sc, bb;
+  float rc[4], rs[4];  // RoPE cos / sin per token (q and k heads)
+  float res[4];        // down: the attention-block output a (residual)
+  float* dst[4];       // output element per token
+};
+
+__device__ __forceinline__ void epi_const(const Args& a, const WorkerCtx& w, const Item it, int l, EpiConst& k) {
+  const LayerDev& L = a.layers[l];
+  const int r = w.r, s = it.stage;
+#pragma unroll
+  for (int t = 0; t < 4; ++t) {
+    k.rc[t] = k.rs[t] = k.res[t] = 0.f;
+    k.dst[t] = nullptr;
+  }
+  k.bb = 0.f;
+  if (s == kQkv) {
+    const int row = it.tile * kTileM + r, h = it.tile;
+    k.sc = __ldg(L.qkv_s + row);
+    k.bb = __ldg(L.qkv_b + row);
+    for (int t = 0; t < a.nt; ++t) {
+      if (h < kHeads + kKvHeads) {
+        const size_t ri = (size_t)w.pos[t] * 64 + (r & 63);
+        k.rc[t] = __ldg(a.rope_cos + ri);
+        k.rs[t] = __ldg(a.rope_sin + ri);
+      }
+      if (h < kHeads) {
+        k.dst[t] = a.q + (size_t)t * kHidden + row;
+      } else {
+        const int which = h < kHeads + kKvHeads ? 0 : 1;
+        k.dst[t] = w.kvrow[t] + ((size_t)l * 2 + which) * kPage * kKvWidth + (row - kHidden - which * kKvWidth);
+      }
+    }
+  } else if (s == kO) {
+    const int row = it.tile * kTileM + r;
+    k.sc = __ldg(L.o_s + row);
+    for (int t = 0; t < a.nt; ++t) k.dst[t] = a.a + (size_t)t * kHidden + row;
+  } else if (s == kGu) {
+    const int row = r < 64 ? it.tile * 64 + r : kInter + it.tile * 64 + (r - 64);
+    k.sc = __ldg(L.gu_s + row);
+    for (int t = 0; t < a.nt; ++t) k.dst[t] = a.h + (size_t)t * kInter + it.tile * 64 + (r & 63);
+  } else {
+    const int row = it.tile * kTileM + r;
+    k.sc = __ldg(L.down_s + row);
+    float* yout = (l & 1) ? a.y1 : a.y0;
+    for (int t = 0; t < a.nt; ++t) {
+      k.res[t] = __ldcg(a.a + (size_t)t * kHidden + row);
+      k.dst[t] = yout + (size_t)t * kHidden + row;
+    }
+  }
+}
 
 __device__ void item_epilogue(const Args& a, Ctrl& cs, WorkerCtx& w, const Item it, int l, const float (&step)[4],
                               unsigned* abort_flag) {
   const int nt = a.nt, r = w.r, tid = w.tid;
+  EpiConst k;
+  epi_const(a, w, it, l, k);
   const unsigned b = w.item_no & 1;
   mwait(&cs.acc_full[b], (w.item_no >> 1) & 1, abort_flag);
+  const int s = it.stage;
+  const int ts = s == kQkv ? 0 : s == kO ? 1 : s == kDown ? 2 : -1;  // trace slots of split stages
+  if (tid == 0 && ts >= 0) stamp(a, l, kTraceAcc + ts);
   __syncwarp();
   fence_after();
   int v[16];
@@ -364,19 +451,17 @@ __device__ void item_epilogue(const Args& a, Ctrl& cs, WorkerCtx& w, const Item 
   fence_before();
   mbar_arrive(&cs.acc_empty[b]);
   ++w.item_no;
-  const int s = it.stage;
   if (split(s) > 1) {
     const int at = acc_tile_base(s) + it.tile;
     int* g = a.acc + ((size_t)at * kTileM + r) * 12;
 #pragma unroll
     for (int c = 0; c < 12; ++c)
       if ((c & 3) < nt) atomicAdd(&g[c], v[c]);
-    __threadfence();
     named_sync(kBarW, kWorkers);
-    if (tid == 0) cs.flag = atomicAdd(&a.sync->tile_cnt[at], 1u) == (unsigned)(split(s) - 1);
+    if (tid == 0) cs.flag = atom_add_acq_rel(&a.sync->tile_cnt[at].v, 1u) == (unsigned)(split(s) - 1);
     named_sync(kBarW, kWorkers);
+    if (tid == 0 && ts >= 0) stamp(a, l, kTraceArrived + ts);
     if (!cs.flag) return;
-    __threadfence();
 #pragma unroll
     for (int c = 0; c < 12; ++c) {
       if ((c & 3) < nt) {
@@ -384,7 +469,7 @@ __device__ void item_epilogue(const Args& a, Ctrl& cs, WorkerCtx& w, const Item 
         g[c] = 0;
       }
     }
-    if (tid == 0) a.sync->tile_cnt[at] = 0u;
+    if (tid == 0) a.sync->tile_cnt[at].v = 0u;
   }
   float yv[4];
 #pragma unroll
@@ -392,95 +477,102 @@ __device__ void item_epilogue(const Args& a, Ctrl& cs, WorkerCtx& w, const Item 
     const long long tot = (long long)v[t] + 256ll * (long long)v[4 + t] + 65536ll * (long long)v[8 + t];
     yv[t] = (float)((double)tot * (double)step[t]);
   }
-  const LayerDev& L = a.layers[l];
   int done_slot = kDoneQkv;
   if (s == kQkv) {
     // tile = head (12 q, 2 k, 2 v); rotate-half pairs (r, r ^ 64) exchanged through shared memory
-    const int row = it.tile * kTileM + r;
-    const float bb = __ldg(L.qkv_b + row), sc = __ldg(L.qkv_s + row);
 #pragma unroll
-    for (int t = 0; t < 4; ++t) cs.ys[r][t] = __fmaf_rn(sc, yv[t], bb);
+    for (int t = 0; t < 4; ++t) cs.ys[r][t] = __fmaf_rn(k.sc, yv[t], k.bb);
     named_sync(kBarW, kWorkers);
-    const int h = it.tile;
-    const KvView kv{a.kv_pool, nullptr, a.page_table, l, a.max_pages};
+    const bool rope = it.tile < kHeads + kKvHeads;
     for (int t = 0; t < nt; ++t) {
       const float mine = cs.ys[r][t], other = cs.ys[r ^ 64][t];
       float y = mine;
-      const int pos = __ldcg(&a.pos[t]);
-      if (h < kHeads + kKvHeads) {
-        const int p = r & 63;
-        const float c = __ldg(a.rope_cos + (size_t)pos * 64 + p), sn = __ldg(a.rope_sin + (size_t)pos * 64 + p);
-        y = r < 64 ? __fsub_rn(__fmul_rn(mine, c), __fmul_rn(other, sn))
-                   : __fadd_rn(__fmul_rn(mine, c), __fmul_rn(other, sn));
-      }
-      if (h < kHeads) {
-        a.q[(size_t)t * kHidden + row] = y;
-      } else {
-        const int which = h < kHeads + kKvHeads ? 0 : 1;
-        kv_row(kv, __ldcg(&a.seq[t]), pos, which)[row - kHidden - which * kKvWidth] = y;
-      }
+      if (rope)
+        y = r < 64 ? __fsub_rn(__fmul_rn(mine, k.rc[t]), __fmul_rn(other, k.rs[t]))
+                   : __fadd_rn(__fmul_rn(mine, k.rc[t]), __fmul_rn(other, k.rs[t]));
+      *k.dst[t] = y;
     }
     done_slot = kDoneQkv;
   } else if (s == kO) {
-    const int row = it.tile * kTileM + r;
-    const float sc = __ldg(L.o_s + row);
-    for (int t = 0; t < nt; ++t) a.a[(size_t)t * kHidden + row] = sc * yv[t];
+    for (int t = 0; t < nt; ++t) *k.dst[t] = k.sc * yv[t];
     done_slot = kDoneO;
   } else if (s == kGu) {
     // tile rows 0..63: gate rows 64 j.., rows 64..127: the matching up rows
-    const int row = r < 64 ? it.tile * 64 + r : kInter + it.tile * 64 + (r - 64);
-    const float sc = __ldg(L.gu_s + row);
 #pragma unroll
-    for (int t = 0; t < 4; ++t) cs.ys[r][t] = sc * yv[t];
+    for (int t = 0; t < 4; ++t) cs.ys[r][t] = k.sc * yv[t];
     named_sync(kBarW, kWorkers);
     if (r < 64) {  // warps of TMEM quarters 0 and 1
       for (int t = 0; t < nt; ++t) {
         const float gv = cs.ys[r][t], uv = cs.ys[r + 64][t];
         const float silu = __fdiv_rn(gv, __fadd_rn(1.0f, expf(-gv)));
         const float hv = __fmul_rn(silu, uv);
-        a.h[(size_t)t * kInter + it.tile * 64 + r] = hv;
+        *k.dst[t] = hv;
         const float m = warp_max(fabsf(hv));
-        if (w.lane == 0) atomicMax(&a.sync->hmax[l][t], __float_as_uint(m));
+        if (w.lane == 0) atomicMax(&a.sync->hmax[l].pad[t], __float_as_uint(m));
       }
     }
     done_slot = kDoneGu;
   } else {
     const int row = it.tile * kTileM + r;
-    const float sc = __ldg(L.down_s + row);
-    float* yout = (l & 1) ? a.y1 : a.y0;
     for (int t = 0; t < nt; ++t) {
-      float y = __fadd_rn(__ldcg(&a.a[(size_t)t * kHidden + row]), sc * yv[t]);
-      y = round_bf16(y);
-      yout[(size_t)t * kHidden + row] = y;
+      const float y = round_bf16(__fadd_rn(k.res[t], k.sc * yv[t]));
+      *k.dst[t] = y;
       if (a.dump != nullptr) a.dump[((size_t)l * nt + t) * kHidden + row] = y;
     }
     done_slot = kDoneDown;
   }
-  __threadfence();
   named_sync(kBarW, kWorkers);
-  if (tid == 0) atomicAdd(&a.sync->done[l][done_slot], 1u);
+  if (tid == 0) red_release(&a.sync->done[l][done_slot].v, 1u);
 }
 
 // ---------------------------------------------------------------------------------------------------
 // workers: attention (hls/decode_only/qwen_decode_attention_kernel.cpp:113-162), one 64-key chunk of one
 // (token, KV head) per item; chunk partials merged in chunk order by the last chunk to finish.
 // ---------------------------------------------------------------------------------------------------
-__device__ void attn_item(const Args& a, AttnSmem& sm, Ctrl& cs, int l, int t, int g, int c, int nchunks, int tid) {
-  const int warp = tid >> 5, lane = tid & 31;
-  const int L = __ldcg(&a.pos[t]) + 1;
-  const int seq = __ldcg(&a.seq[t]);
-  const int k0 = c * kChunk;
-  const int n = min(kChunk, L - k0);
-  const KvView kv{a.kv_pool, nullptr, a.page_table, l, a.max_pages};
-  static_assert(kChunk == kPage, "an attention chunk must map onto one KV page");
-  const float* kbase = kv_row(kv, seq, k0, 0) + g * kHeadDim;
-  const float* vbase = kv_row(kv, seq, k0, 1) + g * kHeadDim;
-  named_sync(kBarW, kWorkers);  // the previous item is done with the shared buffers
-  for (int i = tid; i < n * 32; i += kWorkers) {
-    const int rr = i >> 5, f = i & 31;
-    cp_async16(&sm.ks[rr][4 * f], kbase + (size_t)rr * kKvWidth + 4 * f);
-    cp_async16(&sm.vs[rr][4 * f], vbase + (size_t)rr * kKvWidth + 4 * f);
+struct AttnItem {
+  int t, g, c, nchunks, n, nhist;
+  const float* kbase;
+  const float* vbase;
+};
+
+__device__ __forceinline__ AttnItem attn_decode(const Args& a, const WorkerCtx& w, int l, int i, const int (&nch)[4]) {
+  AttnItem it;
+  int t = 0, rem = i;
+  while (rem >= kKvHeads * nch[t]) {
+    rem -= kKvHeads * nch[t];
+    ++t;
   }
+  it.t = t;
+  it.g = rem / nch[t];
+  it.c = rem % nch[t];
+  it.nchunks = nch[t];
+  const int L = w.pos[t] + 1;
+  const int k0 = it.c * kChunk;
+  it.n = min(kChunk, L - k0);
+  it.nhist = min(it.n, w.pos[t] - k0);  // rows written by earlier steps
+  static_assert(kChunk == kPage, "an attention chunk must map onto one KV page");
+  const KvView kv{a.kv_pool, nullptr, a.page_table, l, a.max_pages};
+  it.kbase = kv_row(kv, w.seq[t], k0, 0) + it.g * kHeadDim;
+  it.vbase = kv_row(kv, w.seq[t], k0, 1) + it.g * kHeadDim;
+  return it;
+}
+
+// cp.async of chunk rows [r0, r1) of K and V (the rows of a chunk are 256 floats apart: one KV page)
+__device__ __forceinline__ void attn_load_rows(AttnSmem& sm, const AttnItem& it, int r0, int r1, int tid) {
+  for (int i = r0 * 32 + tid; i < r1 * 32; i += kWorkers) {
+    const int rr = i >> 5, f = i & 31;
+    cp_async16(&sm.ks[rr][4 * f], it.kbase + (size_t)rr * kKvWidth + 4 * f);
+    cp_async16(&sm.vs[rr][4 * f], it.vbase + (size_t)rr * kKvWidth + 4 * f);
+  }
+}
+
+// One 64-key chunk of one (token, KV head): the history rows are already in flight; loads the new row
+// (when it falls in this chunk) and the six query heads, then scores, softmax statistics and P.V; the last
+// chunk of a (token, KV head) to finish merges all chunks in chunk order.
+__device__ void attn_item(const Args& a, AttnSmem& sm, Ctrl& cs, int l, const AttnItem& it, int tid) {
+  const int warp = tid >> 5, lane = tid & 31;
+  const int t = it.t, g = it.g, n = it.n, nchunks = it.nchunks;
+  attn_load_rows(sm, it, it.nhist, it.n, tid);
   for (int i = tid; i < kGroups * 32; i += kWorkers) {
     const int hh = i >> 5, f = i & 31;
     cp_async16(&sm.qs[hh][4 * f], a.q + (size_t)t * kHidden + (g * kGroups + hh) * kHeadDim + 4 * f);
@@ -518,12 +610,12 @@ __device__ void attn_item(const Args& a, AttnSmem& sm, Ctrl& cs, int l, int t, i
       const float e1 = lane + 32 < n ? expf(x1 - m) : 0.f;
       sm.es[lane][hh] = e0;
       sm.es[lane + 32][hh] = e1;
-      float s = e0 + e1;
+      float sum = e0 + e1;
 #pragma unroll
-      for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+      for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
       if (lane == 0) {
         sm.ms[hh] = m;
-        sm.ls[hh] = s;
+        sm.ls[hh] = sum;
       }
     }
   }
@@ -553,19 +645,19 @@ __device__ void attn_item(const Args& a, AttnSmem& sm, Ctrl& cs, int l, int t, i
     }
     finished = true;
   } else {
-    float* my = a.attn_part + (((size_t)t * kKvHeads + g) * a.attn_max_chunks + c) * kGroups * kPartStride;
+    float* my = a.attn_part + (((size_t)t * kKvHeads + g) * a.attn_max_chunks + it.c) * kGroups * kPartStride;
 #pragma unroll
     for (int hh = 0; hh < kGroups; ++hh) my[hh * kPartStride + 2 + tid] = acc[hh];
     if (tid < kGroups) {
       my[tid * kPartStride + 0] = sm.ms[tid];
       my[tid * kPartStride + 1] = sm.ls[tid];
     }
-    __threadfence();
     named_sync(kBarW, kWorkers);
-    if (tid == 0) cs.flag = atomicAdd(&a.sync->attn_cnt[t][g], 1u) == (unsigned)nchunks - 1u;
+    if (tid == 0) cs.flag = atom_add_acq_rel(&a.sync->attn_cnt[t][g].v, 1u) == (unsigned)nchunks - 1u;
     named_sync(kBarW, kWorkers);
     if (cs.flag) {
-      __threadfence();
+      // merge in chunk order: M = max of the chunk maxima, then o = sum acc_c w_c, L = sum l_c w_c with
+      // w_c = expf(m_c - M); every thread reads the (small) statistics itself, no shared-memory staging
       const float* base = a.attn_part + ((size_t)t * kKvHeads + g) * a.attn_max_chunks * kGroups * kPartStride;
       float o[kGroups], Lsum[kGroups], M[kGroups];
 #pragma unroll
@@ -578,24 +670,29 @@ __device__ void attn_item(const Args& a, AttnSmem& sm, Ctrl& cs, int l, int t, i
 #pragma unroll
         for (int hh = 0; hh < kGroups; ++hh) M[hh] = fmaxf(M[hh], __ldcg(&base[(cc * kGroups + hh) * kPartStride]));
       }
-      for (int c0 = 0; c0 < nchunks; c0 += kChunk) {
-        const int cn = min(kChunk, nchunks - c0);
-        named_sync(kBarW, kWorkers);
-        for (int i = tid; i < cn * kGroups; i += kWorkers) {
-          const int cc = i / kGroups, hh = i % kGroups;
-          const float* pc = base + ((c0 + cc) * kGroups + hh) * kPartStride;
-          const float wgt = expf(__ldcg(&pc[0]) - M[hh]);
-          sm.es[cc][hh] = wgt;
-          sm.vs[cc][hh] = __ldcg(&pc[1]) * wgt;
-        }
-        named_sync(kBarW, kWorkers);
-#pragma unroll 4
-        for (int cc = 0; cc < cn; ++cc) {
-          const float* pc = base + (size_t)(c0 + cc) * kGroups * kPartStride + 2 + tid;
+      constexpr int kB = 8;
+      for (int c0 = 0; c0 < nchunks; c0 += kB) {
+        float av[kB][kGroups], mv[kB][kGroups], lv[kB][kGroups];
+#pragma unroll
+        for (int cc = 0; cc < kB; ++cc) {
 #pragma unroll
           for (int hh = 0; hh < kGroups; ++hh) {
-            o[hh] = fmaf(__ldcg(&pc[hh * kPartStride]), sm.es[cc][hh], o[hh]);
-            Lsum[hh] += sm.vs[cc][hh];
+            const bool in = c0 + cc < nchunks;
+            const float* pc = base + ((size_t)(c0 + cc) * kGroups + hh) * kPartStride;
+            av[cc][hh] = in ? __ldcg(&pc[2 + tid]) : 0.f;
+            mv[cc][hh] = in ? __ldcg(&pc[0]) : 0.f;
+            lv[cc][hh] = in ? __ldcg(&pc[1]) : 0.f;
+          }
+        }
+#pragma unroll
+        for (int cc = 0; cc < kB; ++cc) {
+          if (c0 + cc < nchunks) {
+#pragma unroll
+            for (int hh = 0; hh < kGroups; ++hh) {
+              const float wgt = expf(mv[cc][hh] - M[hh]);
+              o[hh] = fmaf(av[cc][hh], wgt, o[hh]);
+              Lsum[hh] = __fadd_rn(Lsum[hh], __fmul_rn(lv[cc][hh], wgt));  // rounded product, then sum
+            }
           }
         }
       }
@@ -604,33 +701,39 @@ __device__ void attn_item(const Args& a, AttnSmem& sm, Ctrl& cs, int l, int t, i
         const float inv = Lsum[hh] > 0.0f ? 1.0f / Lsum[hh] : 0.0f;
         out_base[hh * kHeadDim] = o[hh] * inv;
       }
-      if (tid == 0) a.sync->attn_cnt[t][g] = 0u;
+      if (tid == 0) a.sync->attn_cnt[t][g].v = 0u;
       finished = true;
     }
   }
   if (finished) {  // uniform across the workers
-    __threadfence();
     named_sync(kBarW, kWorkers);
-    if (tid == 0) atomicAdd(&a.sync->done[l][kDoneAttn], 1u);
+    if (tid == 0) red_release(&a.sync->done[l][kDoneAttn].v, 1u);
   }
 }
 
-__device__ void attention_stage(const Args& a, AttnSmem& sm, Ctrl& cs, int l, int tid, unsigned* abort_flag) {
+// Attention of layer l over this CTA's chunks (items blockIdx.x, + gridDim.x, ...). The history rows of
+// the first chunk do not depend on this step and are requested before the wait for q|k|v.
+__device__ void attention_stage(const Args& a, AttnSmem& sm, Ctrl& cs, const WorkerCtx& w, int l,
+                                unsigned* abort_flag) {
+  const int tid = w.tid;
   int nch[4] = {0, 0, 0, 0}, total = 0;
   for (int t = 0; t < a.nt; ++t) {
-    nch[t] = (__ldcg(&a.pos[t]) + 1 + kChunk - 1) / kChunk;
+    nch[t] = (w.pos[t] + 1 + kChunk - 1) / kChunk;
     total += kKvHeads * nch[t];
   }
   if ((int)blockIdx.x >= total) return;
-  workers_wait(&a.sync->done[l][kDoneQkv], (unsigned)tiles(kQkv), abort_flag, tid);
+  named_sync(kBarW, kWorkers);  // shared memory free: this CTA's earlier epilogues are done
+  AttnItem it = attn_decode(a, w, l, blockIdx.x, nch);
+  attn_load_rows(sm, it, 0, it.nhist, tid);
+  workers_wait(&a.sync->done[l][kDoneQkv].v, (unsigned)tiles(kQkv), abort_flag, tid);
   if (tid == 0) stamp(a, l, kTraceWait + 1);
-  for (int i = blockIdx.x; i < total; i += gridDim.x) {
-    int t = 0, rem = i;
-    while (rem >= kKvHeads * nch[t]) {
-      rem -= kKvHeads * nch[t];
-      ++t;
-    }
-    attn_item(a, sm, cs, l, t, rem / nch[t], rem % nch[t], nch[t], tid);
+  for (int i = blockIdx.x;;) {
+    attn_item(a, sm, cs, l, it, tid);
+    i += gridDim.x;
+    if (i >= total) break;
+    it = attn_decode(a, w, l, i, nch);
+    named_sync(kBarW, kWorkers);  // previous chunk done with the shared buffers
+    attn_load_rows(sm, it, 0, it.nhist, tid);
   }
   if (tid == 0) stamp(a, l, kTraceDone + 1);
 }
@@ -644,6 +747,14 @@ __device__ void workers(const Args& a, uint8_t* uni, Ctrl& cs, uint32_t tmem, ui
   w.r = w.quarter * 32 + w.lane;
   w.item_no = 0;
   w.tmem = tmem;
+  {
+    const KvView kv0{a.kv_pool, nullptr, a.page_table, 0, a.max_pages};
+    for (int t = 0; t < 4; ++t) {
+      w.pos[t] = t < a.nt ? __ldcg(&a.pos[t]) : 0;
+      w.seq[t] = t < a.nt ? __ldcg(&a.seq[t]) : 0;
+      w.kvrow[t] = t < a.nt ? kv_row(kv0, w.seq[t], w.pos[t], 0) : nullptr;
+    }
+  }
   uint32_t sb[kNumProj], se[kNumProj];
   for (int s = 0; s < kNumProj; ++s) sb[s] = se[s] = i0;
   for (uint32_t i = i0; i < i1; ++i) {
@@ -663,39 +774,42 @@ __device__ void workers(const Args& a, uint8_t* uni, Ctrl& cs, uint32_t tmem, ui
   const bool tr = w.tid == 0;
   for (int l = 0; l < kLayers; ++l) {
     const LayerDev& L = a.layers[l];
-    unsigned* done = a.sync->done[l];
+    SyncWord* done = a.sync->done[l];
     // q|k|v (input: previous layer's output, or the token embeddings)
+    float4 wv[3];
     if (sb[kQkv] < se[kQkv]) {
-      if (l > 0) workers_wait(&a.sync->done[l - 1][kDoneDown], (unsigned)tiles(kDown), abort_flag, w.tid);
+      load_norm(L.input_ln, w.tid, wv);
+      if (l > 0) workers_wait(&a.sync->done[l - 1][kDoneDown].v, (unsigned)tiles(kDown), abort_flag, w.tid);
       if (tr) stamp(a, l, kTraceWait + 0);
       const float* xin = l == 0 ? nullptr : (((l - 1) & 1) ? a.y1 : a.y0);
-      build_full(a, cs, digits(inst), xin, L.input_ln, w.tid, step);
+      build_full(a, cs, digits(inst), xin, true, wv, w.tid, step);
       ready();
       if (tr) stamp(a, l, kTraceBuilt + 0);
       for (uint32_t i = sb[kQkv]; i < se[kQkv]; ++i) item_epilogue(a, cs, w, a.items[i], l, step, abort_flag);
       if (tr) stamp(a, l, kTraceDone + 0);
     }
-    attention_stage(a, asm_, cs, l, w.tid, abort_flag);
+    attention_stage(a, asm_, cs, w, l, abort_flag);
     if (sb[kO] < se[kO]) {
-      workers_wait(&done[kDoneAttn], (unsigned)(kKvHeads * a.nt), abort_flag, w.tid);
+      workers_wait(&done[kDoneAttn].v, (unsigned)(kKvHeads * a.nt), abort_flag, w.tid);
       if (tr) stamp(a, l, kTraceWait + 2);
-      build_full(a, cs, digits(inst), a.ctx, nullptr, w.tid, step);
+      build_full(a, cs, digits(inst), a.ctx, false, wv, w.tid, step);
       ready();
       if (tr) stamp(a, l, kTraceBuilt + 2);
       for (uint32_t i = sb[kO]; i < se[kO]; ++i) item_epilogue(a, cs, w, a.items[i], l, step, abort_flag);
       if (tr) stamp(a, l, kTraceDone + 2);
     }
     if (sb[kGu] < se[kGu]) {
-      workers_wait(&done[kDoneO], (unsigned)tiles(kO), abort_flag, w.tid);
+      load_norm(L.post_ln, w.tid, wv);
+      workers_wait(&done[kDoneO].v, (unsigned)tiles(kO), abort_flag, w.tid);
       if (tr) stamp(a, l, kTraceWait + 3);
-      build_full(a, cs, digits(inst), a.a, L.post_ln, w.tid, step);
+      build_full(a, cs, digits(inst), a.a, true, wv, w.tid, step);
       ready();
       if (tr) stamp(a, l, kTraceBuilt + 3);
       for (uint32_t i = sb[kGu]; i < se[kGu]; ++i) item_epilogue(a, cs, w, a.items[i], l, step, abort_flag);
       if (tr) stamp(a, l, kTraceDone + 3);
     }
     if (sb[kDown] < se[kDown]) {
-      workers_wait(&done[kDoneGu], (unsigned)tiles(kGu), abort_flag, w.tid);
+      workers_wait(&done[kDoneGu].v, (unsigned)tiles(kGu), abort_flag, w.tid);
       if (tr) stamp(a, l, kTraceWait + 4);
       build_down(a, digits(inst), l, sb[kDown], se[kDown], w.tid, step);
       ready();
@@ -714,7 +828,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_stack_kernel(const __grid_
   Ctrl& cs = *reinterpret_cast<Ctrl*>(uni + kUnionBytes);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t i0 = a.item_off[blockIdx.x], i1 = a.item_off[blockIdx.x + 1];
-  unsigned* abort_flag = &a.sync->abort_flag;
+  unsigned* abort_flag = &a.sync->abort_flag.v;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kRing; ++s) {
@@ -750,11 +864,14 @@ __global__ void __launch_bounds__(kThreads, 1) decode_stack_kernel(const __grid_
   }
   if (threadIdx.x == 0) {
     __threadfence();
-    const unsigned prev = atomicAdd(&a.sync->exit_cnt, 1u);
+    const unsigned prev = atomicAdd(&a.sync->exit_cnt.v, 1u);
     if (prev == gridDim.x - 1) {  // every CTA is past its last wait: clear the words for the next launch
       __threadfence();
-      unsigned* wds = reinterpret_cast<unsigned*>(a.sync);
-      for (size_t i = 0; i < sizeof(SyncWords) / 4; ++i) wds[i] = 0u;
+      SyncWord* wds = reinterpret_cast<SyncWord*>(a.sync);
+      for (size_t i = 0; i < sizeof(SyncWords) / sizeof(SyncWord); ++i) {
+        wds[i].v = 0u;
+        for (int j = 0; j < 4; ++j) wds[i].pad[j] = 0u;  // hmax keeps its words here
+      }
       __threadfence();
     }
   }
@@ -791,19 +908,28 @@ Schedule build_schedule(int ctas) {
         const int kb0 = seg * seg_blocks(s), kb1 = std::min(nkb(s), kb0 + seg_blocks(s));
         if (kb0 < kb1) all.push_back({s, tile, seg, kb0, kb1});
       }
-  // largest items first onto the least-loaded CTA (load = 16 KB units streamed per layer)
+  // Largest items first onto the least-loaded CTA (load = 16 KB units streamed per layer), preferring CTAs
+  // that have no item of the same stage yet: a CTA's epilogues of one stage run one after another, so one
+  // item per stage and CTA keeps every stage's tail short.
   std::stable_sort(all.begin(), all.end(), [](const Cand& x, const Cand& y) { return x.kb1 - x.kb0 > y.kb1 - y.kb0; });
   std::vector<int> load(ctas, 0), down_blocks(ctas, 0);
+  std::vector<std::vector<int>> per_stage(kNumProj, std::vector<int>(ctas, 0));
   std::vector<std::vector<Cand>> per(ctas);
   for (const Cand& c : all) {
     const int units = c.kb1 - c.kb0;
     int best = -1;
     for (int k = 0; k < ctas; ++k) {
       if (c.stage == kDown && down_blocks[k] + units > kDigitBlocks) continue;
-      if (best < 0 || load[k] < load[best]) best = k;
+      if (best < 0) {
+        best = k;
+        continue;
+      }
+      const int nk = per_stage[c.stage][k], nb = per_stage[c.stage][best];
+      if (nk < nb || (nk == nb && load[k] < load[best])) best = k;
     }
     per[best].push_back(c);
     load[best] += units;
+    ++per_stage[c.stage][best];
     if (c.stage == kDown) down_blocks[best] += units;
   }
   Schedule sc;

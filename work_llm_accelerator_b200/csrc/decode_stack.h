@@ -43,14 +43,21 @@ struct Item {
 };
 static_assert(sizeof(Item) == 8, "item packing");
 
+// One synchronisation word per 128-byte line, so that polling one counter does not queue behind atomics
+// on its neighbours.
+struct alignas(128) SyncWord {
+  unsigned v;
+  unsigned pad[31];
+};
+
 // Device-side synchronisation words (zero between launches; the kernel leaves them zero).
 struct SyncWords {
-  unsigned done[kLayers][kDoneSlots];
-  unsigned hmax[kLayers][4];  // max |h| per token (float bits), for the down projection's digit step
-  unsigned tile_cnt[kAccTiles];
-  unsigned attn_cnt[4][2];
-  unsigned exit_cnt;
-  unsigned abort_flag;
+  SyncWord done[kLayers][kDoneSlots];
+  SyncWord hmax[kLayers];      // .pad[0..3]: max |h| per token (float bits), for the down projection's step
+  SyncWord tile_cnt[kAccTiles];
+  SyncWord attn_cnt[4][2];
+  SyncWord exit_cnt;
+  SyncWord abort_flag;
 };
 
 // Static per-layer work split over `ctas` CTAs: items of CTA c are items[off[c] .. off[c + 1]), in stage
@@ -89,6 +96,7 @@ struct Args {
   const uint32_t* item_off;   // [ctas + 1]
   const Item* items;
   unsigned long long* trace;  // optional [ctas][28][kTraceSlots] global-timer stamps (ns), see kTrace*
+  int ring;                   // weight stages in flight per CTA (2..9)
 };
 
 // Timeline slots of the optional trace, per CTA and layer (stage index: 0 q|k|v, 1 attention, 2 o,
@@ -98,8 +106,11 @@ struct Args {
 //   kTraceDone + i   workers: every epilogue of stage i done
 //   kTraceIssue + s  producer: first weight unit of projection s issued
 //   kTraceMma + s    MMA issuer: last MMA of projection s committed
+//   kTraceAcc + j    workers: accumulator of the CTA's last item of split stage j (0 q|k|v, 1 o, 2 down) ready
+//   kTraceArrived + j   workers: that item's split-K partial added and counted
 constexpr int kTraceSlots = 32;
-constexpr int kTraceWait = 0, kTraceBuilt = 5, kTraceDone = 10, kTraceIssue = 16, kTraceMma = 20;
+constexpr int kTraceWait = 0, kTraceBuilt = 5, kTraceDone = 10, kTraceIssue = 16, kTraceMma = 20, kTraceAcc = 24,
+              kTraceArrived = 27;
 
 // Launch over `ctas` CTAs (cooperative: all resident). Requires wbits 8 weights in the tiled layout.
 cudaError_t launch_decode_stack(const Args& a, int ctas, cudaStream_t s);

@@ -141,6 +141,7 @@ struct qwen_engine {
   int stack_ctas = 0;
   int attn_max_chunks = 0;
   unsigned long long* trace = nullptr;  // optional timeline of the persistent kernel
+  int stack_ring = 9;                   // weight stages in flight per CTA
 };
 
 namespace {
@@ -296,6 +297,7 @@ int enqueue_decode(qwen_engine* e, int nt, int max_len, bool advance) {
     a.item_off = e->d_item_off;
     a.items = e->d_items;
     a.trace = e->trace;
+    a.ring = e->stack_ring;
     E_TRY(stack::launch_decode_stack(a, e->stack_ctas, e->stream));
     xin = ((kLayers - 1) & 1) ? e->y1 : e->y0;
   }
@@ -532,6 +534,11 @@ int qwen_engine_set_option(qwen_engine* e, const char* name, long long value) {
       E_TRY(cudaFree(e->trace));
       e->trace = nullptr;
     }
+    for (auto& kv : e->graphs) cudaGraphExecDestroy(kv.second);
+    e->graphs.clear();
+  } else if (n == "stack_ring") {
+    if (value < 2 || value > 9) return kStatusInvalid;
+    e->stack_ring = (int)value;
     for (auto& kv : e->graphs) cudaGraphExecDestroy(kv.second);
     e->graphs.clear();
   } else if (n == "stack") {
