@@ -51,9 +51,16 @@ def step_bytes(wbits: int, history: float) -> float:
     return LAYERS * per_layer + VOCAB * HIDDEN * 2 + HIDDEN * 4
 
 
-def gateup_bytes(wbits: int) -> int:
-    """Algorithmic bytes of one gate|up GEMV launch (batch 1): codes, scales, norm weight, input, output."""
-    return 2 * INTER * HIDDEN * wbits // 8 + 2 * INTER * 4 + HIDDEN * 4 + HIDDEN * 4 + INTER * 4
+def layers_bytes(wbits: int, history: float) -> float:
+    """Algorithmic HBM bytes of the 28-layer part of one batch-1 decode step (the persistent kernel): every
+    layer's weight codes and fp32 vectors, the K/V history read and the new K/V row written."""
+    per_layer = layer_weight_bytes(wbits) + LAYER_FLOAT_BYTES + (history + 1) * 2 * KV_WIDTH * 4 + 2 * KV_WIDTH * 4
+    return LAYERS * per_layer
+
+
+def lm_head_bytes() -> float:
+    """Algorithmic HBM bytes of the final norm + fp16 LM head + argmax (batch 1)."""
+    return VOCAB * HIDDEN * 2 + HIDDEN * 4
 
 
 def peaks() -> tuple[float, str]:
@@ -250,10 +257,9 @@ def run_b200(args, world: int, rank: int, local: int) -> dict | None:
     os.environ["QWEN_B200_DEVICE"] = str(local)
     wbits = args.wbits
     total_steps = args.warmup + args.steps
-    max_len = PROMPT + 2 * total_steps + 64
+    max_len = PROMPT + 2 * total_steps + 3 + 32 + 64  # device loop, e2e steps, per-kernel profile, margin
     eng = host.Engine(local, wbits, max_seqs=1, max_len=max_len)
     eng.init_synthetic(SEED)
-    prof = eng.profile_kernels(1, PROMPT, iters=56)
     rng = np.random.default_rng(SEED + rank)
     prompt = rng.integers(0, VOCAB, PROMPT).astype(np.int32)
     first = eng.prefill(0, prompt)
@@ -307,6 +313,10 @@ def run_b200(args, world: int, rank: int, local: int) -> dict | None:
         e1.synchronize()
     ms_e2e = e0.elapsed_time(e1) / args.steps
 
+    # per-kernel device time over the same histories: the 28-layer kernel and the LM head, each timed with
+    # CUDA events on the engine stream (eager launches, otherwise the same work as one graph step)
+    prof = eng.profile_decode(0, cur, max(8, min(args.steps, 32)))
+
     t = torch.tensor([ms, ms_e2e], dtype=torch.float64, device="cuda")
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
@@ -317,14 +327,17 @@ def run_b200(args, world: int, rank: int, local: int) -> dict | None:
         return None
 
     peak, peak_kind = peaks()
-    gu_ms = prof["gate_up"]
-    gu_achieved = gateup_bytes(wbits) / (gu_ms * 1e-3) / 1e9
+    hist_prof = history_mid + args.steps  # histories of the profiled steps (after the e2e steps)
+    lb = layers_bytes(wbits, hist_prof)
+    layers_achieved = lb / (prof["layers"] * 1e-3) / 1e9
+    head_achieved = lm_head_bytes() / (prof["lm_head"] * 1e-3) / 1e9
     sb = step_bytes(wbits, history_mid)
     step_achieved = sb / (ms * 1e-3) / 1e9
     traffic = None
-    tr = ROOT / "profiles" / "gateup_w8_dram_bytes.json"
-    if tr.exists():
-        traffic = json.loads(tr.read_text()).get("dram_bytes_per_launch")
+    tr = ROOT / "profiles" / "decode_stack_w8_bs1_dram.json"
+    if tr.exists() and wbits == 8:
+        d = json.loads(tr.read_text())
+        traffic = d.get("dram_bytes_per_launch")
     out = {
         "metric": METRIC,
         "value": world / (ms * 1e-3),
@@ -345,10 +358,14 @@ def run_b200(args, world: int, rank: int, local: int) -> dict | None:
                    "l2": f"inputs larger than L2: {sb / 1e9:.2f} GB of weights/KV per step vs 126 MB L2",
                    "wbits": wbits},
         "e2e": {"value": world / (ms_e2e * 1e-3), "unit": "tok/s", "h2d_bytes_per_step": 12, "d2h_bytes_per_step": 4},
-        "roofline": {"bound": "hbm", "kernel": "decode gate|up GEMV (W8, batch 1)", "achieved": gu_achieved,
-                     "peak": peak, "unit": "GB/s", "frac": gu_achieved / peak, "traffic": traffic,
-                     "peak_source": peak_kind, "algorithmic_bytes_per_launch": gateup_bytes(wbits),
-                     "launch_ms": gu_ms},
+        "roofline": {"bound": "hbm",
+                     "kernel": ("decode_stack_kernel: persistent 28-layer W8 decode step (1 launch per step)"
+                                if wbits == 8 else "28 layers x 5 CUDA-core kernels (W4)"),
+                     "achieved": layers_achieved, "peak": peak, "unit": "GB/s", "frac": layers_achieved / peak,
+                     "traffic": traffic, "peak_source": peak_kind, "algorithmic_bytes_per_launch": lb,
+                     "launch_ms": prof["layers"]},
+        "lm_head_roofline": {"achieved": head_achieved, "frac": head_achieved / peak, "launch_ms": prof["lm_head"],
+                             "algorithmic_bytes_per_launch": lm_head_bytes()},
         "step_roofline": {"achieved": step_achieved, "peak": peak, "unit": "GB/s", "frac": step_achieved / peak,
                           "algorithmic_bytes_per_step": sb},
         "kernel_ms": prof,

@@ -86,6 +86,10 @@ int qwen_engine_read_layer(qwen_engine* e, int layer, uint8_t* weight_ddr, float
  * that weights come from HBM, not L2) for `n` tokens at history `past`; ms_out[6] receives the mean
  * per-launch milliseconds of {qkv, attention, o, gate_up, down, lm_head}. */
 int qwen_engine_profile_kernels(qwen_engine* e, int n, int past, int iters, float* ms_out);
+/* Per-kernel device time of `steps` eager greedy decode steps of one sequence (device-resident tokens,
+ * starting from first_token): ms_out[0] = mean milliseconds of the 28-layer part (the persistent W8 kernel,
+ * or the five kernels per layer otherwise), ms_out[1] = the final norm + LM head + argmax kernel. */
+int qwen_engine_profile_decode(qwen_engine* e, int slot, int first_token, int steps, float* ms_out);
 /* The engine's CUDA stream (cudaStream_t) for callers that record their own events. */
 void* qwen_engine_stream(qwen_engine* e);
 /* Number of kernels one decode step of `n` sequences launches. */

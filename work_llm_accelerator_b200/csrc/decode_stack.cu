@@ -224,6 +224,7 @@ __device__ void mma_issuer(const Args& a, uint8_t* ring_smem, uint8_t* digits, C
         const unsigned p = inst & 1;
         ok = ok && mwait(&cs.dig_ready[p], (inst >> 1) & 1, abort_flag);
         fence_after();
+        stamp(a, l, kTraceMmaStart + cur);
         dbase = smem_u32(digits + (size_t)p * kDigitBytes);
         ++inst;
       }
@@ -273,42 +274,99 @@ __device__ __forceinline__ void put_digits(uint8_t* blk, int t, int kk, const fl
   *reinterpret_cast<uint32_t*>(blk + sw128_offset(8 + t, kk)) = w2;
 }
 
-// Digits of a whole 1536-wide row per token: x (or the embedding rows of the tokens when x is null),
-// optionally RMS-normalised with norm_w (double accumulation, as the decode reference). Thread tid owns
-// elements 512 j + 4 tid .. +3, j < 3.
-__device__ __forceinline__ void load_norm(const float* norm_w, int tid, float4 (&wv)[3]) {
+// This thread's 12 elements (512 j + 4 tid .. +3, j < 3) of a 1536-float parameter vector.
+__device__ __forceinline__ void load_norm(const float* vec, int tid, float4 (&wv)[3]) {
 #pragma unroll
-  for (int j = 0; j < 3; ++j) wv[j] = __ldg(reinterpret_cast<const float4*>(norm_w + 512 * j + 4 * tid));
+  for (int j = 0; j < 3; ++j) wv[j] = __ldg(reinterpret_cast<const float4*>(vec + 512 * j + 4 * tid));
 }
 
-// wv: the norm weights of this thread's elements (loaded before the wait for x), used when norm is true.
-__device__ void build_full(const Args& a, Ctrl& cs, uint8_t* dbuf, const float* x, bool norm, const float4 (&wv)[3],
-                           int tid, float (&step)[4]) {
+// Where a 1536-wide projection input comes from.
+enum InMode { kInEmbed = 0, kInY = 1, kInCtx = 2, kInA = 3 };
+
+__device__ __forceinline__ int* acc_ptr(const Args& a, int parity, int t, int d) {
+  return a.acc + ((size_t)(parity * 4 + t) * 3 + d) * kAccRows;
+}
+
+// Finished value of 4 consecutive output rows of a split projection from its integer accumulators:
+// (float)(step * (acc0 + 256 acc1 + 65536 acc2)), the exact integer sum scaled once.
+__device__ __forceinline__ void acc_values(const Args& a, int parity, int t, int row, float step, float (&out)[4]) {
+  const int4 d0 = __ldcg(reinterpret_cast<const int4*>(acc_ptr(a, parity, t, 0) + row));
+  const int4 d1 = __ldcg(reinterpret_cast<const int4*>(acc_ptr(a, parity, t, 1) + row));
+  const int4 d2 = __ldcg(reinterpret_cast<const int4*>(acc_ptr(a, parity, t, 2) + row));
+  const int x0[4] = {d0.x, d0.y, d0.z, d0.w}, x1[4] = {d1.x, d1.y, d1.z, d1.w}, x2[4] = {d2.x, d2.y, d2.z, d2.w};
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+    const long long tot = (long long)x0[e] + 256ll * (long long)x1[e] + 65536ll * (long long)x2[e];
+    out[e] = (float)((double)tot * (double)step);
+  }
+}
+
+struct InSrc {
+  int mode;
+  int parity;           // kInA / kInY: accumulator parity of the layer that produced them
+  int layer;            // kInA / kInY: that layer
+  float4 os[3], ds[3];  // o_s / down_s of this thread's elements (kInA: os; kInY: both)
+  float* y_write;       // kInY: also store the layer output here ([nt][1536]) when non-null
+  float* dump_write;    // kInY: and here when non-null
+};
+
+// This thread's elements 512 j + 4 tid .. +3 of token t's input row.
+__device__ __forceinline__ void load_input(const Args& a, const InSrc& src, int t, int tid, float (&v)[3][4]) {
+  if (src.mode == kInEmbed) {
+    const int tok = __ldcg(&a.tokens[t]);
+    const __half* row = reinterpret_cast<const __half*>(a.embed) + (size_t)tok * kHidden;
+#pragma unroll
+    for (int j = 0; j < 3; ++j) {
+      const uint2 u = __ldg(reinterpret_cast<const uint2*>(row + 512 * j + 4 * tid));
+      const __half2 h0 = *reinterpret_cast<const __half2*>(&u.x), h1 = *reinterpret_cast<const __half2*>(&u.y);
+      v[j][0] = __low2float(h0);
+      v[j][1] = __high2float(h0);
+      v[j][2] = __low2float(h1);
+      v[j][3] = __high2float(h1);
+    }
+  } else if (src.mode == kInCtx) {
+#pragma unroll
+    for (int j = 0; j < 3; ++j) {
+      const float4 f = __ldcg(reinterpret_cast<const float4*>(a.ctx + (size_t)t * kHidden + 512 * j + 4 * tid));
+      v[j][0] = f.x;
+      v[j][1] = f.y;
+      v[j][2] = f.z;
+      v[j][3] = f.w;
+    }
+  } else {
+    // o_proj output a = o_s * (step * acc); for kInY the layer output y = bf16(a + down_s * (step * acc))
+    const float st_o = __ldcg(&a.steps[(src.layer * 4 + kO) * 4 + t]);
+    const float st_d = src.mode == kInY ? __ldcg(&a.steps[(src.layer * 4 + kDown) * 4 + t]) : 0.f;
+#pragma unroll
+    for (int j = 0; j < 3; ++j) {
+      const int k = 512 * j + 4 * tid;
+      float o[4], dn[4];
+      acc_values(a, src.parity, t, acc_row_base(kO) + k, st_o, o);
+      const float osc[4] = {src.os[j].x, src.os[j].y, src.os[j].z, src.os[j].w};
+#pragma unroll
+      for (int e = 0; e < 4; ++e) v[j][e] = osc[e] * o[e];
+      if (src.mode == kInY) {
+        acc_values(a, src.parity, t, acc_row_base(kDown) + k, st_d, dn);
+        const float dsc[4] = {src.ds[j].x, src.ds[j].y, src.ds[j].z, src.ds[j].w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) v[j][e] = round_bf16(__fadd_rn(v[j][e], dsc[e] * dn[e]));
+        const float4 yv = make_float4(v[j][0], v[j][1], v[j][2], v[j][3]);
+        if (src.y_write) *reinterpret_cast<float4*>(src.y_write + (size_t)t * kHidden + k) = yv;
+        if (src.dump_write) *reinterpret_cast<float4*>(src.dump_write + (size_t)t * kHidden + k) = yv;
+      }
+    }
+  }
+}
+
+// Digits of a whole 1536-wide input row per token, optionally RMS-normalised (double accumulation, as the
+// decode reference; wv = this thread's norm weights). Records the step of each token in step[] and, for
+// the designated CTA, in the global step table (every CTA computes the same value).
+__device__ void build_full(const Args& a, Ctrl& cs, uint8_t* dbuf, const InSrc& src, bool norm, const float4 (&wv)[3],
+                           int tid, float (&step)[4], float* step_out) {
   const int warp = tid >> 5, lane = tid & 31;
   for (int t = 0; t < a.nt; ++t) {
     float v[3][4];
-    if (x != nullptr) {
-#pragma unroll
-      for (int j = 0; j < 3; ++j) {
-        const float4 f = __ldcg(reinterpret_cast<const float4*>(x + (size_t)t * kHidden + 512 * j + 4 * tid));
-        v[j][0] = f.x;
-        v[j][1] = f.y;
-        v[j][2] = f.z;
-        v[j][3] = f.w;
-      }
-    } else {
-      const int tok = __ldcg(&a.tokens[t]);
-      const __half* row = reinterpret_cast<const __half*>(a.embed) + (size_t)tok * kHidden;
-#pragma unroll
-      for (int j = 0; j < 3; ++j) {
-        const uint2 u = __ldg(reinterpret_cast<const uint2*>(row + 512 * j + 4 * tid));
-        const __half2 h0 = *reinterpret_cast<const __half2*>(&u.x), h1 = *reinterpret_cast<const __half2*>(&u.y);
-        v[j][0] = __low2float(h0);
-        v[j][1] = __high2float(h0);
-        v[j][2] = __low2float(h1);
-        v[j][3] = __high2float(h1);
-      }
-    }
+    load_input(a, src, t, tid, v);
     if (norm) {
       double ss = 0.0;
 #pragma unroll
@@ -341,6 +399,7 @@ __device__ void build_full(const Args& a, Ctrl& cs, uint8_t* dbuf, const float* 
     const float mx = fmaxf(fmaxf(cs.redf[0][t], cs.redf[1][t]), fmaxf(cs.redf[2][t], cs.redf[3][t]));
     const float st = mx > 0.0f ? mx / kDigitRange : 1.0f;
     step[t] = st;
+    if (step_out != nullptr && tid == 0) step_out[t] = st;
 #pragma unroll
     for (int j = 0; j < 3; ++j) {
       const int k = 512 * j + 4 * tid;
@@ -351,11 +410,13 @@ __device__ void build_full(const Args& a, Ctrl& cs, uint8_t* dbuf, const float* 
 
 // Digits of the down projection's input h (8960 wide) for this CTA's items only; the step comes from
 // max|h| gathered by the gate|up epilogues.
-__device__ void build_down(const Args& a, uint8_t* dbuf, int l, uint32_t b0, uint32_t b1, int tid, float (&step)[4]) {
+__device__ void build_down(const Args& a, uint8_t* dbuf, int l, uint32_t b0, uint32_t b1, int tid, float (&step)[4],
+                           float* step_out) {
   for (int t = 0; t < a.nt; ++t) {
     const float mx = __uint_as_float(__ldcg(&a.sync->hmax[l].pad[t]));
     const float st = mx > 0.0f ? mx / kDigitRange : 1.0f;
     step[t] = st;
+    if (step_out != nullptr && tid == 0) step_out[t] = st;
     for (uint32_t i = b0; i < b1; ++i) {
       const Item it = a.items[i];
       const int n4 = (it.kb1 - it.kb0) * 32;
@@ -380,68 +441,33 @@ struct WorkerCtx {
   float* kvrow[4];        // this step's KV row of layer 0 (K), per token; other layers/V at fixed offsets
 };
 
-// Per-item constants, loaded before the accumulator is ready so that no dependent global load is left on
-// the path from the MMA to the completion signal.
-struct EpiConst {
-  float sc, bb;
-  float rc[4], rs[4];  // RoPE cos / sin per token (q and k heads)
-  float res[4];        // down: the attention-block output a (residual)
-  float* dst[4];       // output element per token
-};
-
-__device__ __forceinline__ void epi_const(const Args& a, const WorkerCtx& w, const Item it, int l, EpiConst& k) {
-  const LayerDev& L = a.layers[l];
-  const int r = w.r, s = it.stage;
-#pragma unroll
-  for (int t = 0; t < 4; ++t) {
-    k.rc[t] = k.rs[t] = k.res[t] = 0.f;
-    k.dst[t] = nullptr;
-  }
-  k.bb = 0.f;
-  if (s == kQkv) {
-    const int row = it.tile * kTileM + r, h = it.tile;
-    k.sc = __ldg(L.qkv_s + row);
-    k.bb = __ldg(L.qkv_b + row);
-    for (int t = 0; t < a.nt; ++t) {
-      if (h < kHeads + kKvHeads) {
-        const size_t ri = (size_t)w.pos[t] * 64 + (r & 63);
-        k.rc[t] = __ldg(a.rope_cos + ri);
-        k.rs[t] = __ldg(a.rope_sin + ri);
-      }
-      if (h < kHeads) {
-        k.dst[t] = a.q + (size_t)t * kHidden + row;
-      } else {
-        const int which = h < kHeads + kKvHeads ? 0 : 1;
-        k.dst[t] = w.kvrow[t] + ((size_t)l * 2 + which) * kPage * kKvWidth + (row - kHidden - which * kKvWidth);
-      }
-    }
-  } else if (s == kO) {
-    const int row = it.tile * kTileM + r;
-    k.sc = __ldg(L.o_s + row);
-    for (int t = 0; t < a.nt; ++t) k.dst[t] = a.a + (size_t)t * kHidden + row;
-  } else if (s == kGu) {
-    const int row = r < 64 ? it.tile * 64 + r : kInter + it.tile * 64 + (r - 64);
-    k.sc = __ldg(L.gu_s + row);
-    for (int t = 0; t < a.nt; ++t) k.dst[t] = a.h + (size_t)t * kInter + it.tile * 64 + (r & 63);
-  } else {
-    const int row = it.tile * kTileM + r;
-    k.sc = __ldg(L.down_s + row);
-    float* yout = (l & 1) ? a.y1 : a.y0;
-    for (int t = 0; t < a.nt; ++t) {
-      k.res[t] = __ldcg(a.a + (size_t)t * kHidden + row);
-      k.dst[t] = yout + (size_t)t * kHidden + row;
-    }
-  }
-}
-
+// Accumulator read-out of one item. Split projections (q|k|v, o, down) add their partial sums to the
+// integer accumulators with atomics and signal; the consumers of the next step read the exact totals
+// themselves, so no CTA waits for the other K segments of its tile. The item also clears its share of
+// the accumulator rows of the other parity, which the next layer uses (every reader of those rows has
+// finished by now). gate|up (one CTA per tile) finishes here: SiLU(gate) * up and max |h|.
 __device__ void item_epilogue(const Args& a, Ctrl& cs, WorkerCtx& w, const Item it, int l, const float (&step)[4],
                               unsigned* abort_flag) {
   const int nt = a.nt, r = w.r, tid = w.tid;
-  EpiConst k;
-  epi_const(a, w, it, l, k);
+  const int s = it.stage;
+  float gsc = 0.f;
+  float* hdst = nullptr;
+  if (s == kGu) {
+    const int row = r < 64 ? it.tile * 64 + r : kInter + it.tile * 64 + (r - 64);
+    gsc = __ldg(a.layers[l].gu_s + row);
+    hdst = a.h + it.tile * 64 + (r & 63);
+  } else {
+    // clear this item's share of the rows for layer l + 1 (other parity)
+    const int row = acc_row_base(s) + it.tile * kTileM + r;
+    if (r % split(s) == it.seg) {
+#pragma unroll
+      for (int t = 0; t < 4; ++t)
+#pragma unroll
+        for (int d = 0; d < 3; ++d) acc_ptr(a, (l + 1) & 1, t, d)[row] = 0;
+    }
+  }
   const unsigned b = w.item_no & 1;
   mwait(&cs.acc_full[b], (w.item_no >> 1) & 1, abort_flag);
-  const int s = it.stage;
   const int ts = s == kQkv ? 0 : s == kO ? 1 : s == kDown ? 2 : -1;  // trace slots of split stages
   if (tid == 0 && ts >= 0) stamp(a, l, kTraceAcc + ts);
   __syncwarp();
@@ -451,78 +477,38 @@ __device__ void item_epilogue(const Args& a, Ctrl& cs, WorkerCtx& w, const Item 
   fence_before();
   mbar_arrive(&cs.acc_empty[b]);
   ++w.item_no;
-  if (split(s) > 1) {
-    const int at = acc_tile_base(s) + it.tile;
-    int* g = a.acc + ((size_t)at * kTileM + r) * 12;
+  int done_slot;
+  if (s != kGu) {
+    const int row = acc_row_base(s) + it.tile * kTileM + r;
+    for (int t = 0; t < nt; ++t)
 #pragma unroll
-    for (int c = 0; c < 12; ++c)
-      if ((c & 3) < nt) atomicAdd(&g[c], v[c]);
-    named_sync(kBarW, kWorkers);
-    if (tid == 0) cs.flag = atom_add_acq_rel(&a.sync->tile_cnt[at].v, 1u) == (unsigned)(split(s) - 1);
-    named_sync(kBarW, kWorkers);
-    if (tid == 0 && ts >= 0) stamp(a, l, kTraceArrived + ts);
-    if (!cs.flag) return;
-#pragma unroll
-    for (int c = 0; c < 12; ++c) {
-      if ((c & 3) < nt) {
-        v[c] = __ldcg(&g[c]);
-        g[c] = 0;
-      }
-    }
-    if (tid == 0) a.sync->tile_cnt[at].v = 0u;
-  }
-  float yv[4];
-#pragma unroll
-  for (int t = 0; t < 4; ++t) {
-    const long long tot = (long long)v[t] + 256ll * (long long)v[4 + t] + 65536ll * (long long)v[8 + t];
-    yv[t] = (float)((double)tot * (double)step[t]);
-  }
-  int done_slot = kDoneQkv;
-  if (s == kQkv) {
-    // tile = head (12 q, 2 k, 2 v); rotate-half pairs (r, r ^ 64) exchanged through shared memory
-#pragma unroll
-    for (int t = 0; t < 4; ++t) cs.ys[r][t] = __fmaf_rn(k.sc, yv[t], k.bb);
-    named_sync(kBarW, kWorkers);
-    const bool rope = it.tile < kHeads + kKvHeads;
-    for (int t = 0; t < nt; ++t) {
-      const float mine = cs.ys[r][t], other = cs.ys[r ^ 64][t];
-      float y = mine;
-      if (rope)
-        y = r < 64 ? __fsub_rn(__fmul_rn(mine, k.rc[t]), __fmul_rn(other, k.rs[t]))
-                   : __fadd_rn(__fmul_rn(mine, k.rc[t]), __fmul_rn(other, k.rs[t]));
-      *k.dst[t] = y;
-    }
-    done_slot = kDoneQkv;
-  } else if (s == kO) {
-    for (int t = 0; t < nt; ++t) *k.dst[t] = k.sc * yv[t];
-    done_slot = kDoneO;
-  } else if (s == kGu) {
+      for (int d = 0; d < 3; ++d) atomicAdd(acc_ptr(a, l & 1, t, d) + row, v[4 * d + t]);
+    done_slot = s == kQkv ? kDoneQkv : s == kO ? kDoneO : kDoneDown;
+  } else {
     // tile rows 0..63: gate rows 64 j.., rows 64..127: the matching up rows
 #pragma unroll
-    for (int t = 0; t < 4; ++t) cs.ys[r][t] = k.sc * yv[t];
+    for (int t = 0; t < 4; ++t) {
+      const long long tot = (long long)v[t] + 256ll * (long long)v[4 + t] + 65536ll * (long long)v[8 + t];
+      cs.ys[r][t] = gsc * (float)((double)tot * (double)step[t]);
+    }
     named_sync(kBarW, kWorkers);
     if (r < 64) {  // warps of TMEM quarters 0 and 1
       for (int t = 0; t < nt; ++t) {
         const float gv = cs.ys[r][t], uv = cs.ys[r + 64][t];
         const float silu = __fdiv_rn(gv, __fadd_rn(1.0f, expf(-gv)));
         const float hv = __fmul_rn(silu, uv);
-        *k.dst[t] = hv;
+        hdst[(size_t)t * kInter] = hv;
         const float m = warp_max(fabsf(hv));
         if (w.lane == 0) atomicMax(&a.sync->hmax[l].pad[t], __float_as_uint(m));
       }
     }
     done_slot = kDoneGu;
-  } else {
-    const int row = it.tile * kTileM + r;
-    for (int t = 0; t < nt; ++t) {
-      const float y = round_bf16(__fadd_rn(k.res[t], k.sc * yv[t]));
-      *k.dst[t] = y;
-      if (a.dump != nullptr) a.dump[((size_t)l * nt + t) * kHidden + row] = y;
-    }
-    done_slot = kDoneDown;
   }
   named_sync(kBarW, kWorkers);
-  if (tid == 0) red_release(&a.sync->done[l][done_slot].v, 1u);
+  if (tid == 0) {
+    red_release(&a.sync->done[l][done_slot].v, 1u);
+    if (ts >= 0) stamp(a, l, kTraceArrived + ts);
+  }
 }
 
 // ---------------------------------------------------------------------------------------------------
@@ -534,6 +520,48 @@ struct AttnItem {
   const float* kbase;
   const float* vbase;
 };
+
+// Constants of the q|k|v epilogue for the rows this thread finishes in attention: dim d = tid of the six
+// query heads of KV group g, of the K head and of the V head, plus the RoPE factors at the token position.
+struct QkvConst {
+  float qs[kGroups], qb[kGroups];
+  float ks, kb, vs, vb;
+  float rc, rs;
+};
+
+__device__ __forceinline__ void qkv_const(const Args& a, const WorkerCtx& w, int l, int t, int g, QkvConst& k) {
+  const LayerDev& L = a.layers[l];
+  const int d = w.tid;
+#pragma unroll
+  for (int hh = 0; hh < kGroups; ++hh) {
+    const int row = (g * kGroups + hh) * kHeadDim + d;
+    k.qs[hh] = __ldg(L.qkv_s + row);
+    k.qb[hh] = __ldg(L.qkv_b + row);
+  }
+  const int krow = kHidden + g * kHeadDim + d, vrow = kHidden + kKvWidth + g * kHeadDim + d;
+  k.ks = __ldg(L.qkv_s + krow);
+  k.kb = __ldg(L.qkv_b + krow);
+  k.vs = __ldg(L.qkv_s + vrow);
+  k.vb = __ldg(L.qkv_b + vrow);
+  const size_t ri = (size_t)w.pos[t] * 64 + (d & 63);
+  k.rc = __ldg(a.rope_cos + ri);
+  k.rs = __ldg(a.rope_sin + ri);
+}
+
+// q|k|v value of one row from the integer accumulators: bias + scale * (step * acc)
+__device__ __forceinline__ float qkv_value(const Args& a, int parity, int t, int row, float step, float sc, float bb) {
+  const int* p0 = acc_ptr(a, parity, t, 0);
+  const int* p1 = acc_ptr(a, parity, t, 1);
+  const int* p2 = acc_ptr(a, parity, t, 2);
+  const long long tot =
+      (long long)__ldcg(p0 + row) + 256ll * (long long)__ldcg(p1 + row) + 65536ll * (long long)__ldcg(p2 + row);
+  return __fmaf_rn(sc, (float)((double)tot * (double)step), bb);
+}
+
+// rotate-half RoPE of dim d given its partner dim d ^ 64
+__device__ __forceinline__ float rope(float mine, float other, int d, float c, float sn) {
+  return d < 64 ? __fsub_rn(__fmul_rn(mine, c), __fmul_rn(other, sn)) : __fadd_rn(__fmul_rn(mine, c), __fmul_rn(other, sn));
+}
 
 __device__ __forceinline__ AttnItem attn_decode(const Args& a, const WorkerCtx& w, int l, int i, const int (&nch)[4]) {
   AttnItem it;
@@ -569,16 +597,47 @@ __device__ __forceinline__ void attn_load_rows(AttnSmem& sm, const AttnItem& it,
 // One 64-key chunk of one (token, KV head): the history rows are already in flight; loads the new row
 // (when it falls in this chunk) and the six query heads, then scores, softmax statistics and P.V; the last
 // chunk of a (token, KV head) to finish merges all chunks in chunk order.
-__device__ void attn_item(const Args& a, AttnSmem& sm, Ctrl& cs, int l, const AttnItem& it, int tid) {
-  const int warp = tid >> 5, lane = tid & 31;
+__device__ void attn_item(const Args& a, AttnSmem& sm, Ctrl& cs, const WorkerCtx& w, int l, const AttnItem& it,
+                          const QkvConst& qc) {
+  const int tid = w.tid, warp = tid >> 5, lane = tid & 31;
   const int t = it.t, g = it.g, n = it.n, nchunks = it.nchunks;
-  attn_load_rows(sm, it, it.nhist, it.n, tid);
-  for (int i = tid; i < kGroups * 32; i += kWorkers) {
-    const int hh = i >> 5, f = i & 31;
-    cp_async16(&sm.qs[hh][4 * f], a.q + (size_t)t * kHidden + (g * kGroups + hh) * kHeadDim + 4 * f);
+  // q (six heads) and, in the chunk that holds it, the new token's K/V row, finished from the q|k|v
+  // accumulators: this thread owns dim d = tid, RoPE pairs meet through shared memory
+  {
+    const int d = tid, parity = l & 1;
+    const float st = __ldcg(&a.steps[(l * 4 + kQkv) * 4 + t]);
+    const bool has_new = it.nhist < n;  // the new token is row nhist of this chunk
+    float qv[kGroups], kv = 0.f, vv = 0.f;
+#pragma unroll
+    for (int hh = 0; hh < kGroups; ++hh)
+      qv[hh] = qkv_value(a, parity, t, (g * kGroups + hh) * kHeadDim + d, st, qc.qs[hh], qc.qb[hh]);
+    if (has_new) {
+      kv = qkv_value(a, parity, t, kHidden + g * kHeadDim + d, st, qc.ks, qc.kb);
+      vv = qkv_value(a, parity, t, kHidden + kKvWidth + g * kHeadDim + d, st, qc.vs, qc.vb);
+    }
+#pragma unroll
+    for (int hh = 0; hh < kGroups; ++hh) sm.qs[hh][d] = qv[hh];
+    if (has_new) sm.ks[it.nhist][d] = kv;
+    named_sync(kBarW, kWorkers);
+    float qr[kGroups], kr = 0.f;
+#pragma unroll
+    for (int hh = 0; hh < kGroups; ++hh) qr[hh] = rope(qv[hh], sm.qs[hh][d ^ 64], d, qc.rc, qc.rs);
+    if (has_new) kr = rope(kv, sm.ks[it.nhist][d ^ 64], d, qc.rc, qc.rs);
+    named_sync(kBarW, kWorkers);
+#pragma unroll
+    for (int hh = 0; hh < kGroups; ++hh) sm.qs[hh][d] = qr[hh];
+    if (has_new) {
+      sm.ks[it.nhist][d] = kr;
+      sm.vs[it.nhist][d] = vv;
+      // the cache row of this step, for later steps
+      float* krow = w.kvrow[t] + ((size_t)l * 2) * kPage * kKvWidth + g * kHeadDim + d;
+      krow[0] = kr;
+      krow[kPage * kKvWidth] = vv;
+    }
   }
   cp_async_wait_all();
   named_sync(kBarW, kWorkers);
+  if (tid == 0) stamp(a, l, kTraceAttnQ);
   const float scaling = kAttentionScaling;
   {
     const int key = tid >> 1, h0 = (tid & 1) * 3;
@@ -653,7 +712,10 @@ __device__ void attn_item(const Args& a, AttnSmem& sm, Ctrl& cs, int l, const At
       my[tid * kPartStride + 1] = sm.ls[tid];
     }
     named_sync(kBarW, kWorkers);
-    if (tid == 0) cs.flag = atom_add_acq_rel(&a.sync->attn_cnt[t][g].v, 1u) == (unsigned)nchunks - 1u;
+    if (tid == 0) {
+      cs.flag = atom_add_acq_rel(&a.sync->attn_cnt[t][g].v, 1u) == (unsigned)nchunks - 1u;
+      stamp(a, l, kTraceAttnPart);
+    }
     named_sync(kBarW, kWorkers);
     if (cs.flag) {
       // merge in chunk order: M = max of the chunk maxima, then o = sum acc_c w_c, L = sum l_c w_c with
@@ -701,7 +763,10 @@ __device__ void attn_item(const Args& a, AttnSmem& sm, Ctrl& cs, int l, const At
         const float inv = Lsum[hh] > 0.0f ? 1.0f / Lsum[hh] : 0.0f;
         out_base[hh * kHeadDim] = o[hh] * inv;
       }
-      if (tid == 0) a.sync->attn_cnt[t][g].v = 0u;
+      if (tid == 0) {
+        a.sync->attn_cnt[t][g].v = 0u;
+        stamp(a, l, kTraceAttnMerge);
+      }
       finished = true;
     }
   }
@@ -725,13 +790,17 @@ __device__ void attention_stage(const Args& a, AttnSmem& sm, Ctrl& cs, const Wor
   named_sync(kBarW, kWorkers);  // shared memory free: this CTA's earlier epilogues are done
   AttnItem it = attn_decode(a, w, l, blockIdx.x, nch);
   attn_load_rows(sm, it, 0, it.nhist, tid);
-  workers_wait(&a.sync->done[l][kDoneQkv].v, (unsigned)tiles(kQkv), abort_flag, tid);
+  QkvConst qc;
+  qkv_const(a, w, l, it.t, it.g, qc);
+  workers_wait(&a.sync->done[l][kDoneQkv].v, (unsigned)stage_items(kQkv), abort_flag, tid);
   if (tid == 0) stamp(a, l, kTraceWait + 1);
   for (int i = blockIdx.x;;) {
-    attn_item(a, sm, cs, l, it, tid);
+    attn_item(a, sm, cs, w, l, it, qc);
     i += gridDim.x;
     if (i >= total) break;
-    it = attn_decode(a, w, l, i, nch);
+    const AttnItem nx = attn_decode(a, w, l, i, nch);
+    if (nx.t != it.t || nx.g != it.g) qkv_const(a, w, l, nx.t, nx.g, qc);
+    it = nx;
     named_sync(kBarW, kWorkers);  // previous chunk done with the shared buffers
     attn_load_rows(sm, it, 0, it.nhist, tid);
   }
@@ -771,18 +840,34 @@ __device__ void workers(const Args& a, uint8_t* uni, Ctrl& cs, uint32_t tmem, ui
     mbar_arrive(&cs.dig_ready[inst & 1]);
     ++inst;
   };
+  // The CTA holding q|k|v tile 0, segment 0 writes each layer's output y (needed by the LM head and the
+  // hidden-state dump); every other CTA only uses it on chip.
+  bool y_writer = false;
+  for (uint32_t i = sb[kQkv]; i < se[kQkv]; ++i) y_writer |= a.items[i].tile == 0 && a.items[i].seg == 0;
   const bool tr = w.tid == 0;
   for (int l = 0; l < kLayers; ++l) {
     const LayerDev& L = a.layers[l];
     SyncWord* done = a.sync->done[l];
-    // q|k|v (input: previous layer's output, or the token embeddings)
+    float* const step_tab = a.steps + (size_t)l * 16;
     float4 wv[3];
+    InSrc src;
+    // q|k|v: input = previous layer's output, finished here from its o_proj and down accumulators (or the
+    // token embeddings for layer 0)
     if (sb[kQkv] < se[kQkv]) {
       load_norm(L.input_ln, w.tid, wv);
-      if (l > 0) workers_wait(&a.sync->done[l - 1][kDoneDown].v, (unsigned)tiles(kDown), abort_flag, w.tid);
+      src.mode = l == 0 ? kInEmbed : kInY;
+      if (l > 0) {
+        const LayerDev& P = a.layers[l - 1];
+        src.parity = (l - 1) & 1;
+        src.layer = l - 1;
+        load_norm(P.o_s, w.tid, src.os);
+        load_norm(P.down_s, w.tid, src.ds);
+        src.y_write = y_writer ? (((l - 1) & 1) ? a.y1 : a.y0) : nullptr;
+        src.dump_write = y_writer && a.dump ? a.dump + (size_t)(l - 1) * a.nt * kHidden : nullptr;
+        workers_wait(&a.sync->done[l - 1][kDoneDown].v, (unsigned)stage_items(kDown), abort_flag, w.tid);
+      }
       if (tr) stamp(a, l, kTraceWait + 0);
-      const float* xin = l == 0 ? nullptr : (((l - 1) & 1) ? a.y1 : a.y0);
-      build_full(a, cs, digits(inst), xin, true, wv, w.tid, step);
+      build_full(a, cs, digits(inst), src, true, wv, w.tid, step, step_tab + kQkv * 4);
       ready();
       if (tr) stamp(a, l, kTraceBuilt + 0);
       for (uint32_t i = sb[kQkv]; i < se[kQkv]; ++i) item_epilogue(a, cs, w, a.items[i], l, step, abort_flag);
@@ -790,32 +875,55 @@ __device__ void workers(const Args& a, uint8_t* uni, Ctrl& cs, uint32_t tmem, ui
     }
     attention_stage(a, asm_, cs, w, l, abort_flag);
     if (sb[kO] < se[kO]) {
+      src.mode = kInCtx;
       workers_wait(&done[kDoneAttn].v, (unsigned)(kKvHeads * a.nt), abort_flag, w.tid);
       if (tr) stamp(a, l, kTraceWait + 2);
-      build_full(a, cs, digits(inst), a.ctx, false, wv, w.tid, step);
+      build_full(a, cs, digits(inst), src, false, wv, w.tid, step, step_tab + kO * 4);
       ready();
       if (tr) stamp(a, l, kTraceBuilt + 2);
       for (uint32_t i = sb[kO]; i < se[kO]; ++i) item_epilogue(a, cs, w, a.items[i], l, step, abort_flag);
       if (tr) stamp(a, l, kTraceDone + 2);
     }
     if (sb[kGu] < se[kGu]) {
+      // input = RMSNorm(a), a finished here from the o_proj accumulators
       load_norm(L.post_ln, w.tid, wv);
-      workers_wait(&done[kDoneO].v, (unsigned)tiles(kO), abort_flag, w.tid);
+      src.mode = kInA;
+      src.parity = l & 1;
+      src.layer = l;
+      load_norm(L.o_s, w.tid, src.os);
+      workers_wait(&done[kDoneO].v, (unsigned)stage_items(kO), abort_flag, w.tid);
       if (tr) stamp(a, l, kTraceWait + 3);
-      build_full(a, cs, digits(inst), a.a, true, wv, w.tid, step);
+      build_full(a, cs, digits(inst), src, true, wv, w.tid, step, step_tab + kGu * 4);
       ready();
       if (tr) stamp(a, l, kTraceBuilt + 3);
       for (uint32_t i = sb[kGu]; i < se[kGu]; ++i) item_epilogue(a, cs, w, a.items[i], l, step, abort_flag);
       if (tr) stamp(a, l, kTraceDone + 3);
     }
     if (sb[kDown] < se[kDown]) {
-      workers_wait(&done[kDoneGu].v, (unsigned)tiles(kGu), abort_flag, w.tid);
+      workers_wait(&done[kDoneGu].v, (unsigned)stage_items(kGu), abort_flag, w.tid);
       if (tr) stamp(a, l, kTraceWait + 4);
-      build_down(a, digits(inst), l, sb[kDown], se[kDown], w.tid, step);
+      build_down(a, digits(inst), l, sb[kDown], se[kDown], w.tid, step, step_tab + kDown * 4);
       ready();
       if (tr) stamp(a, l, kTraceBuilt + 4);
       for (uint32_t i = sb[kDown]; i < se[kDown]; ++i) item_epilogue(a, cs, w, a.items[i], l, step, abort_flag);
       if (tr) stamp(a, l, kTraceDone + 4);
+    }
+  }
+  // the last layer's output, for the LM head (and the dump)
+  if (y_writer) {
+    const int l = kLayers - 1;
+    InSrc src;
+    src.mode = kInY;
+    src.parity = l & 1;
+    src.layer = l;
+    load_norm(a.layers[l].o_s, w.tid, src.os);
+    load_norm(a.layers[l].down_s, w.tid, src.ds);
+    src.y_write = (l & 1) ? a.y1 : a.y0;
+    src.dump_write = a.dump ? a.dump + (size_t)l * a.nt * kHidden : nullptr;
+    workers_wait(&a.sync->done[l][kDoneDown].v, (unsigned)stage_items(kDown), abort_flag, w.tid);
+    for (int t = 0; t < a.nt; ++t) {
+      float v[3][4];
+      load_input(a, src, t, w.tid, v);
     }
   }
 }

@@ -28,9 +28,13 @@ __host__ __device__ constexpr int unit_base(int s) {
 }
 constexpr int kUnitsPerLayer = 16 * 12 + 12 * 12 + 140 * 12 + 12 * 70;  // 2856
 constexpr uint64_t kLayerTileBytes = (uint64_t)kUnitsPerLayer * 16384;   // 46.8 MB
-// split-K accumulator tiles: q|k|v 0..15, o 16..27, down 28..39
-__host__ __device__ constexpr int acc_tile_base(int s) { return s == kQkv ? 0 : s == kO ? 16 : 28; }
-constexpr int kAccTiles = 40;
+// Work items of a stage (every K segment of every tile): the stage's completion count.
+__host__ __device__ constexpr int stage_items(int s) { return tiles(s) * split(s); }
+// Split-K integer accumulators of the q|k|v, o and down projections, consumed directly by the next step:
+// [parity (layer & 1)][token 4][digit 3][kAccRows]; rows of q|k|v at 0, o at 2048, down at 3584.
+constexpr int kAccRows = 2048 + 1536 + 1536;
+__host__ __device__ constexpr int acc_row_base(int s) { return s == kQkv ? 0 : s == kO ? 2048 : 3584; }
+constexpr size_t kAccInts = (size_t)2 * 4 * 3 * kAccRows;
 
 // One work item: K blocks [kb0, kb1) of one tile; its digit operand starts at block `dslot` of the CTA's
 // digit buffer for the stage.
@@ -54,7 +58,6 @@ struct alignas(128) SyncWord {
 struct SyncWords {
   SyncWord done[kLayers][kDoneSlots];
   SyncWord hmax[kLayers];      // .pad[0..3]: max |h| per token (float bits), for the down projection's step
-  SyncWord tile_cnt[kAccTiles];
   SyncWord attn_cnt[4][2];
   SyncWord exit_cnt;
   SyncWord abort_flag;
@@ -91,7 +94,8 @@ struct Args {
   float* dump;                // optional [28][nt][1536] copies of the layer outputs
   float* attn_part;           // attention chunk partials
   int attn_max_chunks;
-  int* acc;                   // [kAccTiles][128][12] split-K integer accumulators (zero between uses)
+  int* acc;                   // [kAccInts] split-K integer accumulators (zero before their layer's use)
+  float* steps;               // [28][4][4] digit step per layer, projection and token
   SyncWords* sync;
   const uint32_t* item_off;   // [ctas + 1]
   const Item* items;
@@ -107,10 +111,14 @@ struct Args {
 //   kTraceIssue + s  producer: first weight unit of projection s issued
 //   kTraceMma + s    MMA issuer: last MMA of projection s committed
 //   kTraceAcc + j    workers: accumulator of the CTA's last item of split stage j (0 q|k|v, 1 o, 2 down) ready
-//   kTraceArrived + j   workers: that item's split-K partial added and counted
-constexpr int kTraceSlots = 32;
+//   kTraceArrived + j   workers: that item's split-K partial added and signalled
+//   kTraceMmaStart + s  MMA issuer: digits of projection s seen, first MMA about to issue
+//   kTraceAttnQ      workers: attention inputs (q, new K/V row, history) in shared memory
+//   kTraceAttnPart   workers: attention chunk partial written and counted
+//   kTraceAttnMerge  workers: attention chunks merged (last chunk only)
+constexpr int kTraceSlots = 40;
 constexpr int kTraceWait = 0, kTraceBuilt = 5, kTraceDone = 10, kTraceIssue = 16, kTraceMma = 20, kTraceAcc = 24,
-              kTraceArrived = 27;
+              kTraceArrived = 27, kTraceMmaStart = 30, kTraceAttnQ = 34, kTraceAttnPart = 35, kTraceAttnMerge = 36;
 
 // Launch over `ctas` CTAs (cooperative: all resident). Requires wbits 8 weights in the tiled layout.
 cudaError_t launch_decode_stack(const Args& a, int ctas, cudaStream_t s);

@@ -136,12 +136,15 @@ struct qwen_engine {
   LayerDev* d_layers = nullptr;
   stack::SyncWords* sync = nullptr;
   int* stack_acc = nullptr;
+  float* stack_steps = nullptr;
   uint32_t* d_item_off = nullptr;
   stack::Item* d_items = nullptr;
   int stack_ctas = 0;
   int attn_max_chunks = 0;
   unsigned long long* trace = nullptr;  // optional timeline of the persistent kernel
   int stack_ring = 9;                   // weight stages in flight per CTA
+  cudaEvent_t kev[3] = {nullptr, nullptr, nullptr};  // per-kernel timing (profile_decode)
+  bool time_kernels = false;
 };
 
 namespace {
@@ -268,6 +271,7 @@ int enqueue_decode(qwen_engine* e, int nt, int max_len, bool advance) {
   const size_t down_bytes = (size_t)kInter * kHidden * wb / 8;
   const size_t qkv_bytes = (size_t)kQkvRows * kHidden * wb / 8;
   const size_t lm_head_prefetch = (size_t)32 << 20;
+  if (e->time_kernels) E_TRY(cudaEventRecord(e->kev[0], e->stream));
   if (stack_enabled(e)) {
     if (int st = ensure_tiles(e)) return st;
     stack::Args a{};
@@ -293,6 +297,7 @@ int enqueue_decode(qwen_engine* e, int nt, int max_len, bool advance) {
     a.attn_part = e->attn_part;
     a.attn_max_chunks = e->attn_max_chunks;
     a.acc = e->stack_acc;
+    a.steps = e->stack_steps;
     a.sync = e->sync;
     a.item_off = e->d_item_off;
     a.items = e->d_items;
@@ -337,8 +342,11 @@ int enqueue_decode(qwen_engine* e, int nt, int max_len, bool advance) {
     }
     xin = yout;
   }
+  if (e->time_kernels) E_TRY(cudaEventRecord(e->kev[1], e->stream));
   E_TRY(launch_lm_head_argmax(e->embed, e->final_norm, xin, nt, e->keep_logits ? e->logits : nullptr, e->lm_part,
-                              e->lm_cnt, e->d_next, e->stream, pdl && !e->dump_hidden && !stack_enabled(e)));
+                              e->lm_cnt, e->d_next, e->stream,
+                              pdl && !e->dump_hidden && !stack_enabled(e) && !e->time_kernels));
+  if (e->time_kernels) E_TRY(cudaEventRecord(e->kev[2], e->stream));
   if (advance) {
     E_TRY(launch_k(advance_kernel, dim3(1), dim3(32), 0, e->stream, pdl, e->d_tokens, (const int*)e->d_next,
                    e->d_pos, nt));
@@ -420,8 +428,10 @@ int qwen_engine_create(int device, int wbits, int max_seqs, int max_len, qwen_en
       E_TRY(cudaMemcpy(e->d_layers, e->layers, sizeof(LayerDev) * kLayers, cudaMemcpyHostToDevice));
       E_TRY(cudaMalloc(&e->sync, sizeof(stack::SyncWords)));
       E_TRY(cudaMemset(e->sync, 0, sizeof(stack::SyncWords)));
-      E_TRY(dalloc(&e->stack_acc, (size_t)stack::kAccTiles * 128 * 12));
-      E_TRY(cudaMemset(e->stack_acc, 0, (size_t)stack::kAccTiles * 128 * 12 * 4));
+      E_TRY(dalloc(&e->stack_acc, stack::kAccInts));
+      E_TRY(cudaMemset(e->stack_acc, 0, stack::kAccInts * 4));
+      E_TRY(dalloc(&e->stack_steps, (size_t)kLayers * 16));
+      E_TRY(cudaMemset(e->stack_steps, 0, (size_t)kLayers * 16 * 4));
       E_TRY(dalloc(&e->d_item_off, sc.off.size()));
       E_TRY(cudaMemcpy(e->d_item_off, sc.off.data(), sc.off.size() * 4, cudaMemcpyHostToDevice));
       E_TRY(dalloc(&e->d_items, sc.items.size()));
@@ -472,10 +482,12 @@ void qwen_engine_destroy(qwen_engine* e) {
                   e->d_seq, e->d_next, e->x, e->q, e->ctx, e->a, e->y0, e->y1, e->h, e->attn_part, e->attn_cnt,
                   e->lm_part, e->lm_cnt, e->dump, e->logits, e->rope_dec_cos, e->rope_dec_sin, e->rope_pre_cos,
                   e->rope_pre_sin, e->p_x, e->p_xn, e->p_q, e->p_ctx, e->p_a, e->p_h, e->p_k, e->p_v, e->p_tokens,
-                  e->qsc.acc, e->qsc.cnt, e->wtiles, e->d_layers, e->sync, e->stack_acc, e->d_item_off,
-                  e->d_items};
+                  e->qsc.acc, e->qsc.cnt, e->wtiles, e->d_layers, e->sync, e->stack_acc, e->stack_steps,
+                  e->d_item_off, e->d_items};
   for (void* p : ptrs) cudaFree(p);
   cudaFree(e->trace);
+  for (cudaEvent_t ev : e->kev)
+    if (ev) cudaEventDestroy(ev);
   if (e->h_io) cudaFreeHost(e->h_io);
   if (e->stream) cudaStreamDestroy(e->stream);
   delete e;
@@ -671,6 +683,44 @@ int qwen_engine_bench_decode(qwen_engine* e, const int32_t* slots, const int32_t
   cudaEventDestroy(t1);
   for (int i = 0; i < n; ++i) e->seq_len[slots[i]] += warmup + steps;
   if (ms_per_step) *ms_per_step = ms / steps;
+  return 0;
+}
+
+int qwen_engine_profile_decode(qwen_engine* e, int slot, int first_token, int steps, float* ms_out) {
+  if (!e || slot < 0 || slot >= e->max_seqs || steps <= 0 || !ms_out) return kStatusInvalid;
+  E_TRY(cudaSetDevice(e->device));
+  const int end = e->seq_len[slot] + steps;
+  if (int st = ensure_pages(e, slot, end)) return st;
+  if (int st = ensure_rope_dec(e, end)) return st;
+  if (int st = ensure_tiles(e)) return st;
+  for (int i = 0; i < 3; ++i)
+    if (e->kev[i] == nullptr) E_TRY(cudaEventCreate(&e->kev[i]));
+  e->h_io[0] = first_token;
+  e->h_io[4] = e->seq_len[slot];
+  e->h_io[8] = slot;
+  e->dev_slots.clear();
+  E_TRY(cudaMemcpyAsync(e->d_tokens, e->h_io, 4, cudaMemcpyHostToDevice, e->stream));
+  E_TRY(cudaMemcpyAsync(e->d_pos, e->h_io + 4, 4, cudaMemcpyHostToDevice, e->stream));
+  E_TRY(cudaMemcpyAsync(e->d_seq, e->h_io + 8, 4, cudaMemcpyHostToDevice, e->stream));
+  double layers_ms = 0.0, head_ms = 0.0;
+  e->time_kernels = true;
+  int st = 0;
+  for (int i = 0; i < steps && st == 0; ++i) {
+    st = enqueue_decode(e, 1, ((end + 63) / 64) * 64, true);
+    if (st == 0 && cudaEventSynchronize(e->kev[2]) != cudaSuccess) st = kStatusCuda;
+    float a = 0.f, b = 0.f;
+    if (st == 0 && (cudaEventElapsedTime(&a, e->kev[0], e->kev[1]) != cudaSuccess ||
+                    cudaEventElapsedTime(&b, e->kev[1], e->kev[2]) != cudaSuccess))
+      st = kStatusCuda;
+    layers_ms += a;
+    head_ms += b;
+  }
+  e->time_kernels = false;
+  if (st) return st;
+  E_TRY(cudaStreamSynchronize(e->stream));
+  e->seq_len[slot] += steps;
+  ms_out[0] = (float)(layers_ms / steps);
+  ms_out[1] = (float)(head_ms / steps);
   return 0;
 }
 

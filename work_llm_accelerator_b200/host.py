@@ -169,6 +169,7 @@ def _configure_engine(lib: ctypes.CDLL) -> None:
     lib.qwen_engine_decode_device.argtypes = [vp, _I32, vp, i, vp]
     lib.qwen_engine_read_layer.argtypes = [vp, i, _B, _F]
     lib.qwen_engine_profile_kernels.argtypes = [vp, i, i, i, _F]
+    lib.qwen_engine_profile_decode.argtypes = [vp, i, i, i, _F]
     lib.qwen_engine_stream.argtypes = [vp]
     lib.qwen_engine_stream.restype = vp
     lib.qwen_engine_kernels_per_decode_step.argtypes = [vp, i]
@@ -177,7 +178,7 @@ def _configure_engine(lib: ctypes.CDLL) -> None:
               "qwen_engine_set_seq_len", "qwen_engine_seq_len", "qwen_engine_reset", "qwen_engine_set_option",
               "qwen_engine_read_hidden", "qwen_engine_read_logits", "qwen_engine_bench_decode",
               "qwen_engine_kernels_per_decode_step", "qwen_engine_decode_device", "qwen_engine_read_layer",
-              "qwen_engine_profile_kernels", "qwen_engine_read_trace"):
+              "qwen_engine_profile_kernels", "qwen_engine_read_trace", "qwen_engine_profile_decode"):
         getattr(lib, n).restype = i
 
 
@@ -269,7 +270,7 @@ class Engine:
     def read_trace(self, ctas: int = 148) -> np.ndarray:
         """Timeline of the last persistent-kernel step: [ctas][28][slots] global-timer ns (option "trace")."""
         c, sl = ctypes.c_int(), ctypes.c_int()
-        out = np.zeros(ctas * 28 * 32, np.uint64)
+        out = np.zeros(ctas * 28 * 64, np.uint64)
         _check(self.lib.qwen_engine_read_trace(self.handle, out, out.size, ctypes.byref(c), ctypes.byref(sl)),
                "read_trace")
         return out[:c.value * 28 * sl.value].reshape(c.value, 28, sl.value)
@@ -308,6 +309,12 @@ class Engine:
         out = np.zeros(6, np.float32)
         _check(self.lib.qwen_engine_profile_kernels(self.handle, n, past, iters, out), "profile_kernels")
         return dict(zip(("qkv", "attention", "o", "gate_up", "down", "lm_head"), map(float, out)))
+
+    def profile_decode(self, slot: int, first_token: int, steps: int) -> dict[str, float]:
+        """Mean device milliseconds per eager decode step of the layer part and of the LM head kernel."""
+        out = np.zeros(2, np.float32)
+        _check(self.lib.qwen_engine_profile_decode(self.handle, slot, first_token, steps, out), "profile_decode")
+        return {"layers": float(out[0]), "lm_head": float(out[1])}
 
     def stream(self) -> int:
         return int(self.lib.qwen_engine_stream(self.handle) or 0)
