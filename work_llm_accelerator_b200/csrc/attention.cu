@@ -102,21 +102,32 @@ __global__ void __launch_bounds__(kAttnThreads) decode_attn_kernel(const float* 
   __syncthreads();
   griddep_launch();
 
-  // scores: thread = (key, three of the six heads); K read once per key pair (broadcast)
+  // scores: thread = (key, three of the six heads); K read once per key pair (broadcast). Each score is
+  // the sum of two 64-dim halves (FMA chains over dims 0..63 and 64..127), the order the persistent
+  // decode kernel uses, so both paths round alike.
   const float scaling = kAttentionScaling;  // == float(1 / sqrt(128)), qwen_decode_attention_kernel.cpp:119
   {
     const int key = tid >> 1, h0 = (tid & 1) * 3;
-    float s0 = 0.f, s1 = 0.f, s2 = 0.f;
+    float lo[3], hi[3];
+#pragma unroll
+    for (int half = 0; half < 2; ++half) {
+      float s0 = 0.f, s1 = 0.f, s2 = 0.f;
 #pragma unroll 8
-    for (int f = 0; f < 32; ++f) {
-      const float4 kk = *reinterpret_cast<const float4*>(&sm.ks[key][4 * f]);
-      const float4 a = *reinterpret_cast<const float4*>(&sm.qs[h0][4 * f]);
-      const float4 b = *reinterpret_cast<const float4*>(&sm.qs[h0 + 1][4 * f]);
-      const float4 d = *reinterpret_cast<const float4*>(&sm.qs[h0 + 2][4 * f]);
-      s0 = fmaf(a.x, kk.x, fmaf(a.y, kk.y, fmaf(a.z, kk.z, fmaf(a.w, kk.w, s0))));
-      s1 = fmaf(b.x, kk.x, fmaf(b.y, kk.y, fmaf(b.z, kk.z, fmaf(b.w, kk.w, s1))));
-      s2 = fmaf(d.x, kk.x, fmaf(d.y, kk.y, fmaf(d.z, kk.z, fmaf(d.w, kk.w, s2))));
+      for (int f = 16 * half; f < 16 * half + 16; ++f) {
+        const float4 kk = *reinterpret_cast<const float4*>(&sm.ks[key][4 * f]);
+        const float4 a = *reinterpret_cast<const float4*>(&sm.qs[h0][4 * f]);
+        const float4 b = *reinterpret_cast<const float4*>(&sm.qs[h0 + 1][4 * f]);
+        const float4 d = *reinterpret_cast<const float4*>(&sm.qs[h0 + 2][4 * f]);
+        s0 = fmaf(a.x, kk.x, fmaf(a.y, kk.y, fmaf(a.z, kk.z, fmaf(a.w, kk.w, s0))));
+        s1 = fmaf(b.x, kk.x, fmaf(b.y, kk.y, fmaf(b.z, kk.z, fmaf(b.w, kk.w, s1))));
+        s2 = fmaf(d.x, kk.x, fmaf(d.y, kk.y, fmaf(d.z, kk.z, fmaf(d.w, kk.w, s2))));
+      }
+      float* dst = half ? hi : lo;
+      dst[0] = s0;
+      dst[1] = s1;
+      dst[2] = s2;
     }
+    const float s0 = __fadd_rn(lo[0], hi[0]), s1 = __fadd_rn(lo[1], hi[1]), s2 = __fadd_rn(lo[2], hi[2]);
     const bool ok = key < n;
     sm.es[key][h0] = ok ? s0 * scaling : -INFINITY;
     sm.es[key][h0 + 1] = ok ? s1 * scaling : -INFINITY;
@@ -188,9 +199,8 @@ __global__ void __launch_bounds__(kAttnThreads) decode_attn_kernel(const float* 
   __syncthreads();
   if (!sm.last) return;
   __threadfence();
-  // Merge this (token, KV head)'s chunks in chunk order (deterministic). The per-chunk statistics go
-  // through shared memory (reusing the score buffer: up to kChunk chunks per pass), so every thread's
-  // accumulator loads are independent and stay in flight together.
+  // Merge this (token, KV head)'s chunks in chunk order, online (deterministic, the same operations as the
+  // persistent decode kernel): M' = max(M, m_c), o = o e^(M - M') + acc_c e^(m_c - M'), L likewise.
   const float* base = part + ((size_t)t * kKvHeads + g) * max_chunks * kGroups * kPartStride;
   float o[kGroups], Lsum[kGroups], M[kGroups];
 #pragma unroll
@@ -199,29 +209,22 @@ __global__ void __launch_bounds__(kAttnThreads) decode_attn_kernel(const float* 
     Lsum[h] = 0.f;
     M[h] = -INFINITY;
   }
-  for (int cc = 0; cc < nchunks; ++cc) {  // global max per head (the m values are tiny and cached)
+  for (int cc = 0; cc < nchunks; ++cc) {
+    const float* pc = base + (size_t)cc * kGroups * kPartStride;
+    float mv[kGroups], lv[kGroups], av[kGroups];
 #pragma unroll
-    for (int h = 0; h < kGroups; ++h) M[h] = fmaxf(M[h], __ldcg(&base[(cc * kGroups + h) * kPartStride]));
-  }
-  for (int c0 = 0; c0 < nchunks; c0 += kChunk) {
-    const int cn = min(kChunk, nchunks - c0);
-    __syncthreads();
-    for (int i = tid; i < cn * kGroups; i += kAttnThreads) {
-      const int cc = i / kGroups, h = i % kGroups;
-      const float* pc = base + ((c0 + cc) * kGroups + h) * kPartStride;
-      const float w = expf(__ldcg(&pc[0]) - M[h]);
-      sm.es[cc][h] = w;
-      sm.vs[cc][h] = __fmul_rn(__ldcg(&pc[1]), w);
+    for (int h = 0; h < kGroups; ++h) {
+      mv[h] = __ldcg(&pc[h * kPartStride]);
+      lv[h] = __ldcg(&pc[h * kPartStride + 1]);
+      av[h] = __ldcg(&pc[h * kPartStride + 2 + tid]);
     }
-    __syncthreads();
-#pragma unroll 4
-    for (int cc = 0; cc < cn; ++cc) {
-      const float* pc = base + (size_t)(c0 + cc) * kGroups * kPartStride + 2 + tid;
 #pragma unroll
-      for (int h = 0; h < kGroups; ++h) {
-        o[h] = fmaf(__ldcg(&pc[h * kPartStride]), sm.es[cc][h], o[h]);
-        Lsum[h] = __fadd_rn(Lsum[h], sm.vs[cc][h]);
-      }
+    for (int h = 0; h < kGroups; ++h) {
+      const float Mn = fmaxf(M[h], mv[h]);
+      const float sa = expf(M[h] - Mn), sb = expf(mv[h] - Mn);
+      o[h] = __fadd_rn(__fmul_rn(o[h], sa), __fmul_rn(av[h], sb));
+      Lsum[h] = __fadd_rn(__fmul_rn(Lsum[h], sa), __fmul_rn(lv[h], sb));
+      M[h] = Mn;
     }
   }
 #pragma unroll

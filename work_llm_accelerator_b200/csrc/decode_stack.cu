@@ -39,15 +39,20 @@ namespace {
 
 using namespace umma;
 
+static_assert(kKBlock == 4 * 32, "one 128-byte K block = four kind::i8 MMAs of K = 32 bytes");
 constexpr int kRing = 9;           // weight stages per CTA (shared memory); Args::ring uses 2..kRing of them
-constexpr int kThreads = 192;
+constexpr int kThreads = 224;      // producer, MMA issuer, 4 worker warps, second MMA issuer
 constexpr int kWorkers = 128;
 constexpr int kBarW = 1;           // named barrier of the worker warps
-constexpr int kTmemCols = 32;
+// Two MMA-issuing warps (1 and 6) take alternate 16 KB units of an item, each into its own accumulator
+// (summed when read out): one thread's wait-on-data and commit latencies then overlap the other's MMAs
+// (measured on B200: 491 -> ~260 cycles per unit). Two items in flight: 2 x 2 x 16 TMEM columns.
+constexpr int kIssuers = 2;
+constexpr int kAccParts = kIssuers;
+constexpr int kTmemCols = 2 * kAccParts * kTileN;
 constexpr int kDigitBlocks = 12;   // digit buffer capacity in 128-byte K blocks
 constexpr int kDigitBytes = kDigitBlocks * kDigitBlockBytes;
 constexpr int kChunk = 64;         // attention keys per work item (one KV page)
-constexpr int kPartStride = 2 + kHeadDim;
 constexpr int kRow = kHeadDim + 4;
 constexpr long long kSpinLimit = 2000000000ll;  // clock cycles, ~1 s
 
@@ -209,14 +214,18 @@ __device__ void producer(const Args& a, uint8_t* ring_smem, Ctrl& cs, uint32_t i
 }
 
 __device__ void mma_issuer(const Args& a, uint8_t* ring_smem, uint8_t* digits, Ctrl& cs, uint32_t tmem, uint32_t i0,
-                           uint32_t i1, unsigned* abort_flag) {
+                           uint32_t i1, unsigned* abort_flag, int issuer) {
   const int ring = ring_depth(a);
   int s = 0;
   unsigned ph = 0, item_no = 0, inst = 0;
   bool ok = true;
+  // Descriptors are built once; a unit / digit block / 32-byte K step only moves the start-address field
+  // (16-byte units, far from overflowing its 14 bits inside shared memory).
+  const uint64_t ring_desc = sw128_desc(smem_u32(ring_smem));
+  constexpr uint64_t kUnitStep = kUnitBytes >> 4, kBlockStep = kDigitBlockBytes >> 4, kKStep = 32 >> 4;
   for (int l = 0; l < kLayers; ++l) {
     int cur = -1;
-    uint32_t dbase = 0;
+    uint64_t dig_desc = 0;
     for (uint32_t i = i0; i < i1; ++i) {
       const Item it = a.items[i];
       if (it.stage != cur) {  // first item of a stage: its digits must be in shared memory
@@ -224,25 +233,35 @@ __device__ void mma_issuer(const Args& a, uint8_t* ring_smem, uint8_t* digits, C
         const unsigned p = inst & 1;
         ok = ok && mwait(&cs.dig_ready[p], (inst >> 1) & 1, abort_flag);
         fence_after();
-        stamp(a, l, kTraceMmaStart + cur);
-        dbase = smem_u32(digits + (size_t)p * kDigitBytes);
+        if (issuer == 0) stamp(a, l, kTraceMmaStart + cur);
+        if (a.trace != nullptr && issuer == 0)  // SM clock at the same point, to relate the unit times
+          a.trace[((size_t)blockIdx.x * kLayers + l) * kTraceSlots + 36 + (cur == kGu ? 1 : cur == kDown ? 2 : 3)] =
+              (unsigned long long)clock64();
+        dig_desc = sw128_desc(smem_u32(digits + (size_t)p * kDigitBytes));
         ++inst;
       }
       const unsigned b = item_no & 1;
       ok = ok && mwait(&cs.acc_empty[b], ((item_no >> 1) & 1) ^ 1, abort_flag);
       fence_after();
-      const uint32_t d = tmem + b * kTileN;
-      for (int kb = it.kb0; kb < it.kb1; ++kb) {
-        ok = ok && mwait(&cs.full[s], ph, abort_flag);
-        fence_after();
-        if (ok) {
-          const uint32_t abase = smem_u32(ring_smem + (size_t)s * kUnitBytes);
-          const uint32_t bbase = dbase + (uint32_t)(it.dslot + kb - it.kb0) * kDigitBlockBytes;
-#pragma unroll
-          for (int j = 0; j < kKBlock / 32; ++j)
-            mma_i8(d, sw128_desc(abase + 32 * j), sw128_desc(bbase + 32 * j), (kb > it.kb0 || j > 0) ? 1u : 0u);
+      const uint32_t d = tmem + b * (kAccParts * kTileN) + issuer * kTileN;
+      uint64_t bd = dig_desc + (uint64_t)it.dslot * kBlockStep;
+      for (int kb = it.kb0; kb < it.kb1; ++kb, bd += kBlockStep) {
+        const int u = kb - it.kb0;
+        if (u % kIssuers == issuer) {  // this issuer's unit; the ring position advances for every unit
+          ok = ok && mwait(&cs.full[s], ph, abort_flag);
+          fence_after();
+          if (a.trace != nullptr && u < 12 && (it.stage == kGu || it.stage == kDown))  // SM clock, not global time
+            a.trace[((size_t)blockIdx.x * kLayers + l) * kTraceSlots + kTraceUnit + (it.stage == kGu ? 0 : 12) + u] =
+                (unsigned long long)clock64();
+          if (ok) {
+            const uint64_t ad = ring_desc + (uint64_t)s * kUnitStep;
+            mma_i8(d, ad, bd, u >= kIssuers ? 1u : 0u);
+            mma_i8_acc(d, ad + kKStep, bd + kKStep);
+            mma_i8_acc(d, ad + 2 * kKStep, bd + 2 * kKStep);
+            mma_i8_acc(d, ad + 3 * kKStep, bd + 3 * kKStep);
+          }
+          mma_commit(&cs.empty[s]);
         }
-        mma_commit(&cs.empty[s]);
         if (++s == ring) {
           s = 0;
           ph ^= 1;
@@ -250,7 +269,7 @@ __device__ void mma_issuer(const Args& a, uint8_t* ring_smem, uint8_t* digits, C
       }
       mma_commit(&cs.acc_full[b]);
       ++item_no;
-      if (i + 1 == i1 || a.items[i + 1].stage != it.stage) stamp(a, l, kTraceMma + it.stage);
+      if (issuer == 0 && (i + 1 == i1 || a.items[i + 1].stage != it.stage)) stamp(a, l, kTraceMma + it.stage);
     }
   }
 }
@@ -278,6 +297,54 @@ __device__ __forceinline__ void put_digits(uint8_t* blk, int t, int kk, const fl
 __device__ __forceinline__ void load_norm(const float* vec, int tid, float4 (&wv)[3]) {
 #pragma unroll
   for (int j = 0; j < 3; ++j) wv[j] = __ldg(reinterpret_cast<const float4*>(vec + 512 * j + 4 * tid));
+}
+
+// Chunk partials: [token][q head][chunk] x {m, l, -, -, acc[128]} (acc 16-byte aligned).
+constexpr int kPartStride = 4 + kHeadDim;
+__device__ __forceinline__ float* part_ptr(const Args& a, int t, int h, int c) {
+  return a.attn_part + (((size_t)t * kHeads + h) * a.attn_max_chunks + c) * kPartStride;
+}
+
+// Merge of chunk partials in chunk order for 4 consecutive dims d0.. of head h, online: for each chunk c,
+// M' = max(M, m_c), o = o e^(M - M') + acc_c e^(m_c - M'), L likewise; out = o / L. Loads are issued a
+// batch of kMergeBatch chunks at a time so that one L2 round trip serves the whole batch.
+constexpr int kMergeBatch = 16;
+
+__device__ __forceinline__ void merge_chunks(const Args& a, int t, int h, int nch, int d0, float (&out)[4]) {
+  float M = -INFINITY, L = 0.f, o[4] = {0.f, 0.f, 0.f, 0.f};
+  for (int c0 = 0; c0 < nch; c0 += kMergeBatch) {
+    float mv[kMergeBatch], lv[kMergeBatch];
+    float4 av[kMergeBatch];
+#pragma unroll
+    for (int j = 0; j < kMergeBatch; ++j) {
+      if (c0 + j < nch) {
+        const float* pc = part_ptr(a, t, h, c0 + j);
+        mv[j] = __ldcg(pc);
+        lv[j] = __ldcg(pc + 1);
+        av[j] = __ldcg(reinterpret_cast<const float4*>(pc + 4 + d0));
+      } else {
+        mv[j] = -INFINITY;
+        lv[j] = 0.f;
+        av[j] = make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < kMergeBatch; ++j) {
+      if (c0 + j < nch) {
+        const float Mn = fmaxf(M, mv[j]);
+        const float sa = expf(M - Mn), sb = expf(mv[j] - Mn);
+        o[0] = __fadd_rn(__fmul_rn(o[0], sa), __fmul_rn(av[j].x, sb));
+        o[1] = __fadd_rn(__fmul_rn(o[1], sa), __fmul_rn(av[j].y, sb));
+        o[2] = __fadd_rn(__fmul_rn(o[2], sa), __fmul_rn(av[j].z, sb));
+        o[3] = __fadd_rn(__fmul_rn(o[3], sa), __fmul_rn(av[j].w, sb));
+        L = __fadd_rn(__fmul_rn(L, sa), __fmul_rn(lv[j], sb));
+        M = Mn;
+      }
+    }
+  }
+  const float inv = L > 0.0f ? 1.0f / L : 0.0f;
+#pragma unroll
+  for (int e = 0; e < 4; ++e) out[e] = o[e] * inv;
 }
 
 // Where a 1536-wide projection input comes from.
@@ -334,22 +401,42 @@ __device__ __forceinline__ void load_input(const Args& a, const InSrc& src, int 
       v[j][3] = f.w;
     }
   } else {
-    // o_proj output a = o_s * (step * acc); for kInY the layer output y = bf16(a + down_s * (step * acc))
+    // o_proj output a = o_s * (step * acc); for kInY the layer output y = bf16(a + down_s * (step * acc)).
+    // Every load is issued before any is used: one L2 round trip.
+    const bool y = src.mode == kInY;
     const float st_o = __ldcg(&a.steps[(src.layer * 4 + kO) * 4 + t]);
-    const float st_d = src.mode == kInY ? __ldcg(&a.steps[(src.layer * 4 + kDown) * 4 + t]) : 0.f;
+    const float st_d = y ? __ldcg(&a.steps[(src.layer * 4 + kDown) * 4 + t]) : 0.f;
+    int4 ro[3][3], rd[3][3];
+#pragma unroll
+    for (int j = 0; j < 3; ++j)
+#pragma unroll
+      for (int d = 0; d < 3; ++d) {
+        const int k = 512 * j + 4 * tid;
+        ro[j][d] = __ldcg(reinterpret_cast<const int4*>(acc_ptr(a, src.parity, t, d) + acc_row_base(kO) + k));
+        rd[j][d] = y ? __ldcg(reinterpret_cast<const int4*>(acc_ptr(a, src.parity, t, d) + acc_row_base(kDown) + k))
+                     : make_int4(0, 0, 0, 0);
+      }
 #pragma unroll
     for (int j = 0; j < 3; ++j) {
       const int k = 512 * j + 4 * tid;
-      float o[4], dn[4];
-      acc_values(a, src.parity, t, acc_row_base(kO) + k, st_o, o);
       const float osc[4] = {src.os[j].x, src.os[j].y, src.os[j].z, src.os[j].w};
+      const float dsc[4] = {src.ds[j].x, src.ds[j].y, src.ds[j].z, src.ds[j].w};
+      const int o0[4] = {ro[j][0].x, ro[j][0].y, ro[j][0].z, ro[j][0].w};
+      const int o1[4] = {ro[j][1].x, ro[j][1].y, ro[j][1].z, ro[j][1].w};
+      const int o2[4] = {ro[j][2].x, ro[j][2].y, ro[j][2].z, ro[j][2].w};
+      const int d0[4] = {rd[j][0].x, rd[j][0].y, rd[j][0].z, rd[j][0].w};
+      const int d1[4] = {rd[j][1].x, rd[j][1].y, rd[j][1].z, rd[j][1].w};
+      const int d2[4] = {rd[j][2].x, rd[j][2].y, rd[j][2].z, rd[j][2].w};
 #pragma unroll
-      for (int e = 0; e < 4; ++e) v[j][e] = osc[e] * o[e];
-      if (src.mode == kInY) {
-        acc_values(a, src.parity, t, acc_row_base(kDown) + k, st_d, dn);
-        const float dsc[4] = {src.ds[j].x, src.ds[j].y, src.ds[j].z, src.ds[j].w};
-#pragma unroll
-        for (int e = 0; e < 4; ++e) v[j][e] = round_bf16(__fadd_rn(v[j][e], dsc[e] * dn[e]));
+      for (int e = 0; e < 4; ++e) {
+        const long long to = (long long)o0[e] + 256ll * (long long)o1[e] + 65536ll * (long long)o2[e];
+        v[j][e] = osc[e] * (float)((double)to * (double)st_o);
+        if (y) {
+          const long long td = (long long)d0[e] + 256ll * (long long)d1[e] + 65536ll * (long long)d2[e];
+          v[j][e] = round_bf16(__fadd_rn(v[j][e], dsc[e] * (float)((double)td * (double)st_d)));
+        }
+      }
+      if (y) {
         const float4 yv = make_float4(v[j][0], v[j][1], v[j][2], v[j][3]);
         if (src.y_write) *reinterpret_cast<float4*>(src.y_write + (size_t)t * kHidden + k) = yv;
         if (src.dump_write) *reinterpret_cast<float4*>(src.dump_write + (size_t)t * kHidden + k) = yv;
@@ -473,7 +560,20 @@ __device__ void item_epilogue(const Args& a, Ctrl& cs, WorkerCtx& w, const Item 
   __syncwarp();
   fence_after();
   int v[16];
-  tmem_ld16(w.tmem + b * kTileN + ((uint32_t)(w.quarter * 32) << 16), v);
+  {
+    const uint32_t ta = w.tmem + b * (kAccParts * kTileN) + ((uint32_t)(w.quarter * 32) << 16);
+    tmem_ld16(ta, v);
+    // issuer p wrote part p only if the item has more than p units
+#pragma unroll
+    for (int p = 1; p < kAccParts; ++p) {
+      if (it.kb1 - it.kb0 > p) {
+        int u[16];
+        tmem_ld16(ta + p * kTileN, u);
+#pragma unroll
+        for (int c = 0; c < 16; ++c) v[c] += u[c];
+      }
+    }
+  }
   fence_before();
   mbar_arrive(&cs.acc_empty[b]);
   ++w.item_no;
@@ -515,63 +615,28 @@ __device__ void item_epilogue(const Args& a, Ctrl& cs, WorkerCtx& w, const Item 
 // workers: attention (hls/decode_only/qwen_decode_attention_kernel.cpp:113-162), one 64-key chunk of one
 // (token, KV head) per item; chunk partials merged in chunk order by the last chunk to finish.
 // ---------------------------------------------------------------------------------------------------
+// Attention work items: one 64-key chunk (= one KV page) x one KV group x one half of its six query
+// heads, so each of the many small items keeps all 128 workers busy.
+constexpr int kHalf = 3;  // query heads per item
+
 struct AttnItem {
-  int t, g, c, nchunks, n, nhist;
+  int t, g, hp, c, nchunks, n, nhist;
   const float* kbase;
   const float* vbase;
 };
 
-// Constants of the q|k|v epilogue for the rows this thread finishes in attention: dim d = tid of the six
-// query heads of KV group g, of the K head and of the V head, plus the RoPE factors at the token position.
-struct QkvConst {
-  float qs[kGroups], qb[kGroups];
-  float ks, kb, vs, vb;
-  float rc, rs;
-};
-
-__device__ __forceinline__ void qkv_const(const Args& a, const WorkerCtx& w, int l, int t, int g, QkvConst& k) {
-  const LayerDev& L = a.layers[l];
-  const int d = w.tid;
-#pragma unroll
-  for (int hh = 0; hh < kGroups; ++hh) {
-    const int row = (g * kGroups + hh) * kHeadDim + d;
-    k.qs[hh] = __ldg(L.qkv_s + row);
-    k.qb[hh] = __ldg(L.qkv_b + row);
-  }
-  const int krow = kHidden + g * kHeadDim + d, vrow = kHidden + kKvWidth + g * kHeadDim + d;
-  k.ks = __ldg(L.qkv_s + krow);
-  k.kb = __ldg(L.qkv_b + krow);
-  k.vs = __ldg(L.qkv_s + vrow);
-  k.vb = __ldg(L.qkv_b + vrow);
-  const size_t ri = (size_t)w.pos[t] * 64 + (d & 63);
-  k.rc = __ldg(a.rope_cos + ri);
-  k.rs = __ldg(a.rope_sin + ri);
-}
-
-// q|k|v value of one row from the integer accumulators: bias + scale * (step * acc)
-__device__ __forceinline__ float qkv_value(const Args& a, int parity, int t, int row, float step, float sc, float bb) {
-  const int* p0 = acc_ptr(a, parity, t, 0);
-  const int* p1 = acc_ptr(a, parity, t, 1);
-  const int* p2 = acc_ptr(a, parity, t, 2);
-  const long long tot =
-      (long long)__ldcg(p0 + row) + 256ll * (long long)__ldcg(p1 + row) + 65536ll * (long long)__ldcg(p2 + row);
-  return __fmaf_rn(sc, (float)((double)tot * (double)step), bb);
-}
-
-// rotate-half RoPE of dim d given its partner dim d ^ 64
-__device__ __forceinline__ float rope(float mine, float other, int d, float c, float sn) {
-  return d < 64 ? __fsub_rn(__fmul_rn(mine, c), __fmul_rn(other, sn)) : __fadd_rn(__fmul_rn(mine, c), __fmul_rn(other, sn));
-}
+__device__ __forceinline__ int attn_items_of(int nch) { return kKvHeads * 2 * nch; }
 
 __device__ __forceinline__ AttnItem attn_decode(const Args& a, const WorkerCtx& w, int l, int i, const int (&nch)[4]) {
   AttnItem it;
   int t = 0, rem = i;
-  while (rem >= kKvHeads * nch[t]) {
-    rem -= kKvHeads * nch[t];
+  while (rem >= attn_items_of(nch[t])) {
+    rem -= attn_items_of(nch[t]);
     ++t;
   }
   it.t = t;
-  it.g = rem / nch[t];
+  it.g = rem / (2 * nch[t]);
+  it.hp = (rem / nch[t]) & 1;
   it.c = rem % nch[t];
   it.nchunks = nch[t];
   const int L = w.pos[t] + 1;
@@ -594,45 +659,88 @@ __device__ __forceinline__ void attn_load_rows(AttnSmem& sm, const AttnItem& it,
   }
 }
 
-// One 64-key chunk of one (token, KV head): the history rows are already in flight; loads the new row
-// (when it falls in this chunk) and the six query heads, then scores, softmax statistics and P.V; the last
-// chunk of a (token, KV head) to finish merges all chunks in chunk order.
+// Constants of the q|k|v epilogue for the rows this thread finishes in attention: dim d = tid of the item's
+// three query heads, of the K head and of the V head, plus the RoPE factors at the token position.
+struct QkvConst {
+  float qs[kHalf], qb[kHalf];
+  float ks, kb, vs, vb;
+  float rc, rs;
+};
+
+__device__ __forceinline__ int q_head(const AttnItem& it, int j) { return it.g * kGroups + it.hp * kHalf + j; }
+
+__device__ __forceinline__ void qkv_const(const Args& a, const WorkerCtx& w, int l, const AttnItem& it, QkvConst& k) {
+  const LayerDev& L = a.layers[l];
+  const int d = w.tid;
+#pragma unroll
+  for (int j = 0; j < kHalf; ++j) {
+    const int row = q_head(it, j) * kHeadDim + d;
+    k.qs[j] = __ldg(L.qkv_s + row);
+    k.qb[j] = __ldg(L.qkv_b + row);
+  }
+  const int krow = kHidden + it.g * kHeadDim + d, vrow = kHidden + kKvWidth + it.g * kHeadDim + d;
+  k.ks = __ldg(L.qkv_s + krow);
+  k.kb = __ldg(L.qkv_b + krow);
+  k.vs = __ldg(L.qkv_s + vrow);
+  k.vb = __ldg(L.qkv_b + vrow);
+  const size_t ri = (size_t)w.pos[it.t] * 64 + (d & 63);
+  k.rc = __ldg(a.rope_cos + ri);
+  k.rs = __ldg(a.rope_sin + ri);
+}
+
+// q|k|v value of one row from the integer accumulators: bias + scale * (step * acc)
+__device__ __forceinline__ float qkv_value(const Args& a, int parity, int t, int row, float step, float sc, float bb) {
+  const int* p0 = acc_ptr(a, parity, t, 0);
+  const int* p1 = acc_ptr(a, parity, t, 1);
+  const int* p2 = acc_ptr(a, parity, t, 2);
+  const long long tot =
+      (long long)__ldcg(p0 + row) + 256ll * (long long)__ldcg(p1 + row) + 65536ll * (long long)__ldcg(p2 + row);
+  return __fmaf_rn(sc, (float)((double)tot * (double)step), bb);
+}
+
+// rotate-half RoPE of dim d given its partner dim d ^ 64
+__device__ __forceinline__ float rope(float mine, float other, int d, float c, float sn) {
+  return d < 64 ? __fsub_rn(__fmul_rn(mine, c), __fmul_rn(other, sn)) : __fadd_rn(__fmul_rn(mine, c), __fmul_rn(other, sn));
+}
+
+// One item: the history rows are already in flight; finishes q (three heads) and, in the chunk that holds
+// it, the new token's K/V row from the q|k|v accumulators, then scores, softmax statistics and P.V of the
+// chunk, written as a partial; the last chunk of a (token, group, half) to finish merges them in chunk
+// order and writes the three heads' context.
 __device__ void attn_item(const Args& a, AttnSmem& sm, Ctrl& cs, const WorkerCtx& w, int l, const AttnItem& it,
                           const QkvConst& qc) {
   const int tid = w.tid, warp = tid >> 5, lane = tid & 31;
-  const int t = it.t, g = it.g, n = it.n, nchunks = it.nchunks;
-  // q (six heads) and, in the chunk that holds it, the new token's K/V row, finished from the q|k|v
-  // accumulators: this thread owns dim d = tid, RoPE pairs meet through shared memory
+  const int t = it.t, n = it.n, nchunks = it.nchunks;
   {
     const int d = tid, parity = l & 1;
     const float st = __ldcg(&a.steps[(l * 4 + kQkv) * 4 + t]);
     const bool has_new = it.nhist < n;  // the new token is row nhist of this chunk
-    float qv[kGroups], kv = 0.f, vv = 0.f;
+    float qv[kHalf], kv = 0.f, vv = 0.f;
 #pragma unroll
-    for (int hh = 0; hh < kGroups; ++hh)
-      qv[hh] = qkv_value(a, parity, t, (g * kGroups + hh) * kHeadDim + d, st, qc.qs[hh], qc.qb[hh]);
+    for (int j = 0; j < kHalf; ++j) qv[j] = qkv_value(a, parity, t, q_head(it, j) * kHeadDim + d, st, qc.qs[j], qc.qb[j]);
     if (has_new) {
-      kv = qkv_value(a, parity, t, kHidden + g * kHeadDim + d, st, qc.ks, qc.kb);
-      vv = qkv_value(a, parity, t, kHidden + kKvWidth + g * kHeadDim + d, st, qc.vs, qc.vb);
+      kv = qkv_value(a, parity, t, kHidden + it.g * kHeadDim + d, st, qc.ks, qc.kb);
+      vv = qkv_value(a, parity, t, kHidden + kKvWidth + it.g * kHeadDim + d, st, qc.vs, qc.vb);
     }
 #pragma unroll
-    for (int hh = 0; hh < kGroups; ++hh) sm.qs[hh][d] = qv[hh];
+    for (int j = 0; j < kHalf; ++j) sm.qs[j][d] = qv[j];
     if (has_new) sm.ks[it.nhist][d] = kv;
     named_sync(kBarW, kWorkers);
-    float qr[kGroups], kr = 0.f;
+    float qr[kHalf], kr = 0.f;
 #pragma unroll
-    for (int hh = 0; hh < kGroups; ++hh) qr[hh] = rope(qv[hh], sm.qs[hh][d ^ 64], d, qc.rc, qc.rs);
+    for (int j = 0; j < kHalf; ++j) qr[j] = rope(qv[j], sm.qs[j][d ^ 64], d, qc.rc, qc.rs);
     if (has_new) kr = rope(kv, sm.ks[it.nhist][d ^ 64], d, qc.rc, qc.rs);
     named_sync(kBarW, kWorkers);
 #pragma unroll
-    for (int hh = 0; hh < kGroups; ++hh) sm.qs[hh][d] = qr[hh];
+    for (int j = 0; j < kHalf; ++j) sm.qs[j][d] = qr[j];
     if (has_new) {
       sm.ks[it.nhist][d] = kr;
       sm.vs[it.nhist][d] = vv;
-      // the cache row of this step, for later steps
-      float* krow = w.kvrow[t] + ((size_t)l * 2) * kPage * kKvWidth + g * kHeadDim + d;
-      krow[0] = kr;
-      krow[kPage * kKvWidth] = vv;
+      if (it.hp == 0) {  // the cache row of this step, for later steps
+        float* krow = w.kvrow[t] + ((size_t)l * 2) * kPage * kKvWidth + it.g * kHeadDim + d;
+        krow[0] = kr;
+        krow[kPage * kKvWidth] = vv;
+      }
     }
   }
   cp_async_wait_all();
@@ -640,158 +748,111 @@ __device__ void attn_item(const Args& a, AttnSmem& sm, Ctrl& cs, const WorkerCtx
   if (tid == 0) stamp(a, l, kTraceAttnQ);
   const float scaling = kAttentionScaling;
   {
-    const int key = tid >> 1, h0 = (tid & 1) * 3;
+    // thread = (key, half of the head dims): three heads over 64 dims, the two halves added
+    const int key = tid >> 1, f0 = (tid & 1) * 16;
     float s0 = 0.f, s1 = 0.f, s2 = 0.f;
-#pragma unroll 8
-    for (int f = 0; f < 32; ++f) {
+#pragma unroll
+    for (int f = f0; f < f0 + 16; ++f) {
       const float4 kk = *reinterpret_cast<const float4*>(&sm.ks[key][4 * f]);
-      const float4 x0 = *reinterpret_cast<const float4*>(&sm.qs[h0][4 * f]);
-      const float4 x1 = *reinterpret_cast<const float4*>(&sm.qs[h0 + 1][4 * f]);
-      const float4 x2 = *reinterpret_cast<const float4*>(&sm.qs[h0 + 2][4 * f]);
+      const float4 x0 = *reinterpret_cast<const float4*>(&sm.qs[0][4 * f]);
+      const float4 x1 = *reinterpret_cast<const float4*>(&sm.qs[1][4 * f]);
+      const float4 x2 = *reinterpret_cast<const float4*>(&sm.qs[2][4 * f]);
       s0 = fmaf(x0.x, kk.x, fmaf(x0.y, kk.y, fmaf(x0.z, kk.z, fmaf(x0.w, kk.w, s0))));
       s1 = fmaf(x1.x, kk.x, fmaf(x1.y, kk.y, fmaf(x1.z, kk.z, fmaf(x1.w, kk.w, s1))));
       s2 = fmaf(x2.x, kk.x, fmaf(x2.y, kk.y, fmaf(x2.z, kk.z, fmaf(x2.w, kk.w, s2))));
     }
-    const bool ok = key < n;
-    sm.es[key][h0] = ok ? s0 * scaling : -INFINITY;
-    sm.es[key][h0 + 1] = ok ? s1 * scaling : -INFINITY;
-    sm.es[key][h0 + 2] = ok ? s2 * scaling : -INFINITY;
-  }
-  named_sync(kBarW, kWorkers);
-  if (warp < 3) {
-#pragma unroll
-    for (int j = 0; j < 2; ++j) {
-      const int hh = 2 * warp + j;
-      const float x0 = sm.es[lane][hh], x1 = sm.es[lane + 32][hh];
-      float m = warp_max(fmaxf(x0, x1));
-      m = fmaxf(m, -1.0e30f);  // the reference's initial max
-      const float e0 = lane < n ? expf(x0 - m) : 0.f;
-      const float e1 = lane + 32 < n ? expf(x1 - m) : 0.f;
-      sm.es[lane][hh] = e0;
-      sm.es[lane + 32][hh] = e1;
-      float sum = e0 + e1;
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
-      if (lane == 0) {
-        sm.ms[hh] = m;
-        sm.ls[hh] = sum;
-      }
+    s0 = __fadd_rn(s0, __shfl_xor_sync(0xffffffffu, s0, 1));
+    s1 = __fadd_rn(s1, __shfl_xor_sync(0xffffffffu, s1, 1));
+    s2 = __fadd_rn(s2, __shfl_xor_sync(0xffffffffu, s2, 1));
+    if ((tid & 1) == 0) {
+      const bool ok = key < n;
+      sm.es[key][0] = ok ? s0 * scaling : -INFINITY;
+      sm.es[key][1] = ok ? s1 * scaling : -INFINITY;
+      sm.es[key][2] = ok ? s2 * scaling : -INFINITY;
     }
   }
   named_sync(kBarW, kWorkers);
-  float acc[kGroups];
+  if (warp < kHalf) {
+    const int j = warp;
+    const float x0 = sm.es[lane][j], x1 = sm.es[lane + 32][j];
+    float m = warp_max(fmaxf(x0, x1));
+    m = fmaxf(m, -1.0e30f);  // the reference's initial max
+    const float e0 = lane < n ? expf(x0 - m) : 0.f;
+    const float e1 = lane + 32 < n ? expf(x1 - m) : 0.f;
+    sm.es[lane][j] = e0;
+    sm.es[lane + 32][j] = e1;
+    float sum = e0 + e1;
 #pragma unroll
-  for (int hh = 0; hh < kGroups; ++hh) acc[hh] = 0.f;
+    for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+    if (lane == 0) {
+      sm.ms[j] = m;
+      sm.ls[j] = sum;
+    }
+  }
+  named_sync(kBarW, kWorkers);
+  float acc[kHalf] = {0.f, 0.f, 0.f};
 #pragma unroll 4
   for (int key = 0; key < n; ++key) {
     const float vv = sm.vs[key][tid];
-    const float4 e03 = *reinterpret_cast<const float4*>(&sm.es[key][0]);
-    const float2 e45 = *reinterpret_cast<const float2*>(&sm.es[key][4]);
-    acc[0] = fmaf(e03.x, vv, acc[0]);
-    acc[1] = fmaf(e03.y, vv, acc[1]);
-    acc[2] = fmaf(e03.z, vv, acc[2]);
-    acc[3] = fmaf(e03.w, vv, acc[3]);
-    acc[4] = fmaf(e45.x, vv, acc[4]);
-    acc[5] = fmaf(e45.y, vv, acc[5]);
+    const float4 e = *reinterpret_cast<const float4*>(&sm.es[key][0]);
+    acc[0] = fmaf(e.x, vv, acc[0]);
+    acc[1] = fmaf(e.y, vv, acc[1]);
+    acc[2] = fmaf(e.z, vv, acc[2]);
   }
-  float* out_base = a.ctx + (size_t)t * kHidden + g * kGroups * kHeadDim + tid;
-  bool finished = false;
-  if (nchunks == 1) {
+  // the chunk partial
 #pragma unroll
-    for (int hh = 0; hh < kGroups; ++hh) {
-      const float inv = sm.ls[hh] > 0.0f ? 1.0f / sm.ls[hh] : 0.0f;
-      out_base[hh * kHeadDim] = acc[hh] * inv;
-    }
-    finished = true;
-  } else {
-    float* my = a.attn_part + (((size_t)t * kKvHeads + g) * a.attn_max_chunks + it.c) * kGroups * kPartStride;
-#pragma unroll
-    for (int hh = 0; hh < kGroups; ++hh) my[hh * kPartStride + 2 + tid] = acc[hh];
-    if (tid < kGroups) {
-      my[tid * kPartStride + 0] = sm.ms[tid];
-      my[tid * kPartStride + 1] = sm.ls[tid];
-    }
-    named_sync(kBarW, kWorkers);
+  for (int j = 0; j < kHalf; ++j) {
+    float* pc = part_ptr(a, t, q_head(it, j), it.c);
+    pc[4 + tid] = acc[j];
     if (tid == 0) {
-      cs.flag = atom_add_acq_rel(&a.sync->attn_cnt[t][g].v, 1u) == (unsigned)nchunks - 1u;
-      stamp(a, l, kTraceAttnPart);
-    }
-    named_sync(kBarW, kWorkers);
-    if (cs.flag) {
-      // merge in chunk order: M = max of the chunk maxima, then o = sum acc_c w_c, L = sum l_c w_c with
-      // w_c = expf(m_c - M); every thread reads the (small) statistics itself, no shared-memory staging
-      const float* base = a.attn_part + ((size_t)t * kKvHeads + g) * a.attn_max_chunks * kGroups * kPartStride;
-      float o[kGroups], Lsum[kGroups], M[kGroups];
-#pragma unroll
-      for (int hh = 0; hh < kGroups; ++hh) {
-        o[hh] = 0.f;
-        Lsum[hh] = 0.f;
-        M[hh] = -INFINITY;
-      }
-      for (int cc = 0; cc < nchunks; ++cc) {
-#pragma unroll
-        for (int hh = 0; hh < kGroups; ++hh) M[hh] = fmaxf(M[hh], __ldcg(&base[(cc * kGroups + hh) * kPartStride]));
-      }
-      constexpr int kB = 8;
-      for (int c0 = 0; c0 < nchunks; c0 += kB) {
-        float av[kB][kGroups], mv[kB][kGroups], lv[kB][kGroups];
-#pragma unroll
-        for (int cc = 0; cc < kB; ++cc) {
-#pragma unroll
-          for (int hh = 0; hh < kGroups; ++hh) {
-            const bool in = c0 + cc < nchunks;
-            const float* pc = base + ((size_t)(c0 + cc) * kGroups + hh) * kPartStride;
-            av[cc][hh] = in ? __ldcg(&pc[2 + tid]) : 0.f;
-            mv[cc][hh] = in ? __ldcg(&pc[0]) : 0.f;
-            lv[cc][hh] = in ? __ldcg(&pc[1]) : 0.f;
-          }
-        }
-#pragma unroll
-        for (int cc = 0; cc < kB; ++cc) {
-          if (c0 + cc < nchunks) {
-#pragma unroll
-            for (int hh = 0; hh < kGroups; ++hh) {
-              const float wgt = expf(mv[cc][hh] - M[hh]);
-              o[hh] = fmaf(av[cc][hh], wgt, o[hh]);
-              Lsum[hh] = __fadd_rn(Lsum[hh], __fmul_rn(lv[cc][hh], wgt));  // rounded product, then sum
-            }
-          }
-        }
-      }
-#pragma unroll
-      for (int hh = 0; hh < kGroups; ++hh) {
-        const float inv = Lsum[hh] > 0.0f ? 1.0f / Lsum[hh] : 0.0f;
-        out_base[hh * kHeadDim] = o[hh] * inv;
-      }
-      if (tid == 0) {
-        a.sync->attn_cnt[t][g].v = 0u;
-        stamp(a, l, kTraceAttnMerge);
-      }
-      finished = true;
+      pc[0] = sm.ms[j];
+      pc[1] = sm.ls[j];
     }
   }
-  if (finished) {  // uniform across the workers
-    named_sync(kBarW, kWorkers);
-    if (tid == 0) red_release(&a.sync->done[l][kDoneAttn].v, 1u);
+  named_sync(kBarW, kWorkers);
+  if (tid == 0) {
+    cs.flag = atom_add_acq_rel(&a.sync->attn_cnt[t][it.g * 2 + it.hp].v, 1u) == (unsigned)nchunks - 1u;
+    stamp(a, l, kTraceAttnPart);
+  }
+  named_sync(kBarW, kWorkers);
+  if (!cs.flag) return;
+  // last chunk of this (token, group, half): merge and write the three heads' context; thread = 4 dims of
+  // one head (96 threads)
+  if (tid < kHalf * 32) {
+    const int j = tid >> 5, d0 = 4 * (tid & 31), h = q_head(it, j);
+    float out[4];
+    merge_chunks(a, t, h, nchunks, d0, out);
+    *reinterpret_cast<float4*>(a.ctx + (size_t)t * kHidden + h * kHeadDim + d0) = make_float4(out[0], out[1], out[2], out[3]);
+  }
+  named_sync(kBarW, kWorkers);
+  if (tid == 0) {
+    a.sync->attn_cnt[t][it.g * 2 + it.hp].v = 0u;
+    red_release(&a.sync->done[l][kDoneAttn].v, 1u);
+    stamp(a, l, kTraceAttnMerge);
   }
 }
 
-// Attention of layer l over this CTA's chunks (items blockIdx.x, + gridDim.x, ...). The history rows of
-// the first chunk do not depend on this step and are requested before the wait for q|k|v.
+__device__ __forceinline__ int attn_chunks(const WorkerCtx& w, int t) { return (w.pos[t] + 1 + kChunk - 1) / kChunk; }
+
+// Completion count of the attention step: one per (token, group, half), by its merging chunk.
+__device__ __forceinline__ unsigned attn_done_target(const Args& a) { return (unsigned)(a.nt * kKvHeads * 2); }
+
+// Attention of layer l over this CTA's items (blockIdx.x, + gridDim.x, ...). The history rows of the
+// first item do not depend on this step and are requested before the wait for q|k|v.
 __device__ void attention_stage(const Args& a, AttnSmem& sm, Ctrl& cs, const WorkerCtx& w, int l,
                                 unsigned* abort_flag) {
   const int tid = w.tid;
   int nch[4] = {0, 0, 0, 0}, total = 0;
   for (int t = 0; t < a.nt; ++t) {
-    nch[t] = (w.pos[t] + 1 + kChunk - 1) / kChunk;
-    total += kKvHeads * nch[t];
+    nch[t] = attn_chunks(w, t);
+    total += attn_items_of(nch[t]);
   }
   if ((int)blockIdx.x >= total) return;
   named_sync(kBarW, kWorkers);  // shared memory free: this CTA's earlier epilogues are done
   AttnItem it = attn_decode(a, w, l, blockIdx.x, nch);
   attn_load_rows(sm, it, 0, it.nhist, tid);
   QkvConst qc;
-  qkv_const(a, w, l, it.t, it.g, qc);
+  qkv_const(a, w, l, it, qc);
   workers_wait(&a.sync->done[l][kDoneQkv].v, (unsigned)stage_items(kQkv), abort_flag, tid);
   if (tid == 0) stamp(a, l, kTraceWait + 1);
   for (int i = blockIdx.x;;) {
@@ -799,7 +860,7 @@ __device__ void attention_stage(const Args& a, AttnSmem& sm, Ctrl& cs, const Wor
     i += gridDim.x;
     if (i >= total) break;
     const AttnItem nx = attn_decode(a, w, l, i, nch);
-    if (nx.t != it.t || nx.g != it.g) qkv_const(a, w, l, nx.t, nx.g, qc);
+    if (nx.t != it.t || nx.g != it.g || nx.hp != it.hp) qkv_const(a, w, l, nx, qc);
     it = nx;
     named_sync(kBarW, kWorkers);  // previous chunk done with the shared buffers
     attn_load_rows(sm, it, 0, it.nhist, tid);
@@ -876,7 +937,7 @@ __device__ void workers(const Args& a, uint8_t* uni, Ctrl& cs, uint32_t tmem, ui
     attention_stage(a, asm_, cs, w, l, abort_flag);
     if (sb[kO] < se[kO]) {
       src.mode = kInCtx;
-      workers_wait(&done[kDoneAttn].v, (unsigned)(kKvHeads * a.nt), abort_flag, w.tid);
+      workers_wait(&done[kDoneAttn].v, attn_done_target(a), abort_flag, w.tid);
       if (tr) stamp(a, l, kTraceWait + 2);
       build_full(a, cs, digits(inst), src, false, wv, w.tid, step, step_tab + kO * 4);
       ready();
@@ -945,7 +1006,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_stack_kernel(const __grid_
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&cs.dig_ready[b], kWorkers);
-      mbar_init(&cs.acc_full[b], 1);
+      mbar_init(&cs.acc_full[b], kIssuers);
       mbar_init(&cs.acc_empty[b], kWorkers);
     }
     mbar_fence_init();
@@ -958,8 +1019,8 @@ __global__ void __launch_bounds__(kThreads, 1) decode_stack_kernel(const __grid_
 
   if (warp == 0) {
     if (lane == 0) producer(a, ring, cs, i0, i1, abort_flag);
-  } else if (warp == 1) {
-    if (lane == 0) mma_issuer(a, ring, uni, cs, tmem, i0, i1, abort_flag);
+  } else if (warp == 1 || warp == 6) {
+    if (lane == 0) mma_issuer(a, ring, uni, cs, tmem, i0, i1, abort_flag, warp == 1 ? 0 : 1);
   } else {
     workers(a, uni, cs, tmem, i0, i1, abort_flag);
   }

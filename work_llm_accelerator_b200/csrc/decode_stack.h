@@ -58,7 +58,7 @@ struct alignas(128) SyncWord {
 struct SyncWords {
   SyncWord done[kLayers][kDoneSlots];
   SyncWord hmax[kLayers];      // .pad[0..3]: max |h| per token (float bits), for the down projection's step
-  SyncWord attn_cnt[4][2];
+  SyncWord attn_cnt[4][4];     // per token, KV group x head half
   SyncWord exit_cnt;
   SyncWord abort_flag;
 };
@@ -116,9 +116,15 @@ struct Args {
 //   kTraceAttnQ      workers: attention inputs (q, new K/V row, history) in shared memory
 //   kTraceAttnPart   workers: attention chunk partial written and counted
 //   kTraceAttnMerge  workers: attention chunks merged (last chunk only)
-constexpr int kTraceSlots = 40;
+//   kTraceUnit + u   MMA issuer: unit u (< 12) of the CTA's gate|up item present in shared memory
+//   kTraceUnit + 12 + u   MMA issuer: unit u (< 12) of the CTA's down item present in shared memory
+constexpr int kTraceSlots = 64;
+constexpr int kTraceUnit = 40;
 constexpr int kTraceWait = 0, kTraceBuilt = 5, kTraceDone = 10, kTraceIssue = 16, kTraceMma = 20, kTraceAcc = 24,
               kTraceArrived = 27, kTraceMmaStart = 30, kTraceAttnQ = 34, kTraceAttnPart = 35, kTraceAttnMerge = 36;
+
+// Floats of the attention chunk-partial scratch for `nt` tokens and `max_chunks` 64-key chunks.
+inline size_t attn_part_floats(int nt, int max_chunks) { return (size_t)nt * kHeads * max_chunks * (4 + kHeadDim); }
 
 // Launch over `ctas` CTAs (cooperative: all resident). Requires wbits 8 weights in the tiled layout.
 cudaError_t launch_decode_stack(const Args& a, int ctas, cudaStream_t s);

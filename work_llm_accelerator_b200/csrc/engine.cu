@@ -460,8 +460,9 @@ int qwen_engine_create(int device, int wbits, int max_seqs, int max_len, qwen_en
   E_TRY(dalloc(&e->y0, (size_t)T * kHidden));
   E_TRY(dalloc(&e->y1, (size_t)T * kHidden));
   E_TRY(dalloc(&e->h, (size_t)T * kInter));
-  E_TRY(dalloc(&e->attn_part, attn_partial_floats(T, max_len + 512 + 64)));
   e->attn_max_chunks = (max_len + 512 + 64 + 63) / 64;
+  E_TRY(dalloc(&e->attn_part, std::max(attn_partial_floats(T, max_len + 512 + 64),
+                                       stack::attn_part_floats(T, e->attn_max_chunks))));
   E_TRY(dalloc(&e->attn_cnt, (size_t)T * kKvHeads));
   E_TRY(cudaMemset(e->attn_cnt, 0, (size_t)T * kKvHeads * 4));
   E_TRY(dalloc(&e->lm_part, (size_t)lm_head_partial_floats()));

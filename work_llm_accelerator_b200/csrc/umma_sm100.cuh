@@ -48,6 +48,12 @@ __device__ __forceinline__ void mma_i8(uint32_t d_tmem, uint64_t a, uint64_t b, 
       : "memory");
 }
 
+// Same, always accumulating (no predicate set-up on the issue path).
+__device__ __forceinline__ void mma_i8_acc(uint32_t d_tmem, uint64_t a, uint64_t b) {
+  asm volatile("tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, 1;" ::"r"(d_tmem), "l"(a), "l"(b), "r"(kIdescI8)
+               : "memory");
+}
+
 // The mbarrier completes one arrival once every MMA this thread issued before has finished.
 __device__ __forceinline__ void mma_commit(uint64_t* bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))

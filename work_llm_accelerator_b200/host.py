@@ -270,7 +270,7 @@ class Engine:
     def read_trace(self, ctas: int = 148) -> np.ndarray:
         """Timeline of the last persistent-kernel step: [ctas][28][slots] global-timer ns (option "trace")."""
         c, sl = ctypes.c_int(), ctypes.c_int()
-        out = np.zeros(ctas * 28 * 64, np.uint64)
+        out = np.zeros(ctas * 28 * 64, np.uint64)  # up to 64 slots
         _check(self.lib.qwen_engine_read_trace(self.handle, out, out.size, ctypes.byref(c), ctypes.byref(sl)),
                "read_trace")
         return out[:c.value * 28 * sl.value].reshape(c.value, 28, sl.value)
