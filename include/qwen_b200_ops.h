@@ -48,6 +48,14 @@ int qwen_b200_decode_attention_noalloc(const float* q, const float* k_cache, con
 int qwen_b200_w8_digit_products(const signed char* codes, int rows, int k, const float* x, int n_tokens, int* acc,
                                 float* step, void* stream);
 
+/* Many-token form of the same integer core (the prefill and batched projections): x [n_tokens][k] fp32
+ * (16-byte aligned) becomes three digit planes with the per-token step as above, and
+ *   acc[d][t][r] = sum_i codes[r][i] * d_d(t, i)      (int32, exact), d < 3, t < n_tokens, r < rows
+ * acc is [3][n_tokens][rows] int32, step [n_tokens] fp32 (device memory). Uses stream-ordered temporary
+ * allocations for the planes. rows % 128 == 0, k % 128 == 0, 1 <= n_tokens <= 65536. */
+int qwen_b200_w8_digit_planes(const signed char* codes, int rows, int k, const float* x, int n_tokens, int* acc,
+                              float* step, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -101,3 +101,43 @@ def test_digit_products_rejects_bad_shapes(built_libs, gpu_available):
     for rows, k, nt in [(100, 128, 1), (128, 100, 1), (128, 128, 5), (128, 128, 0)]:
         with pytest.raises(host.EngineError):
             host.w8_digit_products(a.data_ptr(), rows, k, a.data_ptr(), nt, a.data_ptr(), a.data_ptr())
+
+
+@pytest.mark.parametrize("rows,k,nt", [
+    (128, 128, 1),      # one tile, one K block, one token
+    (256, 1536, 130),   # two token tiles, the second ragged
+    (2048, 1536, 300),  # q|k|v rows, three token tiles
+    (128, 8960, 129),   # down_proj K, ragged tokens
+])
+def test_digit_planes_exact(built_libs, gpu_available, rows, k, nt):
+    """Many-token tensor-core path (prefill / batched projections): three int32 planes per output, exact."""
+    import torch
+
+    from work_llm_accelerator_b200 import host
+
+    if not gpu_available:
+        pytest.fail("no CUDA device")
+    rng = np.random.default_rng(rows * 7 + nt)
+    codes = rng.integers(-127, 128, size=(rows, k), dtype=np.int8)
+    codes[0, :] = 127
+    codes[rows - 1, :] = -128
+    x = rng.standard_normal((nt, k)).astype(np.float32)
+    x[:, rng.integers(0, k, 5)] *= 40.0
+    x[nt // 2, :] = 0.0  # an all-zero token row (step 1)
+    step_ref, d = digits_numpy(x)
+    c64 = codes.astype(np.int64)
+    acc_ref = np.stack([d[p] @ c64.T for p in range(3)])  # [3][nt][rows]
+    assert np.abs(acc_ref).max() < 2**31
+    dev = torch.device("cuda")
+    codes_d = torch.from_numpy(codes).to(dev)
+    x_d = torch.from_numpy(x).to(dev)
+    acc_d = torch.full((3, nt, rows), -7, dtype=torch.int32, device=dev)
+    step_d = torch.zeros(nt, dtype=torch.float32, device=dev)
+    host.w8_digit_planes(codes_d.data_ptr(), rows, k, x_d.data_ptr(), nt, acc_d.data_ptr(), step_d.data_ptr(),
+                         torch.cuda.current_stream().cuda_stream)
+    torch.cuda.synchronize()
+    assert host.kernel_error(reset=True) == 0
+    np.testing.assert_array_equal(step_d.cpu().numpy().view(np.uint32), step_ref.view(np.uint32))
+    acc = acc_d.cpu().numpy().astype(np.int64)
+    bad = np.argwhere(acc != acc_ref)
+    assert bad.size == 0, f"{len(bad)} mismatches, first {bad[:4].tolist()}"

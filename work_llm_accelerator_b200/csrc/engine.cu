@@ -19,6 +19,7 @@
 #include "../../include/qwen_b200_engine.h"
 #include "decode_stack.h"
 #include "qgemm.h"
+#include "tgemm.h"
 #include "qwen_kernels.cuh"
 #include "runtime.h"
 
@@ -121,6 +122,8 @@ struct qwen_engine {
   float *p_x = nullptr, *p_xn = nullptr, *p_q = nullptr, *p_ctx = nullptr, *p_a = nullptr, *p_h = nullptr,
         *p_k = nullptr, *p_v = nullptr;
   int* p_tokens = nullptr;
+  int8_t* p_planes = nullptr;  // W8 prefill: digit planes [3][Spad][8960] and steps [Spad]
+  float* p_steps = nullptr;
   // options
   bool use_graphs = true, use_pdl = true, dump_hidden = false, keep_logits = false, prefetch = true;
   std::map<long long, cudaGraphExec_t> graphs;
@@ -238,6 +241,12 @@ int ensure_prefill_buffers(qwen_engine* e, int n) {
   E_TRY(dalloc(&e->p_v, (size_t)cap * kKvWidth));
   cudaFree(e->p_tokens);
   E_TRY(dalloc(&e->p_tokens, (size_t)cap));
+  if (e->wbits == 8) {
+    cudaFree(e->p_planes);
+    cudaFree(e->p_steps);
+    E_TRY(dalloc(&e->p_planes, tgemm_plane_bytes(cap, kInter)));
+    E_TRY(dalloc(&e->p_steps, (size_t)tgemm_pad(cap)));
+  }
   e->pre_cap = cap;
   return 0;
 }
@@ -487,6 +496,8 @@ void qwen_engine_destroy(qwen_engine* e) {
                   e->d_item_off, e->d_items};
   for (void* p : ptrs) cudaFree(p);
   cudaFree(e->trace);
+  cudaFree(e->p_planes);
+  cudaFree(e->p_steps);
   for (cudaEvent_t ev : e->kev)
     if (ev) cudaEventDestroy(ev);
   if (e->h_io) cudaFreeHost(e->h_io);
@@ -584,17 +595,37 @@ int qwen_engine_prefill(qwen_engine* e, int slot, const int32_t* tokens, int n, 
   E_TRY(cudaMemcpyAsync(e->p_tokens, tokens, (size_t)n * 4, cudaMemcpyHostToDevice, s));
   embed_gather_kernel<<<n, 256, 0, s>>>(e->embed, e->p_tokens, n, e->p_x);
   E_TRY(cudaGetLastError());
+  const bool tc = e->wbits == 8;
+  const DigitPlanes dp{e->p_planes, e->p_steps, n, tgemm_pad(n), kHidden};
+  const DigitPlanes dph{e->p_planes, e->p_steps, n, tgemm_pad(n), kInter};
   for (int l = 0; l < kLayers; ++l) {
     const LayerDev& L = e->layers[l];
     E_TRY(launch_prefill_rmsnorm(e->p_x, L.input_ln, n, e->p_xn, s));
-    E_TRY(launch_prefill_qkv(e->wbits, L, e->p_xn, n, e->rope_pre_cos, e->rope_pre_sin, e->p_q, e->p_k, e->p_v, s));
+    if (tc) {  // W8: projections on the int8 tensor cores
+      E_TRY(tgemm_digitize(e->p_xn, dp, s));
+      E_TRY(tgemm_qkv(L, dp, e->rope_pre_cos, e->rope_pre_sin, e->p_q, e->p_k, e->p_v, s));
+    } else {
+      E_TRY(launch_prefill_qkv(e->wbits, L, e->p_xn, n, e->rope_pre_cos, e->rope_pre_sin, e->p_q, e->p_k, e->p_v, s));
+    }
     E_TRY(launch_prefill_attention(e->p_q, e->p_k, e->p_v, n, e->p_ctx, s));
-    E_TRY(launch_prefill_o(e->wbits, L, e->p_ctx, n, e->p_a, s));
+    if (tc) {
+      E_TRY(tgemm_digitize(e->p_ctx, dp, s));
+      E_TRY(tgemm_o(L, dp, e->p_a, s));
+    } else {
+      E_TRY(launch_prefill_o(e->wbits, L, e->p_ctx, n, e->p_a, s));
+    }
     kv_scatter_kernel<<<n, 256, 0, s>>>(e->p_k, e->p_v, n, paged_view(e, l), slot, 1);
     E_TRY(cudaGetLastError());
     E_TRY(launch_prefill_rmsnorm(e->p_a, L.post_ln, n, e->p_xn, s));
-    E_TRY(launch_prefill_gateup(e->wbits, L, e->p_xn, n, e->p_h, s));
-    E_TRY(launch_prefill_down(e->wbits, L, e->p_h, e->p_a, n, e->p_x, true, s));
+    if (tc) {
+      E_TRY(tgemm_digitize(e->p_xn, dp, s));
+      E_TRY(tgemm_gateup(L, dp, e->p_h, s));
+      E_TRY(tgemm_digitize(e->p_h, dph, s));
+      E_TRY(tgemm_down(L, dph, e->p_a, e->p_x, true, s));
+    } else {
+      E_TRY(launch_prefill_gateup(e->wbits, L, e->p_xn, n, e->p_h, s));
+      E_TRY(launch_prefill_down(e->wbits, L, e->p_h, e->p_a, n, e->p_x, true, s));
+    }
     if (e->dump_hidden) {
       // prefill keeps each layer's output row of the last prompt token
       E_TRY(cudaMemcpyAsync(e->dump + (size_t)l * kHidden, e->p_x + (size_t)(n - 1) * kHidden, kHidden * 4,

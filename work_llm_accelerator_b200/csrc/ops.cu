@@ -5,6 +5,7 @@
 
 #include "../../include/qwen_b200_ops.h"
 #include "qgemm.h"
+#include "tgemm.h"
 #include "qwen_kernels.cuh"
 #include "runtime.h"
 
@@ -136,6 +137,39 @@ extern "C" int qwen_b200_w8_digit_products(const signed char* codes, int rows, i
   }
   if (e != cudaSuccess) {
     set_error("qwen_b200_w8_digit_products: %s", cudaGetErrorString(e));
+    return kStatusCuda;
+  }
+  return 0;
+}
+
+extern "C" int qwen_b200_w8_digit_planes(const signed char* codes, int rows, int k, const float* x, int n_tokens,
+                                         int* acc, float* step, void* stream) {
+  using namespace qb;
+  if (!codes || !x || !acc || !step || rows <= 0 || rows % 128 || k <= 0 || k % 128 || n_tokens < 1 ||
+      n_tokens > (1 << 16) || (reinterpret_cast<uintptr_t>(codes) & 15) || (reinterpret_cast<uintptr_t>(x) & 15)) {
+    set_error("qwen_b200_w8_digit_planes: rows %d / k %d must be positive multiples of 128, n_tokens %d in 1..65536, "
+              "codes and x 16-byte aligned",
+              rows, k, n_tokens);
+    return kStatusInvalid;
+  }
+  if (!device_accessible(codes) || !device_accessible(x) || !device_accessible(acc) || !device_accessible(step)) {
+    set_error("qwen_b200_w8_digit_planes: every buffer must be device (or managed) memory");
+    return kStatusInvalid;
+  }
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  int8_t* planes = nullptr;
+  float* steps = nullptr;
+  const int spad = tgemm_pad(n_tokens);
+  cudaError_t e = cudaMallocAsync(&planes, tgemm_plane_bytes(n_tokens, k), s);
+  if (e == cudaSuccess) e = cudaMallocAsync(&steps, (size_t)spad * 4, s);
+  const DigitPlanes dp{planes, steps, n_tokens, spad, k};
+  if (e == cudaSuccess) e = tgemm_digitize(x, dp, s);
+  if (e == cudaSuccess) e = tgemm_raw(reinterpret_cast<const uint8_t*>(codes), rows, dp, acc, s);
+  if (e == cudaSuccess) e = cudaMemcpyAsync(step, steps, (size_t)n_tokens * 4, cudaMemcpyDeviceToDevice, s);
+  if (planes) cudaFreeAsync(planes, s);
+  if (steps) cudaFreeAsync(steps, s);
+  if (e != cudaSuccess) {
+    set_error("qwen_b200_w8_digit_planes: %s", cudaGetErrorString(e));
     return kStatusCuda;
   }
   return 0;

@@ -20,6 +20,7 @@
 
 #include "decode_stack.h"
 #include "qgemm.h"
+#include "tgemm.h"
 #include "qwen_kernels.cuh"
 #include "runtime.h"
 
@@ -57,8 +58,9 @@ struct Ctx {
   std::vector<float> host_cos, host_sin;
   bool counters_zeroed = false;
   size_t counters_bytes = 0;
-  // int8 tensor-core projections (wbits 8): split-K scratch
+  // int8 tensor-core projections (wbits 8): split-K scratch (decode), digit planes and steps (prefill)
   QgemmScratch qsc{nullptr, nullptr};
+  Buf planes, psteps;
   // zero-weight layer for the stub entry points
   Buf zw, zs;
   LayerPtrs zero{};
@@ -329,6 +331,16 @@ int run_prefill(int wbits, const LayerPtrs& L, bool attention, bool mlp, const f
   QB_TRY(ensure(c.out, SH));
   QB_TRY(cudaMemcpyAsync(c.x.p, x, SH, cudaMemcpyDefault, c.stream));
   float* a_dev = (float*)c.x.p;
+  // W8: projections on the int8 tensor cores, inputs as digit planes
+  const bool tc = wbits == 8;
+  DigitPlanes dp{}, dph{};
+  if (tc) {
+    QB_TRY(ensure(c.planes, tgemm_plane_bytes(S, kInter)));
+    QB_TRY(ensure(c.psteps, (size_t)tgemm_pad(S) * 4));
+    dp = DigitPlanes{(int8_t*)c.planes.p, (float*)c.psteps.p, S, tgemm_pad(S), kHidden};
+    dph = dp;
+    dph.K = kInter;
+  }
   if (attention) {
     if (int st = ensure_prefill_rope(c, S)) return st;
     const size_t kvb = (size_t)S * kKvWidth * 4;
@@ -337,12 +349,23 @@ int run_prefill(int wbits, const LayerPtrs& L, bool attention, bool mlp, const f
     QB_TRY(ensure(c.ctx, SH));
     // xn reuses `out` as scratch
     QB_TRY(launch_prefill_rmsnorm((const float*)c.x.p, D.input_ln, S, (float*)c.out.p, c.stream));
-    QB_TRY(launch_prefill_qkv(wbits, D, (const float*)c.out.p, S, (const float*)c.rope_pre_cos.p,
-                              (const float*)c.rope_pre_sin.p, (float*)c.q.p, (float*)c.kc.p, (float*)c.vc.p,
-                              c.stream));
+    if (tc) {
+      QB_TRY(tgemm_digitize((const float*)c.out.p, dp, c.stream));
+      QB_TRY(tgemm_qkv(D, dp, (const float*)c.rope_pre_cos.p, (const float*)c.rope_pre_sin.p, (float*)c.q.p,
+                       (float*)c.kc.p, (float*)c.vc.p, c.stream));
+    } else {
+      QB_TRY(launch_prefill_qkv(wbits, D, (const float*)c.out.p, S, (const float*)c.rope_pre_cos.p,
+                                (const float*)c.rope_pre_sin.p, (float*)c.q.p, (float*)c.kc.p, (float*)c.vc.p,
+                                c.stream));
+    }
     QB_TRY(launch_prefill_attention((const float*)c.q.p, (const float*)c.kc.p, (const float*)c.vc.p, S,
                                     (float*)c.ctx.p, c.stream));
-    QB_TRY(launch_prefill_o(wbits, D, (const float*)c.ctx.p, S, (float*)c.a.p, c.stream));
+    if (tc) {
+      QB_TRY(tgemm_digitize((const float*)c.ctx.p, dp, c.stream));
+      QB_TRY(tgemm_o(D, dp, (float*)c.a.p, c.stream));
+    } else {
+      QB_TRY(launch_prefill_o(wbits, D, (const float*)c.ctx.p, S, (float*)c.a.p, c.stream));
+    }
     a_dev = (float*)c.a.p;
     QB_TRY(cudaMemcpyAsync(k_cache, c.kc.p, kvb, cudaMemcpyDefault, c.stream));
     QB_TRY(cudaMemcpyAsync(v_cache, c.vc.p, kvb, cudaMemcpyDefault, c.stream));
@@ -351,8 +374,15 @@ int run_prefill(int wbits, const LayerPtrs& L, bool attention, bool mlp, const f
   if (mlp) {
     QB_TRY(ensure(c.h, (size_t)S * kInter * 4));
     QB_TRY(launch_prefill_rmsnorm(a_dev, D.post_ln, S, (float*)c.q.p, c.stream));
-    QB_TRY(launch_prefill_gateup(wbits, D, (const float*)c.q.p, S, (float*)c.h.p, c.stream));
-    QB_TRY(launch_prefill_down(wbits, D, (const float*)c.h.p, a_dev, S, (float*)c.out.p, false, c.stream));
+    if (tc) {
+      QB_TRY(tgemm_digitize((const float*)c.q.p, dp, c.stream));
+      QB_TRY(tgemm_gateup(D, dp, (float*)c.h.p, c.stream));
+      QB_TRY(tgemm_digitize((const float*)c.h.p, dph, c.stream));
+      QB_TRY(tgemm_down(D, dph, a_dev, (float*)c.out.p, false, c.stream));
+    } else {
+      QB_TRY(launch_prefill_gateup(wbits, D, (const float*)c.q.p, S, (float*)c.h.p, c.stream));
+      QB_TRY(launch_prefill_down(wbits, D, (const float*)c.h.p, a_dev, S, (float*)c.out.p, false, c.stream));
+    }
     QB_TRY(cudaMemcpyAsync(out, c.out.p, SH, cudaMemcpyDefault, c.stream));
   }
   QB_TRY(cudaStreamSynchronize(c.stream));
@@ -399,7 +429,7 @@ int qwen_b200_set_prefill_seq_capacity(int capacity) {
 
 unsigned qwen_b200_kernel_error(int reset) {
   return qb::gemv_kernel_error(reset != 0) | qb::qgemm_kernel_error(reset != 0) |
-         qb::stack::decode_stack_kernel_error(reset != 0);
+         qb::stack::decode_stack_kernel_error(reset != 0) | qb::tgemm_kernel_error(reset != 0);
 }
 
 int qwen_b200_device_count(void) {

@@ -1,0 +1,464 @@
+// Many-token int8 tensor-core projections (prefill; the same kernel serves any token count).
+//
+// Y[t][o] = scale[o] * s_t * sum_k code(o, k) * X_t[k]: each token row of fp32 activations is written
+// exactly as s_t * (d0 + 256 d1 + 65536 d2) with three int8 digit planes (24-bit fixed point per token,
+// the representation the decode path's qgemm.cu uses), so the tensor cores compute three exact int32
+// products per output and the result differs from the reference's fp32 dot product
+// (hls/prefill_only/qwen_prefill_attention_kernel.cpp:163-202, qwen_prefill_mlp_kernel.cpp:217-254) only by
+// the 24-bit rounding of x (relative ~1e-7) and the fp32 summation order.
+//
+// One CTA computes a 128-row x 128-token tile. Per 128-byte K block the TMA producer stages the weight
+// tile (16 KB) and the three plane tiles (3 x 16 KB) into one of three 64 KB stages; one thread issues
+// 12 tcgen05.mma (M = 128, N = 128, K = 32 bytes; accumulator plane p in TMEM columns 128 p ..); four
+// warps read the accumulators back 16 tokens at a time, combine the planes exactly in int64 and run the
+// epilogue of the projection (the same operations as the CUDA-core prefill kernels in prefill_simt.cu).
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include <mutex>
+
+#include "tgemm.h"
+#include "umma_sm100.cuh"
+
+namespace qb {
+namespace {
+
+using namespace umma;
+
+constexpr int kTN = 128;       // tokens per tile
+constexpr int kPlanes = 3;
+constexpr int kStagesT = 3;
+constexpr int kThreadsT = 192;
+constexpr int kEpiT = 128;
+constexpr int kBarT = 1;       // named barrier of the epilogue warps
+constexpr int kTmemColsT = 512;
+constexpr int kPlaneTile = kTN * kKBlock;                     // 16 KB
+constexpr int kStageBytes = kUnitBytes + kPlanes * kPlaneTile;  // 64 KB
+constexpr int kChunkN = 16;    // tokens per TMEM read
+constexpr uint32_t kIdescT = idesc_i8(kTileM, kTN);
+static_assert(kPlanes * kTN <= kTmemColsT, "accumulators fit in TMEM");
+
+struct TSmem {
+  uint64_t full[kStagesT], empty[kStagesT], acc_full;
+  uint32_t tmem_base;
+  float steps[kTN];
+  float ys[kTileM][kChunkN + 1];  // partner exchange (RoPE pairs, gate|up pairs)
+};
+
+enum TEpi { kTQkv = 0, kTScale = 1, kTGateUp = 2, kTDown = 3, kTRaw = 4 };
+
+struct TArgs {
+  int nkb;           // 128-byte K blocks
+  int box_rows;      // weight rows per TMA box: 128, or 64 twice (gate|up)
+  int second_row0;   // gate|up: first row of the up half
+  int S, Spad, rows;
+  const float* steps;
+  const float* scale;
+  const float* bias;
+  const float* cosv;
+  const float* sinv;
+  float* out;
+  float* k_cache;
+  float* v_cache;
+  const float* resid;
+  bool round_out;
+  int* raw;
+};
+
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int c0, int c1, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], "
+      "[%4];" ::"r"(smem_u32(dst)),
+      "l"(map), "r"(c0), "r"(c1), "r"(smem_u32(bar))
+      : "memory");
+}
+
+__device__ __forceinline__ void mma_t(uint32_t d, uint64_t a, uint64_t b, uint32_t acc) {
+  asm volatile(
+      "{\n.reg .pred p;\nsetp.ne.b32 p, %4, 0;\ntcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n}" ::"r"(d),
+      "l"(a), "l"(b), "r"(kIdescT), "r"(acc)
+      : "memory");
+}
+
+template <int EPI>
+__global__ void __launch_bounds__(kThreadsT, 1)
+    tgemm_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ CUtensorMap pmap, TArgs a) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* stages = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  TSmem& sm = *reinterpret_cast<TSmem*>(stages + (size_t)kStagesT * kStageBytes);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int mtile = blockIdx.x, n0 = blockIdx.y * kTN;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStagesT; ++s) {
+      mbar_init(&sm.full[s], 1);
+      mbar_init(&sm.empty[s], 1);
+    }
+    mbar_init(&sm.acc_full, 1);
+    mbar_fence_init();
+  }
+  if (warp == 1) tmem_alloc(&sm.tmem_base, kTmemColsT);
+  for (int i = threadIdx.x; i < kTN; i += blockDim.x) sm.steps[i] = a.steps[n0 + i];
+  fence_before();
+  __syncthreads();
+  fence_after();
+  const uint32_t tmem = sm.tmem_base;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      asm volatile("prefetch.tensormap [%0];" ::"l"(&wmap) : "memory");
+      asm volatile("prefetch.tensormap [%0];" ::"l"(&pmap) : "memory");
+      const int row0 = a.box_rows == kTileM ? mtile * kTileM : mtile * a.box_rows;
+      int s = 0;
+      unsigned ph = 0;
+      bool ok = true;
+      for (int kb = 0; kb < a.nkb && ok; ++kb) {
+        if (!(ok = mbar_wait(&sm.empty[s], ph ^ 1))) break;
+        mbar_arrive_expect_tx(&sm.full[s], kStageBytes);
+        uint8_t* st = stages + (size_t)s * kStageBytes;
+        tma_load_2d(st, &wmap, kb * kKBlock, row0, &sm.full[s]);
+        if (a.box_rows != kTileM)
+          tma_load_2d(st + a.box_rows * kKBlock, &wmap, kb * kKBlock, row0 + a.second_row0, &sm.full[s]);
+#pragma unroll
+        for (int p = 0; p < kPlanes; ++p)
+          tma_load_2d(st + kUnitBytes + p * kPlaneTile, &pmap, kb * kKBlock, p * a.Spad + n0, &sm.full[s]);
+        if (++s == kStagesT) {
+          s = 0;
+          ph ^= 1;
+        }
+      }
+      // every issued stage consumed before leaving (no copy in flight at exit)
+      for (int i = 0; i < kStagesT && ok; ++i) {
+        ok = mbar_wait(&sm.empty[s], ph ^ 1);
+        if (++s == kStagesT) {
+          s = 0;
+          ph ^= 1;
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      int s = 0;
+      unsigned ph = 0;
+      bool ok = true;
+      for (int kb = 0; kb < a.nkb; ++kb) {
+        ok = ok && mbar_wait(&sm.full[s], ph);
+        fence_after();
+        if (ok) {
+          const uint32_t sb = smem_u32(stages + (size_t)s * kStageBytes);
+          const uint64_t ad = sw128_desc(sb);
+#pragma unroll
+          for (int p = 0; p < kPlanes; ++p) {
+            const uint64_t bd = sw128_desc(sb + kUnitBytes + p * kPlaneTile);
+#pragma unroll
+            for (int j = 0; j < kKBlock / 32; ++j)
+              mma_t(tmem + p * kTN, ad + 2 * j, bd + 2 * j, (kb > 0 || j > 0) ? 1u : 0u);
+          }
+        }
+        mma_commit(&sm.empty[s]);
+        if (++s == kStagesT) {
+          s = 0;
+          ph ^= 1;
+        }
+      }
+      mma_commit(&sm.acc_full);
+    }
+  } else {
+    // ---- epilogue: thread = one tile row (TMEM lane), 16 tokens per read
+    const int q = warp & 3, r = q * 32 + lane;
+    const bool ok = mbar_wait(&sm.acc_full, 0);
+    fence_after();
+    int row;
+    float sc = 0.f, bb = 0.f;
+    if constexpr (EPI == kTGateUp) {
+      row = r < 64 ? mtile * 64 + r : a.second_row0 + mtile * 64 + (r - 64);
+    } else {
+      row = mtile * kTileM + r;
+    }
+    if constexpr (EPI != kTRaw) sc = __ldg(a.scale + row);
+    if constexpr (EPI == kTQkv) bb = __ldg(a.bias + row);
+    const uint32_t lane_base = tmem + ((uint32_t)(q * 32) << 16);
+    for (int c0 = 0; c0 < kTN; c0 += kChunkN) {
+      int v0[16], v1[16], v2[16];
+      if (ok) {
+        tmem_ld16(lane_base + c0, v0);
+        tmem_ld16(lane_base + kTN + c0, v1);
+        tmem_ld16(lane_base + 2 * kTN + c0, v2);
+      } else {
+#pragma unroll
+        for (int c = 0; c < 16; ++c) v0[c] = v1[c] = v2[c] = 0;
+      }
+      if constexpr (EPI == kTRaw) {
+#pragma unroll
+        for (int c = 0; c < kChunkN; ++c) {
+          const int n = n0 + c0 + c;
+          if (n < a.S) {
+            a.raw[((size_t)0 * a.S + n) * a.rows + row] = v0[c];
+            a.raw[((size_t)1 * a.S + n) * a.rows + row] = v1[c];
+            a.raw[((size_t)2 * a.S + n) * a.rows + row] = v2[c];
+          }
+        }
+        continue;
+      } else {
+        float yv[kChunkN];
+#pragma unroll
+        for (int c = 0; c < kChunkN; ++c) {
+          const long long tot = (long long)v0[c] + 256ll * (long long)v1[c] + 65536ll * (long long)v2[c];
+          yv[c] = (float)((double)tot * (double)sm.steps[c0 + c]);
+        }
+        // every global load of the chunk is issued before any result is used (one round trip per chunk)
+        if constexpr (EPI == kTScale || EPI == kTDown) {
+          float res[kChunkN];
+#pragma unroll
+          for (int c = 0; c < kChunkN; ++c) {
+            const int n = n0 + c0 + c;
+            res[c] = (EPI == kTDown && n < a.S) ? __ldg(a.resid + (size_t)n * kHidden + row) : 0.f;
+          }
+#pragma unroll
+          for (int c = 0; c < kChunkN; ++c) {
+            const int n = n0 + c0 + c;
+            float y = sc * yv[c];
+            if constexpr (EPI == kTDown) {
+              y = __fadd_rn(res[c], y);
+              if (a.round_out) y = round_bf16(y);
+            }
+            if (n < a.S) a.out[(size_t)n * kHidden + row] = y;
+          }
+        } else if constexpr (EPI == kTQkv) {
+          // tile = head: rows r and r ^ 64 are RoPE partners (q and k heads); token index = position
+          const int h = mtile, p = r & 63;
+          const bool rope = h < kHeads + kKvHeads;
+          float cs[kChunkN], sn[kChunkN];
+#pragma unroll
+          for (int c = 0; c < kChunkN; ++c) {
+            const int n = min(n0 + c0 + c, a.S - 1);
+            cs[c] = rope ? __ldg(a.cosv + (size_t)n * 64 + p) : 1.f;
+            sn[c] = rope ? __ldg(a.sinv + (size_t)n * 64 + p) : 0.f;
+          }
+#pragma unroll
+          for (int c = 0; c < kChunkN; ++c) sm.ys[r][c] = __fmaf_rn(sc, yv[c], bb);
+          named_sync(kBarT, kEpiT);
+          float* dst;
+          size_t stride;
+          if (h < kHeads) {
+            dst = a.out + row;
+            stride = kHidden;
+          } else if (h < kHeads + kKvHeads) {
+            dst = a.k_cache + (row - kHidden);
+            stride = kKvWidth;
+          } else {
+            dst = a.v_cache + (row - kHidden - kKvWidth);
+            stride = kKvWidth;
+          }
+#pragma unroll
+          for (int c = 0; c < kChunkN; ++c) {
+            const int n = n0 + c0 + c;
+            const float mine = sm.ys[r][c], other = sm.ys[r ^ 64][c];
+            float y = mine;
+            if (rope)
+              y = r < 64 ? __fsub_rn(__fmul_rn(mine, cs[c]), __fmul_rn(other, sn[c]))
+                         : __fadd_rn(__fmul_rn(mine, cs[c]), __fmul_rn(other, sn[c]));
+            if (n < a.S) dst[(size_t)n * stride] = y;
+          }
+          named_sync(kBarT, kEpiT);
+        } else {  // gate|up: tile rows 0..63 gate rows 64 j.., 64..127 the matching up rows
+#pragma unroll
+          for (int c = 0; c < kChunkN; ++c) sm.ys[r][c] = sc * yv[c];
+          named_sync(kBarT, kEpiT);
+          // all 128 threads: gate row (r & 63), tokens (r >> 6) * 8 .. +8 of the chunk
+          const int gr = r & 63, cb = (r >> 6) * (kChunkN / 2);
+#pragma unroll
+          for (int c = cb; c < cb + kChunkN / 2; ++c) {
+            const int n = n0 + c0 + c;
+            const float gv = sm.ys[gr][c], uv = sm.ys[gr + 64][c];
+            const float silu = __fdiv_rn(gv, __fadd_rn(1.0f, approx_exp(-gv)));
+            if (n < a.S) a.out[(size_t)n * kInter + mtile * 64 + gr] = __fmul_rn(silu, uv);
+          }
+          named_sync(kBarT, kEpiT);
+        }
+      }
+    }
+  }
+  fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    fence_after();
+    tmem_dealloc(tmem, kTmemColsT);
+  }
+}
+
+// One CTA per token row: per-token step and the three digit planes; padded rows become zero.
+__global__ void __launch_bounds__(256) digitize_kernel(const float* __restrict__ x, int S, int K, int Spad,
+                                                       int8_t* __restrict__ planes, float* __restrict__ steps) {
+  const int t = blockIdx.x;
+  __shared__ float red[8];
+  int8_t* p0 = planes + (size_t)t * K;
+  int8_t* p1 = planes + ((size_t)Spad + t) * K;
+  int8_t* p2 = planes + ((size_t)2 * Spad + t) * K;
+  if (t >= S) {
+    for (int k = threadIdx.x * 4; k < K; k += 1024) {
+      *reinterpret_cast<uint32_t*>(p0 + k) = 0u;
+      *reinterpret_cast<uint32_t*>(p1 + k) = 0u;
+      *reinterpret_cast<uint32_t*>(p2 + k) = 0u;
+    }
+    if (threadIdx.x == 0) steps[t] = 1.0f;
+    return;
+  }
+  const float* row = x + (size_t)t * K;
+  float m = 0.f;
+  for (int k = threadIdx.x * 4; k < K; k += 1024) {
+    const float4 v = *reinterpret_cast<const float4*>(row + k);
+    m = fmaxf(m, fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = m;
+  __syncthreads();
+  float mx = 0.f;
+  for (int i = 0; i < 8; ++i) mx = fmaxf(mx, red[i]);
+  const float st = mx > 0.0f ? mx / kDigitRange : 1.0f;
+  if (threadIdx.x == 0) steps[t] = st;
+  for (int k = threadIdx.x * 4; k < K; k += 1024) {
+    const float4 v = *reinterpret_cast<const float4*>(row + k);
+    const float vv[4] = {v.x, v.y, v.z, v.w};
+    uint32_t w0 = 0, w1 = 0, w2 = 0;
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      int d0, d1, d2;
+      split_digits((int)rintf(__fdiv_rn(vv[e], st)), d0, d1, d2);
+      w0 |= (uint32_t)(d0 & 255) << (8 * e);
+      w1 |= (uint32_t)(d1 & 255) << (8 * e);
+      w2 |= (uint32_t)(d2 & 255) << (8 * e);
+    }
+    *reinterpret_cast<uint32_t*>(p0 + k) = w0;
+    *reinterpret_cast<uint32_t*>(p1 + k) = w1;
+    *reinterpret_cast<uint32_t*>(p2 + k) = w2;
+  }
+}
+
+// ---------------------------------------------------------------------------------------------------
+// host side
+// ---------------------------------------------------------------------------------------------------
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
+}
+
+// 2D int8 map over [rows][k_bytes], box 128 bytes x box_rows, 128-byte swizzle
+bool make_map(CUtensorMap* m, const void* base, uint64_t rows, uint64_t k_bytes, uint32_t box_rows) {
+  auto fn = encode_fn();
+  if (!fn) return false;
+  cuuint64_t dims[2] = {(cuuint64_t)k_bytes, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)k_bytes};
+  cuuint32_t box[2] = {(cuuint32_t)kKBlock, box_rows};
+  cuuint32_t es[2] = {1, 1};
+  return fn(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box, es,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+template <int EPI>
+cudaError_t run_tgemm(const uint8_t* w, int rows_total, int K, int mtiles, int box_rows, int second_row0,
+                      const DigitPlanes& x, TArgs a, cudaStream_t s) {
+  if (x.K != K || K % kKBlock || x.Spad % kTN || x.S < 1 || x.S > x.Spad) return cudaErrorInvalidValue;
+  CUtensorMap wmap, pmap;
+  if (!make_map(&wmap, w, (uint64_t)rows_total, (uint64_t)K, (uint32_t)box_rows) ||
+      !make_map(&pmap, x.planes, (uint64_t)kPlanes * x.Spad, (uint64_t)K, kTN))
+    return cudaErrorInvalidValue;
+  a.nkb = K / kKBlock;
+  a.box_rows = box_rows;
+  a.second_row0 = second_row0;
+  a.S = x.S;
+  a.Spad = x.Spad;
+  a.steps = x.steps;
+  auto kern = tgemm_kernel<EPI>;
+  const size_t smem = 1024 + (size_t)kStagesT * kStageBytes + sizeof(TSmem);
+  static std::mutex mu;
+  static unsigned long long attr_set = 0;
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  {
+    std::lock_guard<std::mutex> lock(mu);
+    if (dev < 64 && !((attr_set >> dev) & 1ull)) {
+      if ((e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem)) != cudaSuccess)
+        return e;
+      attr_set |= 1ull << dev;
+    }
+  }
+  kern<<<dim3(mtiles, x.Spad / kTN), kThreadsT, smem, s>>>(wmap, pmap, a);
+  return cudaGetLastError();
+}
+
+}  // namespace
+
+cudaError_t tgemm_digitize(const float* x, DigitPlanes d, cudaStream_t s) {
+  if (d.K % 4 || d.Spad % kTN || d.S < 1 || d.S > d.Spad) return cudaErrorInvalidValue;
+  digitize_kernel<<<d.Spad, 256, 0, s>>>(x, d.S, d.K, d.Spad, d.planes, d.steps);
+  return cudaGetLastError();
+}
+
+cudaError_t tgemm_qkv(const LayerDev& L, const DigitPlanes& x, const float* rope_cos, const float* rope_sin, float* q_out,
+                      float* k_cache, float* v_cache, cudaStream_t s) {
+  TArgs a{};
+  a.scale = L.qkv_s;
+  a.bias = L.qkv_b;
+  a.cosv = rope_cos;
+  a.sinv = rope_sin;
+  a.out = q_out;
+  a.k_cache = k_cache;
+  a.v_cache = v_cache;
+  return run_tgemm<kTQkv>(L.qkv_w, kQkvRows, kHidden, kQkvRows / kTileM, kTileM, 0, x, a, s);
+}
+
+cudaError_t tgemm_o(const LayerDev& L, const DigitPlanes& x, float* out, cudaStream_t s) {
+  TArgs a{};
+  a.scale = L.o_s;
+  a.out = out;
+  return run_tgemm<kTScale>(L.o_w, kHidden, kHidden, kHidden / kTileM, kTileM, 0, x, a, s);
+}
+
+cudaError_t tgemm_gateup(const LayerDev& L, const DigitPlanes& x, float* h, cudaStream_t s) {
+  TArgs a{};
+  a.scale = L.gu_s;
+  a.out = h;
+  return run_tgemm<kTGateUp>(L.gu_w, 2 * kInter, kHidden, kInter / 64, 64, kInter, x, a, s);
+}
+
+cudaError_t tgemm_down(const LayerDev& L, const DigitPlanes& x, const float* resid, float* out, bool round_out,
+                       cudaStream_t s) {
+  TArgs a{};
+  a.scale = L.down_s;
+  a.resid = resid;
+  a.out = out;
+  a.round_out = round_out;
+  return run_tgemm<kTDown>(L.down_w, kHidden, kInter, kHidden / kTileM, kTileM, 0, x, a, s);
+}
+
+cudaError_t tgemm_raw(const uint8_t* codes, int rows, const DigitPlanes& x, int* acc, cudaStream_t s) {
+  if (rows % kTileM) return cudaErrorInvalidValue;
+  TArgs a{};
+  a.raw = acc;
+  a.rows = rows;
+  return run_tgemm<kTRaw>(codes, rows, x.K, rows / kTileM, kTileM, 0, x, a, s);
+}
+
+unsigned tgemm_kernel_error(bool reset) {
+  unsigned v = 0;
+  if (cudaMemcpyFromSymbol(&v, g_kernel_error, sizeof(v)) != cudaSuccess) return 0xFFFFFFFFu;
+  if (reset && v) {
+    const unsigned z = 0;
+    cudaMemcpyToSymbol(g_kernel_error, &z, sizeof(z));
+  }
+  return v;
+}
+
+}  // namespace qb

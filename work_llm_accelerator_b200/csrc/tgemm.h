@@ -1,0 +1,41 @@
+// Many-token int8 tensor-core projections (tgemm.cu): prefill and batched decode.
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include <cstdint>
+
+#include "qwen_kernels.cuh"
+
+namespace qb {
+
+// Digit planes of S token rows of width K: planes [3][Spad][K] int8 (Spad = S rounded up to 128, padded
+// rows zero) and the per-token steps [Spad]. Row t: x = step[t] * (d0 + 256 d1 + 65536 d2).
+struct DigitPlanes {
+  int8_t* planes;
+  float* steps;
+  int S, Spad, K;
+};
+
+inline int tgemm_pad(int S) { return (S + 127) / 128 * 128; }
+inline size_t tgemm_plane_bytes(int S, int K) { return (size_t)3 * tgemm_pad(S) * K; }
+
+// x [S][K] fp32 -> digit planes (one CTA per token row).
+cudaError_t tgemm_digitize(const float* x, DigitPlanes d, cudaStream_t s);
+
+// Projections of all S tokens with the prefill epilogues (the same operations as the CUDA-core prefill
+// GEMMs in prefill_simt.cu): q|k|v + RoPE (table rows = token index) + K/V rows of a flat cache; o_proj;
+// gate|up + SiLU(approx_exp) * up; down + residual (optional bf16 rounding).
+cudaError_t tgemm_qkv(const LayerDev& L, const DigitPlanes& x, const float* rope_cos, const float* rope_sin, float* q_out,
+                      float* k_cache, float* v_cache, cudaStream_t s);
+cudaError_t tgemm_o(const LayerDev& L, const DigitPlanes& x, float* out, cudaStream_t s);
+cudaError_t tgemm_gateup(const LayerDev& L, const DigitPlanes& x, float* h, cudaStream_t s);
+cudaError_t tgemm_down(const LayerDev& L, const DigitPlanes& x, const float* resid, float* out, bool round_out,
+                       cudaStream_t s);
+
+// Raw integer products for tests: acc [3][S][rows] int32 = sum_k code(row, k) * digit_p(t, k).
+cudaError_t tgemm_raw(const uint8_t* codes, int rows, const DigitPlanes& x, int* acc, cudaStream_t s);
+
+unsigned tgemm_kernel_error(bool reset);
+
+}  // namespace qb

@@ -69,6 +69,9 @@ def core_lib() -> ctypes.CDLL:
         lib.qwen_b200_w8_digit_products.argtypes = [ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_void_p,
                                                     ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p]
         lib.qwen_b200_w8_digit_products.restype = ctypes.c_int
+        lib.qwen_b200_w8_digit_planes.argtypes = [ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_void_p,
+                                                  ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p]
+        lib.qwen_b200_w8_digit_planes.restype = ctypes.c_int
         lib.qwen_b200_kernel_error.argtypes = [ctypes.c_int]
         lib.qwen_b200_kernel_error.restype = ctypes.c_uint
         _core = lib
@@ -384,3 +387,11 @@ def w8_digit_products(codes_ptr: int, rows: int, k: int, x_ptr: int, n_tokens: i
 def kernel_error(reset: bool = False) -> int:
     """Error flag of the streaming kernels on the current device (1 = a bounded pipeline wait gave up)."""
     return int(core_lib().qwen_b200_kernel_error(1 if reset else 0))
+
+
+def w8_digit_planes(codes_ptr: int, rows: int, k: int, x_ptr: int, n_tokens: int, acc_ptr: int, step_ptr: int,
+                    stream: int = 0) -> None:
+    """Many-token integer core (include/qwen_b200_ops.h): acc[d][t][r] = sum_i codes[r][i] * digit_d(x[t])[i]."""
+    st = core_lib().qwen_b200_w8_digit_planes(codes_ptr, rows, k, x_ptr, n_tokens, acc_ptr, step_ptr, stream or None)
+    if st != 0:
+        raise EngineError(f"qwen_b200_w8_digit_planes failed with status {st}: {last_error()}")

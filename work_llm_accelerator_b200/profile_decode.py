@@ -6,6 +6,9 @@
     python -m work_llm_accelerator_b200.profile_decode steps --wbits 8 --prompt 512 --steps 3
         prefills one sequence and runs full 28-layer decode steps (CUDA graphs by default): the launch
         list of a whole step.
+    python -m work_llm_accelerator_b200.profile_decode prefill --wbits 8 --prompt 4096 --steps 2
+        times full 28-layer prefills of one sequence (CUDA events on the engine stream) and prints
+        tokens/s.
 
 Both hold about 2.2 GB (W8) of weights on the device plus a 1024-position KV pool.
 """
@@ -21,7 +24,7 @@ from . import host
 
 def main(argv=None) -> int:
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
-    ap.add_argument("mode", choices=["kernels", "steps"])
+    ap.add_argument("mode", choices=["kernels", "steps", "prefill"])
     ap.add_argument("--wbits", type=int, default=8, choices=[4, 8])
     ap.add_argument("--seed", type=int, default=7)
     ap.add_argument("--iters", type=int, default=2, help="kernels: launches of each kernel")
@@ -33,13 +36,30 @@ def main(argv=None) -> int:
                     help="engine option (e.g. qgemm=0, prefetch=0, pdl=0)")
     a = ap.parse_args(argv)
 
-    eng = host.Engine(0, a.wbits, max_seqs=1, max_len=1024)
+    eng = host.Engine(0, a.wbits, max_seqs=1, max_len=max(1024, a.prompt + 8))
     try:
         eng.init_synthetic(a.seed)
         for opt in a.option:
             name, value = opt.split("=", 1)
             eng.set_option(name, int(value))
-        if a.mode == "kernels":
+        if a.mode == "prefill":
+            import torch
+
+            prompt = np.random.default_rng(1).integers(0, 151936, a.prompt).astype(np.int32)
+            stream = torch.cuda.ExternalStream(eng.stream())
+            eng.prefill(0, prompt)  # warm-up (allocations, first launches)
+            times = []
+            for _ in range(a.steps):
+                eng.reset(0)
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record(stream)
+                eng.prefill(0, prompt)
+                e1.record(stream)
+                e1.synchronize()
+                times.append(e0.elapsed_time(e1))
+            ms = min(times)
+            print(json.dumps({"prompt": a.prompt, "ms": ms, "tok_per_s": a.prompt / (ms * 1e-3)}))
+        elif a.mode == "kernels":
             us = eng.profile_kernels(1, a.past, iters=a.iters)
             print(json.dumps({k: round(v * 1000.0, 3) for k, v in us.items()}))
         else:
