@@ -230,3 +230,66 @@ def test_persistent_step_kernel_matches_separate_kernels(host, prompt_len):
     assert toks_s == toks_k
     for step, (a, b) in enumerate(zip(hid_s, hid_k)):
         assert np.array_equal(a, b), (step, rel_l2(a, b))
+
+
+@pytest.mark.parametrize("n", [5, 12])
+def test_batched_w8_decode_matches_single(host, n):
+    """More than four sequences per step take the batched path (every projection of all tokens in one
+    many-token tensor-core GEMM, paged attention over all tokens); it performs the same per-token
+    arithmetic as the persistent single-sequence kernel, so tokens and every layer's output are identical."""
+    rng = np.random.default_rng(100 + n)
+    prompts = [[int(t) for t in rng.integers(0, qo.VOCAB, int(rng.integers(3, 90)))] for _ in range(n)]
+    steps = 3
+    eng = host.Engine(0, 8, max_seqs=n, max_len=256)
+    try:
+        eng.init_synthetic(17)
+        eng.set_option("dump_hidden", 1)
+        single_tok, single_hid = [], []
+        for i, p in enumerate(prompts):
+            toks, hids = [eng.prefill(i, p)], []
+            for _ in range(steps):
+                toks.append(int(eng.decode([i], [toks[-1]])[0]))
+                hids.append(eng.read_hidden(1)[:, 0].copy())
+            single_tok.append(toks)
+            single_hid.append(hids)
+            eng.reset(i)
+        cur = [eng.prefill(i, p) for i, p in enumerate(prompts)]
+        batched = [[c] for c in cur]
+        for step in range(steps):
+            cur = [int(t) for t in eng.decode(list(range(n)), cur)]
+            hid = eng.read_hidden(n)
+            for i, t in enumerate(cur):
+                batched[i].append(t)
+                assert np.array_equal(hid[:, i], single_hid[i][step]), (i, step, rel_l2(hid[:, i], single_hid[i][step]))
+        assert batched == single_tok
+        assert host.kernel_error(reset=True) == 0
+    finally:
+        eng.close()
+
+
+def test_tensor_core_lm_head_matches_cuda_core_head(host):
+    """The tensor-core LM head (fp16 table x two fp16 planes of the normalised activations, 22 significant
+    bits; tensor-core fp32 accumulation) and the CUDA-core GEMV head give the same greedy tokens and logits
+    within 1e-5 relative L2, the tolerance the LM head has against the oracle (1 and 9 rows)."""
+    rng = np.random.default_rng(3)
+    prompts = [[int(t) for t in rng.integers(0, qo.VOCAB, 6)] for _ in range(9)]
+    eng = host.Engine(0, 8, max_seqs=9, max_len=64)
+    try:
+        eng.init_synthetic(23)
+        eng.set_option("logits", 1)
+        out = {}
+        for lm_tc in (1, 0):
+            eng.set_option("lm_tc", lm_tc)
+            toks = [eng.prefill(i, p) for i, p in enumerate(prompts)]
+            l1 = eng.read_logits(1).copy()
+            nxt = [int(t) for t in eng.decode(list(range(9)), toks)]
+            l9 = eng.read_logits(9).copy()
+            out[lm_tc] = (toks, nxt, l1, l9)
+            for i in range(9):
+                eng.reset(i)
+        assert out[1][0] == out[0][0] and out[1][1] == out[0][1]
+        assert rel_l2(out[1][2], out[0][2]) <= 1e-5
+        assert rel_l2(out[1][3], out[0][3]) <= 1e-5
+        assert host.kernel_error(reset=True) == 0
+    finally:
+        eng.close()

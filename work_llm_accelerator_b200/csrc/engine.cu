@@ -19,6 +19,7 @@
 #include "../../include/qwen_b200_engine.h"
 #include "decode_stack.h"
 #include "qgemm.h"
+#include "lmhead.h"
 #include "tgemm.h"
 #include "qwen_kernels.cuh"
 #include "runtime.h"
@@ -60,7 +61,7 @@ __global__ void advance_pos_kernel(int* __restrict__ pos, int n) {
 // end of a device-resident decode step: next input token = argmax, position + 1
 __global__ void advance_kernel(int* __restrict__ tokens, const int* __restrict__ next, int* __restrict__ pos, int n) {
   griddep_wait();
-  const int t = threadIdx.x;
+  const int t = blockIdx.x * blockDim.x + threadIdx.x;
   if (t < n) {
     tokens[t] = next[t];
     pos[t] += 1;
@@ -106,6 +107,9 @@ struct qwen_engine {
   // decode state (up to kGemvMaxTokens tokens per group)
   int *d_tokens = nullptr, *d_pos = nullptr, *d_seq = nullptr, *d_next = nullptr;
   int* h_io = nullptr;  // pinned: [4 tokens][4 pos][4 seq][4 next]
+  int* hb_io = nullptr;  // pinned, batched path: [tokens][pos][seq][next], batch_cap each
+  int batch_cap = 4;
+  bool use_batched = true;
   float *x = nullptr, *q = nullptr, *ctx = nullptr, *a = nullptr, *h = nullptr, *y0 = nullptr, *y1 = nullptr;
   float* attn_part = nullptr;
   unsigned* attn_cnt = nullptr;
@@ -148,6 +152,9 @@ struct qwen_engine {
   int stack_ring = 9;                   // weight stages in flight per CTA
   cudaEvent_t kev[3] = {nullptr, nullptr, nullptr};  // per-kernel timing (profile_decode)
   bool time_kernels = false;
+  // tensor-core LM head
+  bool use_lm_tc = true;
+  LmScratch lm{nullptr, nullptr, nullptr};
 };
 
 namespace {
@@ -268,6 +275,21 @@ int ensure_tiles(qwen_engine* e) {
 
 bool stack_enabled(const qwen_engine* e) { return e->wbits == 8 && e->use_stack && e->wtiles != nullptr; }
 
+// Final norm + LM head + argmax of n rows of x into d_next (logits kept when requested).
+int enqueue_lm_head(qwen_engine* e, const float* x, int n, int* next, float* logits, bool pdl) {
+  if (e->use_lm_tc && e->lm.planes != nullptr) {
+    E_TRY(lm_head_tc(e->embed, e->final_norm, x, n, logits, next, e->lm, e->stream));
+    return 0;
+  }
+  for (int g = 0; g < n; g += kGemvMaxTokens) {
+    const int m = std::min(kGemvMaxTokens, n - g);
+    E_TRY(launch_lm_head_argmax(e->embed, e->final_norm, x + (size_t)g * kHidden, m,
+                                logits ? logits + (size_t)g * kVocab : nullptr, e->lm_part, e->lm_cnt, next + g,
+                                e->stream, pdl && g == 0));
+  }
+  return 0;
+}
+
 // Enqueue one decode step for nt tokens whose ids/positions/slots are already in d_tokens/d_pos/d_seq.
 // max_len bounds the attention grid (positions + 1 of every token must be <= max_len).
 int enqueue_decode(qwen_engine* e, int nt, int max_len, bool advance) {
@@ -352,13 +374,54 @@ int enqueue_decode(qwen_engine* e, int nt, int max_len, bool advance) {
     xin = yout;
   }
   if (e->time_kernels) E_TRY(cudaEventRecord(e->kev[1], e->stream));
-  E_TRY(launch_lm_head_argmax(e->embed, e->final_norm, xin, nt, e->keep_logits ? e->logits : nullptr, e->lm_part,
-                              e->lm_cnt, e->d_next, e->stream,
-                              pdl && !e->dump_hidden && !stack_enabled(e) && !e->time_kernels));
+  if (int st = enqueue_lm_head(e, xin, nt, e->d_next, e->keep_logits ? e->logits : nullptr,
+                               pdl && !e->dump_hidden && !stack_enabled(e) && !e->time_kernels))
+    return st;
   if (e->time_kernels) E_TRY(cudaEventRecord(e->kev[2], e->stream));
   if (advance) {
     E_TRY(launch_k(advance_kernel, dim3(1), dim3(32), 0, e->stream, pdl, e->d_tokens, (const int*)e->d_next,
                    e->d_pos, nt));
+  }
+  return 0;
+}
+
+bool batched_ok(const qwen_engine* e, int n) {
+  return e->wbits == 8 && e->use_batched && n > kGemvMaxTokens && n <= e->batch_cap;
+}
+
+// One greedy decode step of n > 4 tokens (W8): every projection of all tokens in one many-token tensor-core
+// GEMM per layer (weights read once per step), paged-KV attention over all tokens, LM head in groups of 4.
+// Tokens / positions / slots are in d_tokens / d_pos / d_seq. Eager launches (no graph).
+int enqueue_decode_batched(qwen_engine* e, int n, int max_len, bool advance) {
+  cudaStream_t s = e->stream;
+  if (int st = ensure_tiles(e)) return st;
+  embed_gather_kernel<<<n, 256, 0, s>>>(e->embed, e->d_tokens, n, e->p_x);
+  E_TRY(cudaGetLastError());
+  const DigitPlanes dp{e->p_planes, e->p_steps, n, tgemm_pad(n), kHidden};
+  const DigitPlanes dph{e->p_planes, e->p_steps, n, tgemm_pad(n), kInter};
+  const DecodeTokens tok{e->d_pos, e->d_seq, n};
+  for (int l = 0; l < kLayers; ++l) {
+    const LayerDev& L = e->layers[l];
+    const KvView kv = paged_view(e, l);
+    E_TRY(decode_rmsnorm(e->p_x, L.input_ln, n, e->p_xn, s));
+    E_TRY(tgemm_digitize(e->p_xn, dp, s));
+    E_TRY(tgemm_qkv_decode(L, dp, e->d_pos, e->d_seq, kv, e->rope_dec_cos, e->rope_dec_sin, e->p_q, s));
+    E_TRY(launch_decode_attention(e->p_q, kv, tok, max_len, e->p_ctx, e->attn_part, e->attn_cnt, s, false));
+    E_TRY(tgemm_digitize(e->p_ctx, dp, s));
+    E_TRY(tgemm_o(L, dp, e->p_a, s));
+    E_TRY(decode_rmsnorm(e->p_a, L.post_ln, n, e->p_xn, s));
+    E_TRY(tgemm_digitize(e->p_xn, dp, s));
+    E_TRY(tgemm_gateup_decode(L, dp, e->p_h, s));
+    E_TRY(tgemm_digitize(e->p_h, dph, s));
+    E_TRY(tgemm_down(L, dph, e->p_a, e->p_x, true, s));
+    if (e->dump_hidden)
+      E_TRY(cudaMemcpyAsync(e->dump + (size_t)l * n * kHidden, e->p_x, (size_t)n * kHidden * 4,
+                            cudaMemcpyDeviceToDevice, s));
+  }
+  if (int st = enqueue_lm_head(e, e->p_x, n, e->d_next, e->keep_logits ? e->logits : nullptr, false)) return st;
+  if (advance) {
+    advance_kernel<<<(n + 127) / 128, 128, 0, s>>>(e->d_tokens, e->d_next, e->d_pos, n);
+    E_TRY(cudaGetLastError());
   }
   return 0;
 }
@@ -456,12 +519,15 @@ int qwen_engine_create(int device, int wbits, int max_seqs, int max_len, qwen_en
   E_TRY(cudaMemcpy(e->d_page_table, e->page_table.data(), e->page_table.size() * 4, cudaMemcpyHostToDevice));
   for (int p = e->n_pages - 1; p >= 0; --p) e->free_pages.push_back(p);
   e->seq_len.assign(max_seqs, 0);
-  const int T = kGemvMaxTokens;
+  // tokens per decode step: up to 4 in the persistent kernel, up to max_seqs in the batched W8 path
+  const int T = std::max(kGemvMaxTokens, max_seqs);
+  e->batch_cap = T;
   E_TRY(dalloc(&e->d_tokens, T));
   E_TRY(dalloc(&e->d_pos, T));
   E_TRY(dalloc(&e->d_seq, T));
   E_TRY(dalloc(&e->d_next, T));
   E_TRY(cudaMallocHost(&e->h_io, 16 * sizeof(int)));
+  E_TRY(cudaMallocHost(&e->hb_io, (size_t)4 * T * sizeof(int)));
   E_TRY(dalloc(&e->x, (size_t)T * kHidden));
   E_TRY(dalloc(&e->q, (size_t)T * kHidden));
   E_TRY(dalloc(&e->ctx, (size_t)T * kHidden));
@@ -474,10 +540,18 @@ int qwen_engine_create(int device, int wbits, int max_seqs, int max_len, qwen_en
                                        stack::attn_part_floats(T, e->attn_max_chunks))));
   E_TRY(dalloc(&e->attn_cnt, (size_t)T * kKvHeads));
   E_TRY(cudaMemset(e->attn_cnt, 0, (size_t)T * kKvHeads * 4));
+  {
+    uint8_t* lm = nullptr;
+    E_TRY(cudaMalloc(&lm, lm_scratch_bytes()));
+    E_TRY(cudaMemset(lm, 0, lm_scratch_bytes()));
+    e->lm.planes = reinterpret_cast<__half*>(lm);
+    e->lm.packed = reinterpret_cast<unsigned long long*>(lm + (size_t)2 * 128 * kHidden * 2);
+    e->lm.counter = reinterpret_cast<unsigned*>(lm + (size_t)2 * 128 * kHidden * 2 + 128 * 8);
+  }
   E_TRY(dalloc(&e->lm_part, (size_t)lm_head_partial_floats()));
   E_TRY(dalloc(&e->lm_cnt, 1));
   E_TRY(cudaMemset(e->lm_cnt, 0, 4));
-  E_TRY(dalloc(&e->dump, (size_t)kLayers * std::max(T, 1) * kHidden));
+  E_TRY(dalloc(&e->dump, (size_t)kLayers * T * kHidden));
   E_TRY(dalloc(&e->logits, (size_t)T * kVocab));
   if (int st = ensure_rope_dec(e, max_len + 1)) return st;
   *out = e;
@@ -496,11 +570,13 @@ void qwen_engine_destroy(qwen_engine* e) {
                   e->d_item_off, e->d_items};
   for (void* p : ptrs) cudaFree(p);
   cudaFree(e->trace);
+  cudaFree(e->lm.planes);
   cudaFree(e->p_planes);
   cudaFree(e->p_steps);
   for (cudaEvent_t ev : e->kev)
     if (ev) cudaEventDestroy(ev);
   if (e->h_io) cudaFreeHost(e->h_io);
+  if (e->hb_io) cudaFreeHost(e->hb_io);
   if (e->stream) cudaStreamDestroy(e->stream);
   delete e;
 }
@@ -565,6 +641,12 @@ int qwen_engine_set_option(qwen_engine* e, const char* name, long long value) {
     e->stack_ring = (int)value;
     for (auto& kv : e->graphs) cudaGraphExecDestroy(kv.second);
     e->graphs.clear();
+  } else if (n == "lm_tc") {
+    e->use_lm_tc = value != 0;
+    for (auto& kv : e->graphs) cudaGraphExecDestroy(kv.second);
+    e->graphs.clear();
+  } else if (n == "batched") {
+    e->use_batched = value != 0;
   } else if (n == "stack") {
     e->use_stack = value != 0;
     for (auto& kv : e->graphs) cudaGraphExecDestroy(kv.second);
@@ -632,8 +714,9 @@ int qwen_engine_prefill(qwen_engine* e, int slot, const int32_t* tokens, int n, 
                             cudaMemcpyDeviceToDevice, s));
     }
   }
-  E_TRY(launch_lm_head_argmax(e->embed, e->final_norm, e->p_x + (size_t)(n - 1) * kHidden, 1,
-                              e->keep_logits ? e->logits : nullptr, e->lm_part, e->lm_cnt, e->d_next, s, false));
+  if (int st = enqueue_lm_head(e, e->p_x + (size_t)(n - 1) * kHidden, 1, e->d_next,
+                               e->keep_logits ? e->logits : nullptr, false))
+    return st;
   E_TRY(cudaMemcpyAsync(e->h_io + 12, e->d_next, 4, cudaMemcpyDeviceToHost, s));
   E_TRY(cudaStreamSynchronize(s));
   e->seq_len[slot] = n;
@@ -645,6 +728,36 @@ int qwen_engine_prefill(qwen_engine* e, int slot, const int32_t* tokens, int n, 
 int qwen_engine_decode(qwen_engine* e, const int32_t* slots, const int32_t* tokens, int n, int32_t* next_tokens) {
   if (!e || !slots || !tokens || n <= 0) return kStatusInvalid;
   E_TRY(cudaSetDevice(e->device));
+  if (batched_ok(e, n)) {
+    int max_len = 0;
+    std::vector<char> seen(e->max_seqs, 0);
+    for (int i = 0; i < n; ++i) {
+      const int slot = slots[i];
+      if (slot < 0 || slot >= e->max_seqs || seen[slot] || tokens[i] < 0 || tokens[i] >= kVocab) return kStatusInvalid;
+      seen[slot] = 1;
+      const int pos = e->seq_len[slot];
+      if (int st = ensure_pages(e, slot, pos + 1)) return st;
+      e->hb_io[i] = tokens[i];
+      e->hb_io[e->batch_cap + i] = pos;
+      e->hb_io[2 * e->batch_cap + i] = slot;
+      max_len = std::max(max_len, pos + 1);
+    }
+    if (int st = ensure_rope_dec(e, max_len)) return st;
+    if (int st = ensure_prefill_buffers(e, n)) return st;
+    e->dev_slots.clear();
+    E_TRY(cudaMemcpyAsync(e->d_tokens, e->hb_io, n * 4, cudaMemcpyHostToDevice, e->stream));
+    E_TRY(cudaMemcpyAsync(e->d_pos, e->hb_io + e->batch_cap, n * 4, cudaMemcpyHostToDevice, e->stream));
+    E_TRY(cudaMemcpyAsync(e->d_seq, e->hb_io + 2 * e->batch_cap, n * 4, cudaMemcpyHostToDevice, e->stream));
+    if (int st = enqueue_decode_batched(e, n, ((max_len + 63) / 64) * 64, false)) return st;
+    E_TRY(cudaMemcpyAsync(e->hb_io + 3 * e->batch_cap, e->d_next, n * 4, cudaMemcpyDeviceToHost, e->stream));
+    E_TRY(cudaStreamSynchronize(e->stream));
+    for (int i = 0; i < n; ++i) {
+      next_tokens[i] = e->hb_io[3 * e->batch_cap + i];
+      e->seq_len[slots[i]] += 1;
+    }
+    e->last_rows = n;
+    return 0;
+  }
   for (int base = 0; base < n; base += kGemvMaxTokens) {
     const int nt = std::min(kGemvMaxTokens, n - base);
     int max_len = 0;
@@ -679,8 +792,47 @@ int qwen_engine_decode(qwen_engine* e, const int32_t* slots, const int32_t* toke
 
 int qwen_engine_bench_decode(qwen_engine* e, const int32_t* slots, const int32_t* first_tokens, int n, int steps,
                              int warmup, float* ms_per_step) {
-  if (!e || !slots || !first_tokens || n <= 0 || n > kGemvMaxTokens || steps <= 0 || warmup < 0) return kStatusInvalid;
+  if (!e || !slots || !first_tokens || n <= 0 || steps <= 0 || warmup < 0) return kStatusInvalid;
+  if (n > kGemvMaxTokens && !batched_ok(e, n)) return kStatusInvalid;
   E_TRY(cudaSetDevice(e->device));
+  if (n > kGemvMaxTokens) {
+    int max_end = 0;
+    for (int i = 0; i < n; ++i) {
+      const int slot = slots[i];
+      if (slot < 0 || slot >= e->max_seqs) return kStatusInvalid;
+      const int end = e->seq_len[slot] + warmup + steps;
+      if (int st = ensure_pages(e, slot, end)) return st;
+      e->hb_io[i] = first_tokens[i];
+      e->hb_io[e->batch_cap + i] = e->seq_len[slot];
+      e->hb_io[2 * e->batch_cap + i] = slot;
+      max_end = std::max(max_end, end);
+    }
+    if (int st = ensure_rope_dec(e, max_end)) return st;
+    if (int st = ensure_prefill_buffers(e, n)) return st;
+    e->dev_slots.clear();
+    E_TRY(cudaMemcpyAsync(e->d_tokens, e->hb_io, n * 4, cudaMemcpyHostToDevice, e->stream));
+    E_TRY(cudaMemcpyAsync(e->d_pos, e->hb_io + e->batch_cap, n * 4, cudaMemcpyHostToDevice, e->stream));
+    E_TRY(cudaMemcpyAsync(e->d_seq, e->hb_io + 2 * e->batch_cap, n * 4, cudaMemcpyHostToDevice, e->stream));
+    const int grid_len = ((max_end + 63) / 64) * 64;
+    for (int i = 0; i < warmup; ++i)
+      if (int st = enqueue_decode_batched(e, n, grid_len, true)) return st;
+    cudaEvent_t t0, t1;
+    E_TRY(cudaEventCreate(&t0));
+    E_TRY(cudaEventCreate(&t1));
+    E_TRY(cudaStreamSynchronize(e->stream));
+    E_TRY(cudaEventRecord(t0, e->stream));
+    for (int i = 0; i < steps; ++i)
+      if (int st = enqueue_decode_batched(e, n, grid_len, true)) return st;
+    E_TRY(cudaEventRecord(t1, e->stream));
+    E_TRY(cudaEventSynchronize(t1));
+    float ms = 0.f;
+    E_TRY(cudaEventElapsedTime(&ms, t0, t1));
+    cudaEventDestroy(t0);
+    cudaEventDestroy(t1);
+    for (int i = 0; i < n; ++i) e->seq_len[slots[i]] += warmup + steps;
+    if (ms_per_step) *ms_per_step = ms / steps;
+    return 0;
+  }
   int max_end = 0;
   for (int i = 0; i < n; ++i) {
     const int slot = slots[i];

@@ -63,6 +63,12 @@ struct TArgs {
   const float* resid;
   bool round_out;
   int* raw;
+  // decode (batched): RoPE row = pos[t], K/V rows written through the paged view at (seq[t], pos[t]),
+  // SiLU with expf (the decode reference) instead of approx_exp (the prefill reference)
+  bool decode;
+  const int* pos;
+  const int* seq;
+  KvView kv;
 };
 
 __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int c0, int c1, uint64_t* bar) {
@@ -229,11 +235,18 @@ __global__ void __launch_bounds__(kThreadsT, 1)
           const int h = mtile, p = r & 63;
           const bool rope = h < kHeads + kKvHeads;
           float cs[kChunkN], sn[kChunkN];
+          float* kvp[kChunkN];
 #pragma unroll
           for (int c = 0; c < kChunkN; ++c) {
             const int n = min(n0 + c0 + c, a.S - 1);
-            cs[c] = rope ? __ldg(a.cosv + (size_t)n * 64 + p) : 1.f;
-            sn[c] = rope ? __ldg(a.sinv + (size_t)n * 64 + p) : 0.f;
+            const int pos = a.decode ? __ldg(a.pos + n) : n;
+            cs[c] = rope ? __ldg(a.cosv + (size_t)pos * 64 + p) : 1.f;
+            sn[c] = rope ? __ldg(a.sinv + (size_t)pos * 64 + p) : 0.f;
+            kvp[c] = nullptr;
+            if (a.decode && h >= kHeads) {
+              const int which = h < kHeads + kKvHeads ? 0 : 1;
+              kvp[c] = kv_row(a.kv, __ldg(a.seq + n), pos, which) + (row - kHidden - which * kKvWidth);
+            }
           }
 #pragma unroll
           for (int c = 0; c < kChunkN; ++c) sm.ys[r][c] = __fmaf_rn(sc, yv[c], bb);
@@ -258,7 +271,10 @@ __global__ void __launch_bounds__(kThreadsT, 1)
             if (rope)
               y = r < 64 ? __fsub_rn(__fmul_rn(mine, cs[c]), __fmul_rn(other, sn[c]))
                          : __fadd_rn(__fmul_rn(mine, cs[c]), __fmul_rn(other, sn[c]));
-            if (n < a.S) dst[(size_t)n * stride] = y;
+            if (n < a.S) {
+              if (kvp[c] != nullptr) *kvp[c] = y;
+              else dst[(size_t)n * stride] = y;
+            }
           }
           named_sync(kBarT, kEpiT);
         } else {  // gate|up: tile rows 0..63 gate rows 64 j.., 64..127 the matching up rows
@@ -271,7 +287,7 @@ __global__ void __launch_bounds__(kThreadsT, 1)
           for (int c = cb; c < cb + kChunkN / 2; ++c) {
             const int n = n0 + c0 + c;
             const float gv = sm.ys[gr][c], uv = sm.ys[gr + 64][c];
-            const float silu = __fdiv_rn(gv, __fadd_rn(1.0f, approx_exp(-gv)));
+            const float silu = __fdiv_rn(gv, __fadd_rn(1.0f, a.decode ? expf(-gv) : approx_exp(-gv)));
             if (n < a.S) a.out[(size_t)n * kInter + mtile * 64 + gr] = __fmul_rn(silu, uv);
           }
           named_sync(kBarT, kEpiT);
@@ -333,6 +349,47 @@ __global__ void __launch_bounds__(256) digitize_kernel(const float* __restrict__
     *reinterpret_cast<uint32_t*>(p0 + k) = w0;
     *reinterpret_cast<uint32_t*>(p1 + k) = w1;
     *reinterpret_cast<uint32_t*>(p2 + k) = w2;
+  }
+}
+
+// Decode RMSNorm of n token rows (hls/decode_only/qwen_decode_attention_kernel.cpp:13-27): double sum of
+// squares, inv = 1 / sqrt(ms + eps) in double, out = float(x * inv * w). 128 threads per token with the
+// element assignment and reduction order of the persistent decode kernel (thread tid sums elements
+// 512 j + 4 tid + e, xor-shuffle within the warp, the four warps in order), so both give identical rows.
+__global__ void __launch_bounds__(128) decode_rmsnorm_kernel(const float* __restrict__ x, const float* __restrict__ w,
+                                                             float* __restrict__ out) {
+  __shared__ double red[4];
+  const int t = blockIdx.x, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const float* row = x + (size_t)t * kHidden;
+  float v[3][4];
+#pragma unroll
+  for (int j = 0; j < 3; ++j) {
+    const float4 f = *reinterpret_cast<const float4*>(row + 512 * j + 4 * tid);
+    v[j][0] = f.x;
+    v[j][1] = f.y;
+    v[j][2] = f.z;
+    v[j][3] = f.w;
+  }
+  double ss = 0.0;
+#pragma unroll
+  for (int j = 0; j < 3; ++j)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) ss += (double)v[j][e] * (double)v[j][e];
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+  if (lane == 0) red[warp] = ss;
+  __syncthreads();
+  const double tot = red[0] + red[1] + red[2] + red[3];
+  const double inv = 1.0 / sqrt(tot / (double)kHidden + (double)kEps);
+#pragma unroll
+  for (int j = 0; j < 3; ++j) {
+    const float4 wv = *reinterpret_cast<const float4*>(w + 512 * j + 4 * tid);
+    float4 o;
+    o.x = (float)((double)v[j][0] * inv * (double)wv.x);
+    o.y = (float)((double)v[j][1] * inv * (double)wv.y);
+    o.z = (float)((double)v[j][2] * inv * (double)wv.z);
+    o.w = (float)((double)v[j][3] * inv * (double)wv.w);
+    *reinterpret_cast<float4*>(out + (size_t)t * kHidden + 512 * j + 4 * tid) = o;
   }
 }
 
@@ -443,12 +500,41 @@ cudaError_t tgemm_down(const LayerDev& L, const DigitPlanes& x, const float* res
   return run_tgemm<kTDown>(L.down_w, kHidden, kInter, kHidden / kTileM, kTileM, 0, x, a, s);
 }
 
+cudaError_t tgemm_qkv_decode(const LayerDev& L, const DigitPlanes& x, const int* pos, const int* seq, KvView kv,
+                             const float* rope_cos, const float* rope_sin, float* q_out, cudaStream_t s) {
+  TArgs a{};
+  a.scale = L.qkv_s;
+  a.bias = L.qkv_b;
+  a.cosv = rope_cos;
+  a.sinv = rope_sin;
+  a.out = q_out;
+  a.decode = true;
+  a.pos = pos;
+  a.seq = seq;
+  a.kv = kv;
+  return run_tgemm<kTQkv>(L.qkv_w, kQkvRows, kHidden, kQkvRows / kTileM, kTileM, 0, x, a, s);
+}
+
+cudaError_t tgemm_gateup_decode(const LayerDev& L, const DigitPlanes& x, float* h, cudaStream_t s) {
+  TArgs a{};
+  a.scale = L.gu_s;
+  a.out = h;
+  a.decode = true;
+  return run_tgemm<kTGateUp>(L.gu_w, 2 * kInter, kHidden, kInter / 64, 64, kInter, x, a, s);
+}
+
 cudaError_t tgemm_raw(const uint8_t* codes, int rows, const DigitPlanes& x, int* acc, cudaStream_t s) {
   if (rows % kTileM) return cudaErrorInvalidValue;
   TArgs a{};
   a.raw = acc;
   a.rows = rows;
   return run_tgemm<kTRaw>(codes, rows, x.K, rows / kTileM, kTileM, 0, x, a, s);
+}
+
+cudaError_t decode_rmsnorm(const float* x, const float* w, int n, float* out, cudaStream_t s) {
+  if (n < 1) return cudaErrorInvalidValue;
+  decode_rmsnorm_kernel<<<n, 128, 0, s>>>(x, w, out);
+  return cudaGetLastError();
 }
 
 unsigned tgemm_kernel_error(bool reset) {

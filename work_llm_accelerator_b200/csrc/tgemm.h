@@ -33,6 +33,15 @@ cudaError_t tgemm_gateup(const LayerDev& L, const DigitPlanes& x, float* h, cuda
 cudaError_t tgemm_down(const LayerDev& L, const DigitPlanes& x, const float* resid, float* out, bool round_out,
                        cudaStream_t s);
 
+// Batched-decode forms (the decode reference's operations): q|k|v with RoPE at pos[t] from the decode
+// tables and the new K/V rows written through the paged view at (seq[t], pos[t]); gate|up with expf SiLU.
+// o_proj and down are the same as for prefill.
+cudaError_t tgemm_qkv_decode(const LayerDev& L, const DigitPlanes& x, const int* pos, const int* seq, KvView kv,
+                             const float* rope_cos, const float* rope_sin, float* q_out, cudaStream_t s);
+cudaError_t tgemm_gateup_decode(const LayerDev& L, const DigitPlanes& x, float* h, cudaStream_t s);
+// Decode RMSNorm (double accumulation) of n rows of 1536.
+cudaError_t decode_rmsnorm(const float* x, const float* w, int n, float* out, cudaStream_t s);
+
 // Raw integer products for tests: acc [3][S][rows] int32 = sum_k code(row, k) * digit_p(t, k).
 cudaError_t tgemm_raw(const uint8_t* codes, int rows, const DigitPlanes& x, int* acc, cudaStream_t s);
 

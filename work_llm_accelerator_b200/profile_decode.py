@@ -9,6 +9,9 @@
     python -m work_llm_accelerator_b200.profile_decode prefill --wbits 8 --prompt 4096 --steps 2
         times full 28-layer prefills of one sequence (CUDA events on the engine stream) and prints
         tokens/s.
+    python -m work_llm_accelerator_b200.profile_decode batched --batch 64 --prompt 2048 --steps 8
+        prefills `batch` sequences, then times device-resident greedy decode steps of all of them
+        together (the batched W8 path) and prints tokens/s.
 
 Both hold about 2.2 GB (W8) of weights on the device plus a 1024-position KV pool.
 """
@@ -24,7 +27,8 @@ from . import host
 
 def main(argv=None) -> int:
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
-    ap.add_argument("mode", choices=["kernels", "steps", "prefill"])
+    ap.add_argument("mode", choices=["kernels", "steps", "prefill", "batched"])
+    ap.add_argument("--batch", type=int, default=64, help="batched: sequences decoded together")
     ap.add_argument("--wbits", type=int, default=8, choices=[4, 8])
     ap.add_argument("--seed", type=int, default=7)
     ap.add_argument("--iters", type=int, default=2, help="kernels: launches of each kernel")
@@ -36,7 +40,8 @@ def main(argv=None) -> int:
                     help="engine option (e.g. qgemm=0, prefetch=0, pdl=0)")
     a = ap.parse_args(argv)
 
-    eng = host.Engine(0, a.wbits, max_seqs=1, max_len=max(1024, a.prompt + 8))
+    max_seqs = a.batch if a.mode == "batched" else 1
+    eng = host.Engine(0, a.wbits, max_seqs=max_seqs, max_len=max(1024, a.prompt + 2 * a.steps + 16))
     try:
         eng.init_synthetic(a.seed)
         for opt in a.option:
@@ -59,6 +64,14 @@ def main(argv=None) -> int:
                 times.append(e0.elapsed_time(e1))
             ms = min(times)
             print(json.dumps({"prompt": a.prompt, "ms": ms, "tok_per_s": a.prompt / (ms * 1e-3)}))
+        elif a.mode == "batched":
+            rng = np.random.default_rng(1)
+            first = []
+            for i in range(a.batch):
+                first.append(eng.prefill(i, rng.integers(0, 151936, a.prompt).astype(np.int32)))
+            ms = eng.bench_decode(list(range(a.batch)), first, a.steps, 2)
+            print(json.dumps({"batch": a.batch, "history": a.prompt, "ms_per_step": ms,
+                              "tok_per_s": a.batch / (ms * 1e-3)}))
         elif a.mode == "kernels":
             us = eng.profile_kernels(1, a.past, iters=a.iters)
             print(json.dumps({k: round(v * 1000.0, 3) for k, v in us.items()}))
