@@ -93,6 +93,11 @@ int qwen_engine_profile_kernels(qwen_engine* e, int n, int past, int iters, floa
  * starting from first_token): ms_out[0] = mean milliseconds of the 28-layer part (the persistent W8 kernel,
  * or the five kernels per layer otherwise), ms_out[1] = the final norm + LM head + argmax kernel. */
 int qwen_engine_profile_decode(qwen_engine* e, int slot, int first_token, int steps, float* ms_out);
+/* Device time per kernel group of `steps` batched (W8, n > 4) greedy decode steps, eager launches, mean
+ * milliseconds per step: ms_out[8] = {RMSNorm, digit planes, q|k|v GEMM, attention, o_proj GEMM, gate|up
+ * GEMM, down GEMM, LM head}. */
+int qwen_engine_profile_batched(qwen_engine* e, const int32_t* slots, const int32_t* first_tokens, int n, int steps,
+                                float* ms_out);
 /* The engine's CUDA stream (cudaStream_t) for callers that record their own events. */
 void* qwen_engine_stream(qwen_engine* e);
 /* Number of kernels one decode step of `n` sequences launches. */

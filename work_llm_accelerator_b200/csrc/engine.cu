@@ -152,6 +152,11 @@ struct qwen_engine {
   int stack_ring = 9;                   // weight stages in flight per CTA
   cudaEvent_t kev[3] = {nullptr, nullptr, nullptr};  // per-kernel timing (profile_decode)
   bool time_kernels = false;
+  // per-category timing of the batched step (profile_batched): events around each kernel group
+  std::vector<cudaEvent_t> bev;
+  std::vector<int> bev_cat;  // category of the group each event opens
+  int bev_used = 0;
+  bool time_batched = false;
   // tensor-core LM head
   bool use_lm_tc = true;
   LmScratch lm{nullptr, nullptr, nullptr};
@@ -392,9 +397,28 @@ bool batched_ok(const qwen_engine* e, int n) {
 // One greedy decode step of n > 4 tokens (W8): every projection of all tokens in one many-token tensor-core
 // GEMM per layer (weights read once per step), paged-KV attention over all tokens, LM head in groups of 4.
 // Tokens / positions / slots are in d_tokens / d_pos / d_seq. Eager launches (no graph).
+// Timing categories of the batched step (profile_batched).
+enum BatchedCat { kBcNorm = 0, kBcDigits, kBcQkv, kBcAttn, kBcO, kBcGateUp, kBcDown, kBcHead, kBcCats };
+
 int enqueue_decode_batched(qwen_engine* e, int n, int max_len, bool advance) {
   cudaStream_t s = e->stream;
   if (int st = ensure_tiles(e)) return st;
+  // optional timing: an event before each kernel group, tagged with its category
+  if (e->time_batched) {
+    e->bev_used = 0;
+    e->bev_cat.clear();
+  }
+  auto mark = [&](int cat) -> cudaError_t {
+    if (!e->time_batched) return cudaSuccess;
+    if (e->bev_used == (int)e->bev.size()) {
+      cudaEvent_t ev;
+      cudaError_t err = cudaEventCreate(&ev);
+      if (err != cudaSuccess) return err;
+      e->bev.push_back(ev);
+    }
+    e->bev_cat.push_back(cat);
+    return cudaEventRecord(e->bev[e->bev_used++], s);
+  };
   embed_gather_kernel<<<n, 256, 0, s>>>(e->embed, e->d_tokens, n, e->p_x);
   E_TRY(cudaGetLastError());
   const DigitPlanes dp{e->p_planes, e->p_steps, n, tgemm_pad(n), kHidden};
@@ -403,26 +427,68 @@ int enqueue_decode_batched(qwen_engine* e, int n, int max_len, bool advance) {
   for (int l = 0; l < kLayers; ++l) {
     const LayerDev& L = e->layers[l];
     const KvView kv = paged_view(e, l);
+    E_TRY(mark(kBcNorm));
     E_TRY(decode_rmsnorm(e->p_x, L.input_ln, n, e->p_xn, s));
+    E_TRY(mark(kBcDigits));
     E_TRY(tgemm_digitize(e->p_xn, dp, s));
+    E_TRY(mark(kBcQkv));
     E_TRY(tgemm_qkv_decode(L, dp, e->d_pos, e->d_seq, kv, e->rope_dec_cos, e->rope_dec_sin, e->p_q, s));
+    E_TRY(mark(kBcAttn));
     E_TRY(launch_decode_attention(e->p_q, kv, tok, max_len, e->p_ctx, e->attn_part, e->attn_cnt, s, false));
+    E_TRY(mark(kBcDigits));
     E_TRY(tgemm_digitize(e->p_ctx, dp, s));
+    E_TRY(mark(kBcO));
     E_TRY(tgemm_o(L, dp, e->p_a, s));
+    E_TRY(mark(kBcNorm));
     E_TRY(decode_rmsnorm(e->p_a, L.post_ln, n, e->p_xn, s));
+    E_TRY(mark(kBcDigits));
     E_TRY(tgemm_digitize(e->p_xn, dp, s));
+    E_TRY(mark(kBcGateUp));
     E_TRY(tgemm_gateup_decode(L, dp, e->p_h, s));
+    E_TRY(mark(kBcDigits));
     E_TRY(tgemm_digitize(e->p_h, dph, s));
+    E_TRY(mark(kBcDown));
     E_TRY(tgemm_down(L, dph, e->p_a, e->p_x, true, s));
     if (e->dump_hidden)
       E_TRY(cudaMemcpyAsync(e->dump + (size_t)l * n * kHidden, e->p_x, (size_t)n * kHidden * 4,
                             cudaMemcpyDeviceToDevice, s));
   }
+  E_TRY(mark(kBcHead));
   if (int st = enqueue_lm_head(e, e->p_x, n, e->d_next, e->keep_logits ? e->logits : nullptr, false)) return st;
+  E_TRY(mark(kBcCats));  // end marker
   if (advance) {
     advance_kernel<<<(n + 127) / 128, 128, 0, s>>>(e->d_tokens, e->d_next, e->d_pos, n);
     E_TRY(cudaGetLastError());
   }
+  return 0;
+}
+
+// Batched step through a CUDA graph per (token count, 512-position bucket): removes the host cost of the
+// ~340 launches (tensor-map encoding included) from the step.
+int run_decode_step_batched(qwen_engine* e, int n, int max_len, bool advance) {
+  const int chunks = (max_len + 63) / 64;
+  const int bucket = ((chunks + 7) / 8) * 8;
+  const int grid_len = bucket * 64;
+  if (!e->use_graphs || e->dump_hidden || e->keep_logits || e->time_batched)
+    return enqueue_decode_batched(e, n, grid_len, advance);
+  const long long key = (1ll << 62) | ((long long)n << 40) | ((long long)advance << 39) | bucket;
+  auto it = e->graphs.find(key);
+  if (it == e->graphs.end()) {
+    // one eager pass first (same positions: it writes exactly what the graph will rewrite), so that every
+    // kernel's one-time set-up happens outside stream capture
+    if (int st = enqueue_decode_batched(e, n, grid_len, false)) return st;
+    cudaGraph_t g;
+    E_TRY(cudaStreamBeginCapture(e->stream, cudaStreamCaptureModeThreadLocal));
+    const int st = enqueue_decode_batched(e, n, grid_len, advance);
+    cudaError_t ce = cudaStreamEndCapture(e->stream, &g);
+    if (st) return st;
+    E_TRY(ce);
+    cudaGraphExec_t exec;
+    E_TRY(cudaGraphInstantiate(&exec, g, 0));
+    cudaGraphDestroy(g);
+    it = e->graphs.emplace(key, exec).first;
+  }
+  E_TRY(cudaGraphLaunch(it->second, e->stream));
   return 0;
 }
 
@@ -575,6 +641,7 @@ void qwen_engine_destroy(qwen_engine* e) {
   cudaFree(e->p_steps);
   for (cudaEvent_t ev : e->kev)
     if (ev) cudaEventDestroy(ev);
+  for (cudaEvent_t ev : e->bev) cudaEventDestroy(ev);
   if (e->h_io) cudaFreeHost(e->h_io);
   if (e->hb_io) cudaFreeHost(e->hb_io);
   if (e->stream) cudaStreamDestroy(e->stream);
@@ -748,7 +815,7 @@ int qwen_engine_decode(qwen_engine* e, const int32_t* slots, const int32_t* toke
     E_TRY(cudaMemcpyAsync(e->d_tokens, e->hb_io, n * 4, cudaMemcpyHostToDevice, e->stream));
     E_TRY(cudaMemcpyAsync(e->d_pos, e->hb_io + e->batch_cap, n * 4, cudaMemcpyHostToDevice, e->stream));
     E_TRY(cudaMemcpyAsync(e->d_seq, e->hb_io + 2 * e->batch_cap, n * 4, cudaMemcpyHostToDevice, e->stream));
-    if (int st = enqueue_decode_batched(e, n, ((max_len + 63) / 64) * 64, false)) return st;
+    if (int st = run_decode_step_batched(e, n, max_len, false)) return st;
     E_TRY(cudaMemcpyAsync(e->hb_io + 3 * e->batch_cap, e->d_next, n * 4, cudaMemcpyDeviceToHost, e->stream));
     E_TRY(cudaStreamSynchronize(e->stream));
     for (int i = 0; i < n; ++i) {
@@ -813,16 +880,15 @@ int qwen_engine_bench_decode(qwen_engine* e, const int32_t* slots, const int32_t
     E_TRY(cudaMemcpyAsync(e->d_tokens, e->hb_io, n * 4, cudaMemcpyHostToDevice, e->stream));
     E_TRY(cudaMemcpyAsync(e->d_pos, e->hb_io + e->batch_cap, n * 4, cudaMemcpyHostToDevice, e->stream));
     E_TRY(cudaMemcpyAsync(e->d_seq, e->hb_io + 2 * e->batch_cap, n * 4, cudaMemcpyHostToDevice, e->stream));
-    const int grid_len = ((max_end + 63) / 64) * 64;
     for (int i = 0; i < warmup; ++i)
-      if (int st = enqueue_decode_batched(e, n, grid_len, true)) return st;
+      if (int st = run_decode_step_batched(e, n, max_end, true)) return st;
     cudaEvent_t t0, t1;
     E_TRY(cudaEventCreate(&t0));
     E_TRY(cudaEventCreate(&t1));
     E_TRY(cudaStreamSynchronize(e->stream));
     E_TRY(cudaEventRecord(t0, e->stream));
     for (int i = 0; i < steps; ++i)
-      if (int st = enqueue_decode_batched(e, n, grid_len, true)) return st;
+      if (int st = run_decode_step_batched(e, n, max_end, true)) return st;
     E_TRY(cudaEventRecord(t1, e->stream));
     E_TRY(cudaEventSynchronize(t1));
     float ms = 0.f;
@@ -905,6 +971,47 @@ int qwen_engine_profile_decode(qwen_engine* e, int slot, int first_token, int st
   e->seq_len[slot] += steps;
   ms_out[0] = (float)(layers_ms / steps);
   ms_out[1] = (float)(head_ms / steps);
+  return 0;
+}
+
+int qwen_engine_profile_batched(qwen_engine* e, const int32_t* slots, const int32_t* first_tokens, int n, int steps,
+                                float* ms_out) {
+  if (!e || !slots || !first_tokens || !ms_out || steps <= 0 || !batched_ok(e, n)) return kStatusInvalid;
+  E_TRY(cudaSetDevice(e->device));
+  int max_end = 0;
+  for (int i = 0; i < n; ++i) {
+    const int slot = slots[i];
+    if (slot < 0 || slot >= e->max_seqs) return kStatusInvalid;
+    const int end = e->seq_len[slot] + steps;
+    if (int st = ensure_pages(e, slot, end)) return st;
+    e->hb_io[i] = first_tokens[i];
+    e->hb_io[e->batch_cap + i] = e->seq_len[slot];
+    e->hb_io[2 * e->batch_cap + i] = slot;
+    max_end = std::max(max_end, end);
+  }
+  if (int st = ensure_rope_dec(e, max_end)) return st;
+  if (int st = ensure_prefill_buffers(e, n)) return st;
+  e->dev_slots.clear();
+  E_TRY(cudaMemcpyAsync(e->d_tokens, e->hb_io, n * 4, cudaMemcpyHostToDevice, e->stream));
+  E_TRY(cudaMemcpyAsync(e->d_pos, e->hb_io + e->batch_cap, n * 4, cudaMemcpyHostToDevice, e->stream));
+  E_TRY(cudaMemcpyAsync(e->d_seq, e->hb_io + 2 * e->batch_cap, n * 4, cudaMemcpyHostToDevice, e->stream));
+  double acc[kBcCats] = {0};
+  e->time_batched = true;
+  int st = 0;
+  for (int i = 0; i < steps && st == 0; ++i) {
+    st = enqueue_decode_batched(e, n, ((max_end + 63) / 64) * 64, true);
+    if (st == 0 && cudaStreamSynchronize(e->stream) != cudaSuccess) st = kStatusCuda;
+    // event k opens the group of category bev_cat[k]; the last event closes the LM head
+    for (int k = 0; st == 0 && k + 1 < e->bev_used; ++k) {
+      float ms = 0.f;
+      if (cudaEventElapsedTime(&ms, e->bev[k], e->bev[k + 1]) != cudaSuccess) st = kStatusCuda;
+      acc[e->bev_cat[k]] += ms;
+    }
+  }
+  e->time_batched = false;
+  if (st) return st;
+  for (int i = 0; i < n; ++i) e->seq_len[slots[i]] += steps;
+  for (int c = 0; c < kBcCats; ++c) ms_out[c] = (float)(acc[c] / steps);
   return 0;
 }
 

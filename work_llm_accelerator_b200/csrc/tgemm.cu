@@ -25,23 +25,30 @@ namespace {
 
 using namespace umma;
 
-constexpr int kTN = 128;       // tokens per tile
 constexpr int kPlanes = 3;
-constexpr int kStagesT = 3;
 constexpr int kThreadsT = 192;
 constexpr int kEpiT = 128;
 constexpr int kBarT = 1;       // named barrier of the epilogue warps
-constexpr int kTmemColsT = 512;
-constexpr int kPlaneTile = kTN * kKBlock;                     // 16 KB
-constexpr int kStageBytes = kUnitBytes + kPlanes * kPlaneTile;  // 64 KB
 constexpr int kChunkN = 16;    // tokens per TMEM read
-constexpr uint32_t kIdescT = idesc_i8(kTileM, kTN);
-static_assert(kPlanes * kTN <= kTmemColsT, "accumulators fit in TMEM");
+constexpr int kMaxStages = 8;
+
+// Token-tile geometry: TN tokens per tile (16, 32, 64 or 128 = the padded token count up to 128), so that a
+// small batch does not move or multiply padding.
+template <int TN>
+struct TCfg {
+  static constexpr int kPlaneTile = TN * kKBlock;
+  static constexpr int kStage = kUnitBytes + kPlanes * kPlaneTile;
+  static constexpr int kStages = (200 * 1024) / kStage > kMaxStages ? kMaxStages : (200 * 1024) / kStage;
+  static constexpr uint32_t kIdesc = idesc_i8(kTileM, TN);
+  static constexpr int kTmemCols = kPlanes * TN <= 32 ? 32 : kPlanes * TN <= 64 ? 64 : kPlanes * TN <= 128 ? 128
+                                   : kPlanes * TN <= 256 ? 256 : 512;
+  static_assert(TN % 16 == 0 && TN <= 128, "token tile");
+};
 
 struct TSmem {
-  uint64_t full[kStagesT], empty[kStagesT], acc_full;
+  uint64_t full[kMaxStages], empty[kMaxStages], acc_full;
   uint32_t tmem_base;
-  float steps[kTN];
+  float steps[128];
   float ys[kTileM][kChunkN + 1];  // partner exchange (RoPE pairs, gate|up pairs)
 };
 
@@ -79,16 +86,23 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, i
       : "memory");
 }
 
+template <uint32_t IDESC>
 __device__ __forceinline__ void mma_t(uint32_t d, uint64_t a, uint64_t b, uint32_t acc) {
   asm volatile(
       "{\n.reg .pred p;\nsetp.ne.b32 p, %4, 0;\ntcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n}" ::"r"(d),
-      "l"(a), "l"(b), "r"(kIdescT), "r"(acc)
+      "l"(a), "l"(b), "r"(IDESC), "r"(acc)
       : "memory");
 }
 
-template <int EPI>
+template <int EPI, int TN>
 __global__ void __launch_bounds__(kThreadsT, 1)
     tgemm_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ CUtensorMap pmap, TArgs a) {
+  using C = TCfg<TN>;
+  constexpr int kTN = TN;
+  constexpr int kStagesT = C::kStages;
+  constexpr int kStageBytes = C::kStage;
+  constexpr int kPlaneTile = C::kPlaneTile;
+  constexpr int kTmemColsT = C::kTmemCols;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* stages = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   TSmem& sm = *reinterpret_cast<TSmem*>(stages + (size_t)kStagesT * kStageBytes);
@@ -158,7 +172,7 @@ __global__ void __launch_bounds__(kThreadsT, 1)
             const uint64_t bd = sw128_desc(sb + kUnitBytes + p * kPlaneTile);
 #pragma unroll
             for (int j = 0; j < kKBlock / 32; ++j)
-              mma_t(tmem + p * kTN, ad + 2 * j, bd + 2 * j, (kb > 0 || j > 0) ? 1u : 0u);
+              mma_t<C::kIdesc>(tmem + p * kTN, ad + 2 * j, bd + 2 * j, (kb > 0 || j > 0) ? 1u : 0u);
           }
         }
         mma_commit(&sm.empty[s]);
@@ -184,7 +198,7 @@ __global__ void __launch_bounds__(kThreadsT, 1)
     if constexpr (EPI != kTRaw) sc = __ldg(a.scale + row);
     if constexpr (EPI == kTQkv) bb = __ldg(a.bias + row);
     const uint32_t lane_base = tmem + ((uint32_t)(q * 32) << 16);
-    for (int c0 = 0; c0 < kTN; c0 += kChunkN) {
+    for (int c0 = 0; c0 < kTN && n0 + c0 < a.S; c0 += kChunkN) {  // chunks holding real tokens only
       int v0[16], v1[16], v2[16];
       if (ok) {
         tmem_ld16(lane_base + c0, v0);
@@ -422,13 +436,14 @@ bool make_map(CUtensorMap* m, const void* base, uint64_t rows, uint64_t k_bytes,
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-template <int EPI>
-cudaError_t run_tgemm(const uint8_t* w, int rows_total, int K, int mtiles, int box_rows, int second_row0,
-                      const DigitPlanes& x, TArgs a, cudaStream_t s) {
-  if (x.K != K || K % kKBlock || x.Spad % kTN || x.S < 1 || x.S > x.Spad) return cudaErrorInvalidValue;
+template <int EPI, int TN>
+cudaError_t run_tgemm_tn(const uint8_t* w, int rows_total, int K, int mtiles, int box_rows, int second_row0,
+                         const DigitPlanes& x, TArgs a, cudaStream_t s) {
+  using C = TCfg<TN>;
+  if (x.K != K || K % kKBlock || x.Spad % TN || x.S < 1 || x.S > x.Spad) return cudaErrorInvalidValue;
   CUtensorMap wmap, pmap;
   if (!make_map(&wmap, w, (uint64_t)rows_total, (uint64_t)K, (uint32_t)box_rows) ||
-      !make_map(&pmap, x.planes, (uint64_t)kPlanes * x.Spad, (uint64_t)K, kTN))
+      !make_map(&pmap, x.planes, (uint64_t)kPlanes * x.Spad, (uint64_t)K, TN))
     return cudaErrorInvalidValue;
   a.nkb = K / kKBlock;
   a.box_rows = box_rows;
@@ -436,8 +451,8 @@ cudaError_t run_tgemm(const uint8_t* w, int rows_total, int K, int mtiles, int b
   a.S = x.S;
   a.Spad = x.Spad;
   a.steps = x.steps;
-  auto kern = tgemm_kernel<EPI>;
-  const size_t smem = 1024 + (size_t)kStagesT * kStageBytes + sizeof(TSmem);
+  auto kern = tgemm_kernel<EPI, TN>;
+  const size_t smem = 1024 + (size_t)C::kStages * C::kStage + sizeof(TSmem);
   static std::mutex mu;
   static unsigned long long attr_set = 0;
   int dev = 0;
@@ -451,14 +466,27 @@ cudaError_t run_tgemm(const uint8_t* w, int rows_total, int K, int mtiles, int b
       attr_set |= 1ull << dev;
     }
   }
-  kern<<<dim3(mtiles, x.Spad / kTN), kThreadsT, smem, s>>>(wmap, pmap, a);
+  kern<<<dim3(mtiles, x.Spad / TN), kThreadsT, smem, s>>>(wmap, pmap, a);
   return cudaGetLastError();
+}
+
+template <int EPI>
+cudaError_t run_tgemm(const uint8_t* w, int rows_total, int K, int mtiles, int box_rows, int second_row0,
+                      const DigitPlanes& x, TArgs a, cudaStream_t s) {
+  const int tn = x.Spad < 128 ? x.Spad : 128;
+  switch (tn) {
+    case 16: return run_tgemm_tn<EPI, 16>(w, rows_total, K, mtiles, box_rows, second_row0, x, a, s);
+    case 32: return run_tgemm_tn<EPI, 32>(w, rows_total, K, mtiles, box_rows, second_row0, x, a, s);
+    case 64: return run_tgemm_tn<EPI, 64>(w, rows_total, K, mtiles, box_rows, second_row0, x, a, s);
+    case 128: return run_tgemm_tn<EPI, 128>(w, rows_total, K, mtiles, box_rows, second_row0, x, a, s);
+    default: return cudaErrorInvalidValue;
+  }
 }
 
 }  // namespace
 
 cudaError_t tgemm_digitize(const float* x, DigitPlanes d, cudaStream_t s) {
-  if (d.K % 4 || d.Spad % kTN || d.S < 1 || d.S > d.Spad) return cudaErrorInvalidValue;
+  if (d.K % 4 || d.Spad != tgemm_pad(d.S) || d.S < 1) return cudaErrorInvalidValue;
   digitize_kernel<<<d.Spad, 256, 0, s>>>(x, d.S, d.K, d.Spad, d.planes, d.steps);
   return cudaGetLastError();
 }

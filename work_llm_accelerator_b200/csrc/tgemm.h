@@ -9,15 +9,16 @@
 
 namespace qb {
 
-// Digit planes of S token rows of width K: planes [3][Spad][K] int8 (Spad = S rounded up to 128, padded
-// rows zero) and the per-token steps [Spad]. Row t: x = step[t] * (d0 + 256 d1 + 65536 d2).
+// Digit planes of S token rows of width K: planes [3][Spad][K] int8 (Spad = tgemm_pad(S), padded rows zero)
+// and the per-token steps [Spad]. Row t: x = step[t] * (d0 + 256 d1 + 65536 d2).
 struct DigitPlanes {
   int8_t* planes;
   float* steps;
   int S, Spad, K;
 };
 
-inline int tgemm_pad(int S) { return (S + 127) / 128 * 128; }
+// Padded token count: 16, 32 or 64 for small batches (one token tile of that size), else a multiple of 128.
+inline int tgemm_pad(int S) { return S <= 16 ? 16 : S <= 32 ? 32 : S <= 64 ? 64 : (S + 127) / 128 * 128; }
 inline size_t tgemm_plane_bytes(int S, int K) { return (size_t)3 * tgemm_pad(S) * K; }
 
 // x [S][K] fp32 -> digit planes (one CTA per token row).

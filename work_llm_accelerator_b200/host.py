@@ -173,6 +173,7 @@ def _configure_engine(lib: ctypes.CDLL) -> None:
     lib.qwen_engine_read_layer.argtypes = [vp, i, _B, _F]
     lib.qwen_engine_profile_kernels.argtypes = [vp, i, i, i, _F]
     lib.qwen_engine_profile_decode.argtypes = [vp, i, i, i, _F]
+    lib.qwen_engine_profile_batched.argtypes = [vp, _I32, _I32, i, i, _F]
     lib.qwen_engine_stream.argtypes = [vp]
     lib.qwen_engine_stream.restype = vp
     lib.qwen_engine_kernels_per_decode_step.argtypes = [vp, i]
@@ -181,7 +182,8 @@ def _configure_engine(lib: ctypes.CDLL) -> None:
               "qwen_engine_set_seq_len", "qwen_engine_seq_len", "qwen_engine_reset", "qwen_engine_set_option",
               "qwen_engine_read_hidden", "qwen_engine_read_logits", "qwen_engine_bench_decode",
               "qwen_engine_kernels_per_decode_step", "qwen_engine_decode_device", "qwen_engine_read_layer",
-              "qwen_engine_profile_kernels", "qwen_engine_read_trace", "qwen_engine_profile_decode"):
+              "qwen_engine_profile_kernels", "qwen_engine_read_trace", "qwen_engine_profile_decode",
+              "qwen_engine_profile_batched"):
         getattr(lib, n).restype = i
 
 
@@ -318,6 +320,15 @@ class Engine:
         out = np.zeros(2, np.float32)
         _check(self.lib.qwen_engine_profile_decode(self.handle, slot, first_token, steps, out), "profile_decode")
         return {"layers": float(out[0]), "lm_head": float(out[1])}
+
+    def profile_batched(self, slots: Sequence[int], first_tokens: Sequence[int], steps: int) -> dict[str, float]:
+        """Mean device milliseconds per batched decode step by kernel group."""
+        s = np.ascontiguousarray(slots, np.int32)
+        t = np.ascontiguousarray(first_tokens, np.int32)
+        out = np.zeros(8, np.float32)
+        _check(self.lib.qwen_engine_profile_batched(self.handle, s, t, s.size, steps, out), "profile_batched")
+        names = ("rmsnorm", "digits", "qkv", "attention", "o", "gate_up", "down", "lm_head")
+        return dict(zip(names, map(float, out)))
 
     def stream(self) -> int:
         return int(self.lib.qwen_engine_stream(self.handle) or 0)

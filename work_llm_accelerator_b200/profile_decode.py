@@ -70,8 +70,9 @@ def main(argv=None) -> int:
             for i in range(a.batch):
                 first.append(eng.prefill(i, rng.integers(0, 151936, a.prompt).astype(np.int32)))
             ms = eng.bench_decode(list(range(a.batch)), first, a.steps, 2)
+            cats = eng.profile_batched(list(range(a.batch)), first, 2)
             print(json.dumps({"batch": a.batch, "history": a.prompt, "ms_per_step": ms,
-                              "tok_per_s": a.batch / (ms * 1e-3)}))
+                              "tok_per_s": a.batch / (ms * 1e-3), "ms_by_group": cats}))
         elif a.mode == "kernels":
             us = eng.profile_kernels(1, a.past, iters=a.iters)
             print(json.dumps({k: round(v * 1000.0, 3) for k, v in us.items()}))
