@@ -63,6 +63,17 @@ def lm_head_bytes() -> float:
     return VOCAB * HIDDEN * 2 + HIDDEN * 4
 
 
+def bench_config(world: int, warmup: int, steps: int, wbits: int) -> dict:
+    """The workload both arms report: batch 1 per GPU after a 512-token prompt."""
+    sb = step_bytes(wbits, PROMPT + warmup + steps / 2)
+    return {"workload": "config2_decode_bs1", "model": "Qwen2.5-1.5B (28 layers, random init)",
+            "global_batch": world, "seq_len": PROMPT, "prompt": PROMPT,
+            "history_during_timing": [PROMPT + warmup, PROMPT + warmup + steps],
+            "parallelism": f"dp{world} (independent sequences)",
+            "l2": f"inputs larger than L2: {sb / 1e9:.2f} GB of weights/KV per step vs 126 MB L2",
+            "wbits": wbits}
+
+
 def peaks() -> tuple[float, str]:
     p = ROOT / "MEASURED_PEAKS.json"
     if p.exists():
@@ -187,14 +198,14 @@ def run_reference(args) -> dict:
     sec_per_token = statistics.median(secs) * LAYERS / layers
     value = procs / sec_per_token
     sample = (f"reference host library (oracle/_ref/libqwen_decode_stub.so, int4 weights: its only format), "
-              f"{procs} concurrent single-threaded processes, each one sequence at history {PROMPT}; each step times "
-              f"{layers} of 28 decoder layers through qwen_decode_top_smoke_forward (scaled x{LAYERS / layers:.0f}); "
-              "embedding/LM head excluded")
+              f"{procs} concurrent single-threaded processes (all host cores), each one batch-1 sequence at history "
+              f"{PROMPT}; value = their aggregate tokens/s; each step times {layers} of 28 decoder layers through "
+              f"qwen_decode_top_smoke_forward (scaled x{LAYERS / layers:.0f}); embedding/LM head excluded")
     return {
         "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": args.gpus, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": sec_per_token * 1e3, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "f32 activations x int4 weights", "data": "synthetic",
-        "config": {"workload": "config2_decode_bs1", "global_batch": procs, "seq_len": PROMPT, "parallelism": "cpu"},
+        "config": bench_config(args.gpus, args.warmup, args.steps, args.wbits),
         "impl": "reference",
         "cpu_baseline": {"value": value, "unit": "tok/s", "cores": procs, "kind": "reference", "sample": sample},
         "e2e": {"value": value, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
@@ -351,12 +362,7 @@ def run_b200(args, world: int, rank: int, local: int) -> dict | None:
         "vs_baseline": None,
         "dtype": "f32 activations x int8 weights (fp32 accumulate)" if wbits == 8 else "f32 x int4",
         "data": "synthetic: seeded N(0,0.02) weights quantized per channel, uniform-random prompt ids",
-        "config": {"workload": "config2_decode_bs1", "model": "Qwen2.5-1.5B (28 layers, random init)",
-                   "global_batch": world, "seq_len": PROMPT, "prompt": PROMPT,
-                   "history_during_timing": [PROMPT + args.warmup, PROMPT + args.warmup + args.steps],
-                   "parallelism": f"dp{world} (independent sequences)",
-                   "l2": f"inputs larger than L2: {sb / 1e9:.2f} GB of weights/KV per step vs 126 MB L2",
-                   "wbits": wbits},
+        "config": bench_config(world, args.warmup, args.steps, wbits),
         "e2e": {"value": world / (ms_e2e * 1e-3), "unit": "tok/s", "h2d_bytes_per_step": 12, "d2h_bytes_per_step": 4},
         "roofline": {"bound": "hbm",
                      "kernel": ("decode_stack_kernel: persistent 28-layer W8 decode step (1 launch per step)"
