@@ -333,6 +333,14 @@ def run_b200(args, world: int, rank: int, local: int) -> dict | None:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     ms, ms_e2e = float(t[0]), float(t[1])
     kernels = eng.kernels_per_decode_step(1) + 1  # + the position-advance kernel
+    # Tensors that were used on the engine's stream (and on NCCL's) must be released while that stream
+    # still exists: free them, then let the engine destroy its stream.
+    torch.cuda.synchronize()
+    del bufs, gathered, host_tok, t, stream
+    import gc
+
+    gc.collect()
+    torch.cuda.synchronize()
     eng.close()
     if rank != 0:
         return None
