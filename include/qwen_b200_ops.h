@@ -56,6 +56,26 @@ int qwen_b200_w8_digit_products(const signed char* codes, int rows, int k, const
 int qwen_b200_w8_digit_planes(const signed char* codes, int rows, int k, const float* x, int n_tokens, int* acc,
                               float* step, void* stream);
 
+/* Causal prefill attention context of seq_len tokens (replaces the reference's two-pass prefill context,
+ * hls/prefill_only/qwen_prefill_attention_kernel.cpp:204-289): for every query t and head h,
+ *   max = max_{j<=t} s_j,  e_j = approx_exp(s_j - max),  context = (sum_j e_j v_j) * (1 / sum_j e_j)
+ * with s_j = (q_h . k_j) * 0.08838834764831845 and the reference's approx_exp.
+ *   q        [seq_len][1536] fp32 post-RoPE queries (device memory, 16-byte aligned)
+ *   k_cache  [seq_len][256] fp32 token-major keys (device memory, 16-byte aligned)
+ *   v_cache  [seq_len][256] fp32 token-major values (device memory)
+ *   context  [seq_len][1536] fp32 output (device memory, 16-byte aligned)
+ *   mode     0: tensor cores (operands as fp16 hi + lo pairs, fp32 accumulation; inputs with |x| >= 32768
+ *               or non-finite values are computed by the CUDA-core kernel instead), 1: CUDA cores (fp32)
+ * Mode 0 uses stream-ordered temporary allocations (about 8 KB per token). */
+int qwen_b200_prefill_attention(const float* q, const float* k_cache, const float* v_cache, int seq_len,
+                                float* context, int mode, void* stream);
+
+/* The prefill softmax exponential as the tensor-core attention evaluates it: y[i] = approx_exp(x[i])
+ * (hls/prefill_only/qwen_prefill_attention_kernel.cpp:47-110, degree-6 Taylor series with halving and
+ * squaring), for finite x; exposed so that its bit-identity with the reference's function can be checked.
+ * x, y [n] fp32 device memory. */
+int qwen_b200_prefill_approx_exp(const float* x, float* y, long long n, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

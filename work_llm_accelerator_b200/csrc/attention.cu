@@ -254,7 +254,8 @@ struct PrefillSmem {
 
 __global__ void __launch_bounds__(256) prefill_attn_kernel(const float* __restrict__ q, const float* __restrict__ kc,
                                                            const float* __restrict__ vc, int S,
-                                                           float* __restrict__ ctx) {
+                                                           float* __restrict__ ctx, const int* only_if) {
+  if (only_if != nullptr && *reinterpret_cast<const volatile int*>(only_if) == 0) return;
   extern __shared__ float4 smem4[];
   PrefillSmem& sm = *reinterpret_cast<PrefillSmem*>(smem4);
   const int q0 = blockIdx.x * kPQ, g = blockIdx.y;
@@ -375,7 +376,16 @@ cudaError_t launch_prefill_attention(const float* q, const float* k_cache, const
   const size_t smem = sizeof(PrefillSmem);
   cudaError_t e = cudaFuncSetAttribute(prefill_attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
-  prefill_attn_kernel<<<dim3((S + kPQ - 1) / kPQ, kKvHeads), 256, smem, s>>>(q, k_cache, v_cache, S, ctx);
+  prefill_attn_kernel<<<dim3((S + kPQ - 1) / kPQ, kKvHeads), 256, smem, s>>>(q, k_cache, v_cache, S, ctx, nullptr);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_prefill_attention_gated(const float* q, const float* k_cache, const float* v_cache, int S,
+                                           float* ctx, const int* only_if, cudaStream_t s) {
+  const size_t smem = sizeof(PrefillSmem);
+  cudaError_t e = cudaFuncSetAttribute(prefill_attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (e != cudaSuccess) return e;
+  prefill_attn_kernel<<<dim3((S + kPQ - 1) / kPQ, kKvHeads), 256, smem, s>>>(q, k_cache, v_cache, S, ctx, only_if);
   return cudaGetLastError();
 }
 

@@ -1,0 +1,463 @@
+// Causal prefill attention on the tensor cores (tcgen05 kind::f16), the prefill context of
+// hls/prefill_only/qwen_prefill_attention_kernel.cpp:204-289 (12 query heads over 2 KV heads, head_dim 128).
+//
+// Numerics. Every fp32 operand x (Q, K, V and the softmax weights) is written as two fp16 values
+// x = hi + lo with hi = fp16(x) and lo = fp16(x - hi) (22 significant bits), and every product as
+// hi.hi + hi.lo + lo.hi accumulated in fp32 in TMEM; the dropped lo.lo term is 2^-22 of the product, so
+// scores and context keep fp32-level error against the reference's serial fp32 sums. The softmax keeps the
+// reference's two passes: pass 1 takes the row maximum of score * scaling over the causal keys, pass 2
+// recomputes the scores and accumulates e = approx_exp(score * scaling - max) (the reference's exponential,
+// bit for bit), the denominator sum e and the context sum e v, and divides once: ctx = acc * (1 / denom).
+// The fp16 split needs |x| < 32768 and finite values; otherwise the split kernel raises a flag, this kernel
+// does nothing and the CUDA-core kernel (attention.cu) computes the context instead.
+//
+// Work split. CTA = (128 queries, one query head); keys in tiles of 64. Warp 0 issues the TMA loads
+// (Q once, then K tiles for both passes and transposed V tiles for pass 2, two stages each), warp 1 issues
+// the MMAs (S = Q K^T into one of two TMEM score buffers; O += P V into the TMEM context accumulator), and
+// eight softmax warps own one query row and 32 keys of each tile per thread: they read the scores from
+// TMEM, compute the weights, and write them as fp16 (hi, lo) tiles to shared memory for the P V product.
+// Query tiles are launched heaviest (longest causal prefix) first.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+#include <cuda_fp16.h>
+
+#include <algorithm>
+#include <mutex>
+
+#include "attention_tc.h"
+#include "umma_sm100.cuh"
+
+namespace qb {
+namespace {
+
+using namespace umma;
+
+constexpr int kBQ = 128;  // query rows per CTA = TMEM lanes
+constexpr int kBK = 64;   // keys per tile
+constexpr int kQPlaneB = kBQ * kHeadDim * 2;  // fp16 [128 queries][128 dims]: two 64-dim swizzle columns
+constexpr int kKPlaneB = kBK * kHeadDim * 2;  // fp16 [64 keys][128 dims]: two 64-dim swizzle columns
+constexpr int kVPlaneB = kHeadDim * kBK * 2;  // fp16 [128 dims][64 keys]: one swizzle column
+constexpr int kPPlaneB = kBQ * kBK * 2;       // fp16 [128 queries][64 keys]: one swizzle column
+constexpr int kOffQ = 0;
+constexpr int kOffK = kOffQ + 2 * kQPlaneB;      // two stages of (hi, lo)
+constexpr int kOffV = kOffK + 2 * 2 * kKPlaneB;  // two stages of (hi, lo)
+constexpr int kOffP = kOffV + 2 * 2 * kVPlaneB;  // (hi, lo)
+constexpr int kTileBytes = kOffP + 2 * kPPlaneB;  // 224 KB
+constexpr int kSoftWarps = 8;
+constexpr int kSoftThreads = 32 * kSoftWarps;
+constexpr int kThreadsA = 64 + kSoftThreads;
+constexpr int kBarSoft = 1;  // named barrier of the softmax warps
+constexpr uint32_t kTmemColsA = 256;  // context accumulator: columns 0..127; score buffers: 128.., 192..
+constexpr uint32_t kColS = 128;
+constexpr uint32_t kIdescS = idesc_f16(kBQ, kBK);
+constexpr uint32_t kIdescO = idesc_f16(kBQ, kHeadDim);
+constexpr float kSplitLimit = 32768.0f;
+
+struct ACtl {
+  uint64_t q_full, k_full[2], k_empty[2], v_full[2], v_empty[2], s_full[2], s_empty[2], p_full, p_empty, o_full;
+  uint32_t tmem_base;
+  float xch[2][kBQ];  // per-row exchange between the two key halves (max, then denominator)
+};
+
+constexpr size_t kSmemA = 1024 + (size_t)kTileBytes + sizeof(ACtl);
+static_assert(kSmemA <= 232448, "shared memory per CTA");
+
+__device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, int c0, int c1, int c2,
+                                            uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], "
+      "[%5];" ::"r"(smem_u32(dst)),
+      "l"(map), "r"(c0), "r"(c1), "r"(c2), "r"(smem_u32(bar))
+      : "memory");
+}
+
+// fp32 -> (hi, lo) fp16 planes. Blocks [0, nvt): V tiles of 64 tokens x 64 features, transposed into
+// vt [2][256][Spad]; the rest: Q [S][1536] -> qp [2][S][1536] and K [S][256] -> kp [2][S][256], four
+// values per thread. A value the split cannot hold (|x| >= 32768, inf, nan) sets *flag.
+__global__ void __launch_bounds__(256) attn_split_kernel(const float* __restrict__ q, const float* __restrict__ k,
+                                                         const float* __restrict__ v, int S, int Spad, int nvt,
+                                                         __half* __restrict__ qp, __half* __restrict__ kp,
+                                                         __half* __restrict__ vt, int* __restrict__ flag) {
+  bool bad = false;
+  if ((int)blockIdx.x < nvt) {
+    __shared__ float tile[64][65];
+    const int tb = blockIdx.x >> 2, fb = blockIdx.x & 3;
+    const int tx = threadIdx.x & 63, ty = threadIdx.x >> 6;  // 64 x 4
+    for (int i = ty; i < 64; i += 4) {
+      const int t = tb * 64 + i;
+      const float x = t < S ? v[(size_t)t * kKvWidth + fb * 64 + tx] : 0.0f;
+      bad |= !(fabsf(x) < kSplitLimit);
+      tile[i][tx] = x;
+    }
+    __syncthreads();
+    for (int i = ty; i < 64; i += 4) {
+      const float x = tile[tx][i];  // token tb*64 + tx, feature fb*64 + i
+      const __half h = __float2half_rn(x);
+      const __half l = __float2half_rn(__fsub_rn(x, __half2float(h)));
+      const size_t o = (size_t)(fb * 64 + i) * Spad + tb * 64 + tx;
+      vt[o] = h;
+      vt[(size_t)kKvWidth * Spad + o] = l;
+    }
+  } else {
+    const size_t nq4 = (size_t)S * kHidden / 4, nk4 = (size_t)S * kKvWidth / 4;
+    const size_t stride = (size_t)(gridDim.x - nvt) * blockDim.x;
+    for (size_t i = (size_t)(blockIdx.x - nvt) * blockDim.x + threadIdx.x; i < nq4 + nk4; i += stride) {
+      const bool isq = i < nq4;
+      const size_t j = isq ? i : i - nq4;
+      const float4 x = reinterpret_cast<const float4*>(isq ? q : k)[j];
+      const float xs[4] = {x.x, x.y, x.z, x.w};
+      __half hs[4], ls[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        bad |= !(fabsf(xs[e]) < kSplitLimit);
+        hs[e] = __float2half_rn(xs[e]);
+        ls[e] = __float2half_rn(__fsub_rn(xs[e], __half2float(hs[e])));
+      }
+      __half* dst = isq ? qp : kp;
+      const size_t plane = isq ? (size_t)S * kHidden : (size_t)S * kKvWidth;
+      uint2 hv, lv;
+      hv.x = (uint32_t)__half_as_ushort(hs[0]) | ((uint32_t)__half_as_ushort(hs[1]) << 16);
+      hv.y = (uint32_t)__half_as_ushort(hs[2]) | ((uint32_t)__half_as_ushort(hs[3]) << 16);
+      lv.x = (uint32_t)__half_as_ushort(ls[0]) | ((uint32_t)__half_as_ushort(ls[1]) << 16);
+      lv.y = (uint32_t)__half_as_ushort(ls[2]) | ((uint32_t)__half_as_ushort(ls[3]) << 16);
+      reinterpret_cast<uint2*>(dst)[j] = hv;
+      reinterpret_cast<uint2*>(dst + plane)[j] = lv;
+    }
+  }
+  if (__syncthreads_or(bad) && threadIdx.x == 0) atomicOr(flag, 1);
+}
+
+__device__ __forceinline__ uint32_t pack_half2(float a, float b) {
+  return (uint32_t)__half_as_ushort(__float2half_rn(a)) | ((uint32_t)__half_as_ushort(__float2half_rn(b)) << 16);
+}
+
+__global__ void __launch_bounds__(kThreadsA, 1)
+    attn_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constant__ CUtensorMap kmap,
+                   const __grid_constant__ CUtensorMap vmap, int S, const int* flag, float* __restrict__ ctx) {
+  if (*reinterpret_cast<const volatile int*>(flag) != 0) return;  // values outside the split: CUDA-core kernel
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* tiles = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  ACtl& c = *reinterpret_cast<ACtl*>(tiles + kTileBytes);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int qt = gridDim.x - 1 - blockIdx.x;  // heaviest query tiles first
+  const int h = blockIdx.y, g = h / kGroups;
+  const int q0 = qt * kBQ;
+  const int T = (min(q0 + kBQ, S) + kBK - 1) / kBK;  // key tiles of the causal prefix
+  const int G = 2 * T;                                // pass 1 tiles, then pass 2 tiles
+
+  if (threadIdx.x == 0) {
+    mbar_init(&c.q_full, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&c.k_full[i], 1);
+      mbar_init(&c.k_empty[i], 1);
+      mbar_init(&c.v_full[i], 1);
+      mbar_init(&c.v_empty[i], 1);
+      mbar_init(&c.s_full[i], 1);
+      mbar_init(&c.s_empty[i], kSoftWarps);
+    }
+    mbar_init(&c.p_full, kSoftWarps);
+    mbar_init(&c.p_empty, 1);
+    mbar_init(&c.o_full, 1);
+    mbar_fence_init();
+  }
+  if (warp == 1) tmem_alloc(&c.tmem_base, kTmemColsA);
+  fence_before();
+  __syncthreads();
+  fence_after();
+  const uint32_t tmem = c.tmem_base;
+
+  if (warp == 0) {
+    // ---- TMA producer
+    if (lane == 0) {
+      asm volatile("prefetch.tensormap [%0];" ::"l"(&qmap) : "memory");
+      asm volatile("prefetch.tensormap [%0];" ::"l"(&kmap) : "memory");
+      asm volatile("prefetch.tensormap [%0];" ::"l"(&vmap) : "memory");
+      mbar_arrive_expect_tx(&c.q_full, 2 * kQPlaneB);
+      for (int p = 0; p < 2; ++p)
+        for (int a = 0; a < 2; ++a)
+          tma_load_3d(tiles + kOffQ + p * kQPlaneB + a * (kBQ * 128), &qmap, h * kHeadDim + a * 64, q0, p,
+                      &c.q_full);
+      bool ok = true;
+      int kn = 0, vn = 0;
+      for (int gi = 0; gi < G && ok; ++gi) {
+        const int j = gi < T ? gi : gi - T;
+        {
+          const int st = kn & 1;
+          if (!(ok = mbar_wait(&c.k_empty[st], ((kn >> 1) & 1) ^ 1))) break;
+          mbar_arrive_expect_tx(&c.k_full[st], 2 * kKPlaneB);
+          uint8_t* dst = tiles + kOffK + st * 2 * kKPlaneB;
+          for (int p = 0; p < 2; ++p)
+            for (int a = 0; a < 2; ++a)
+              tma_load_3d(dst + p * kKPlaneB + a * (kBK * 128), &kmap, g * kHeadDim + a * 64, j * kBK, p,
+                          &c.k_full[st]);
+          ++kn;
+        }
+        if (gi >= T) {
+          const int st = vn & 1;
+          if (!(ok = mbar_wait(&c.v_empty[st], ((vn >> 1) & 1) ^ 1))) break;
+          mbar_arrive_expect_tx(&c.v_full[st], 2 * kVPlaneB);
+          uint8_t* dst = tiles + kOffV + st * 2 * kVPlaneB;
+          for (int p = 0; p < 2; ++p) tma_load_3d(dst + p * kVPlaneB, &vmap, j * kBK, g * kHeadDim, p, &c.v_full[st]);
+          ++vn;
+        }
+      }
+      // every issued stage consumed before leaving (no copy in flight at exit)
+      for (int i = 0; i < 2 && ok; ++i, ++kn) ok = mbar_wait(&c.k_empty[kn & 1], ((kn >> 1) & 1) ^ 1);
+      for (int i = 0; i < 2 && ok; ++i, ++vn) ok = mbar_wait(&c.v_empty[vn & 1], ((vn >> 1) & 1) ^ 1);
+    }
+  } else if (warp == 1) {
+    // ---- MMA issuer
+    if (lane == 0) {
+      bool ok = mbar_wait(&c.q_full, 0);
+      fence_after();
+      const uint32_t qa = smem_u32(tiles + kOffQ);
+      int kn = 0, vn = 0;
+      // (A plane, B plane) of the three products, cross terms first: lo.hi, hi.lo, hi.hi
+      constexpr int kAp[3] = {1, 0, 0}, kBp[3] = {0, 1, 0};
+      auto issue_s = [&](int gi) {
+        const int st = kn & 1;
+        ok = ok && mbar_wait(&c.k_full[st], (kn >> 1) & 1);
+        fence_after();
+        if (ok) {
+          const uint32_t kb = smem_u32(tiles + kOffK + st * 2 * kKPlaneB);
+          const uint32_t d = tmem + kColS + 64 * (gi & 1);
+#pragma unroll
+          for (int t = 0; t < 3; ++t)
+#pragma unroll
+            for (int kk = 0; kk < kHeadDim / 16; ++kk) {
+              const uint32_t off = (uint32_t)((kk & 3) * 32);  // 16 dims = 32 bytes inside the swizzle row
+              const uint64_t ad = sw128_desc(qa + kAp[t] * kQPlaneB + (kk >> 2) * (kBQ * 128) + off);
+              const uint64_t bd = sw128_desc(kb + kBp[t] * kKPlaneB + (kk >> 2) * (kBK * 128) + off);
+              mma_f16<kIdescS>(d, ad, bd, (t > 0 || kk > 0) ? 1u : 0u);
+            }
+        }
+        mma_commit(&c.k_empty[st]);
+        mma_commit(&c.s_full[gi & 1]);
+        ++kn;
+      };
+      issue_s(0);
+      issue_s(1);
+      for (int gi = 0; gi < G; ++gi) {
+        if (gi >= T) {
+          const int j = gi - T;
+          const int st = vn & 1;
+          ok = ok && mbar_wait(&c.p_full, j & 1);
+          ok = ok && mbar_wait(&c.v_full[st], (vn >> 1) & 1);
+          fence_after();
+          if (ok) {
+            const uint32_t pa = smem_u32(tiles + kOffP);
+            const uint32_t vb = smem_u32(tiles + kOffV + st * 2 * kVPlaneB);
+#pragma unroll
+            for (int t = 0; t < 3; ++t)
+#pragma unroll
+              for (int kk = 0; kk < kBK / 16; ++kk) {
+                const uint64_t ad = sw128_desc(pa + kAp[t] * kPPlaneB + kk * 32);
+                const uint64_t bd = sw128_desc(vb + kBp[t] * kVPlaneB + kk * 32);
+                mma_f16<kIdescO>(tmem, ad, bd, (j > 0 || t > 0 || kk > 0) ? 1u : 0u);
+              }
+          }
+          mma_commit(&c.p_empty);
+          mma_commit(&c.v_empty[st]);
+          ++vn;
+        }
+        if (gi + 2 < G) {
+          ok = ok && mbar_wait(&c.s_empty[gi & 1], (gi >> 1) & 1);
+          fence_after();
+          issue_s(gi + 2);
+        }
+      }
+      mma_commit(&c.o_full);
+    }
+  } else {
+    // ---- softmax warps: thread = one query row, 32 keys of each tile
+    const int quarter = warp & 3;        // the TMEM lanes this warp may access
+    const int half = (warp - 2) >> 2;    // key half of each tile
+    const int r = quarter * 32 + lane;
+    const int qrow = q0 + r;
+    const uint32_t lane_addr = tmem + ((uint32_t)(quarter * 32) << 16);
+    bool ok = true;
+    uint32_t v[32];
+    // pass 1: row maximum of score * scaling over keys <= qrow
+    float m = -1.0e30f;
+    for (int gi = 0; gi < T; ++gi) {
+      ok = ok && mbar_wait(&c.s_full[gi & 1], (gi >> 1) & 1);
+      fence_after();
+      if (ok) tmem_ld32(lane_addr + kColS + 64 * (gi & 1) + 32 * half, v);
+      fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&c.s_empty[gi & 1]);
+      const int kb = gi * kBK + 32 * half;
+#pragma unroll
+      for (int i = 0; i < 32; ++i) {
+        const float ss = __fmul_rn(__uint_as_float(v[i]), kAttentionScaling);
+        if (kb + i <= qrow && ss > m) m = ss;
+      }
+    }
+    c.xch[half][r] = m;
+    named_sync(kBarSoft, kSoftThreads);
+    {
+      const float m0 = c.xch[0][r], m1 = c.xch[1][r];
+      m = m1 > m0 ? m1 : m0;
+    }
+    // pass 2: weights, denominator, and the fp16 (hi, lo) weight tiles for O += P V
+    float den = 0.0f;
+    const uint32_t prow = smem_u32(tiles + kOffP) + (uint32_t)((r >> 3) * 1024 + (r & 7) * 128);
+    for (int j = 0; j < T; ++j) {
+      const int gi = T + j;
+      ok = ok && mbar_wait(&c.s_full[gi & 1], (gi >> 1) & 1);
+      fence_after();
+      if (ok) tmem_ld32(lane_addr + kColS + 64 * (gi & 1) + 32 * half, v);
+      fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&c.s_empty[gi & 1]);
+      const int kb = j * kBK + 32 * half;
+      uint32_t ph[16], pl[16];
+#pragma unroll
+      for (int i = 0; i < 32; i += 2) {
+        float e[2];
+#pragma unroll
+        for (int u = 0; u < 2; ++u) {
+          const float ss = __fmul_rn(__uint_as_float(v[i + u]), kAttentionScaling);
+          e[u] = (kb + i + u <= qrow) ? approx_exp_finite(__fsub_rn(ss, m)) : 0.0f;
+          den = __fadd_rn(den, e[u]);
+        }
+        const __half h0 = __float2half_rn(e[0]), h1 = __float2half_rn(e[1]);
+        ph[i >> 1] = (uint32_t)__half_as_ushort(h0) | ((uint32_t)__half_as_ushort(h1) << 16);
+        pl[i >> 1] = pack_half2(__fsub_rn(e[0], __half2float(h0)), __fsub_rn(e[1], __half2float(h1)));
+      }
+      if (j > 0) ok = ok && mbar_wait(&c.p_empty, (j - 1) & 1);
+#pragma unroll
+      for (int ch = 0; ch < 4; ++ch) {
+        const uint32_t off = (uint32_t)((((4 * half + ch) ^ (r & 7))) << 4);
+        asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(prow + off), "r"(ph[4 * ch]),
+                     "r"(ph[4 * ch + 1]), "r"(ph[4 * ch + 2]), "r"(ph[4 * ch + 3])
+                     : "memory");
+        asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(prow + kPPlaneB + off), "r"(pl[4 * ch]),
+                     "r"(pl[4 * ch + 1]), "r"(pl[4 * ch + 2]), "r"(pl[4 * ch + 3])
+                     : "memory");
+      }
+      fence_async_smem();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&c.p_full);
+    }
+    // denominator of the row: the two key halves
+    named_sync(kBarSoft, kSoftThreads);
+    c.xch[half][r] = den;
+    named_sync(kBarSoft, kSoftThreads);
+    den = __fadd_rn(c.xch[0][r], c.xch[1][r]);
+    const float inv = den > 0.0f ? __fdiv_rn(1.0f, den) : 0.0f;
+    ok = ok && mbar_wait(&c.o_full, 0);
+    fence_after();
+#pragma unroll
+    for (int part = 0; part < 2; ++part) {
+      if (ok) tmem_ld32(lane_addr + 64 * half + 32 * part, v);
+      if (ok && qrow < S) {
+        float4* dst = reinterpret_cast<float4*>(ctx + (size_t)qrow * kHidden + h * kHeadDim + 64 * half + 32 * part);
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+          dst[i] = make_float4(__fmul_rn(__uint_as_float(v[4 * i]), inv), __fmul_rn(__uint_as_float(v[4 * i + 1]), inv),
+                               __fmul_rn(__uint_as_float(v[4 * i + 2]), inv),
+                               __fmul_rn(__uint_as_float(v[4 * i + 3]), inv));
+      }
+    }
+  }
+  fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    fence_after();
+    tmem_dealloc(tmem, kTmemColsA);
+  }
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn_a() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
+}
+
+// 3D fp16 map [d2][d1][d0] (d0 contiguous), row stride s1 bytes, plane stride s2 bytes; box b0 x b1 x 1,
+// 128-byte swizzle, zero fill outside the extents.
+bool make_map3(CUtensorMap* m, const void* base, uint64_t d0, uint64_t d1, uint64_t s1, uint64_t s2, uint32_t b0,
+               uint32_t b1) {
+  auto fn = encode_fn_a();
+  if (!fn) return false;
+  cuuint64_t dims[3] = {(cuuint64_t)d0, (cuuint64_t)d1, 2};
+  cuuint64_t strides[2] = {(cuuint64_t)s1, (cuuint64_t)s2};
+  cuuint32_t box[3] = {b0, b1, 1};
+  cuuint32_t es[3] = {1, 1, 1};
+  return fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<void*>(base), dims, strides, box, es,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+size_t round256(size_t b) { return (b + 255) / 256 * 256; }
+int pad64(int S) { return (S + 63) / 64 * 64; }
+
+}  // namespace
+
+size_t prefill_attn_tc_scratch_bytes(int S) {
+  return 256 + round256((size_t)2 * S * kHidden * 2) + round256((size_t)2 * S * kKvWidth * 2) +
+         round256((size_t)2 * kKvWidth * pad64(S) * 2);
+}
+
+cudaError_t launch_prefill_attention_tc(const float* q, const float* k_cache, const float* v_cache, int S, float* ctx,
+                                        void* scratch, size_t scratch_bytes, cudaStream_t s) {
+  if (S < 1 || !scratch || scratch_bytes < prefill_attn_tc_scratch_bytes(S) ||
+      (reinterpret_cast<uintptr_t>(scratch) & 255) || (reinterpret_cast<uintptr_t>(q) & 15) ||
+      (reinterpret_cast<uintptr_t>(k_cache) & 15))
+    return cudaErrorInvalidValue;
+  const int Spad = pad64(S);
+  uint8_t* base = static_cast<uint8_t*>(scratch);
+  int* flag = reinterpret_cast<int*>(base);
+  __half* qp = reinterpret_cast<__half*>(base + 256);
+  __half* kp = reinterpret_cast<__half*>(base + 256 + round256((size_t)2 * S * kHidden * 2));
+  __half* vt = reinterpret_cast<__half*>(reinterpret_cast<uint8_t*>(kp) + round256((size_t)2 * S * kKvWidth * 2));
+  CUtensorMap qmap, kmap, vmap;
+  if (!make_map3(&qmap, qp, kHidden, (uint64_t)S, kHidden * 2, (uint64_t)S * kHidden * 2, 64, kBQ) ||
+      !make_map3(&kmap, kp, kKvWidth, (uint64_t)S, kKvWidth * 2, (uint64_t)S * kKvWidth * 2, 64, kBK) ||
+      !make_map3(&vmap, vt, (uint64_t)S, kKvWidth, (uint64_t)Spad * 2, (uint64_t)kKvWidth * Spad * 2, kBK, kHeadDim))
+    return cudaErrorInvalidValue;
+  cudaError_t e = cudaMemsetAsync(flag, 0, sizeof(int), s);
+  if (e != cudaSuccess) return e;
+  const int nvt = (Spad / 64) * 4;
+  const size_t elems4 = ((size_t)S * (kHidden + kKvWidth)) / 4;
+  const int nqk = (int)std::min<size_t>((elems4 + 255) / 256, 148 * 8);
+  attn_split_kernel<<<nvt + nqk, 256, 0, s>>>(q, k_cache, v_cache, S, Spad, nvt, qp, kp, vt, flag);
+  if ((e = cudaGetLastError()) != cudaSuccess) return e;
+  static std::mutex mu;
+  static unsigned long long attr_set = 0;
+  int dev = 0;
+  if ((e = cudaGetDevice(&dev)) != cudaSuccess) return e;
+  {
+    std::lock_guard<std::mutex> lock(mu);
+    if (dev < 64 && !((attr_set >> dev) & 1ull)) {
+      if ((e = cudaFuncSetAttribute(attn_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemA)) !=
+          cudaSuccess)
+        return e;
+      attr_set |= 1ull << dev;
+    }
+  }
+  attn_tc_kernel<<<dim3((S + kBQ - 1) / kBQ, kHeads), kThreadsA, kSmemA, s>>>(qmap, kmap, vmap, S, flag, ctx);
+  if ((e = cudaGetLastError()) != cudaSuccess) return e;
+  // values outside the fp16 split: the CUDA-core kernel computes the context (it returns at once otherwise)
+  return launch_prefill_attention_gated(q, k_cache, v_cache, S, ctx, flag, s);
+}
+
+unsigned attn_tc_kernel_error(bool reset) {
+  unsigned v = 0;
+  if (cudaMemcpyFromSymbol(&v, g_kernel_error, sizeof(v)) != cudaSuccess) return 0xFFFFFFFFu;
+  if (reset && v) {
+    const unsigned z = 0;
+    cudaMemcpyToSymbol(g_kernel_error, &z, sizeof(z));
+  }
+  return v;
+}
+
+}  // namespace qb

@@ -17,6 +17,7 @@
 #include <vector>
 
 #include "../../include/qwen_b200_engine.h"
+#include "attention_tc.h"
 #include "decode_stack.h"
 #include "qgemm.h"
 #include "lmhead.h"
@@ -128,6 +129,9 @@ struct qwen_engine {
   int* p_tokens = nullptr;
   int8_t* p_planes = nullptr;  // W8 prefill: digit planes [3][Spad][8960] and steps [Spad]
   float* p_steps = nullptr;
+  void* p_attn = nullptr;      // tensor-core prefill attention scratch (fp16 operand planes)
+  size_t p_attn_bytes = 0;
+  bool use_attn_tc = true;
   // options
   bool use_graphs = true, use_pdl = true, dump_hidden = false, keep_logits = false, prefetch = true;
   std::map<long long, cudaGraphExec_t> graphs;
@@ -253,6 +257,10 @@ int ensure_prefill_buffers(qwen_engine* e, int n) {
   E_TRY(dalloc(&e->p_v, (size_t)cap * kKvWidth));
   cudaFree(e->p_tokens);
   E_TRY(dalloc(&e->p_tokens, (size_t)cap));
+  cudaFree(e->p_attn);
+  e->p_attn = nullptr;
+  e->p_attn_bytes = prefill_attn_tc_scratch_bytes(cap);
+  E_TRY(cudaMalloc(&e->p_attn, e->p_attn_bytes));
   if (e->wbits == 8) {
     cudaFree(e->p_planes);
     cudaFree(e->p_steps);
@@ -639,6 +647,7 @@ void qwen_engine_destroy(qwen_engine* e) {
   cudaFree(e->lm.planes);
   cudaFree(e->p_planes);
   cudaFree(e->p_steps);
+  cudaFree(e->p_attn);
   for (cudaEvent_t ev : e->kev)
     if (ev) cudaEventDestroy(ev);
   for (cudaEvent_t ev : e->bev) cudaEventDestroy(ev);
@@ -712,6 +721,8 @@ int qwen_engine_set_option(qwen_engine* e, const char* name, long long value) {
     e->use_lm_tc = value != 0;
     for (auto& kv : e->graphs) cudaGraphExecDestroy(kv.second);
     e->graphs.clear();
+  } else if (n == "prefill_attn_tc") {
+    e->use_attn_tc = value != 0;
   } else if (n == "batched") {
     e->use_batched = value != 0;
   } else if (n == "stack") {
@@ -756,7 +767,11 @@ int qwen_engine_prefill(qwen_engine* e, int slot, const int32_t* tokens, int n, 
     } else {
       E_TRY(launch_prefill_qkv(e->wbits, L, e->p_xn, n, e->rope_pre_cos, e->rope_pre_sin, e->p_q, e->p_k, e->p_v, s));
     }
-    E_TRY(launch_prefill_attention(e->p_q, e->p_k, e->p_v, n, e->p_ctx, s));
+    if (e->use_attn_tc) {
+      E_TRY(launch_prefill_attention_tc(e->p_q, e->p_k, e->p_v, n, e->p_ctx, e->p_attn, e->p_attn_bytes, s));
+    } else {
+      E_TRY(launch_prefill_attention(e->p_q, e->p_k, e->p_v, n, e->p_ctx, s));
+    }
     if (tc) {
       E_TRY(tgemm_digitize(e->p_ctx, dp, s));
       E_TRY(tgemm_o(L, dp, e->p_a, s));

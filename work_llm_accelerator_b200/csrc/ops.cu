@@ -1,9 +1,11 @@
 // Device-pointer operator API (include/qwen_b200_ops.h): hot-path kernels on caller-owned GPU buffers.
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <mutex>
 
 #include "../../include/qwen_b200_ops.h"
+#include "attention_tc.h"
 #include "qgemm.h"
 #include "tgemm.h"
 #include "qwen_kernels.cuh"
@@ -170,6 +172,70 @@ extern "C" int qwen_b200_w8_digit_planes(const signed char* codes, int rows, int
   if (steps) cudaFreeAsync(steps, s);
   if (e != cudaSuccess) {
     set_error("qwen_b200_w8_digit_planes: %s", cudaGetErrorString(e));
+    return kStatusCuda;
+  }
+  return 0;
+}
+
+extern "C" int qwen_b200_prefill_attention(const float* q, const float* k_cache, const float* v_cache, int seq_len,
+                                           float* context, int mode, void* stream) {
+  using namespace qb;
+  if (!q || !k_cache || !v_cache || !context || seq_len <= 0 || seq_len > kMaxSeq || (mode != 0 && mode != 1) ||
+      (reinterpret_cast<uintptr_t>(q) & 15) || (reinterpret_cast<uintptr_t>(k_cache) & 15) ||
+      (reinterpret_cast<uintptr_t>(context) & 15)) {
+    set_error("qwen_b200_prefill_attention: null buffer, seq_len %d outside 1..%d, mode %d not 0/1, or q / k_cache / "
+              "context not 16-byte aligned",
+              seq_len, kMaxSeq, mode);
+    return kStatusInvalid;
+  }
+  if (!device_accessible(q) || !device_accessible(k_cache) || !device_accessible(v_cache) ||
+      !device_accessible(context)) {
+    set_error("qwen_b200_prefill_attention: every buffer must be device (or managed) memory");
+    return kStatusInvalid;
+  }
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  cudaError_t e = cudaSuccess;
+  if (mode == 1) {
+    e = launch_prefill_attention(q, k_cache, v_cache, seq_len, context, s);
+  } else {
+    void* scratch = nullptr;
+    const size_t bytes = prefill_attn_tc_scratch_bytes(seq_len);
+    e = cudaMallocAsync(&scratch, bytes, s);
+    if (e == cudaSuccess) e = launch_prefill_attention_tc(q, k_cache, v_cache, seq_len, context, scratch, bytes, s);
+    if (scratch) cudaFreeAsync(scratch, s);
+  }
+  if (e != cudaSuccess) {
+    set_error("qwen_b200_prefill_attention: %s", cudaGetErrorString(e));
+    return kStatusCuda;
+  }
+  return 0;
+}
+
+namespace qb {
+namespace {
+__global__ void approx_exp_kernel(const float* __restrict__ x, float* __restrict__ y, long long n) {
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x)
+    y[i] = approx_exp_finite(x[i]);
+}
+}  // namespace
+}  // namespace qb
+
+extern "C" int qwen_b200_prefill_approx_exp(const float* x, float* y, long long n, void* stream) {
+  using namespace qb;
+  if (!x || !y || n < 0) {
+    set_error("qwen_b200_prefill_approx_exp: null buffer or negative n");
+    return kStatusInvalid;
+  }
+  if (!device_accessible(x) || !device_accessible(y)) {
+    set_error("qwen_b200_prefill_approx_exp: every buffer must be device (or managed) memory");
+    return kStatusInvalid;
+  }
+  if (n == 0) return 0;
+  const long long blocks = std::min<long long>((n + 255) / 256, 148 * 16);
+  approx_exp_kernel<<<(unsigned)blocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(x, y, n);
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) {
+    set_error("qwen_b200_prefill_approx_exp: %s", cudaGetErrorString(e));
     return kStatusCuda;
   }
   return 0;

@@ -241,6 +241,47 @@ __device__ __forceinline__ float approx_exp(float value) {
   return series > 0.0f ? series : 0.0f;
 }
 
+// Correctly rounded x / 3 and x / 5 without a division instruction: q = RN(x * RN(1/d)), the remainder
+// x - d q is exact under one FMA, and RN(q + r * RN(1/d)) is the correctly rounded quotient (Markstein's
+// correction step, P. Markstein, IBM J. Res. Dev. 34(1), 1990). Checked exhaustively against IEEE division
+// over every finite fp32 x: identical except x = -0, which returns +0.
+__device__ __forceinline__ float div_by_3_rn(float x) {
+  const float c = 0x1.555556p-2f;  // RN(1/3)
+  const float q = __fmul_rn(x, c);
+  return __fmaf_rn(__fmaf_rn(-q, 3.0f, x), c, q);
+}
+__device__ __forceinline__ float div_by_5_rn(float x) {
+  const float c = 0x1.99999ap-3f;  // RN(1/5)
+  const float q = __fmul_rn(x, c);
+  return __fmaf_rn(__fmaf_rn(-q, 5.0f, x), c, q);
+}
+
+// approx_exp with its six divisions by the term degree replaced by exact equivalents: /1 and the
+// power-of-two degrees are exact multiplications, /3 and /5 use the correction step above, and
+// /6 = (x * 0.5) / 3 (x * 0.5 is exact unless |x| < 2^-125, where the sixth term underflows to zero in
+// both forms). Same result as approx_exp for every finite input (the zero sign of a quotient cannot reach
+// the series, whose first term is 1); for +-inf use approx_exp.
+__device__ __forceinline__ float approx_exp_finite(float value) {
+  if (value <= -16.0f) return 0.0f;
+  int half_steps = 0;
+  float scaled = value;
+  while (scaled < -1.0f) {
+    scaled = __fmul_rn(scaled, 0.5f);
+    ++half_steps;
+  }
+  const float half = __fmul_rn(scaled, 0.5f);
+  const float q[6] = {scaled, half, div_by_3_rn(scaled), __fmul_rn(scaled, 0.25f), div_by_5_rn(scaled),
+                      div_by_3_rn(half)};
+  float term = 1.0f, series = 1.0f;
+#pragma unroll
+  for (int i = 0; i < 6; ++i) {
+    term = __fmul_rn(term, q[i]);
+    series = __fadd_rn(series, term);
+  }
+  for (int i = 0; i < half_steps; ++i) series = __fmul_rn(series, series);
+  return series > 0.0f ? series : 0.0f;
+}
+
 // Round-to-nearest-even to bf16, kept in fp32 (verification/reference_wrapper_backend.py:40-46).
 __device__ __forceinline__ float round_bf16(float x) {
   uint32_t b = __float_as_uint(x);

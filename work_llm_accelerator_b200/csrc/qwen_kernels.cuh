@@ -75,6 +75,9 @@ cudaError_t launch_prefill_down(int wbits, const LayerDev& L, const float* h, co
 // Causal two-pass GQA attention with approx_exp (scores and max bit-identical to the reference).
 cudaError_t launch_prefill_attention(const float* q, const float* k_cache, const float* v_cache, int S, float* ctx,
                                      cudaStream_t s);
+// Same kernel, run only when *only_if != 0 (read on the device; the CTAs return at once otherwise).
+cudaError_t launch_prefill_attention_gated(const float* q, const float* k_cache, const float* v_cache, int S,
+                                           float* ctx, const int* only_if, cudaStream_t s);
 
 // --- misc ----------------------------------------------------------------------------------------
 // Deterministic synthetic layer parameters written straight into a device DDR image of `wbits` layout.

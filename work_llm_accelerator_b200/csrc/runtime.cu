@@ -18,6 +18,7 @@
 #include <string>
 #include <vector>
 
+#include "attention_tc.h"
 #include "decode_stack.h"
 #include "qgemm.h"
 #include "lmhead.h"
@@ -62,6 +63,7 @@ struct Ctx {
   // int8 tensor-core projections (wbits 8): split-K scratch (decode), digit planes and steps (prefill)
   QgemmScratch qsc{nullptr, nullptr};
   Buf planes, psteps;
+  Buf attn;  // tensor-core prefill attention scratch
   // zero-weight layer for the stub entry points
   Buf zw, zs;
   LayerPtrs zero{};
@@ -359,8 +361,10 @@ int run_prefill(int wbits, const LayerPtrs& L, bool attention, bool mlp, const f
                                 (const float*)c.rope_pre_sin.p, (float*)c.q.p, (float*)c.kc.p, (float*)c.vc.p,
                                 c.stream));
     }
-    QB_TRY(launch_prefill_attention((const float*)c.q.p, (const float*)c.kc.p, (const float*)c.vc.p, S,
-                                    (float*)c.ctx.p, c.stream));
+    const size_t ab = prefill_attn_tc_scratch_bytes(S);
+    QB_TRY(ensure(c.attn, ab));
+    QB_TRY(launch_prefill_attention_tc((const float*)c.q.p, (const float*)c.kc.p, (const float*)c.vc.p, S,
+                                       (float*)c.ctx.p, c.attn.p, ab, c.stream));
     if (tc) {
       QB_TRY(tgemm_digitize((const float*)c.ctx.p, dp, c.stream));
       QB_TRY(tgemm_o(D, dp, (float*)c.a.p, c.stream));
@@ -431,7 +435,7 @@ int qwen_b200_set_prefill_seq_capacity(int capacity) {
 unsigned qwen_b200_kernel_error(int reset) {
   return qb::gemv_kernel_error(reset != 0) | qb::qgemm_kernel_error(reset != 0) |
          qb::stack::decode_stack_kernel_error(reset != 0) | qb::tgemm_kernel_error(reset != 0) |
-         qb::lm_head_kernel_error(reset != 0);
+         qb::lm_head_kernel_error(reset != 0) | qb::attn_tc_kernel_error(reset != 0);
 }
 
 int qwen_b200_device_count(void) {

@@ -72,6 +72,12 @@ def core_lib() -> ctypes.CDLL:
         lib.qwen_b200_w8_digit_planes.argtypes = [ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_void_p,
                                                   ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p]
         lib.qwen_b200_w8_digit_planes.restype = ctypes.c_int
+        lib.qwen_b200_prefill_attention.argtypes = [ctypes.c_void_p] * 3 + [ctypes.c_int, ctypes.c_void_p,
+                                                                             ctypes.c_int, ctypes.c_void_p]
+        lib.qwen_b200_prefill_attention.restype = ctypes.c_int
+        lib.qwen_b200_prefill_approx_exp.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_longlong,
+                                                     ctypes.c_void_p]
+        lib.qwen_b200_prefill_approx_exp.restype = ctypes.c_int
         lib.qwen_b200_kernel_error.argtypes = [ctypes.c_int]
         lib.qwen_b200_kernel_error.restype = ctypes.c_uint
         _core = lib
@@ -398,6 +404,21 @@ def w8_digit_products(codes_ptr: int, rows: int, k: int, x_ptr: int, n_tokens: i
 def kernel_error(reset: bool = False) -> int:
     """Error flag of the streaming kernels on the current device (1 = a bounded pipeline wait gave up)."""
     return int(core_lib().qwen_b200_kernel_error(1 if reset else 0))
+
+
+def prefill_attention(q_ptr: int, k_ptr: int, v_ptr: int, seq_len: int, ctx_ptr: int, mode: int = 0,
+                      stream: int = 0) -> None:
+    """Device-pointer causal prefill attention (include/qwen_b200_ops.h); mode 0 tensor cores, 1 CUDA cores."""
+    st = core_lib().qwen_b200_prefill_attention(q_ptr, k_ptr, v_ptr, seq_len, ctx_ptr, mode, stream or None)
+    if st != 0:
+        raise EngineError(f"qwen_b200_prefill_attention failed with status {st}: {last_error()}")
+
+
+def prefill_approx_exp(x_ptr: int, y_ptr: int, n: int, stream: int = 0) -> None:
+    """y = the prefill softmax exponential of x, as the tensor-core attention evaluates it (device buffers)."""
+    st = core_lib().qwen_b200_prefill_approx_exp(x_ptr, y_ptr, n, stream or None)
+    if st != 0:
+        raise EngineError(f"qwen_b200_prefill_approx_exp failed with status {st}: {last_error()}")
 
 
 def w8_digit_planes(codes_ptr: int, rows: int, k: int, x_ptr: int, n_tokens: int, acc_ptr: int, step_ptr: int,
