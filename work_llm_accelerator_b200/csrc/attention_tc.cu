@@ -14,7 +14,7 @@
 // Work split. CTA = (128 queries, one query head); keys in tiles of 64. Warp 0 issues the TMA loads
 // (Q once, then K tiles for both passes and transposed V tiles for pass 2, two stages each), warp 1 issues
 // the MMAs (S = Q K^T into one of two TMEM score buffers; O += P V into the TMEM context accumulator), and
-// eight softmax warps own one query row and 32 keys of each tile per thread: they read the scores from
+// sixteen softmax warps own one query row and 16 keys of each tile per thread: they read the scores from
 // TMEM, compute the weights, and write them as fp16 (hi, lo) tiles to shared memory for the P V product.
 // Query tiles are launched heaviest (longest causal prefix) first.
 #include <cuda.h>
@@ -43,8 +43,10 @@ constexpr int kOffK = kOffQ + 2 * kQPlaneB;      // two stages of (hi, lo)
 constexpr int kOffV = kOffK + 2 * 2 * kKPlaneB;  // two stages of (hi, lo)
 constexpr int kOffP = kOffV + 2 * 2 * kVPlaneB;  // (hi, lo)
 constexpr int kTileBytes = kOffP + 2 * kPPlaneB;  // 224 KB
-constexpr int kSoftWarps = 8;
+constexpr int kSoftWarps = 16;                  // four per TMEM lane quarter
 constexpr int kSoftThreads = 32 * kSoftWarps;
+constexpr int kKeyGroups = kSoftWarps / 4;      // key groups of a tile (one per warp of a lane quarter)
+constexpr int kKeysPer = kBK / kKeyGroups;      // keys of a tile per softmax thread
 constexpr int kThreadsA = 64 + kSoftThreads;
 constexpr int kBarSoft = 1;  // named barrier of the softmax warps
 constexpr uint32_t kTmemColsA = 256;  // context accumulator: columns 0..127; score buffers: 128.., 192..
@@ -56,7 +58,6 @@ constexpr float kSplitLimit = 32768.0f;
 struct ACtl {
   uint64_t q_full, k_full[2], k_empty[2], v_full[2], v_empty[2], s_full[2], s_empty[2], p_full, p_empty, o_full;
   uint32_t tmem_base;
-  float xch[2][kBQ];  // per-row exchange between the two key halves (max, then denominator)
 };
 
 constexpr size_t kSmemA = 1024 + (size_t)kTileBytes + sizeof(ACtl);
@@ -127,8 +128,22 @@ __global__ void __launch_bounds__(256) attn_split_kernel(const float* __restrict
   if (__syncthreads_or(bad) && threadIdx.x == 0) atomicOr(flag, 1);
 }
 
-__device__ __forceinline__ uint32_t pack_half2(float a, float b) {
-  return (uint32_t)__half_as_ushort(__float2half_rn(a)) | ((uint32_t)__half_as_ushort(__float2half_rn(b)) << 16);
+// N consecutive 32-bit TMEM columns of the warp's 32 lanes (N = 16 or 32).
+template <int N>
+__device__ __forceinline__ void tmem_ld_cols(uint32_t taddr, uint32_t (&v)[N]) {
+  static_assert(N == 16 || N == 32, "columns");
+  if constexpr (N == 32) {
+    tmem_ld32(taddr, v);
+  } else {
+    tmem_ld16(taddr, reinterpret_cast<int(&)[16]>(v));
+  }
+}
+__device__ __forceinline__ void tmem_ld_keys(uint32_t taddr, uint32_t (&v)[kKeysPer]) { tmem_ld_cols<kKeysPer>(taddr, v); }
+
+// (a, b) -> fp16x2 bits, a in the low half (the lower address), one conversion instruction
+__device__ __forceinline__ uint32_t half2_bits(float a, float b) {
+  const __half2 p = __floats2half2_rn(a, b);
+  return *reinterpret_cast<const uint32_t*>(&p);
 }
 
 __global__ void __launch_bounds__(kThreadsA, 1)
@@ -269,36 +284,41 @@ __global__ void __launch_bounds__(kThreadsA, 1)
       mma_commit(&c.o_full);
     }
   } else {
-    // ---- softmax warps: thread = one query row, 32 keys of each tile
-    const int quarter = warp & 3;        // the TMEM lanes this warp may access
-    const int half = (warp - 2) >> 2;    // key half of each tile
+    // ---- softmax warps: thread = one query row, kKeysPer keys of each tile
+    const int quarter = warp & 3;      // the TMEM lanes this warp may access
+    const int kg = (warp - 2) >> 2;    // key group of each tile
     const int r = quarter * 32 + lane;
     const int qrow = q0 + r;
     const uint32_t lane_addr = tmem + ((uint32_t)(quarter * 32) << 16);
+    // per-row exchange between the key groups, in the weight tile's space while no weight tile is live
+    float* xch = reinterpret_cast<float*>(tiles + kOffP);
     bool ok = true;
-    uint32_t v[32];
+    uint32_t v[kKeysPer];
     // pass 1: row maximum of score * scaling over keys <= qrow
     float m = -1.0e30f;
     for (int gi = 0; gi < T; ++gi) {
       ok = ok && mbar_wait(&c.s_full[gi & 1], (gi >> 1) & 1);
       fence_after();
-      if (ok) tmem_ld32(lane_addr + kColS + 64 * (gi & 1) + 32 * half, v);
+      if (ok) tmem_ld_keys(lane_addr + kColS + 64 * (gi & 1) + kKeysPer * kg, v);
       fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&c.s_empty[gi & 1]);
-      const int kb = gi * kBK + 32 * half;
+      const int kb = gi * kBK + kKeysPer * kg;
 #pragma unroll
-      for (int i = 0; i < 32; ++i) {
+      for (int i = 0; i < kKeysPer; ++i) {
         const float ss = __fmul_rn(__uint_as_float(v[i]), kAttentionScaling);
         if (kb + i <= qrow && ss > m) m = ss;
       }
     }
-    c.xch[half][r] = m;
+    xch[kg * kBQ + r] = m;
     named_sync(kBarSoft, kSoftThreads);
-    {
-      const float m0 = c.xch[0][r], m1 = c.xch[1][r];
-      m = m1 > m0 ? m1 : m0;
+    m = xch[r];
+#pragma unroll
+    for (int g2 = 1; g2 < kKeyGroups; ++g2) {
+      const float mg = xch[g2 * kBQ + r];
+      m = mg > m ? mg : m;
     }
+    named_sync(kBarSoft, kSoftThreads);  // every row maximum read before the weight tile is written
     // pass 2: weights, denominator, and the fp16 (hi, lo) weight tiles for O += P V
     float den = 0.0f;
     const uint32_t prow = smem_u32(tiles + kOffP) + (uint32_t)((r >> 3) * 1024 + (r & 7) * 128);
@@ -306,29 +326,34 @@ __global__ void __launch_bounds__(kThreadsA, 1)
       const int gi = T + j;
       ok = ok && mbar_wait(&c.s_full[gi & 1], (gi >> 1) & 1);
       fence_after();
-      if (ok) tmem_ld32(lane_addr + kColS + 64 * (gi & 1) + 32 * half, v);
+      if (ok) tmem_ld_keys(lane_addr + kColS + 64 * (gi & 1) + kKeysPer * kg, v);
       fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&c.s_empty[gi & 1]);
-      const int kb = j * kBK + 32 * half;
-      uint32_t ph[16], pl[16];
+      const int kb = j * kBK + kKeysPer * kg;
+      // e in [0, 1]: hi = e with the low 13 mantissa bits cleared (11 significant bits, an fp16 value for
+      // e >= 2^-14), lo = e - hi (exact), both converted two at a time; below 2^-14 the pair is within 2^-24
+      // of e, against a denominator >= 1.
+      uint32_t ph[kKeysPer / 2], pl[kKeysPer / 2];
+      float e[kKeysPer];
 #pragma unroll
-      for (int i = 0; i < 32; i += 2) {
-        float e[2];
+      for (int i = 0; i < kKeysPer; ++i) {
+        const float x = approx_exp_finite(__fsub_rn(__fmul_rn(__uint_as_float(v[i]), kAttentionScaling), m));
+        e[i] = select_f32(kb + i <= qrow, x, 0.0f);
+      }
 #pragma unroll
-        for (int u = 0; u < 2; ++u) {
-          const float ss = __fmul_rn(__uint_as_float(v[i + u]), kAttentionScaling);
-          e[u] = (kb + i + u <= qrow) ? approx_exp_finite(__fsub_rn(ss, m)) : 0.0f;
-          den = __fadd_rn(den, e[u]);
-        }
-        const __half h0 = __float2half_rn(e[0]), h1 = __float2half_rn(e[1]);
-        ph[i >> 1] = (uint32_t)__half_as_ushort(h0) | ((uint32_t)__half_as_ushort(h1) << 16);
-        pl[i >> 1] = pack_half2(__fsub_rn(e[0], __half2float(h0)), __fsub_rn(e[1], __half2float(h1)));
+      for (int i = 0; i < kKeysPer; ++i) den = __fadd_rn(den, e[i]);
+#pragma unroll
+      for (int i = 0; i < kKeysPer; i += 2) {
+        const float h0 = __uint_as_float(__float_as_uint(e[i]) & 0xFFFFE000u);
+        const float h1 = __uint_as_float(__float_as_uint(e[i + 1]) & 0xFFFFE000u);
+        ph[i >> 1] = half2_bits(h0, h1);
+        pl[i >> 1] = half2_bits(__fsub_rn(e[i], h0), __fsub_rn(e[i + 1], h1));
       }
       if (j > 0) ok = ok && mbar_wait(&c.p_empty, (j - 1) & 1);
 #pragma unroll
-      for (int ch = 0; ch < 4; ++ch) {
-        const uint32_t off = (uint32_t)((((4 * half + ch) ^ (r & 7))) << 4);
+      for (int ch = 0; ch < kKeysPer / 8; ++ch) {
+        const uint32_t off = (uint32_t)((((kg * kKeysPer / 8 + ch) ^ (r & 7))) << 4);
         asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(prow + off), "r"(ph[4 * ch]),
                      "r"(ph[4 * ch + 1]), "r"(ph[4 * ch + 2]), "r"(ph[4 * ch + 3])
                      : "memory");
@@ -340,25 +365,25 @@ __global__ void __launch_bounds__(kThreadsA, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(&c.p_full);
     }
-    // denominator of the row: the two key halves
-    named_sync(kBarSoft, kSoftThreads);
-    c.xch[half][r] = den;
-    named_sync(kBarSoft, kSoftThreads);
-    den = __fadd_rn(c.xch[0][r], c.xch[1][r]);
-    const float inv = den > 0.0f ? __fdiv_rn(1.0f, den) : 0.0f;
+    // every P V product done (the weight tile is free again), then the row denominator over the key groups
     ok = ok && mbar_wait(&c.o_full, 0);
     fence_after();
+    xch[kg * kBQ + r] = den;
+    named_sync(kBarSoft, kSoftThreads);
+    den = xch[r];
 #pragma unroll
-    for (int part = 0; part < 2; ++part) {
-      if (ok) tmem_ld32(lane_addr + 64 * half + 32 * part, v);
-      if (ok && qrow < S) {
-        float4* dst = reinterpret_cast<float4*>(ctx + (size_t)qrow * kHidden + h * kHeadDim + 64 * half + 32 * part);
+    for (int g2 = 1; g2 < kKeyGroups; ++g2) den = __fadd_rn(den, xch[g2 * kBQ + r]);
+    const float inv = den > 0.0f ? __fdiv_rn(1.0f, den) : 0.0f;
+    constexpr int kCols = kHeadDim / kKeyGroups;  // context columns of this thread
+    uint32_t o[kCols];
+    if (ok) tmem_ld_cols<kCols>(lane_addr + kCols * kg, o);
+    if (ok && qrow < S) {
+      float4* dst = reinterpret_cast<float4*>(ctx + (size_t)qrow * kHidden + h * kHeadDim + kCols * kg);
 #pragma unroll
-        for (int i = 0; i < 8; ++i)
-          dst[i] = make_float4(__fmul_rn(__uint_as_float(v[4 * i]), inv), __fmul_rn(__uint_as_float(v[4 * i + 1]), inv),
-                               __fmul_rn(__uint_as_float(v[4 * i + 2]), inv),
-                               __fmul_rn(__uint_as_float(v[4 * i + 3]), inv));
-      }
+      for (int i = 0; i < kCols / 4; ++i)
+        dst[i] = make_float4(__fmul_rn(__uint_as_float(o[4 * i]), inv), __fmul_rn(__uint_as_float(o[4 * i + 1]), inv),
+                             __fmul_rn(__uint_as_float(o[4 * i + 2]), inv),
+                             __fmul_rn(__uint_as_float(o[4 * i + 3]), inv));
     }
   }
   fence_before();

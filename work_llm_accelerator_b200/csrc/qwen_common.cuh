@@ -256,19 +256,26 @@ __device__ __forceinline__ float div_by_5_rn(float x) {
   return __fmaf_rn(__fmaf_rn(-q, 5.0f, x), c, q);
 }
 
-// approx_exp with its six divisions by the term degree replaced by exact equivalents: /1 and the
-// power-of-two degrees are exact multiplications, /3 and /5 use the correction step above, and
-// /6 = (x * 0.5) / 3 (x * 0.5 is exact unless |x| < 2^-125, where the sixth term underflows to zero in
-// both forms). Same result as approx_exp for every finite input (the zero sign of a quotient cannot reach
-// the series, whose first term is 1); for +-inf use approx_exp.
+// p ? a : b as one predicated select (a chain of ?: on data-dependent conditions can compile to branches).
+__device__ __forceinline__ float select_f32(bool p, float a, float b) {
+  float r;
+  asm("{\n.reg .pred q;\nsetp.ne.u32 q, %3, 0;\nselp.f32 %0, %1, %2, q;\n}" : "=f"(r) : "f"(a), "f"(b), "r"((unsigned)p));
+  return r;
+}
+
+// approx_exp in straight-line form (no loops, no branches, so that many independent evaluations interleave):
+// - the halving loop runs while scaled < -1, i.e. h = [v < -1] + [v < -2] + [v < -4] + [v < -8] times for
+//   v > -16, and each halving is exact (|scaled| >= 1 before it), so scaled = v * 2^-h in one exact multiply;
+// - the six divisions by the term degree: /1 and the power-of-two degrees are exact multiplications, /3 and
+//   /5 use the correction step above, and /6 = (x * 0.5) / 3 (x * 0.5 is exact unless |x| < 2^-125, where
+//   the sixth term underflows to zero in both forms);
+// - the h squarings are the same chain of products, selected by the same comparisons.
+// Same result as approx_exp for every finite input (the zero sign of a quotient cannot reach the series,
+// whose first term is 1); for +-inf use approx_exp.
 __device__ __forceinline__ float approx_exp_finite(float value) {
-  if (value <= -16.0f) return 0.0f;
-  int half_steps = 0;
-  float scaled = value;
-  while (scaled < -1.0f) {
-    scaled = __fmul_rn(scaled, 0.5f);
-    ++half_steps;
-  }
+  const bool c1 = value < -1.0f, c2 = value < -2.0f, c4 = value < -4.0f, c8 = value < -8.0f;
+  const int h = (int)c1 + (int)c2 + (int)c4 + (int)c8;
+  const float scaled = __fmul_rn(value, __int_as_float((127 - h) << 23));  // value * 2^-h
   const float half = __fmul_rn(scaled, 0.5f);
   const float q[6] = {scaled, half, div_by_3_rn(scaled), __fmul_rn(scaled, 0.25f), div_by_5_rn(scaled),
                       div_by_3_rn(half)};
@@ -278,8 +285,13 @@ __device__ __forceinline__ float approx_exp_finite(float value) {
     term = __fmul_rn(term, q[i]);
     series = __fadd_rn(series, term);
   }
-  for (int i = 0; i < half_steps; ++i) series = __fmul_rn(series, series);
-  return series > 0.0f ? series : 0.0f;
+  const float s2 = __fmul_rn(series, series), s4 = __fmul_rn(s2, s2), s8 = __fmul_rn(s4, s4),
+              s16 = __fmul_rn(s8, s8);
+  float r = select_f32(c1, s2, series);
+  r = select_f32(c2, s4, r);
+  r = select_f32(c4, s8, r);
+  r = select_f32(c8, s16, r);
+  return select_f32(value <= -16.0f || !(r > 0.0f), 0.0f, r);
 }
 
 // Round-to-nearest-even to bf16, kept in fp32 (verification/reference_wrapper_backend.py:40-46).
