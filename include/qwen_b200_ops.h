@@ -72,7 +72,8 @@ int qwen_b200_prefill_attention(const float* q, const float* k_cache, const floa
 
 /* The prefill softmax exponential as the tensor-core attention evaluates it: y[i] = approx_exp(x[i])
  * (hls/prefill_only/qwen_prefill_attention_kernel.cpp:47-110, degree-6 Taylor series with halving and
- * squaring), for finite x; exposed so that its bit-identity with the reference's function can be checked.
+ * squaring), evaluated without divisions or branches; exposed so that its bit-identity with the reference's
+ * function can be checked.
  * x, y [n] fp32 device memory. */
 int qwen_b200_prefill_approx_exp(const float* x, float* y, long long n, void* stream);
 

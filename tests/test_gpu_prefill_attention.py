@@ -7,8 +7,9 @@ accumulation. Checked here:
   - mode 0 against mode 1 and against a float64 restatement of the reference's algorithm, over ragged
     lengths (tile edges at 64 keys and 128 queries) up to 4096 tokens;
   - the fallback: inputs the fp16 split cannot hold give exactly the CUDA-core result;
-  - the exponential the kernel evaluates (approx_exp with exact divisions by constants) is bit-identical
-    to the reference's approx_exp for every non-positive float above -16 and every positive finite float.
+  - the exponential the kernels evaluate (approx_exp with exact divisions by constants, no branches) is
+    bit-identical to the reference's approx_exp for every float in [-16, 0], every positive finite float,
+    and on samples below -16 and the special values.
 """
 from __future__ import annotations
 
@@ -184,12 +185,21 @@ def test_kernel_exponential_bit_identical_exhaustive(cuda):
 
     rng = np.random.default_rng(5)
     sample = np.concatenate([rng.uniform(-20, 13, 200_000), -np.exp(rng.uniform(-90, 2.8, 50_000)),
-                             [-16.0, -15.999999, -8.0, -4.0, -2.0, -1.0, -0.0, 0.0, 1e-40, -1e-40, 88.0]])
+                             [-16.0, -15.999999, -8.0, -4.0, -2.0, -1.0, -0.0, 0.0, 1e-40, -1e-40, 88.0, 1e30,
+                              -1e30, np.inf, -np.inf, np.nan], -rng.uniform(16, 1e6, 5000)])
     sample = sample.astype(np.float32)
-    t_ref = approx_exp_torch(torch, torch.from_numpy(sample).cuda()).cpu().numpy()
-    assert t_ref.tobytes() == approx_exp_np(sample).tobytes()
-    for x in sample[:: 997]:
-        assert np.float32(qo.approx_exp(float(x))).tobytes() == approx_exp_np(np.array([x]))[0].tobytes()
+    xs = torch.from_numpy(sample).cuda()
+    t_ref = approx_exp_torch(torch, xs).cpu().numpy()
+    with np.errstate(all="ignore"):
+        assert t_ref.tobytes() == approx_exp_np(sample).tobytes()
+    for x in np.concatenate([sample[:: 997], sample[-5021:-5000]]):
+        with np.errstate(all="ignore"):
+            assert np.float32(qo.approx_exp(float(x))).tobytes() == approx_exp_np(np.array([x]))[0].tobytes(), x
+    # the kernel's function on the same sample, special values included (inf, -inf, nan, below -16)
+    y = torch.empty_like(xs)
+    host.prefill_approx_exp(xs.data_ptr(), y.data_ptr(), xs.numel(), torch.cuda.current_stream().cuda_stream)
+    torch.cuda.synchronize()
+    assert y.cpu().numpy().tobytes() == t_ref.tobytes()
 
     def check(lo_bits: int, hi_bits: int) -> None:
         chunk = 1 << 26

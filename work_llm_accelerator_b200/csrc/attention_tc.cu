@@ -338,7 +338,7 @@ __global__ void __launch_bounds__(kThreadsA, 1)
       float e[kKeysPer];
 #pragma unroll
       for (int i = 0; i < kKeysPer; ++i) {
-        const float x = approx_exp_finite(__fsub_rn(__fmul_rn(__uint_as_float(v[i]), kAttentionScaling), m));
+        const float x = approx_exp_fast(__fsub_rn(__fmul_rn(__uint_as_float(v[i]), kAttentionScaling), m));
         e[i] = select_f32(kb + i <= qrow, x, 0.0f);
       }
 #pragma unroll

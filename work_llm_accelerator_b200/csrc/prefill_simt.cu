@@ -171,7 +171,7 @@ __global__ void __launch_bounds__(256) prefill_gemm_kernel(GemmArgs a) {
         const int j = tile_row<EPI>(tn, tx + 16 * jp);
         const float gv = a.scale[j] * acc[i][jp];
         const float uv = a.scale[kInter + j] * acc[i][jp + 2];
-        const float silu = __fdiv_rn(gv, __fadd_rn(1.0f, approx_exp(-gv)));
+        const float silu = __fdiv_rn(gv, __fadd_rn(1.0f, approx_exp_fast(-gv)));
         a.out[(size_t)t * kInter + j] = __fmul_rn(silu, uv);
       }
     } else {

@@ -270,9 +270,10 @@ __device__ __forceinline__ float select_f32(bool p, float a, float b) {
 //   /5 use the correction step above, and /6 = (x * 0.5) / 3 (x * 0.5 is exact unless |x| < 2^-125, where
 //   the sixth term underflows to zero in both forms);
 // - the h squarings are the same chain of products, selected by the same comparisons.
-// Same result as approx_exp for every finite input (the zero sign of a quotient cannot reach the series,
-// whose first term is 1); for +-inf use approx_exp.
-__device__ __forceinline__ float approx_exp_finite(float value) {
+// Same result as approx_exp for every input: finite ones (the zero sign of a quotient cannot reach the series,
+// whose first term is 1), -inf and nan (0), and +inf (the series diverges to +inf; the correction steps
+// would give nan, so it is selected explicitly).
+__device__ __forceinline__ float approx_exp_fast(float value) {
   const bool c1 = value < -1.0f, c2 = value < -2.0f, c4 = value < -4.0f, c8 = value < -8.0f;
   const int h = (int)c1 + (int)c2 + (int)c4 + (int)c8;
   const float scaled = __fmul_rn(value, __int_as_float((127 - h) << 23));  // value * 2^-h
@@ -291,7 +292,8 @@ __device__ __forceinline__ float approx_exp_finite(float value) {
   r = select_f32(c2, s4, r);
   r = select_f32(c4, s8, r);
   r = select_f32(c8, s16, r);
-  return select_f32(value <= -16.0f || !(r > 0.0f), 0.0f, r);
+  r = select_f32(value <= -16.0f || !(r > 0.0f), 0.0f, r);
+  return select_f32(value > 3.402823466e38f, value, r);
 }
 
 // Round-to-nearest-even to bf16, kept in fp32 (verification/reference_wrapper_backend.py:40-46).

@@ -301,7 +301,7 @@ __global__ void __launch_bounds__(kThreadsT, 1)
           for (int c = cb; c < cb + kChunkN / 2; ++c) {
             const int n = n0 + c0 + c;
             const float gv = sm.ys[gr][c], uv = sm.ys[gr + 64][c];
-            const float silu = __fdiv_rn(gv, __fadd_rn(1.0f, a.decode ? expf(-gv) : approx_exp(-gv)));
+            const float silu = __fdiv_rn(gv, __fadd_rn(1.0f, a.decode ? expf(-gv) : approx_exp_fast(-gv)));
             if (n < a.S) a.out[(size_t)n * kInter + mtile * 64 + gr] = __fmul_rn(silu, uv);
           }
           named_sync(kBarT, kEpiT);
