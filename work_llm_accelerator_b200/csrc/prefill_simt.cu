@@ -15,25 +15,52 @@ namespace qb {
 namespace {
 
 // ---- RMSNorm -------------------------------------------------------------------------------------
-__global__ void __launch_bounds__(32) prefill_rmsnorm_kernel(const float* __restrict__ x, const float* __restrict__ w,
-                                                             int S, float* __restrict__ xn) {
-  __shared__ float inv_s[32];
-  const int t0 = blockIdx.x * 32, lane = threadIdx.x;
-  const int t = t0 + lane;
-  if (t < S) {
-    const float* row = x + (size_t)t * kHidden;
-    float ms = 0.0f;
-    for (int d = 0; d < kHidden; ++d) ms = __fadd_rn(ms, __fmul_rn(row[d], row[d]));
-    ms = __fdiv_rn(ms, (float)kHidden);
-    inv_s[lane] = __fdiv_rn(1.0f, approx_sqrt(__fadd_rn(ms, kEps)));
+// CTA = 32 tokens. The reference's sum of squares is one serial fp32 chain per token (kept bit for bit), so
+// warp 0 runs the 32 chains (thread = token) out of shared memory while all four warps stage the next
+// 128-column chunk of the 32 rows with coalesced loads; then every thread writes normalised columns.
+constexpr int kNormTok = 32, kNormCols = 128, kNormPad = kNormCols + 1;
+
+__global__ void __launch_bounds__(128) prefill_rmsnorm_kernel(const float* __restrict__ x, const float* __restrict__ w,
+                                                              int S, float* __restrict__ xn) {
+  __shared__ float tile[2][kNormTok][kNormPad];
+  __shared__ float inv_s[kNormTok];
+  const int t0 = blockIdx.x * kNormTok, tid = threadIdx.x;
+  const int n = min(kNormTok, S - t0);
+  auto stage = [&](int c, int buf) {
+    for (int i = tid; i < kNormTok * (kNormCols / 4); i += 128) {
+      const int rr = i / (kNormCols / 4), f = i % (kNormCols / 4);
+      float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (rr < n) v = *reinterpret_cast<const float4*>(x + (size_t)(t0 + rr) * kHidden + kNormCols * c + 4 * f);
+      float* dst = &tile[buf][rr][4 * f];
+      dst[0] = v.x;
+      dst[1] = v.y;
+      dst[2] = v.z;
+      dst[3] = v.w;
+    }
+  };
+  stage(0, 0);
+  __syncthreads();
+  float ms = 0.0f;
+  constexpr int kChunks = kHidden / kNormCols;
+  for (int c = 0; c < kChunks; ++c) {
+    if (c + 1 < kChunks) stage(c + 1, (c + 1) & 1);
+    if (tid < kNormTok) {
+      const float* row = tile[c & 1][tid];
+#pragma unroll 8
+      for (int d = 0; d < kNormCols; ++d) ms = __fadd_rn(ms, __fmul_rn(row[d], row[d]));
+    }
+    __syncthreads();
   }
-  __syncwarp();
-  const int n = min(32, S - t0);
+  if (tid < n) {
+    ms = __fdiv_rn(ms, (float)kHidden);
+    inv_s[tid] = __fdiv_rn(1.0f, approx_sqrt(__fadd_rn(ms, kEps)));
+  }
+  __syncthreads();
   for (int i = 0; i < n; ++i) {
     const float inv = inv_s[i];
     const float* row = x + (size_t)(t0 + i) * kHidden;
     float* out = xn + (size_t)(t0 + i) * kHidden;
-    for (int d = lane; d < kHidden; d += 32) out[d] = __fmul_rn(__fmul_rn(row[d], inv), w[d]);
+    for (int d = tid; d < kHidden; d += 128) out[d] = __fmul_rn(__fmul_rn(row[d], inv), w[d]);
   }
 }
 
@@ -198,7 +225,7 @@ cudaError_t run_gemm(const GemmArgs& a, int n_tiles, cudaStream_t s) {
 }  // namespace
 
 cudaError_t launch_prefill_rmsnorm(const float* x, const float* w, int S, float* xn, cudaStream_t s) {
-  prefill_rmsnorm_kernel<<<(S + 31) / 32, 32, 0, s>>>(x, w, S, xn);
+  prefill_rmsnorm_kernel<<<(S + kNormTok - 1) / kNormTok, 128, 0, s>>>(x, w, S, xn);
   return cudaGetLastError();
 }
 
