@@ -7,11 +7,13 @@
 // (hls/prefill_only/qwen_prefill_attention_kernel.cpp:163-202, qwen_prefill_mlp_kernel.cpp:217-254) only by
 // the 24-bit rounding of x (relative ~1e-7) and the fp32 summation order.
 //
-// One CTA computes a 128-row x 128-token tile. Per 128-byte K block the TMA producer stages the weight
-// tile (16 KB) and the three plane tiles (3 x 16 KB) into one of three 64 KB stages; one thread issues
-// 12 tcgen05.mma (M = 128, N = 128, K = 32 bytes; accumulator plane p in TMEM columns 128 p ..); four
-// warps read the accumulators back 16 tokens at a time, combine the planes exactly in int64 and run the
-// epilogue of the projection (the same operations as the CUDA-core prefill kernels in prefill_simt.cu).
+// One CTA computes a 128-row x TN-token tile (TN = 16, 32 or 64 for small batches; 64 with two CTAs per SM
+// for many tokens, so that one CTA's epilogue overlaps the other's main loop). Per 128-byte K block the TMA
+// producer stages the weight tile (16 KB) and the three plane tiles (3 x TN x 128 bytes, back to back, i.e.
+// one 3 TN-row tile); one thread issues 4 tcgen05.mma (M = 128, N = 3 TN, K = 32 bytes; accumulator column
+// p TN + n = plane p of token n); four warps read the accumulators back 16 tokens at a time, combine the
+// planes exactly in int64 and run the epilogue of the projection (the same operations as the CUDA-core
+// prefill kernels in prefill_simt.cu).
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
@@ -34,12 +36,18 @@ constexpr int kMaxStages = 8;
 
 // Token-tile geometry: TN tokens per tile (16, 32, 64 or 128 = the padded token count up to 128), so that a
 // small batch does not move or multiply padding.
-template <int TN>
+// ST > 0 fixes the pipeline depth (ST = 2 with TN = 64 keeps a CTA under half of the shared memory, so
+// two CTAs share an SM and one's epilogue overlaps the other's main loop); ST = 0 fills ~200 KB.
+template <int TN, int ST = 0>
 struct TCfg {
   static constexpr int kPlaneTile = TN * kKBlock;
   static constexpr int kStage = kUnitBytes + kPlanes * kPlaneTile;
-  static constexpr int kStages = (200 * 1024) / kStage > kMaxStages ? kMaxStages : (200 * 1024) / kStage;
-  static constexpr uint32_t kIdesc = idesc_i8(kTileM, TN);
+  static constexpr int kAutoStages = (200 * 1024) / kStage > kMaxStages ? kMaxStages : (200 * 1024) / kStage;
+  static constexpr int kStages = ST > 0 ? ST : kAutoStages;
+  // The three plane tiles sit back to back in a stage, which is the layout of one 3 TN-row tile: up to
+  // N = 256 one MMA covers all three planes (accumulator column p TN + n = plane p, token n).
+  static constexpr bool kFused = kPlanes * TN <= 256;
+  static constexpr uint32_t kIdesc = idesc_i8(kTileM, kFused ? kPlanes * TN : TN);
   static constexpr int kTmemCols = kPlanes * TN <= 32 ? 32 : kPlanes * TN <= 64 ? 64 : kPlanes * TN <= 128 ? 128
                                    : kPlanes * TN <= 256 ? 256 : 512;
   static_assert(TN % 16 == 0 && TN <= 128, "token tile");
@@ -94,10 +102,10 @@ __device__ __forceinline__ void mma_t(uint32_t d, uint64_t a, uint64_t b, uint32
       : "memory");
 }
 
-template <int EPI, int TN>
+template <int EPI, int TN, int ST>
 __global__ void __launch_bounds__(kThreadsT, 1)
     tgemm_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ CUtensorMap pmap, TArgs a) {
-  using C = TCfg<TN>;
+  using C = TCfg<TN, ST>;
   constexpr int kTN = TN;
   constexpr int kStagesT = C::kStages;
   constexpr int kStageBytes = C::kStage;
@@ -168,7 +176,7 @@ __global__ void __launch_bounds__(kThreadsT, 1)
           const uint32_t sb = smem_u32(stages + (size_t)s * kStageBytes);
           const uint64_t ad = sw128_desc(sb);
 #pragma unroll
-          for (int p = 0; p < kPlanes; ++p) {
+          for (int p = 0; p < (C::kFused ? 1 : kPlanes); ++p) {
             const uint64_t bd = sw128_desc(sb + kUnitBytes + p * kPlaneTile);
 #pragma unroll
             for (int j = 0; j < kKBlock / 32; ++j)
@@ -436,10 +444,10 @@ bool make_map(CUtensorMap* m, const void* base, uint64_t rows, uint64_t k_bytes,
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-template <int EPI, int TN>
+template <int EPI, int TN, int ST = 0>
 cudaError_t run_tgemm_tn(const uint8_t* w, int rows_total, int K, int mtiles, int box_rows, int second_row0,
                          const DigitPlanes& x, TArgs a, cudaStream_t s) {
-  using C = TCfg<TN>;
+  using C = TCfg<TN, ST>;
   if (x.K != K || K % kKBlock || x.Spad % TN || x.S < 1 || x.S > x.Spad) return cudaErrorInvalidValue;
   CUtensorMap wmap, pmap;
   if (!make_map(&wmap, w, (uint64_t)rows_total, (uint64_t)K, (uint32_t)box_rows) ||
@@ -451,7 +459,7 @@ cudaError_t run_tgemm_tn(const uint8_t* w, int rows_total, int K, int mtiles, in
   a.S = x.S;
   a.Spad = x.Spad;
   a.steps = x.steps;
-  auto kern = tgemm_kernel<EPI, TN>;
+  auto kern = tgemm_kernel<EPI, TN, ST>;
   const size_t smem = 1024 + (size_t)C::kStages * C::kStage + sizeof(TSmem);
   static std::mutex mu;
   static unsigned long long attr_set = 0;
@@ -473,6 +481,8 @@ cudaError_t run_tgemm_tn(const uint8_t* w, int rows_total, int K, int mtiles, in
 template <int EPI>
 cudaError_t run_tgemm(const uint8_t* w, int rows_total, int K, int mtiles, int box_rows, int second_row0,
                       const DigitPlanes& x, TArgs a, cudaStream_t s) {
+  if (x.Spad >= 128)  // many tokens: 64-token tiles, two CTAs per SM
+    return run_tgemm_tn<EPI, 64, 2>(w, rows_total, K, mtiles, box_rows, second_row0, x, a, s);
   const int tn = x.Spad < 128 ? x.Spad : 128;
   switch (tn) {
     case 16: return run_tgemm_tn<EPI, 16>(w, rows_total, K, mtiles, box_rows, second_row0, x, a, s);
