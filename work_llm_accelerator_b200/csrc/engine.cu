@@ -435,10 +435,8 @@ int enqueue_decode_batched(qwen_engine* e, int n, int max_len, bool advance) {
   for (int l = 0; l < kLayers; ++l) {
     const LayerDev& L = e->layers[l];
     const KvView kv = paged_view(e, l);
-    E_TRY(mark(kBcNorm));
-    E_TRY(decode_rmsnorm(e->p_x, L.input_ln, n, e->p_xn, s));
     E_TRY(mark(kBcDigits));
-    E_TRY(tgemm_digitize(e->p_xn, dp, s));
+    E_TRY(tgemm_rmsnorm_digitize(e->p_x, L.input_ln, dp, s));
     E_TRY(mark(kBcQkv));
     E_TRY(tgemm_qkv_decode(L, dp, e->d_pos, e->d_seq, kv, e->rope_dec_cos, e->rope_dec_sin, e->p_q, s));
     E_TRY(mark(kBcAttn));
@@ -447,10 +445,8 @@ int enqueue_decode_batched(qwen_engine* e, int n, int max_len, bool advance) {
     E_TRY(tgemm_digitize(e->p_ctx, dp, s));
     E_TRY(mark(kBcO));
     E_TRY(tgemm_o(L, dp, e->p_a, s));
-    E_TRY(mark(kBcNorm));
-    E_TRY(decode_rmsnorm(e->p_a, L.post_ln, n, e->p_xn, s));
     E_TRY(mark(kBcDigits));
-    E_TRY(tgemm_digitize(e->p_xn, dp, s));
+    E_TRY(tgemm_rmsnorm_digitize(e->p_a, L.post_ln, dp, s));
     E_TRY(mark(kBcGateUp));
     E_TRY(tgemm_gateup_decode(L, dp, e->p_h, s));
     E_TRY(mark(kBcDigits));

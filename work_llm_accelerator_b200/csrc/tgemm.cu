@@ -17,6 +17,7 @@
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
+#include <algorithm>
 #include <mutex>
 
 #include "tgemm.h"
@@ -64,6 +65,7 @@ enum TEpi { kTQkv = 0, kTScale = 1, kTGateUp = 2, kTDown = 3, kTRaw = 4 };
 
 struct TArgs {
   int nkb;           // 128-byte K blocks
+  int ksplit;        // K segments = CTAs of a cluster (1: no split)
   int box_rows;      // weight rows per TMA box: 128, or 64 twice (gate|up)
   int second_row0;   // gate|up: first row of the up half
   int S, Spad, rows;
@@ -94,6 +96,22 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, i
       : "memory");
 }
 
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+// Every thread of every CTA of the cluster arrives once; release/acquire order shared-memory writes.
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release;\nbarrier.cluster.wait.acquire;" ::: "memory");
+}
+// 32-bit store into the shared memory of CTA `rank` of the cluster, at the address `saddr` has in this CTA.
+__device__ __forceinline__ void st_peer(uint32_t saddr, uint32_t rank, int v) {
+  uint32_t pa;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(pa) : "r"(saddr), "r"(rank));
+  asm volatile("st.shared::cluster.b32 [%0], %1;" ::"r"(pa), "r"(v) : "memory");
+}
+
 template <uint32_t IDESC>
 __device__ __forceinline__ void mma_t(uint32_t d, uint64_t a, uint64_t b, uint32_t acc) {
   asm volatile(
@@ -115,7 +133,11 @@ __global__ void __launch_bounds__(kThreadsT, 1)
   uint8_t* stages = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   TSmem& sm = *reinterpret_cast<TSmem*>(stages + (size_t)kStagesT * kStageBytes);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int mtile = blockIdx.x, n0 = blockIdx.y * kTN;
+  // split K: the ksplit CTAs of a cluster share one output tile, CTA `rank` sums K blocks [kb_lo, kb_hi)
+  const int ks = a.ksplit;
+  const int rank = ks > 1 ? (int)cluster_rank() : 0;
+  const int mtile = blockIdx.x / ks, n0 = blockIdx.y * kTN;
+  const int kb_lo = rank * a.nkb / ks, kb_hi = (rank + 1) * a.nkb / ks;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStagesT; ++s) {
@@ -140,7 +162,7 @@ __global__ void __launch_bounds__(kThreadsT, 1)
       int s = 0;
       unsigned ph = 0;
       bool ok = true;
-      for (int kb = 0; kb < a.nkb && ok; ++kb) {
+      for (int kb = kb_lo; kb < kb_hi && ok; ++kb) {
         if (!(ok = mbar_wait(&sm.empty[s], ph ^ 1))) break;
         mbar_arrive_expect_tx(&sm.full[s], kStageBytes);
         uint8_t* st = stages + (size_t)s * kStageBytes;
@@ -169,7 +191,7 @@ __global__ void __launch_bounds__(kThreadsT, 1)
       int s = 0;
       unsigned ph = 0;
       bool ok = true;
-      for (int kb = 0; kb < a.nkb; ++kb) {
+      for (int kb = kb_lo; kb < kb_hi; ++kb) {
         ok = ok && mbar_wait(&sm.full[s], ph);
         fence_after();
         if (ok) {
@@ -180,7 +202,7 @@ __global__ void __launch_bounds__(kThreadsT, 1)
             const uint64_t bd = sw128_desc(sb + kUnitBytes + p * kPlaneTile);
 #pragma unroll
             for (int j = 0; j < kKBlock / 32; ++j)
-              mma_t<C::kIdesc>(tmem + p * kTN, ad + 2 * j, bd + 2 * j, (kb > 0 || j > 0) ? 1u : 0u);
+              mma_t<C::kIdesc>(tmem + p * kTN, ad + 2 * j, bd + 2 * j, (kb > kb_lo || j > 0) ? 1u : 0u);
           }
         }
         mma_commit(&sm.empty[s]);
@@ -191,11 +213,45 @@ __global__ void __launch_bounds__(kThreadsT, 1)
       }
       mma_commit(&sm.acc_full);
     }
-  } else {
-    // ---- epilogue: thread = one tile row (TMEM lane), 16 tokens per read
-    const int q = warp & 3, r = q * 32 + lane;
-    const bool ok = mbar_wait(&sm.acc_full, 0);
+  }
+  // ---- epilogue: thread = one tile row (TMEM lane), 16 tokens per read
+  // Split K: the tile's tokens are shared out over the cluster (CTA `rank` finishes tokens [tb, te)); once
+  // every main loop is done each CTA pushes the partial sums of the other CTAs' tokens into their shared
+  // memory (inbox [source rank][plane][token][row], in the then idle stage buffers), and after a second
+  // cluster barrier sums its inbox in rank order (exact integers).
+  const int q = warp & 3, r = q * 32 + lane;
+  const int tp = kTN / ks;  // tokens per CTA of the cluster
+  const int tb = rank * tp, te = tb + tp;
+  const int* inbox = reinterpret_cast<const int*>(stages);
+  bool ok = true;
+  if (warp >= 2) {
+    ok = mbar_wait(&sm.acc_full, 0);
     fence_after();
+  }
+  if (ks > 1) {
+    cluster_sync_all();  // every CTA's main loop done: the cluster's stage memory is free
+    if (warp >= 2) {
+      const uint32_t lane_base = tmem + ((uint32_t)(q * 32) << 16);
+      const uint32_t ib = smem_u32(stages);
+      for (int c0 = 0; c0 < kPlanes * kTN; c0 += kChunkN) {
+        int v[16];
+        if (ok) {
+          tmem_ld16(lane_base + c0, v);
+        } else {
+#pragma unroll
+          for (int c = 0; c < 16; ++c) v[c] = 0;
+        }
+#pragma unroll
+        for (int c = 0; c < 16; ++c) {
+          const int col = c0 + c, pl = col / kTN, t = col % kTN;
+          const int dst = t / tp, cc = t - dst * tp;
+          st_peer(ib + (uint32_t)((((rank * kPlanes + pl) * tp + cc) * kTileM + r) * 4), dst, v[c]);
+        }
+      }
+    }
+    cluster_sync_all();  // every partial delivered
+  }
+  if (warp >= 2) {
     int row;
     float sc = 0.f, bb = 0.f;
     if constexpr (EPI == kTGateUp) {
@@ -206,9 +262,24 @@ __global__ void __launch_bounds__(kThreadsT, 1)
     if constexpr (EPI != kTRaw) sc = __ldg(a.scale + row);
     if constexpr (EPI == kTQkv) bb = __ldg(a.bias + row);
     const uint32_t lane_base = tmem + ((uint32_t)(q * 32) << 16);
-    for (int c0 = 0; c0 < kTN && n0 + c0 < a.S; c0 += kChunkN) {  // chunks holding real tokens only
+    for (int c0 = tb; c0 < te && n0 + c0 < a.S; c0 += kChunkN) {  // chunks holding real tokens only
+      const int S_hi = min(a.S, n0 + te);  // tokens of this chunk that exist and belong to this CTA
       int v0[16], v1[16], v2[16];
-      if (ok) {
+      if (ks > 1) {
+#pragma unroll
+        for (int c = 0; c < 16; ++c) {
+          v0[c] = v1[c] = v2[c] = 0;
+          const int cc = c0 + c - tb;
+          if (cc < tp) {
+            for (int src = 0; src < ks; ++src) {
+              const int* bx = inbox + ((src * kPlanes) * tp + cc) * kTileM + r;
+              v0[c] += bx[0];
+              v1[c] += bx[tp * kTileM];
+              v2[c] += bx[2 * tp * kTileM];
+            }
+          }
+        }
+      } else if (ok) {
         tmem_ld16(lane_base + c0, v0);
         tmem_ld16(lane_base + kTN + c0, v1);
         tmem_ld16(lane_base + 2 * kTN + c0, v2);
@@ -220,7 +291,7 @@ __global__ void __launch_bounds__(kThreadsT, 1)
 #pragma unroll
         for (int c = 0; c < kChunkN; ++c) {
           const int n = n0 + c0 + c;
-          if (n < a.S) {
+          if (n < S_hi) {
             a.raw[((size_t)0 * a.S + n) * a.rows + row] = v0[c];
             a.raw[((size_t)1 * a.S + n) * a.rows + row] = v1[c];
             a.raw[((size_t)2 * a.S + n) * a.rows + row] = v2[c];
@@ -240,7 +311,7 @@ __global__ void __launch_bounds__(kThreadsT, 1)
 #pragma unroll
           for (int c = 0; c < kChunkN; ++c) {
             const int n = n0 + c0 + c;
-            res[c] = (EPI == kTDown && n < a.S) ? __ldg(a.resid + (size_t)n * kHidden + row) : 0.f;
+            res[c] = (EPI == kTDown && n < S_hi) ? __ldg(a.resid + (size_t)n * kHidden + row) : 0.f;
           }
 #pragma unroll
           for (int c = 0; c < kChunkN; ++c) {
@@ -250,7 +321,7 @@ __global__ void __launch_bounds__(kThreadsT, 1)
               y = __fadd_rn(res[c], y);
               if (a.round_out) y = round_bf16(y);
             }
-            if (n < a.S) a.out[(size_t)n * kHidden + row] = y;
+            if (n < S_hi) a.out[(size_t)n * kHidden + row] = y;
           }
         } else if constexpr (EPI == kTQkv) {
           // tile = head: rows r and r ^ 64 are RoPE partners (q and k heads); token index = position
@@ -293,7 +364,7 @@ __global__ void __launch_bounds__(kThreadsT, 1)
             if (rope)
               y = r < 64 ? __fsub_rn(__fmul_rn(mine, cs[c]), __fmul_rn(other, sn[c]))
                          : __fadd_rn(__fmul_rn(mine, cs[c]), __fmul_rn(other, sn[c]));
-            if (n < a.S) {
+            if (n < S_hi) {
               if (kvp[c] != nullptr) *kvp[c] = y;
               else dst[(size_t)n * stride] = y;
             }
@@ -310,7 +381,7 @@ __global__ void __launch_bounds__(kThreadsT, 1)
             const int n = n0 + c0 + c;
             const float gv = sm.ys[gr][c], uv = sm.ys[gr + 64][c];
             const float silu = __fdiv_rn(gv, __fadd_rn(1.0f, a.decode ? expf(-gv) : approx_exp_fast(-gv)));
-            if (n < a.S) a.out[(size_t)n * kInter + mtile * 64 + gr] = __fmul_rn(silu, uv);
+            if (n < S_hi) a.out[(size_t)n * kInter + mtile * 64 + gr] = __fmul_rn(silu, uv);
           }
           named_sync(kBarT, kEpiT);
         }
@@ -415,6 +486,86 @@ __global__ void __launch_bounds__(128) decode_rmsnorm_kernel(const float* __rest
   }
 }
 
+// Decode RMSNorm (as decode_rmsnorm_kernel: same element assignment, double sums, reduction order) fused
+// with the digit planes of the normalised row (as digitize_kernel: step = max|xn| / 8355710, digits of
+// rint(xn / step)), one CTA of 128 threads per token; padded rows become zero.
+__global__ void __launch_bounds__(128) rmsnorm_digitize_kernel(const float* __restrict__ x, const float* __restrict__ w,
+                                                               int S, int Spad, int8_t* __restrict__ planes,
+                                                               float* __restrict__ steps) {
+  __shared__ double red[4];
+  __shared__ float redm[4];
+  const int t = blockIdx.x, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  int8_t* p0 = planes + (size_t)t * kHidden;
+  int8_t* p1 = planes + ((size_t)Spad + t) * kHidden;
+  int8_t* p2 = planes + ((size_t)2 * Spad + t) * kHidden;
+  if (t >= S) {
+#pragma unroll
+    for (int j = 0; j < 3; ++j) {
+      const int k = 512 * j + 4 * tid;
+      *reinterpret_cast<uint32_t*>(p0 + k) = 0u;
+      *reinterpret_cast<uint32_t*>(p1 + k) = 0u;
+      *reinterpret_cast<uint32_t*>(p2 + k) = 0u;
+    }
+    if (tid == 0) steps[t] = 1.0f;
+    return;
+  }
+  const float* row = x + (size_t)t * kHidden;
+  float v[3][4];
+#pragma unroll
+  for (int j = 0; j < 3; ++j) {
+    const float4 f = *reinterpret_cast<const float4*>(row + 512 * j + 4 * tid);
+    v[j][0] = f.x;
+    v[j][1] = f.y;
+    v[j][2] = f.z;
+    v[j][3] = f.w;
+  }
+  double ss = 0.0;
+#pragma unroll
+  for (int j = 0; j < 3; ++j)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) ss += (double)v[j][e] * (double)v[j][e];
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+  if (lane == 0) red[warp] = ss;
+  __syncthreads();
+  const double tot = red[0] + red[1] + red[2] + red[3];
+  const double inv = 1.0 / sqrt(tot / (double)kHidden + (double)kEps);
+  float m = 0.f;
+#pragma unroll
+  for (int j = 0; j < 3; ++j) {
+    const float4 wv = *reinterpret_cast<const float4*>(w + 512 * j + 4 * tid);
+    v[j][0] = (float)((double)v[j][0] * inv * (double)wv.x);
+    v[j][1] = (float)((double)v[j][1] * inv * (double)wv.y);
+    v[j][2] = (float)((double)v[j][2] * inv * (double)wv.z);
+    v[j][3] = (float)((double)v[j][3] * inv * (double)wv.w);
+#pragma unroll
+    for (int e = 0; e < 4; ++e) m = fmaxf(m, fabsf(v[j][e]));
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+  if (lane == 0) redm[warp] = m;
+  __syncthreads();
+  const float mx = fmaxf(fmaxf(redm[0], redm[1]), fmaxf(redm[2], redm[3]));
+  const float st = mx > 0.0f ? mx / kDigitRange : 1.0f;
+  if (tid == 0) steps[t] = st;
+#pragma unroll
+  for (int j = 0; j < 3; ++j) {
+    uint32_t w0 = 0, w1 = 0, w2 = 0;
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      int d0, d1, d2;
+      split_digits((int)rintf(__fdiv_rn(v[j][e], st)), d0, d1, d2);
+      w0 |= (uint32_t)(d0 & 255) << (8 * e);
+      w1 |= (uint32_t)(d1 & 255) << (8 * e);
+      w2 |= (uint32_t)(d2 & 255) << (8 * e);
+    }
+    const int k = 512 * j + 4 * tid;
+    *reinterpret_cast<uint32_t*>(p0 + k) = w0;
+    *reinterpret_cast<uint32_t*>(p1 + k) = w1;
+    *reinterpret_cast<uint32_t*>(p2 + k) = w2;
+  }
+}
+
 // ---------------------------------------------------------------------------------------------------
 // host side
 // ---------------------------------------------------------------------------------------------------
@@ -446,9 +597,14 @@ bool make_map(CUtensorMap* m, const void* base, uint64_t rows, uint64_t k_bytes,
 
 template <int EPI, int TN, int ST = 0>
 cudaError_t run_tgemm_tn(const uint8_t* w, int rows_total, int K, int mtiles, int box_rows, int second_row0,
-                         const DigitPlanes& x, TArgs a, cudaStream_t s) {
+                         const DigitPlanes& x, TArgs a, cudaStream_t s, int ksplit = 1) {
   using C = TCfg<TN, ST>;
   if (x.K != K || K % kKBlock || x.Spad % TN || x.S < 1 || x.S > x.Spad) return cudaErrorInvalidValue;
+  // split K: 1, 2, 4 or 8 CTAs per cluster, each with at least one K block; the inbox uses the stage memory
+  if ((ksplit != 1 && ksplit != 2 && ksplit != 4 && ksplit != 8) || ksplit > K / kKBlock ||
+      (ksplit > 1 && (size_t)C::kStages * C::kStage < (size_t)kPlanes * TN * kTileM * 4))
+    return cudaErrorInvalidValue;
+  a.ksplit = ksplit;
   CUtensorMap wmap, pmap;
   if (!make_map(&wmap, w, (uint64_t)rows_total, (uint64_t)K, (uint32_t)box_rows) ||
       !make_map(&pmap, x.planes, (uint64_t)kPlanes * x.Spad, (uint64_t)K, TN))
@@ -474,26 +630,59 @@ cudaError_t run_tgemm_tn(const uint8_t* w, int rows_total, int K, int mtiles, in
       attr_set |= 1ull << dev;
     }
   }
-  kern<<<dim3(mtiles, x.Spad / TN), kThreadsT, smem, s>>>(wmap, pmap, a);
-  return cudaGetLastError();
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(mtiles * ksplit, x.Spad / TN);
+  cfg.blockDim = dim3(kThreadsT);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeClusterDimension;
+  at[0].val.clusterDim.x = ksplit;
+  at[0].val.clusterDim.y = 1;
+  at[0].val.clusterDim.z = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = ksplit > 1 ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, kern, wmap, pmap, a);
+}
+
+// K segments for a grid of `tiles` output tiles: as many (1, 2, 4 or 8, <= K blocks) as keep the grid within one
+// wave of 148 SMs, so that projections with few row tiles (q|k|v, o_proj, down at small token counts) fill
+// the GPU; 1 when the tiles alone fill it.
+int pick_ksplit(int tiles, int nkb) {
+  int k = 1;
+  while (k < 8 && 2 * k <= nkb && tiles * 2 * k <= 148) k *= 2;
+  return k;
 }
 
 template <int EPI>
 cudaError_t run_tgemm(const uint8_t* w, int rows_total, int K, int mtiles, int box_rows, int second_row0,
                       const DigitPlanes& x, TArgs a, cudaStream_t s) {
-  if (x.Spad >= 128)  // many tokens: 64-token tiles, two CTAs per SM
+  const int nkb = K / kKBlock;
+  if (x.Spad >= 128) {  // many tokens: 64-token tiles, two CTAs per SM unless K is split
+    const int ks = pick_ksplit(mtiles * (x.Spad / 64), nkb);
+    if (ks > 1) return run_tgemm_tn<EPI, 64>(w, rows_total, K, mtiles, box_rows, second_row0, x, a, s, ks);
     return run_tgemm_tn<EPI, 64, 2>(w, rows_total, K, mtiles, box_rows, second_row0, x, a, s);
-  const int tn = x.Spad < 128 ? x.Spad : 128;
-  switch (tn) {
-    case 16: return run_tgemm_tn<EPI, 16>(w, rows_total, K, mtiles, box_rows, second_row0, x, a, s);
-    case 32: return run_tgemm_tn<EPI, 32>(w, rows_total, K, mtiles, box_rows, second_row0, x, a, s);
-    case 64: return run_tgemm_tn<EPI, 64>(w, rows_total, K, mtiles, box_rows, second_row0, x, a, s);
-    case 128: return run_tgemm_tn<EPI, 128>(w, rows_total, K, mtiles, box_rows, second_row0, x, a, s);
+  }
+  // few tokens: split the long-K projection (down), and q|k|v so that each CTA finishes one 16-token chunk
+  // (its epilogue has dependent loads per chunk); measured slower for the short-K o_proj and gate|up
+  int ks = 1;
+  if (nkb >= 32) ks = pick_ksplit(mtiles, nkb);
+  else if (EPI == kTQkv) ks = std::min(pick_ksplit(mtiles, nkb), std::max(1, x.Spad / 16));
+  switch (x.Spad) {
+    case 16: return run_tgemm_tn<EPI, 16>(w, rows_total, K, mtiles, box_rows, second_row0, x, a, s, ks);
+    case 32: return run_tgemm_tn<EPI, 32>(w, rows_total, K, mtiles, box_rows, second_row0, x, a, s, ks);
+    case 64: return run_tgemm_tn<EPI, 64>(w, rows_total, K, mtiles, box_rows, second_row0, x, a, s, ks);
     default: return cudaErrorInvalidValue;
   }
 }
 
 }  // namespace
+
+cudaError_t tgemm_rmsnorm_digitize(const float* x, const float* w, DigitPlanes d, cudaStream_t s) {
+  if (d.K != kHidden || d.Spad != tgemm_pad(d.S) || d.S < 1) return cudaErrorInvalidValue;
+  rmsnorm_digitize_kernel<<<d.Spad, 128, 0, s>>>(x, w, d.S, d.Spad, d.planes, d.steps);
+  return cudaGetLastError();
+}
 
 cudaError_t tgemm_digitize(const float* x, DigitPlanes d, cudaStream_t s) {
   if (d.K % 4 || d.Spad != tgemm_pad(d.S) || d.S < 1) return cudaErrorInvalidValue;

@@ -23,6 +23,9 @@ inline size_t tgemm_plane_bytes(int S, int K) { return (size_t)3 * tgemm_pad(S) 
 
 // x [S][K] fp32 -> digit planes (one CTA per token row).
 cudaError_t tgemm_digitize(const float* x, DigitPlanes d, cudaStream_t s);
+// Decode RMSNorm of x [S][1536] with weights w, then digit planes of the normalised rows: the same values
+// as decode_rmsnorm followed by tgemm_digitize, in one kernel.
+cudaError_t tgemm_rmsnorm_digitize(const float* x, const float* w, DigitPlanes d, cudaStream_t s);
 
 // Projections of all S tokens with the prefill epilogues (the same operations as the CUDA-core prefill
 // GEMMs in prefill_simt.cu): q|k|v + RoPE (table rows = token index) + K/V rows of a flat cache; o_proj;
