@@ -11,9 +11,11 @@
 // The fp16 split needs |x| < 32768 and finite values; otherwise the split kernel raises a flag, this kernel
 // does nothing and the CUDA-core kernel (attention.cu) computes the context instead.
 //
-// Work split. CTA = (128 queries, one query head); keys in tiles of 64. Warp 0 issues the TMA loads
-// (Q once, then K tiles for both passes and transposed V tiles for pass 2, two stages each), warp 1 issues
-// the MMAs (S = Q K^T into one of two TMEM score buffers; O += P V into the TMEM context accumulator), and
+// Work split. CTA = (128 queries, one query head); keys in tiles of 64. Q (hi, lo) sits in TMEM as the A
+// operand of S = Q K^T, which leaves shared memory for four K stages (a K tile's TMA latency is longer than
+// one tile's MMAs). Warp 0 issues the TMA loads (K tiles for both passes, transposed V tiles for pass 2),
+// warp 1 issues the MMAs (S into one of two TMEM score buffers; O += P V into the TMEM context
+// accumulator), and
 // sixteen softmax warps own one query row and 16 keys of each tile per thread: they read the scores from
 // TMEM, compute the weights, and write them as fp16 (hi, lo) tiles to shared memory for the P V product.
 // Query tiles are launched heaviest (longest causal prefix) first.
@@ -34,29 +36,32 @@ using namespace umma;
 
 constexpr int kBQ = 128;  // query rows per CTA = TMEM lanes
 constexpr int kBK = 64;   // keys per tile
-constexpr int kQPlaneB = kBQ * kHeadDim * 2;  // fp16 [128 queries][128 dims]: two 64-dim swizzle columns
 constexpr int kKPlaneB = kBK * kHeadDim * 2;  // fp16 [64 keys][128 dims]: two 64-dim swizzle columns
 constexpr int kVPlaneB = kHeadDim * kBK * 2;  // fp16 [128 dims][64 keys]: one swizzle column
 constexpr int kPPlaneB = kBQ * kBK * 2;       // fp16 [128 queries][64 keys]: one swizzle column
-constexpr int kOffQ = 0;
-constexpr int kOffK = kOffQ + 2 * kQPlaneB;      // two stages of (hi, lo)
-constexpr int kOffV = kOffK + 2 * 2 * kKPlaneB;  // two stages of (hi, lo)
+constexpr int kKStages = 4;                      // K tiles in flight (their TMA latency exceeds one tile's MMAs)
+constexpr int kOffK = 0;                         // kKStages stages of (hi, lo)
+constexpr int kOffV = kOffK + kKStages * 2 * kKPlaneB;  // two stages of (hi, lo)
 constexpr int kOffP = kOffV + 2 * 2 * kVPlaneB;  // (hi, lo)
-constexpr int kTileBytes = kOffP + 2 * kPPlaneB;  // 224 KB
+constexpr int kTileBytes = kOffP + 2 * kPPlaneB;  // 160 KB
 constexpr int kSoftWarps = 16;                  // four per TMEM lane quarter
 constexpr int kSoftThreads = 32 * kSoftWarps;
 constexpr int kKeyGroups = kSoftWarps / 4;      // key groups of a tile (one per warp of a lane quarter)
 constexpr int kKeysPer = kBK / kKeyGroups;      // keys of a tile per softmax thread
 constexpr int kThreadsA = 64 + kSoftThreads;
 constexpr int kBarSoft = 1;  // named barrier of the softmax warps
-constexpr uint32_t kTmemColsA = 256;  // context accumulator: columns 0..127; score buffers: 128.., 192..
+// TMEM columns: context accumulator 0..127, score buffers 128.., 192.., Q (the A operand of S = Q K^T)
+// 256..319 (hi) and 320..383 (lo), two fp16 dims per 32-bit column
+constexpr uint32_t kTmemColsA = 512;
 constexpr uint32_t kColS = 128;
+constexpr uint32_t kColQ = 256;
 constexpr uint32_t kIdescS = idesc_f16(kBQ, kBK);
 constexpr uint32_t kIdescO = idesc_f16(kBQ, kHeadDim);
 constexpr float kSplitLimit = 32768.0f;
 
 struct ACtl {
-  uint64_t q_full, k_full[2], k_empty[2], v_full[2], v_empty[2], s_full[2], s_empty[2], p_full, p_empty, o_full;
+  uint64_t q_full, k_full[kKStages], k_empty[kKStages], v_full[2], v_empty[2], s_full[2], s_empty[2], p_full, p_empty,
+      o_full;
   uint32_t tmem_base;
 };
 
@@ -128,6 +133,28 @@ __global__ void __launch_bounds__(256) attn_split_kernel(const float* __restrict
   if (__syncthreads_or(bad) && threadIdx.x == 0) atomicOr(flag, 1);
 }
 
+// D[tmem] (+)= A[tmem] . B[smem]^T, kind::f16, A read from TMEM (row m in lane m, element k of a K step in
+// column k / 2, the lower k in the low half).
+template <uint32_t IDESC>
+__device__ __forceinline__ void mma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b, uint32_t accumulate) {
+  asm volatile(
+      "{\n.reg .pred p;\nsetp.ne.b32 p, %3, 0;\ntcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %4, p;\n}" ::"r"(
+          d_tmem),
+      "r"(a_tmem), "l"(b), "r"(accumulate), "r"(IDESC)
+      : "memory");
+}
+
+// 16 consecutive 32-bit TMEM columns of the warp's 32 lanes <- v (then wait for the stores).
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&v)[16]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(
+          taddr),
+      "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]), "r"(v[9]),
+      "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15])
+      : "memory");
+  asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+}
+
 // N consecutive 32-bit TMEM columns of the warp's 32 lanes (N = 16 or 32).
 template <int N>
 __device__ __forceinline__ void tmem_ld_cols(uint32_t taddr, uint32_t (&v)[N]) {
@@ -147,7 +174,7 @@ __device__ __forceinline__ uint32_t half2_bits(float a, float b) {
 }
 
 __global__ void __launch_bounds__(kThreadsA, 1)
-    attn_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constant__ CUtensorMap kmap,
+    attn_tc_kernel(const __half* __restrict__ qp, const __grid_constant__ CUtensorMap kmap,
                    const __grid_constant__ CUtensorMap vmap, int S, const int* flag, float* __restrict__ ctx) {
   if (*reinterpret_cast<const volatile int*>(flag) != 0) return;  // values outside the split: CUDA-core kernel
   extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -161,10 +188,12 @@ __global__ void __launch_bounds__(kThreadsA, 1)
   const int G = 2 * T;                                // pass 1 tiles, then pass 2 tiles
 
   if (threadIdx.x == 0) {
-    mbar_init(&c.q_full, 1);
-    for (int i = 0; i < 2; ++i) {
+    mbar_init(&c.q_full, kSoftWarps);  // every softmax warp stored its part of Q in TMEM
+    for (int i = 0; i < kKStages; ++i) {
       mbar_init(&c.k_full[i], 1);
       mbar_init(&c.k_empty[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
       mbar_init(&c.v_full[i], 1);
       mbar_init(&c.v_empty[i], 1);
       mbar_init(&c.s_full[i], 1);
@@ -184,21 +213,15 @@ __global__ void __launch_bounds__(kThreadsA, 1)
   if (warp == 0) {
     // ---- TMA producer
     if (lane == 0) {
-      asm volatile("prefetch.tensormap [%0];" ::"l"(&qmap) : "memory");
       asm volatile("prefetch.tensormap [%0];" ::"l"(&kmap) : "memory");
       asm volatile("prefetch.tensormap [%0];" ::"l"(&vmap) : "memory");
-      mbar_arrive_expect_tx(&c.q_full, 2 * kQPlaneB);
-      for (int p = 0; p < 2; ++p)
-        for (int a = 0; a < 2; ++a)
-          tma_load_3d(tiles + kOffQ + p * kQPlaneB + a * (kBQ * 128), &qmap, h * kHeadDim + a * 64, q0, p,
-                      &c.q_full);
       bool ok = true;
       int kn = 0, vn = 0;
       for (int gi = 0; gi < G && ok; ++gi) {
         const int j = gi < T ? gi : gi - T;
         {
-          const int st = kn & 1;
-          if (!(ok = mbar_wait(&c.k_empty[st], ((kn >> 1) & 1) ^ 1))) break;
+          const int st = kn % kKStages;
+          if (!(ok = mbar_wait(&c.k_empty[st], ((kn / kKStages) & 1) ^ 1))) break;
           mbar_arrive_expect_tx(&c.k_full[st], 2 * kKPlaneB);
           uint8_t* dst = tiles + kOffK + st * 2 * kKPlaneB;
           for (int p = 0; p < 2; ++p)
@@ -217,7 +240,7 @@ __global__ void __launch_bounds__(kThreadsA, 1)
         }
       }
       // every issued stage consumed before leaving (no copy in flight at exit)
-      for (int i = 0; i < 2 && ok; ++i, ++kn) ok = mbar_wait(&c.k_empty[kn & 1], ((kn >> 1) & 1) ^ 1);
+      for (int i = 0; i < kKStages && ok; ++i, ++kn) ok = mbar_wait(&c.k_empty[kn % kKStages], ((kn / kKStages) & 1) ^ 1);
       for (int i = 0; i < 2 && ok; ++i, ++vn) ok = mbar_wait(&c.v_empty[vn & 1], ((vn >> 1) & 1) ^ 1);
     }
   } else if (warp == 1) {
@@ -225,13 +248,12 @@ __global__ void __launch_bounds__(kThreadsA, 1)
     if (lane == 0) {
       bool ok = mbar_wait(&c.q_full, 0);
       fence_after();
-      const uint32_t qa = smem_u32(tiles + kOffQ);
       int kn = 0, vn = 0;
       // (A plane, B plane) of the three products, cross terms first: lo.hi, hi.lo, hi.hi
       constexpr int kAp[3] = {1, 0, 0}, kBp[3] = {0, 1, 0};
       auto issue_s = [&](int gi) {
-        const int st = kn & 1;
-        ok = ok && mbar_wait(&c.k_full[st], (kn >> 1) & 1);
+        const int st = kn % kKStages;
+        ok = ok && mbar_wait(&c.k_full[st], (kn / kKStages) & 1);
         fence_after();
         if (ok) {
           const uint32_t kb = smem_u32(tiles + kOffK + st * 2 * kKPlaneB);
@@ -241,9 +263,8 @@ __global__ void __launch_bounds__(kThreadsA, 1)
 #pragma unroll
             for (int kk = 0; kk < kHeadDim / 16; ++kk) {
               const uint32_t off = (uint32_t)((kk & 3) * 32);  // 16 dims = 32 bytes inside the swizzle row
-              const uint64_t ad = sw128_desc(qa + kAp[t] * kQPlaneB + (kk >> 2) * (kBQ * 128) + off);
               const uint64_t bd = sw128_desc(kb + kBp[t] * kKPlaneB + (kk >> 2) * (kBK * 128) + off);
-              mma_f16<kIdescS>(d, ad, bd, (t > 0 || kk > 0) ? 1u : 0u);
+              mma_f16_ts<kIdescS>(d, tmem + kColQ + 64 * kAp[t] + 8 * kk, bd, (t > 0 || kk > 0) ? 1u : 0u);
             }
         }
         mma_commit(&c.k_empty[st]);
@@ -293,6 +314,26 @@ __global__ void __launch_bounds__(kThreadsA, 1)
     // per-row exchange between the key groups, in the weight tile's space while no weight tile is live
     float* xch = reinterpret_cast<float*>(tiles + kOffP);
     bool ok = true;
+    {
+      // Q of this row, dims [32 kg, 32 kg + 32) of head h, both planes -> TMEM (zero past the sequence)
+      uint32_t qv[16];
+#pragma unroll
+      for (int pl = 0; pl < 2; ++pl) {
+        const uint4* src = reinterpret_cast<const uint4*>(qp + ((size_t)pl * S + qrow) * kHidden + h * kHeadDim + 32 * kg);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const uint4 u = qrow < S ? src[i] : make_uint4(0u, 0u, 0u, 0u);
+          qv[4 * i] = u.x;
+          qv[4 * i + 1] = u.y;
+          qv[4 * i + 2] = u.z;
+          qv[4 * i + 3] = u.w;
+        }
+        tmem_st16(lane_addr + kColQ + 64 * pl + 16 * kg, qv);
+      }
+      fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&c.q_full);
+    }
     uint32_t v[kKeysPer];
     // pass 1: row maximum of score * scaling over keys <= qrow
     float m = -1.0e30f;
@@ -444,9 +485,8 @@ cudaError_t launch_prefill_attention_tc(const float* q, const float* k_cache, co
   __half* qp = reinterpret_cast<__half*>(base + 256);
   __half* kp = reinterpret_cast<__half*>(base + 256 + round256((size_t)2 * S * kHidden * 2));
   __half* vt = reinterpret_cast<__half*>(reinterpret_cast<uint8_t*>(kp) + round256((size_t)2 * S * kKvWidth * 2));
-  CUtensorMap qmap, kmap, vmap;
-  if (!make_map3(&qmap, qp, kHidden, (uint64_t)S, kHidden * 2, (uint64_t)S * kHidden * 2, 64, kBQ) ||
-      !make_map3(&kmap, kp, kKvWidth, (uint64_t)S, kKvWidth * 2, (uint64_t)S * kKvWidth * 2, 64, kBK) ||
+  CUtensorMap kmap, vmap;
+  if (!make_map3(&kmap, kp, kKvWidth, (uint64_t)S, kKvWidth * 2, (uint64_t)S * kKvWidth * 2, 64, kBK) ||
       !make_map3(&vmap, vt, (uint64_t)S, kKvWidth, (uint64_t)Spad * 2, (uint64_t)kKvWidth * Spad * 2, kBK, kHeadDim))
     return cudaErrorInvalidValue;
   cudaError_t e = cudaMemsetAsync(flag, 0, sizeof(int), s);
@@ -469,7 +509,7 @@ cudaError_t launch_prefill_attention_tc(const float* q, const float* k_cache, co
       attr_set |= 1ull << dev;
     }
   }
-  attn_tc_kernel<<<dim3((S + kBQ - 1) / kBQ, kHeads), kThreadsA, kSmemA, s>>>(qmap, kmap, vmap, S, flag, ctx);
+  attn_tc_kernel<<<dim3((S + kBQ - 1) / kBQ, kHeads), kThreadsA, kSmemA, s>>>(qp, kmap, vmap, S, flag, ctx);
   if ((e = cudaGetLastError()) != cudaSuccess) return e;
   // values outside the fp16 split: the CUDA-core kernel computes the context (it returns at once otherwise)
   return launch_prefill_attention_gated(q, k_cache, v_cache, S, ctx, flag, s);

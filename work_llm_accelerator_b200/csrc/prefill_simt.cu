@@ -16,8 +16,9 @@ namespace {
 
 // ---- RMSNorm -------------------------------------------------------------------------------------
 // CTA = 32 tokens. The reference's sum of squares is one serial fp32 chain per token (kept bit for bit), so
-// warp 0 runs the 32 chains (thread = token) out of shared memory while all four warps stage the next
-// 128-column chunk of the 32 rows with coalesced loads; then every thread writes normalised columns.
+// warp 0 runs the 32 chains (thread = token) out of shared memory while warps 1-3 stage the next
+// 128-column chunk of the 32 rows with coalesced loads; then all threads write the normalised rows, eight
+// rows of loads in flight at a time.
 constexpr int kNormTok = 32, kNormCols = 128, kNormPad = kNormCols + 1;
 
 __global__ void __launch_bounds__(128) prefill_rmsnorm_kernel(const float* __restrict__ x, const float* __restrict__ w,
@@ -26,8 +27,8 @@ __global__ void __launch_bounds__(128) prefill_rmsnorm_kernel(const float* __res
   __shared__ float inv_s[kNormTok];
   const int t0 = blockIdx.x * kNormTok, tid = threadIdx.x;
   const int n = min(kNormTok, S - t0);
-  auto stage = [&](int c, int buf) {
-    for (int i = tid; i < kNormTok * (kNormCols / 4); i += 128) {
+  auto stage = [&](int c, int buf) {  // warps 1-3
+    for (int i = tid - 32; i < kNormTok * (kNormCols / 4); i += 96) {
       const int rr = i / (kNormCols / 4), f = i % (kNormCols / 4);
       float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
       if (rr < n) v = *reinterpret_cast<const float4*>(x + (size_t)(t0 + rr) * kHidden + kNormCols * c + 4 * f);
@@ -38,13 +39,14 @@ __global__ void __launch_bounds__(128) prefill_rmsnorm_kernel(const float* __res
       dst[3] = v.w;
     }
   };
-  stage(0, 0);
+  if (tid >= 32) stage(0, 0);
   __syncthreads();
   float ms = 0.0f;
   constexpr int kChunks = kHidden / kNormCols;
   for (int c = 0; c < kChunks; ++c) {
-    if (c + 1 < kChunks) stage(c + 1, (c + 1) & 1);
-    if (tid < kNormTok) {
+    if (tid >= 32) {
+      if (c + 1 < kChunks) stage(c + 1, (c + 1) & 1);
+    } else {
       const float* row = tile[c & 1][tid];
 #pragma unroll 8
       for (int d = 0; d < kNormCols; ++d) ms = __fadd_rn(ms, __fmul_rn(row[d], row[d]));
@@ -56,11 +58,32 @@ __global__ void __launch_bounds__(128) prefill_rmsnorm_kernel(const float* __res
     inv_s[tid] = __fdiv_rn(1.0f, approx_sqrt(__fadd_rn(ms, kEps)));
   }
   __syncthreads();
-  for (int i = 0; i < n; ++i) {
-    const float inv = inv_s[i];
-    const float* row = x + (size_t)(t0 + i) * kHidden;
-    float* out = xn + (size_t)(t0 + i) * kHidden;
-    for (int d = tid; d < kHidden; d += 128) out[d] = __fmul_rn(__fmul_rn(row[d], inv), w[d]);
+  // thread: float4 columns tid, tid + 128, tid + 256 of every row
+  float4 wv[3];
+#pragma unroll
+  for (int j = 0; j < 3; ++j) wv[j] = *reinterpret_cast<const float4*>(w + 4 * (tid + 128 * j));
+  for (int i0 = 0; i0 < n; i0 += 8) {
+    float4 xv[8][3];
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+#pragma unroll
+      for (int j = 0; j < 3; ++j)
+        if (i0 + i < n)
+          xv[i][j] = *reinterpret_cast<const float4*>(x + (size_t)(t0 + i0 + i) * kHidden + 4 * (tid + 128 * j));
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      if (i0 + i >= n) break;
+      const float inv = inv_s[i0 + i];
+#pragma unroll
+      for (int j = 0; j < 3; ++j) {
+        float4 o;
+        o.x = __fmul_rn(__fmul_rn(xv[i][j].x, inv), wv[j].x);
+        o.y = __fmul_rn(__fmul_rn(xv[i][j].y, inv), wv[j].y);
+        o.z = __fmul_rn(__fmul_rn(xv[i][j].z, inv), wv[j].z);
+        o.w = __fmul_rn(__fmul_rn(xv[i][j].w, inv), wv[j].w);
+        *reinterpret_cast<float4*>(xn + (size_t)(t0 + i0 + i) * kHidden + 4 * (tid + 128 * j)) = o;
+      }
+    }
   }
 }
 
