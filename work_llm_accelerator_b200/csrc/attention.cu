@@ -23,9 +23,12 @@ constexpr int kChunk = 64;                 // decode keys per CTA
 constexpr int kPartStride = 2 + kHeadDim;  // m, l, acc[128]
 constexpr int kAttnThreads = 128;
 constexpr int kRow = kHeadDim + 4;         // padded smem row (16-byte aligned, conflict-free float4 reads)
+constexpr int kMergeBatch = 8;             // chunk partials staged together by the merging CTA
+
+static_assert(kMergeBatch * kGroups * kPartStride <= kChunk * kRow, "merge staging fits in the K tile");
 
 struct DecodeAttnSmem {
-  float ks[kChunk][kRow];
+  float ks[kChunk][kRow];  // also the merge staging area: kMergeBatch x 6 x 130 floats fit
   float vs[kChunk][kHeadDim];
   float qs[kGroups][kRow];
   float es[kChunk][8];  // per key: the six heads' scores, then weights (padded to 8)
@@ -209,22 +212,26 @@ __global__ void __launch_bounds__(kAttnThreads) decode_attn_kernel(const float* 
     Lsum[h] = 0.f;
     M[h] = -INFINITY;
   }
-  for (int cc = 0; cc < nchunks; ++cc) {
-    const float* pc = base + (size_t)cc * kGroups * kPartStride;
-    float mv[kGroups], lv[kGroups], av[kGroups];
+  // the partials of kMergeBatch chunks at a time are staged in shared memory (the K tile space, free now)
+  // with all loads in flight together, then merged one chunk after the other
+  float* stg = &sm.ks[0][0];
+  for (int c0 = 0; c0 < nchunks; c0 += kMergeBatch) {
+    const int nb = min(kMergeBatch, nchunks - c0);
+    __syncthreads();
+    const float* src = base + (size_t)c0 * kGroups * kPartStride;
+    for (int i = tid; i < nb * kGroups * kPartStride; i += kAttnThreads) stg[i] = __ldcg(src + i);
+    __syncthreads();
+    for (int cc = 0; cc < nb; ++cc) {
+      const float* pc = stg + cc * kGroups * kPartStride;
 #pragma unroll
-    for (int h = 0; h < kGroups; ++h) {
-      mv[h] = __ldcg(&pc[h * kPartStride]);
-      lv[h] = __ldcg(&pc[h * kPartStride + 1]);
-      av[h] = __ldcg(&pc[h * kPartStride + 2 + tid]);
-    }
-#pragma unroll
-    for (int h = 0; h < kGroups; ++h) {
-      const float Mn = fmaxf(M[h], mv[h]);
-      const float sa = expf(M[h] - Mn), sb = expf(mv[h] - Mn);
-      o[h] = __fadd_rn(__fmul_rn(o[h], sa), __fmul_rn(av[h], sb));
-      Lsum[h] = __fadd_rn(__fmul_rn(Lsum[h], sa), __fmul_rn(lv[h], sb));
-      M[h] = Mn;
+      for (int h = 0; h < kGroups; ++h) {
+        const float mv = pc[h * kPartStride], lv = pc[h * kPartStride + 1], av = pc[h * kPartStride + 2 + tid];
+        const float Mn = fmaxf(M[h], mv);
+        const float sa = expf(M[h] - Mn), sb = expf(mv - Mn);
+        o[h] = __fadd_rn(__fmul_rn(o[h], sa), __fmul_rn(av, sb));
+        Lsum[h] = __fadd_rn(__fmul_rn(Lsum[h], sa), __fmul_rn(lv, sb));
+        M[h] = Mn;
+      }
     }
   }
 #pragma unroll
