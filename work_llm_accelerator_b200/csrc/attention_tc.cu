@@ -361,7 +361,8 @@ __global__ void __launch_bounds__(kThreadsA, 1)
     }
     named_sync(kBarSoft, kSoftThreads);  // every row maximum read before the weight tile is written
     // pass 2: weights, denominator, and the fp16 (hi, lo) weight tiles for O += P V
-    float den = 0.0f;
+    const F2 nz = f2_negzero(), sc2 = f2(kAttentionScaling, kAttentionScaling), m2 = f2(-m, -m);
+    F2 den2 = f2(0.0f, 0.0f);
     const uint32_t prow = smem_u32(tiles + kOffP) + (uint32_t)((r >> 3) * 1024 + (r & 7) * 128);
     for (int j = 0; j < T; ++j) {
       const int gi = T + j;
@@ -378,12 +379,15 @@ __global__ void __launch_bounds__(kThreadsA, 1)
       uint32_t ph[kKeysPer / 2], pl[kKeysPer / 2];
       float e[kKeysPer];
 #pragma unroll
-      for (int i = 0; i < kKeysPer; ++i) {
-        const float x = approx_exp_fast(__fsub_rn(__fmul_rn(__uint_as_float(v[i]), kAttentionScaling), m));
-        e[i] = select_f32(kb + i <= qrow, x, 0.0f);
+      for (int i = 0; i < kKeysPer; i += 2) {
+        // score * scaling - max for two keys (the reference's two roundings), then the exponential
+        const F2 a = add2(mul2(f2(__uint_as_float(v[i]), __uint_as_float(v[i + 1])), sc2, nz), m2);
+        float x0, x1;
+        approx_exp_fast2(f2_lo(a), f2_hi(a), x0, x1, nz);
+        e[i] = select_f32(kb + i <= qrow, x0, 0.0f);
+        e[i + 1] = select_f32(kb + i + 1 <= qrow, x1, 0.0f);
+        den2 = add2(den2, f2(e[i], e[i + 1]));  // even and odd keys in two running sums
       }
-#pragma unroll
-      for (int i = 0; i < kKeysPer; ++i) den = __fadd_rn(den, e[i]);
 #pragma unroll
       for (int i = 0; i < kKeysPer; i += 2) {
         const float h0 = __uint_as_float(__float_as_uint(e[i]) & 0xFFFFE000u);
@@ -407,6 +411,7 @@ __global__ void __launch_bounds__(kThreadsA, 1)
       if (lane == 0) mbar_arrive(&c.p_full);
     }
     // every P V product done (the weight tile is free again), then the row denominator over the key groups
+    float den = __fadd_rn(f2_lo(den2), f2_hi(den2));
     ok = ok && mbar_wait(&c.o_full, 0);
     fence_after();
     xch[kg * kBQ + r] = den;

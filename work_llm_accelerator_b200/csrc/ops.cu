@@ -213,9 +213,18 @@ extern "C" int qwen_b200_prefill_attention(const float* q, const float* k_cache,
 
 namespace qb {
 namespace {
+// Pairs of elements through the paired form (the one the attention softmax runs), element 2i in the first
+// lane and 2i + 1 in the second, so both lanes are checked.
 __global__ void approx_exp_kernel(const float* __restrict__ x, float* __restrict__ y, long long n) {
-  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x)
-    y[i] = approx_exp_fast(x[i]);
+  const F2 nz = f2_negzero();
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; 2 * i < n;
+       i += (long long)gridDim.x * blockDim.x) {
+    const bool two = 2 * i + 1 < n;
+    float r0, r1;
+    approx_exp_fast2(x[2 * i], two ? x[2 * i + 1] : 0.0f, r0, r1, nz);
+    y[2 * i] = r0;
+    if (two) y[2 * i + 1] = r1;
+  }
 }
 }  // namespace
 }  // namespace qb
@@ -231,7 +240,7 @@ extern "C" int qwen_b200_prefill_approx_exp(const float* x, float* y, long long 
     return kStatusInvalid;
   }
   if (n == 0) return 0;
-  const long long blocks = std::min<long long>((n + 255) / 256, 148 * 16);
+  const long long blocks = std::min<long long>((n / 2 + 256) / 256, 148 * 16);
   approx_exp_kernel<<<(unsigned)blocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(x, y, n);
   const cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) {

@@ -263,7 +263,51 @@ __device__ __forceinline__ float select_f32(bool p, float a, float b) {
   return r;
 }
 
-// approx_exp in straight-line form (no loops, no branches, so that many independent evaluations interleave):
+// Two fp32 values in one 64-bit register, operated on by the paired fp32 instructions of sm_100
+// (add / fma .rn .f32x2: each lane rounds exactly as the scalar instruction does).
+struct F2 {
+  unsigned long long v;
+};
+__device__ __forceinline__ F2 f2(float a, float b) {
+  F2 r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r.v) : "f"(a), "f"(b));
+  return r;
+}
+__device__ __forceinline__ float f2_lo(F2 x) {
+  float a;
+  asm("{\n.reg .f32 u;\nmov.b64 {%0, u}, %1;\n}" : "=f"(a) : "l"(x.v));
+  return a;
+}
+__device__ __forceinline__ float f2_hi(F2 x) {
+  float b;
+  asm("{\n.reg .f32 u;\nmov.b64 {u, %0}, %1;\n}" : "=f"(b) : "l"(x.v));
+  return b;
+}
+__device__ __forceinline__ F2 add2(F2 a, F2 b) {
+  F2 r;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r.v) : "l"(a.v), "l"(b.v));
+  return r;
+}
+__device__ __forceinline__ F2 fma2(F2 a, F2 b, F2 c) {
+  F2 r;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r.v) : "l"(a.v), "l"(b.v), "l"(c.v));
+  return r;
+}
+// -0 pair read from constant memory, so that the code generator does not know its value (below).
+static __constant__ float c_f2_negzero[2] = {-0.0f, -0.0f};
+__device__ __forceinline__ F2 f2_negzero() { return f2(c_f2_negzero[0], c_f2_negzero[1]); }
+// Paired product a b, rounded once: fma(a, b, -0) = RN(a b) for every a, b. The code generator was measured
+// (B200) to merge mul.rn.f32x2 followed by add.rn.f32x2 into one fused multiply-add, and to fold an fma
+// with a literal -0 addend the same way, either of which drops a rounding; an addend it cannot see through
+// keeps the product rounded on its own.
+__device__ __forceinline__ F2 mul2(F2 a, F2 b, F2 nz) { return fma2(a, b, nz); }
+// RN(x / d) for d = 3 or 5 (correction step above), two lanes at once.
+__device__ __forceinline__ F2 div_const2(F2 x, float d, float rcp, F2 nz) {
+  const F2 c = f2(rcp, rcp), q = mul2(x, c, nz);
+  return fma2(fma2(q, f2(-d, -d), x), c, q);
+}
+
+// approx_exp in straight-line form (no loops, no branches), two values at a time on the paired fp32 pipe:
 // - the halving loop runs while scaled < -1, i.e. h = [v < -1] + [v < -2] + [v < -4] + [v < -8] times for
 //   v > -16, and each halving is exact (|scaled| >= 1 before it), so scaled = v * 2^-h in one exact multiply;
 // - the six divisions by the term degree: /1 and the power-of-two degrees are exact multiplications, /3 and
@@ -272,28 +316,47 @@ __device__ __forceinline__ float select_f32(bool p, float a, float b) {
 // - the h squarings are the same chain of products, selected by the same comparisons.
 // Same result as approx_exp for every input: finite ones (the zero sign of a quotient cannot reach the series,
 // whose first term is 1), -inf and nan (0), and +inf (the series diverges to +inf; the correction steps
-// would give nan, so it is selected explicitly).
+// would give nan, so it is selected explicitly). nz = f2_negzero().
+__device__ __forceinline__ void approx_exp_fast2(float v0, float v1, float& r0, float& r1, F2 nz) {
+  const bool a1 = v0 < -1.0f, a2 = v0 < -2.0f, a4 = v0 < -4.0f, a8 = v0 < -8.0f;
+  const bool b1 = v1 < -1.0f, b2 = v1 < -2.0f, b4 = v1 < -4.0f, b8 = v1 < -8.0f;
+  const int h0 = (int)a1 + (int)a2 + (int)a4 + (int)a8, h1 = (int)b1 + (int)b2 + (int)b4 + (int)b8;
+  const F2 scaled = mul2(f2(v0, v1), f2(__int_as_float((127 - h0) << 23), __int_as_float((127 - h1) << 23)), nz);
+  const F2 half = mul2(scaled, f2(0.5f, 0.5f), nz);
+  const F2 q3 = div_const2(scaled, 3.0f, 0x1.555556p-2f, nz), q4 = mul2(scaled, f2(0.25f, 0.25f), nz);
+  const F2 q5 = div_const2(scaled, 5.0f, 0x1.99999ap-3f, nz), q6 = div_const2(half, 3.0f, 0x1.555556p-2f, nz);
+  F2 term = scaled, series = add2(f2(1.0f, 1.0f), scaled);
+  term = mul2(term, half, nz);
+  series = add2(series, term);
+  term = mul2(term, q3, nz);
+  series = add2(series, term);
+  term = mul2(term, q4, nz);
+  series = add2(series, term);
+  term = mul2(term, q5, nz);
+  series = add2(series, term);
+  term = mul2(term, q6, nz);
+  series = add2(series, term);
+  const F2 s2 = mul2(series, series, nz), s4 = mul2(s2, s2, nz), s8 = mul2(s4, s4, nz), s16 = mul2(s8, s8, nz);
+  float x = f2_lo(series), y = f2_hi(series);
+  x = a1 ? f2_lo(s2) : x;
+  y = b1 ? f2_hi(s2) : y;
+  x = a2 ? f2_lo(s4) : x;
+  y = b2 ? f2_hi(s4) : y;
+  x = a4 ? f2_lo(s8) : x;
+  y = b4 ? f2_hi(s8) : y;
+  x = a8 ? f2_lo(s16) : x;
+  y = b8 ? f2_hi(s16) : y;
+  x = (v0 <= -16.0f || !(x > 0.0f)) ? 0.0f : x;
+  y = (v1 <= -16.0f || !(y > 0.0f)) ? 0.0f : y;
+  r0 = v0 > 3.402823466e38f ? v0 : x;
+  r1 = v1 > 3.402823466e38f ? v1 : y;
+}
+
+// One value (the paired form with both lanes on it).
 __device__ __forceinline__ float approx_exp_fast(float value) {
-  const bool c1 = value < -1.0f, c2 = value < -2.0f, c4 = value < -4.0f, c8 = value < -8.0f;
-  const int h = (int)c1 + (int)c2 + (int)c4 + (int)c8;
-  const float scaled = __fmul_rn(value, __int_as_float((127 - h) << 23));  // value * 2^-h
-  const float half = __fmul_rn(scaled, 0.5f);
-  const float q[6] = {scaled, half, div_by_3_rn(scaled), __fmul_rn(scaled, 0.25f), div_by_5_rn(scaled),
-                      div_by_3_rn(half)};
-  float term = 1.0f, series = 1.0f;
-#pragma unroll
-  for (int i = 0; i < 6; ++i) {
-    term = __fmul_rn(term, q[i]);
-    series = __fadd_rn(series, term);
-  }
-  const float s2 = __fmul_rn(series, series), s4 = __fmul_rn(s2, s2), s8 = __fmul_rn(s4, s4),
-              s16 = __fmul_rn(s8, s8);
-  float r = select_f32(c1, s2, series);
-  r = select_f32(c2, s4, r);
-  r = select_f32(c4, s8, r);
-  r = select_f32(c8, s16, r);
-  r = select_f32(value <= -16.0f || !(r > 0.0f), 0.0f, r);
-  return select_f32(value > 3.402823466e38f, value, r);
+  float r, same;
+  approx_exp_fast2(value, value, r, same, f2_negzero());
+  return r;
 }
 
 // Round-to-nearest-even to bf16, kept in fp32 (verification/reference_wrapper_backend.py:40-46).
