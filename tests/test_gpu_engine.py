@@ -173,6 +173,31 @@ def test_graph_and_eager_paths_agree(host):
         eng.close()
 
 
+@pytest.mark.parametrize("wbits", [4, 8])
+def test_prefill_graph_replay_matches_eager(host, wbits):
+    """A prefill of a length seen before replays its captured CUDA graph: same next token and the same K/V
+    rows, bit for bit, as the eager first call; a different slot gets its own graph."""
+    prompt = [int(x) for x in np.random.default_rng(3).integers(0, 151936, 37)]
+    eng = host.Engine(0, wbits, max_seqs=2, max_len=256)
+    try:
+        eng.init_synthetic(4)
+        first = eng.prefill(0, prompt)  # eager pass + capture
+        k0, v0 = eng.read_kv(0, 27, len(prompt))
+        for _ in range(2):
+            eng.reset(0)
+            assert eng.prefill(0, prompt) == first  # graph replay
+            k, v = eng.read_kv(0, 27, len(prompt))
+            assert np.array_equal(k, k0) and np.array_equal(v, v0)
+        assert eng.prefill(1, prompt) == first  # other slot: eager + capture, same values
+        k1, v1 = eng.read_kv(1, 27, len(prompt))
+        assert np.array_equal(k1, k0) and np.array_equal(v1, v0)
+        eng.set_option("graphs", 0)
+        eng.reset(0)
+        assert eng.prefill(0, prompt) == first
+    finally:
+        eng.close()
+
+
 def test_batched_decode_matches_single(host):
     """Four sequences decoded together equal the same sequences decoded one by one."""
     seed = 12

@@ -523,6 +523,83 @@ int run_decode_step(qwen_engine* e, int nt, int max_len, bool advance) {
   return 0;
 }
 
+// The device work of one prefill (tokens already in p_tokens): embedding gather, 28 layers, LM head of the
+// last token into d_next.
+int enqueue_prefill(qwen_engine* e, int slot, int n) {
+  cudaStream_t s = e->stream;
+  embed_gather_kernel<<<n, 256, 0, s>>>(e->embed, e->p_tokens, n, e->p_x);
+  E_TRY(cudaGetLastError());
+  const bool tc = e->wbits == 8;
+  const DigitPlanes dp{e->p_planes, e->p_steps, n, tgemm_pad(n), kHidden};
+  const DigitPlanes dph{e->p_planes, e->p_steps, n, tgemm_pad(n), kInter};
+  for (int l = 0; l < kLayers; ++l) {
+    const LayerDev& L = e->layers[l];
+    E_TRY(launch_prefill_rmsnorm(e->p_x, L.input_ln, n, e->p_xn, s));
+    if (tc) {  // W8: projections on the int8 tensor cores
+      E_TRY(tgemm_digitize(e->p_xn, dp, s));
+      E_TRY(tgemm_qkv(L, dp, e->rope_pre_cos, e->rope_pre_sin, e->p_q, e->p_k, e->p_v, s));
+    } else {
+      E_TRY(launch_prefill_qkv(e->wbits, L, e->p_xn, n, e->rope_pre_cos, e->rope_pre_sin, e->p_q, e->p_k, e->p_v, s));
+    }
+    if (e->use_attn_tc) {
+      E_TRY(launch_prefill_attention_tc(e->p_q, e->p_k, e->p_v, n, e->p_ctx, e->p_attn, e->p_attn_bytes, s));
+    } else {
+      E_TRY(launch_prefill_attention(e->p_q, e->p_k, e->p_v, n, e->p_ctx, s));
+    }
+    if (tc) {
+      E_TRY(tgemm_digitize(e->p_ctx, dp, s));
+      E_TRY(tgemm_o(L, dp, e->p_a, s));
+    } else {
+      E_TRY(launch_prefill_o(e->wbits, L, e->p_ctx, n, e->p_a, s));
+    }
+    kv_scatter_kernel<<<n, 256, 0, s>>>(e->p_k, e->p_v, n, paged_view(e, l), slot, 1);
+    E_TRY(cudaGetLastError());
+    E_TRY(launch_prefill_rmsnorm(e->p_a, L.post_ln, n, e->p_xn, s));
+    if (tc) {
+      E_TRY(tgemm_digitize(e->p_xn, dp, s));
+      E_TRY(tgemm_gateup(L, dp, e->p_h, s));
+      E_TRY(tgemm_digitize(e->p_h, dph, s));
+      E_TRY(tgemm_down(L, dph, e->p_a, e->p_x, true, s));
+    } else {
+      E_TRY(launch_prefill_gateup(e->wbits, L, e->p_xn, n, e->p_h, s));
+      E_TRY(launch_prefill_down(e->wbits, L, e->p_h, e->p_a, n, e->p_x, true, s));
+    }
+    if (e->dump_hidden) {
+      // prefill keeps each layer's output row of the last prompt token
+      E_TRY(cudaMemcpyAsync(e->dump + (size_t)l * kHidden, e->p_x + (size_t)(n - 1) * kHidden, kHidden * 4,
+                            cudaMemcpyDeviceToDevice, s));
+    }
+  }
+  if (int st = enqueue_lm_head(e, e->p_x + (size_t)(n - 1) * kHidden, 1, e->d_next,
+                               e->keep_logits ? e->logits : nullptr, false))
+    return st;
+  return 0;
+}
+
+// Prefill through a CUDA graph per (token count, slot) once one eager pass has run (kernel set-up outside
+// capture): the ~12 launches per layer of a short prompt otherwise cost host time comparable to the work.
+int run_prefill(qwen_engine* e, int slot, int n) {
+  if (!e->use_graphs || e->dump_hidden || e->keep_logits) return enqueue_prefill(e, slot, n);
+  const long long key = (2ll << 61) | ((long long)n << 20) | slot;
+  auto it = e->graphs.find(key);
+  if (it == e->graphs.end()) {
+    if (int st = enqueue_prefill(e, slot, n)) return st;
+    cudaGraph_t g;
+    E_TRY(cudaStreamBeginCapture(e->stream, cudaStreamCaptureModeThreadLocal));
+    const int st = enqueue_prefill(e, slot, n);
+    cudaError_t ce = cudaStreamEndCapture(e->stream, &g);
+    if (st) return st;
+    E_TRY(ce);
+    cudaGraphExec_t exec;
+    E_TRY(cudaGraphInstantiate(&exec, g, 0));
+    cudaGraphDestroy(g);
+    e->graphs.emplace(key, exec);
+    return 0;  // the eager pass produced this call's result
+  }
+  E_TRY(cudaGraphLaunch(it->second, e->stream));
+  return 0;
+}
+
 }  // namespace
 
 extern "C" {
@@ -749,52 +826,7 @@ int qwen_engine_prefill(qwen_engine* e, int slot, const int32_t* tokens, int n, 
   if (int st = ensure_pages(e, slot, n)) return st;
   cudaStream_t s = e->stream;
   E_TRY(cudaMemcpyAsync(e->p_tokens, tokens, (size_t)n * 4, cudaMemcpyHostToDevice, s));
-  embed_gather_kernel<<<n, 256, 0, s>>>(e->embed, e->p_tokens, n, e->p_x);
-  E_TRY(cudaGetLastError());
-  const bool tc = e->wbits == 8;
-  const DigitPlanes dp{e->p_planes, e->p_steps, n, tgemm_pad(n), kHidden};
-  const DigitPlanes dph{e->p_planes, e->p_steps, n, tgemm_pad(n), kInter};
-  for (int l = 0; l < kLayers; ++l) {
-    const LayerDev& L = e->layers[l];
-    E_TRY(launch_prefill_rmsnorm(e->p_x, L.input_ln, n, e->p_xn, s));
-    if (tc) {  // W8: projections on the int8 tensor cores
-      E_TRY(tgemm_digitize(e->p_xn, dp, s));
-      E_TRY(tgemm_qkv(L, dp, e->rope_pre_cos, e->rope_pre_sin, e->p_q, e->p_k, e->p_v, s));
-    } else {
-      E_TRY(launch_prefill_qkv(e->wbits, L, e->p_xn, n, e->rope_pre_cos, e->rope_pre_sin, e->p_q, e->p_k, e->p_v, s));
-    }
-    if (e->use_attn_tc) {
-      E_TRY(launch_prefill_attention_tc(e->p_q, e->p_k, e->p_v, n, e->p_ctx, e->p_attn, e->p_attn_bytes, s));
-    } else {
-      E_TRY(launch_prefill_attention(e->p_q, e->p_k, e->p_v, n, e->p_ctx, s));
-    }
-    if (tc) {
-      E_TRY(tgemm_digitize(e->p_ctx, dp, s));
-      E_TRY(tgemm_o(L, dp, e->p_a, s));
-    } else {
-      E_TRY(launch_prefill_o(e->wbits, L, e->p_ctx, n, e->p_a, s));
-    }
-    kv_scatter_kernel<<<n, 256, 0, s>>>(e->p_k, e->p_v, n, paged_view(e, l), slot, 1);
-    E_TRY(cudaGetLastError());
-    E_TRY(launch_prefill_rmsnorm(e->p_a, L.post_ln, n, e->p_xn, s));
-    if (tc) {
-      E_TRY(tgemm_digitize(e->p_xn, dp, s));
-      E_TRY(tgemm_gateup(L, dp, e->p_h, s));
-      E_TRY(tgemm_digitize(e->p_h, dph, s));
-      E_TRY(tgemm_down(L, dph, e->p_a, e->p_x, true, s));
-    } else {
-      E_TRY(launch_prefill_gateup(e->wbits, L, e->p_xn, n, e->p_h, s));
-      E_TRY(launch_prefill_down(e->wbits, L, e->p_h, e->p_a, n, e->p_x, true, s));
-    }
-    if (e->dump_hidden) {
-      // prefill keeps each layer's output row of the last prompt token
-      E_TRY(cudaMemcpyAsync(e->dump + (size_t)l * kHidden, e->p_x + (size_t)(n - 1) * kHidden, kHidden * 4,
-                            cudaMemcpyDeviceToDevice, s));
-    }
-  }
-  if (int st = enqueue_lm_head(e, e->p_x + (size_t)(n - 1) * kHidden, 1, e->d_next,
-                               e->keep_logits ? e->logits : nullptr, false))
-    return st;
+  if (int st = run_prefill(e, slot, n)) return st;
   E_TRY(cudaMemcpyAsync(e->h_io + 12, e->d_next, 4, cudaMemcpyDeviceToHost, s));
   E_TRY(cudaStreamSynchronize(s));
   e->seq_len[slot] = n;
