@@ -15,75 +15,42 @@ namespace qb {
 namespace {
 
 // ---- RMSNorm -------------------------------------------------------------------------------------
-// CTA = 32 tokens. The reference's sum of squares is one serial fp32 chain per token (kept bit for bit), so
-// warp 0 runs the 32 chains (thread = token) out of shared memory while warps 1-3 stage the next
-// 128-column chunk of the 32 rows with coalesced loads; then all threads write the normalised rows, eight
-// rows of loads in flight at a time.
-constexpr int kNormTok = 32, kNormCols = 128, kNormPad = kNormCols + 1;
+// CTA = 8 tokens. The reference's sum of squares is one serial fp32 chain per token (kept bit for bit):
+// all 128 threads stage the 8 rows in shared memory with every load in flight at once, lanes 0..7 of warp 0
+// run the 8 chains (rows padded by one float: the lanes read different banks), then all threads write the
+// normalised rows from shared memory.
+constexpr int kNormTok = 8, kNormPad = kHidden + 1;
+constexpr size_t kNormSmem = (size_t)kNormTok * kNormPad * 4 + kNormTok * 4;
 
 __global__ void __launch_bounds__(128) prefill_rmsnorm_kernel(const float* __restrict__ x, const float* __restrict__ w,
                                                               int S, float* __restrict__ xn) {
-  __shared__ float tile[2][kNormTok][kNormPad];
-  __shared__ float inv_s[kNormTok];
+  extern __shared__ float nsm[];
+  float* rows = nsm;                          // [kNormTok][kNormPad]
+  float* inv_s = nsm + kNormTok * kNormPad;   // [kNormTok]
   const int t0 = blockIdx.x * kNormTok, tid = threadIdx.x;
   const int n = min(kNormTok, S - t0);
-  auto stage = [&](int c, int buf) {  // warps 1-3
-    for (int i = tid - 32; i < kNormTok * (kNormCols / 4); i += 96) {
-      const int rr = i / (kNormCols / 4), f = i % (kNormCols / 4);
-      float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-      if (rr < n) v = *reinterpret_cast<const float4*>(x + (size_t)(t0 + rr) * kHidden + kNormCols * c + 4 * f);
-      float* dst = &tile[buf][rr][4 * f];
-      dst[0] = v.x;
-      dst[1] = v.y;
-      dst[2] = v.z;
-      dst[3] = v.w;
-    }
-  };
-  if (tid >= 32) stage(0, 0);
-  __syncthreads();
-  float ms = 0.0f;
-  constexpr int kChunks = kHidden / kNormCols;
-  for (int c = 0; c < kChunks; ++c) {
-    if (tid >= 32) {
-      if (c + 1 < kChunks) stage(c + 1, (c + 1) & 1);
-    } else {
-      const float* row = tile[c & 1][tid];
-#pragma unroll 8
-      for (int d = 0; d < kNormCols; ++d) ms = __fadd_rn(ms, __fmul_rn(row[d], row[d]));
-    }
-    __syncthreads();
+  for (int i = tid; i < n * (kHidden / 4); i += 128) {
+    const int r = i / (kHidden / 4), f = i % (kHidden / 4);
+    const float4 v = *reinterpret_cast<const float4*>(x + (size_t)(t0 + r) * kHidden + 4 * f);
+    float* d = rows + r * kNormPad + 4 * f;
+    d[0] = v.x;
+    d[1] = v.y;
+    d[2] = v.z;
+    d[3] = v.w;
   }
+  __syncthreads();
   if (tid < n) {
+    const float* row = rows + tid * kNormPad;
+    float ms = 0.0f;
+#pragma unroll 16
+    for (int d = 0; d < kHidden; ++d) ms = __fadd_rn(ms, __fmul_rn(row[d], row[d]));
     ms = __fdiv_rn(ms, (float)kHidden);
     inv_s[tid] = __fdiv_rn(1.0f, approx_sqrt(__fadd_rn(ms, kEps)));
   }
   __syncthreads();
-  // thread: float4 columns tid, tid + 128, tid + 256 of every row
-  float4 wv[3];
-#pragma unroll
-  for (int j = 0; j < 3; ++j) wv[j] = *reinterpret_cast<const float4*>(w + 4 * (tid + 128 * j));
-  for (int i0 = 0; i0 < n; i0 += 8) {
-    float4 xv[8][3];
-#pragma unroll
-    for (int i = 0; i < 8; ++i)
-#pragma unroll
-      for (int j = 0; j < 3; ++j)
-        if (i0 + i < n)
-          xv[i][j] = *reinterpret_cast<const float4*>(x + (size_t)(t0 + i0 + i) * kHidden + 4 * (tid + 128 * j));
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      if (i0 + i >= n) break;
-      const float inv = inv_s[i0 + i];
-#pragma unroll
-      for (int j = 0; j < 3; ++j) {
-        float4 o;
-        o.x = __fmul_rn(__fmul_rn(xv[i][j].x, inv), wv[j].x);
-        o.y = __fmul_rn(__fmul_rn(xv[i][j].y, inv), wv[j].y);
-        o.z = __fmul_rn(__fmul_rn(xv[i][j].z, inv), wv[j].z);
-        o.w = __fmul_rn(__fmul_rn(xv[i][j].w, inv), wv[j].w);
-        *reinterpret_cast<float4*>(xn + (size_t)(t0 + i0 + i) * kHidden + 4 * (tid + 128 * j)) = o;
-      }
-    }
+  for (int i = tid; i < n * kHidden; i += 128) {
+    const int r = i / kHidden, d = i % kHidden;
+    xn[(size_t)(t0 + r) * kHidden + d] = __fmul_rn(__fmul_rn(rows[r * kNormPad + d], inv_s[r]), __ldg(w + d));
   }
 }
 
@@ -248,7 +215,10 @@ cudaError_t run_gemm(const GemmArgs& a, int n_tiles, cudaStream_t s) {
 }  // namespace
 
 cudaError_t launch_prefill_rmsnorm(const float* x, const float* w, int S, float* xn, cudaStream_t s) {
-  prefill_rmsnorm_kernel<<<(S + kNormTok - 1) / kNormTok, 128, 0, s>>>(x, w, S, xn);
+  const cudaError_t e =
+      cudaFuncSetAttribute(prefill_rmsnorm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kNormSmem);
+  if (e != cudaSuccess) return e;
+  prefill_rmsnorm_kernel<<<(S + kNormTok - 1) / kNormTok, 128, kNormSmem, s>>>(x, w, S, xn);
   return cudaGetLastError();
 }
 
