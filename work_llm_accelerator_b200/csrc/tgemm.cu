@@ -121,7 +121,7 @@ __device__ __forceinline__ void mma_t(uint32_t d, uint64_t a, uint64_t b, uint32
 }
 
 template <int EPI, int TN, int ST>
-__global__ void __launch_bounds__(kThreadsT, 1)
+__global__ void __launch_bounds__(kThreadsT, ST == 2 ? 2 : 1)
     tgemm_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ CUtensorMap pmap, TArgs a) {
   using C = TCfg<TN, ST>;
   constexpr int kTN = TN;
@@ -224,7 +224,46 @@ __global__ void __launch_bounds__(kThreadsT, 1)
   const int tb = rank * tp, te = tb + tp;
   const int* inbox = reinterpret_cast<const int*>(stages);
   bool ok = true;
+  // Epilogue constants and the global loads of a chunk (RoPE table, K/V row addresses, residual) do not
+  // depend on the accumulators: the first chunk's are issued before the wait, behind the main loop.
+  int row = 0;
+  float sc = 0.f, bb = 0.f;
+  float cs[kChunkN], sn[kChunkN], res[kChunkN];
+  float* kvp[kChunkN];
+  const int S_hi = min(a.S, n0 + te);  // tokens that exist and belong to this CTA
+  auto chunk_loads = [&](int c0) {
+    if constexpr (EPI == kTQkv) {
+      const int h = mtile, p = r & 63;
+      const bool rope = h < kHeads + kKvHeads;
+#pragma unroll
+      for (int c = 0; c < kChunkN; ++c) {
+        const int n = min(n0 + c0 + c, a.S - 1);
+        const int pos = a.decode ? __ldg(a.pos + n) : n;
+        cs[c] = rope ? __ldg(a.cosv + (size_t)pos * 64 + p) : 1.f;
+        sn[c] = rope ? __ldg(a.sinv + (size_t)pos * 64 + p) : 0.f;
+        kvp[c] = nullptr;
+        if (a.decode && h >= kHeads) {
+          const int which = h < kHeads + kKvHeads ? 0 : 1;
+          kvp[c] = kv_row(a.kv, __ldg(a.seq + n), pos, which) + (row - kHidden - which * kKvWidth);
+        }
+      }
+    } else if constexpr (EPI == kTDown) {
+#pragma unroll
+      for (int c = 0; c < kChunkN; ++c) {
+        const int n = n0 + c0 + c;
+        res[c] = n < S_hi ? __ldg(a.resid + (size_t)n * kHidden + row) : 0.f;
+      }
+    }
+  };
   if (warp >= 2) {
+    if constexpr (EPI == kTGateUp) {
+      row = r < 64 ? mtile * 64 + r : a.second_row0 + mtile * 64 + (r - 64);
+    } else {
+      row = mtile * kTileM + r;
+    }
+    if constexpr (EPI != kTRaw) sc = __ldg(a.scale + row);
+    if constexpr (EPI == kTQkv) bb = __ldg(a.bias + row);
+    if (tb < te && n0 + tb < a.S) chunk_loads(tb);
     ok = mbar_wait(&sm.acc_full, 0);
     fence_after();
   }
@@ -252,18 +291,9 @@ __global__ void __launch_bounds__(kThreadsT, 1)
     cluster_sync_all();  // every partial delivered
   }
   if (warp >= 2) {
-    int row;
-    float sc = 0.f, bb = 0.f;
-    if constexpr (EPI == kTGateUp) {
-      row = r < 64 ? mtile * 64 + r : a.second_row0 + mtile * 64 + (r - 64);
-    } else {
-      row = mtile * kTileM + r;
-    }
-    if constexpr (EPI != kTRaw) sc = __ldg(a.scale + row);
-    if constexpr (EPI == kTQkv) bb = __ldg(a.bias + row);
     const uint32_t lane_base = tmem + ((uint32_t)(q * 32) << 16);
     for (int c0 = tb; c0 < te && n0 + c0 < a.S; c0 += kChunkN) {  // chunks holding real tokens only
-      const int S_hi = min(a.S, n0 + te);  // tokens of this chunk that exist and belong to this CTA
+      if (c0 != tb) chunk_loads(c0);
       int v0[16], v1[16], v2[16];
       if (ks > 1) {
 #pragma unroll
@@ -307,12 +337,6 @@ __global__ void __launch_bounds__(kThreadsT, 1)
         }
         // every global load of the chunk is issued before any result is used (one round trip per chunk)
         if constexpr (EPI == kTScale || EPI == kTDown) {
-          float res[kChunkN];
-#pragma unroll
-          for (int c = 0; c < kChunkN; ++c) {
-            const int n = n0 + c0 + c;
-            res[c] = (EPI == kTDown && n < S_hi) ? __ldg(a.resid + (size_t)n * kHidden + row) : 0.f;
-          }
 #pragma unroll
           for (int c = 0; c < kChunkN; ++c) {
             const int n = n0 + c0 + c;
@@ -325,22 +349,8 @@ __global__ void __launch_bounds__(kThreadsT, 1)
           }
         } else if constexpr (EPI == kTQkv) {
           // tile = head: rows r and r ^ 64 are RoPE partners (q and k heads); token index = position
-          const int h = mtile, p = r & 63;
+          const int h = mtile;
           const bool rope = h < kHeads + kKvHeads;
-          float cs[kChunkN], sn[kChunkN];
-          float* kvp[kChunkN];
-#pragma unroll
-          for (int c = 0; c < kChunkN; ++c) {
-            const int n = min(n0 + c0 + c, a.S - 1);
-            const int pos = a.decode ? __ldg(a.pos + n) : n;
-            cs[c] = rope ? __ldg(a.cosv + (size_t)pos * 64 + p) : 1.f;
-            sn[c] = rope ? __ldg(a.sinv + (size_t)pos * 64 + p) : 0.f;
-            kvp[c] = nullptr;
-            if (a.decode && h >= kHeads) {
-              const int which = h < kHeads + kKvHeads ? 0 : 1;
-              kvp[c] = kv_row(a.kv, __ldg(a.seq + n), pos, which) + (row - kHidden - which * kKvWidth);
-            }
-          }
 #pragma unroll
           for (int c = 0; c < kChunkN; ++c) sm.ys[r][c] = __fmaf_rn(sc, yv[c], bb);
           named_sync(kBarT, kEpiT);
