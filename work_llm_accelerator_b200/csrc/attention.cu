@@ -29,7 +29,6 @@ static_assert(kMergeBatch * kGroups * kPartStride <= kChunk * kRow, "merge stagi
 
 struct DecodeAttnSmem {
   float ks[kChunk][kRow];  // also the merge staging area: kMergeBatch x 6 x 130 floats fit
-  float vs[kChunk][kHeadDim];
   float qs[kGroups][kRow];
   float es[kChunk][8];  // per key: the six heads' scores, then weights (padded to 8)
   float ms[kGroups], ls[kGroups];
@@ -85,17 +84,22 @@ __global__ void __launch_bounds__(kAttnThreads) decode_attn_kernel(const float* 
   const float* kbase = kv_row(kv, seq, k0, 0) + g * kHeadDim;
   const float* vbase = kv_row(kv, seq, k0, 1) + g * kHeadDim;
   const int nhist = min(n, pos - k0);  // rows of this chunk that precede the new token
-  // every row of the chunk in flight at once: asynchronous global->shared copies, one wait
+  // every row of the chunk in flight at once: K by asynchronous global->shared copies, V straight into
+  // registers (thread = one of the 128 dims of every key: 512 contiguous bytes per key), one wait. Keeping
+  // V out of shared memory lets more CTAs share an SM.
   for (int i = tid; i < nhist * 32; i += kAttnThreads) {
     const int r = i >> 5, f = i & 31;
     cp_async16(&sm.ks[r][4 * f], kbase + (size_t)r * kKvWidth + 4 * f);
-    cp_async16(&sm.vs[r][4 * f], vbase + (size_t)r * kKvWidth + 4 * f);
   }
+  float vr[kChunk];
+#pragma unroll
+  for (int k = 0; k < kChunk; ++k) vr[k] = k < nhist ? __ldg(vbase + (size_t)k * kKvWidth + tid) : 0.0f;
   griddep_wait();
-  if (pos < k0 + kChunk && tid < 32) {
-    const int r = pos - k0;
-    cp_async16(&sm.ks[r][4 * tid], kbase + (size_t)r * kKvWidth + 4 * tid);
-    cp_async16(&sm.vs[r][4 * tid], vbase + (size_t)r * kKvWidth + 4 * tid);
+  const int knew = pos - k0;  // the new token's row in this chunk (if 0 <= knew < kChunk)
+  float vnew = 0.0f;
+  if (knew >= 0 && knew < kChunk) {
+    if (tid < 32) cp_async16(&sm.ks[knew][4 * tid], kbase + (size_t)knew * kKvWidth + 4 * tid);
+    vnew = vbase[(size_t)knew * kKvWidth + tid];
   }
   for (int i = tid; i < kGroups * 32; i += kAttnThreads) {
     const int h = i >> 5, f = i & 31;
@@ -165,9 +169,10 @@ __global__ void __launch_bounds__(kAttnThreads) decode_attn_kernel(const float* 
   float acc[kGroups];
 #pragma unroll
   for (int h = 0; h < kGroups; ++h) acc[h] = 0.f;
-#pragma unroll 4
-  for (int key = 0; key < n; ++key) {
-    const float vv = sm.vs[key][tid];
+#pragma unroll
+  for (int key = 0; key < kChunk; ++key) {
+    if (key >= n) break;
+    const float vv = key == knew ? vnew : vr[key];
     const float4 e03 = *reinterpret_cast<const float4*>(&sm.es[key][0]);
     const float2 e45 = *reinterpret_cast<const float2*>(&sm.es[key][4]);
     acc[0] = fmaf(e03.x, vv, acc[0]);
