@@ -198,15 +198,17 @@ __global__ void __launch_bounds__(kAttnThreads) decode_attn_kernel(const float* 
     my[tid * kPartStride + 0] = sm.ms[tid];
     my[tid * kPartStride + 1] = sm.ls[tid];
   }
-  __threadfence();
+  // One gpu-scope acquire-release add by one thread publishes the whole CTA's partial (the barrier orders
+  // the other threads' writes before it) and, for the last CTA, acquires every other CTA's partial.
   __syncthreads();
   if (tid == 0) {
-    const unsigned prev = atomicAdd(&counters[t * kKvHeads + g], 1u);
+    unsigned prev;
+    asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;" : "=r"(prev) : "l"(&counters[t * kKvHeads + g])
+                 : "memory");
     sm.last = (prev == (unsigned)nchunks - 1u);
   }
   __syncthreads();
   if (!sm.last) return;
-  __threadfence();
   // Merge this (token, KV head)'s chunks in chunk order, online (deterministic, the same operations as the
   // persistent decode kernel): M' = max(M, m_c), o = o e^(M - M') + acc_c e^(m_c - M'), L likewise.
   const float* base = part + ((size_t)t * kKvHeads + g) * max_chunks * kGroups * kPartStride;
