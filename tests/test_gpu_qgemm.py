@@ -108,6 +108,7 @@ def test_digit_products_rejects_bad_shapes(built_libs, gpu_available):
     (256, 1536, 130),   # two token tiles, the second ragged
     (2048, 1536, 300),  # q|k|v rows, three token tiles
     (128, 8960, 129),   # down_proj K, ragged tokens
+    (256, 8960, 2433),  # many token tiles: the CTA-pair form (256-row tiles), ragged tokens
 ])
 def test_digit_planes_exact(built_libs, gpu_available, rows, k, nt):
     """Many-token tensor-core path (prefill / batched projections): three int32 planes per output, exact."""
@@ -125,10 +126,15 @@ def test_digit_planes_exact(built_libs, gpu_available, rows, k, nt):
     x[:, rng.integers(0, k, 5)] *= 40.0
     x[nt // 2, :] = 0.0  # an all-zero token row (step 1)
     step_ref, d = digits_numpy(x)
-    c64 = codes.astype(np.int64)
-    acc_ref = np.stack([d[p] @ c64.T for p in range(3)])  # [3][nt][rows]
-    assert np.abs(acc_ref).max() < 2**31
     dev = torch.device("cuda")
+    if rows * k * nt <= 2**31:
+        c64 = codes.astype(np.int64)
+        acc_ref = np.stack([d[p] @ c64.T for p in range(3)])  # [3][nt][rows]
+    else:  # float64 products and sums of these integers are exact (|sum| < 2^31 << 2^53)
+        c_f = torch.from_numpy(codes.astype(np.float64)).to(dev)
+        acc_ref = np.stack([(torch.from_numpy(d[p].astype(np.float64)).to(dev) @ c_f.T).cpu().numpy()
+                            for p in range(3)]).astype(np.int64)
+    assert np.abs(acc_ref).max() < 2**31
     codes_d = torch.from_numpy(codes).to(dev)
     x_d = torch.from_numpy(x).to(dev)
     acc_d = torch.full((3, nt, rows), -7, dtype=torch.int32, device=dev)

@@ -39,19 +39,25 @@ constexpr int kMaxStages = 8;
 // small batch does not move or multiply padding.
 // ST > 0 fixes the pipeline depth (ST = 2 with TN = 64 keeps a CTA under half of the shared memory, so
 // two CTAs share an SM and one's epilogue overlaps the other's main loop); ST = 0 fills ~200 KB.
+// ST = kPairST selects the CTA-pair form (TN = 64): two CTAs on two SMs compute a 256-row tile with
+// tcgen05.mma.cta_group::2 (M = 256, N = 192); each holds its 128 weight rows and half of the 192 digit-plane
+// rows, so a stage moves 16 + 12 KB per CTA instead of 16 + 24 KB; three stages, two CTAs per SM.
+constexpr int kPairST = 3;
 template <int TN, int ST = 0>
 struct TCfg {
+  static constexpr bool kPair = ST == kPairST;
   static constexpr int kPlaneTile = TN * kKBlock;
-  static constexpr int kStage = kUnitBytes + kPlanes * kPlaneTile;
+  static constexpr int kStage = kUnitBytes + (kPair ? kPlanes * kPlaneTile / 2 : kPlanes * kPlaneTile);
   static constexpr int kAutoStages = (200 * 1024) / kStage > kMaxStages ? kMaxStages : (200 * 1024) / kStage;
   static constexpr int kStages = ST > 0 ? ST : kAutoStages;
   // The three plane tiles sit back to back in a stage, which is the layout of one 3 TN-row tile: up to
   // N = 256 one MMA covers all three planes (accumulator column p TN + n = plane p, token n).
   static constexpr bool kFused = kPlanes * TN <= 256;
-  static constexpr uint32_t kIdesc = idesc_i8(kTileM, kFused ? kPlanes * TN : TN);
+  static constexpr uint32_t kIdesc = idesc_i8(kPair ? 2 * kTileM : kTileM, kFused ? kPlanes * TN : TN);
   static constexpr int kTmemCols = kPlanes * TN <= 32 ? 32 : kPlanes * TN <= 64 ? 64 : kPlanes * TN <= 128 ? 128
                                    : kPlanes * TN <= 256 ? 256 : 512;
   static_assert(TN % 16 == 0 && TN <= 128, "token tile");
+  static_assert(!kPair || TN == 64, "the pair form splits 3 x 64 plane rows into two halves of 96");
 };
 
 struct TSmem {
@@ -112,6 +118,65 @@ __device__ __forceinline__ void st_peer(uint32_t saddr, uint32_t rank, int v) {
   asm volatile("st.shared::cluster.b32 [%0], %1;" ::"r"(pa), "r"(v) : "memory");
 }
 
+// ---- CTA-pair (cta_group::2) forms ----
+// Address in the shared memory of CTA `rank` of the cluster that `saddr` has in this CTA.
+__device__ __forceinline__ uint32_t peer_addr(uint32_t saddr, uint32_t rank) {
+  uint32_t pa;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(pa) : "r"(saddr), "r"(rank));
+  return pa;
+}
+// Bounded wait with cluster-scope acquire (for barriers another CTA of the cluster arrives on).
+__device__ __forceinline__ bool mbar_try_wait_cluster(uint64_t* bar, unsigned parity) {
+  unsigned ok;
+  asm volatile(
+      "{\n.reg .pred p;\nmbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\nselp.u32 %0, 1, 0, p;\n}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+__device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, unsigned parity) {
+  if (mbar_try_wait_cluster(bar, parity)) return true;
+  const long long t0 = clock64();
+  while (true) {
+    if (mbar_try_wait_cluster(bar, parity)) return true;
+    if (clock64() - t0 > 4000000000ll) {
+      atomicExch(&g_kernel_error, kErrMbarTimeout);
+      return false;
+    }
+  }
+}
+__device__ __forceinline__ void tmem_alloc_pair(uint32_t* dst_smem, uint32_t cols) {
+  asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(dst_smem)), "r"(cols)
+               : "memory");
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc_pair(uint32_t taddr, uint32_t cols) {
+  asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(cols) : "memory");
+}
+// One MMA over the pair: A rows 0..127 from the leader's and 128..255 from the peer's shared memory, B rows
+// split the same way, D rows in each CTA's own TMEM. Issued by the leader.
+template <uint32_t IDESC>
+__device__ __forceinline__ void mma_pair(uint32_t d, uint64_t a, uint64_t b, uint32_t acc) {
+  asm volatile(
+      "{\n.reg .pred p;\nsetp.ne.b32 p, %4, 0;\ntcgen05.mma.cta_group::2.kind::i8 [%0], %1, %2, %3, p;\n}" ::"r"(d),
+      "l"(a), "l"(b), "r"(IDESC), "r"(acc)
+      : "memory");
+}
+// The mbarrier at cluster address `bar` (this CTA's or the peer's) completes one arrival once every pair
+// MMA issued before has finished.
+__device__ __forceinline__ void mma_commit_pair(uint32_t bar) {
+  asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
+}
+// TMA load into this CTA's shared memory whose completion counts on the leader's mbarrier (cluster address).
+__device__ __forceinline__ void tma_load_2d_pair(void* dst, const CUtensorMap* map, int c0, int c1, uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], "
+      "[%4];" ::"r"(smem_u32(dst)),
+      "l"(map), "r"(c0), "r"(c1), "r"(bar)
+      : "memory");
+}
+
 template <uint32_t IDESC>
 __device__ __forceinline__ void mma_t(uint32_t d, uint64_t a, uint64_t b, uint32_t acc) {
   asm volatile(
@@ -121,7 +186,7 @@ __device__ __forceinline__ void mma_t(uint32_t d, uint64_t a, uint64_t b, uint32
 }
 
 template <int EPI, int TN, int ST>
-__global__ void __launch_bounds__(kThreadsT, ST == 2 ? 2 : 1)
+__global__ void __launch_bounds__(kThreadsT, (ST == 2 || ST == kPairST) ? 2 : 1)
     tgemm_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ CUtensorMap pmap, TArgs a) {
   using C = TCfg<TN, ST>;
   constexpr int kTN = TN;
@@ -134,8 +199,11 @@ __global__ void __launch_bounds__(kThreadsT, ST == 2 ? 2 : 1)
   TSmem& sm = *reinterpret_cast<TSmem*>(stages + (size_t)kStagesT * kStageBytes);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   // split K: the ksplit CTAs of a cluster share one output tile, CTA `rank` sums K blocks [kb_lo, kb_hi)
-  const int ks = a.ksplit;
+  // (the pair form does not split K: its cluster of two is the CTA pair, `prank` 0 the leader)
+  constexpr bool kPair = C::kPair;
+  const int ks = kPair ? 1 : a.ksplit;
   const int rank = ks > 1 ? (int)cluster_rank() : 0;
+  const int prank = kPair ? (int)cluster_rank() : 0;
   const int mtile = blockIdx.x / ks, n0 = blockIdx.y * kTN;
   const int kb_lo = rank * a.nkb / ks, kb_hi = (rank + 1) * a.nkb / ks;
 
@@ -147,10 +215,16 @@ __global__ void __launch_bounds__(kThreadsT, ST == 2 ? 2 : 1)
     mbar_init(&sm.acc_full, 1);
     mbar_fence_init();
   }
-  if (warp == 1) tmem_alloc(&sm.tmem_base, kTmemColsT);
+  if (warp == 1) {
+    if constexpr (kPair)
+      tmem_alloc_pair(&sm.tmem_base, kTmemColsT);
+    else
+      tmem_alloc(&sm.tmem_base, kTmemColsT);
+  }
   for (int i = threadIdx.x; i < kTN; i += blockDim.x) sm.steps[i] = a.steps[n0 + i];
   fence_before();
   __syncthreads();
+  if constexpr (kPair) cluster_sync_all();  // both CTAs' barriers initialised before any cross-CTA signal
   fence_after();
   const uint32_t tmem = sm.tmem_base;
 
@@ -162,10 +236,29 @@ __global__ void __launch_bounds__(kThreadsT, ST == 2 ? 2 : 1)
       int s = 0;
       unsigned ph = 0;
       bool ok = true;
+      // pair form: every copy completes on the leader's full barrier
+      const uint32_t full0 = kPair ? peer_addr(smem_u32(&sm.full[0]), 0) : 0u;
       for (int kb = kb_lo; kb < kb_hi && ok; ++kb) {
-        if (!(ok = mbar_wait(&sm.empty[s], ph ^ 1))) break;
-        mbar_arrive_expect_tx(&sm.full[s], kStageBytes);
+        if (!(ok = kPair ? mbar_wait_cluster(&sm.empty[s], ph ^ 1) : mbar_wait(&sm.empty[s], ph ^ 1))) break;
         uint8_t* st = stages + (size_t)s * kStageBytes;
+        if constexpr (kPair) {
+          if (prank == 0) mbar_arrive_expect_tx(&sm.full[s], 2 * kStageBytes);
+          const uint32_t fb = full0 + 8u * s;
+          tma_load_2d_pair(st, &wmap, kb * kKBlock, row0, fb);
+          if (a.box_rows != kTileM) tma_load_2d_pair(st + a.box_rows * kKBlock, &wmap, kb * kKBlock, row0 + a.second_row0, fb);
+#pragma unroll
+          for (int i = 0; i < 3; ++i) {  // plane rows 96 prank + 32 i .. + 32 (row = 64 plane + token)
+            const int pr = 96 * prank + 32 * i;
+            tma_load_2d_pair(st + kUnitBytes + i * 32 * kKBlock, &pmap, kb * kKBlock, (pr / 64) * a.Spad + n0 + pr % 64,
+                             fb);
+          }
+          if (++s == kStagesT) {
+            s = 0;
+            ph ^= 1;
+          }
+          continue;
+        }
+        mbar_arrive_expect_tx(&sm.full[s], kStageBytes);
         tma_load_2d(st, &wmap, kb * kKBlock, row0, &sm.full[s]);
         if (a.box_rows != kTileM)
           tma_load_2d(st + a.box_rows * kKBlock, &wmap, kb * kKBlock, row0 + a.second_row0, &sm.full[s]);
@@ -179,7 +272,7 @@ __global__ void __launch_bounds__(kThreadsT, ST == 2 ? 2 : 1)
       }
       // every issued stage consumed before leaving (no copy in flight at exit)
       for (int i = 0; i < kStagesT && ok; ++i) {
-        ok = mbar_wait(&sm.empty[s], ph ^ 1);
+        ok = kPair ? mbar_wait_cluster(&sm.empty[s], ph ^ 1) : mbar_wait(&sm.empty[s], ph ^ 1);
         if (++s == kStagesT) {
           s = 0;
           ph ^= 1;
@@ -187,7 +280,7 @@ __global__ void __launch_bounds__(kThreadsT, ST == 2 ? 2 : 1)
       }
     }
   } else if (warp == 1) {
-    if (lane == 0) {
+    if (lane == 0 && (!kPair || prank == 0)) {
       int s = 0;
       unsigned ph = 0;
       bool ok = true;
@@ -201,17 +294,31 @@ __global__ void __launch_bounds__(kThreadsT, ST == 2 ? 2 : 1)
           for (int p = 0; p < (C::kFused ? 1 : kPlanes); ++p) {
             const uint64_t bd = sw128_desc(sb + kUnitBytes + p * kPlaneTile);
 #pragma unroll
-            for (int j = 0; j < kKBlock / 32; ++j)
-              mma_t<C::kIdesc>(tmem + p * kTN, ad + 2 * j, bd + 2 * j, (kb > kb_lo || j > 0) ? 1u : 0u);
+            for (int j = 0; j < kKBlock / 32; ++j) {
+              if constexpr (kPair)
+                mma_pair<C::kIdesc>(tmem + p * kTN, ad + 2 * j, bd + 2 * j, (kb > kb_lo || j > 0) ? 1u : 0u);
+              else
+                mma_t<C::kIdesc>(tmem + p * kTN, ad + 2 * j, bd + 2 * j, (kb > kb_lo || j > 0) ? 1u : 0u);
+            }
           }
         }
-        mma_commit(&sm.empty[s]);
+        if constexpr (kPair) {  // both CTAs' stage s is free once the pair MMAs finished
+          mma_commit_pair(smem_u32(&sm.empty[s]));
+          mma_commit_pair(peer_addr(smem_u32(&sm.empty[s]), 1));
+        } else {
+          mma_commit(&sm.empty[s]);
+        }
         if (++s == kStagesT) {
           s = 0;
           ph ^= 1;
         }
       }
-      mma_commit(&sm.acc_full);
+      if constexpr (kPair) {
+        mma_commit_pair(smem_u32(&sm.acc_full));
+        mma_commit_pair(peer_addr(smem_u32(&sm.acc_full), 1));
+      } else {
+        mma_commit(&sm.acc_full);
+      }
     }
   }
   // ---- epilogue: thread = one tile row (TMEM lane), 16 tokens per read
@@ -264,7 +371,7 @@ __global__ void __launch_bounds__(kThreadsT, ST == 2 ? 2 : 1)
     if constexpr (EPI != kTRaw) sc = __ldg(a.scale + row);
     if constexpr (EPI == kTQkv) bb = __ldg(a.bias + row);
     if (tb < te && n0 + tb < a.S) chunk_loads(tb);
-    ok = mbar_wait(&sm.acc_full, 0);
+    ok = kPair ? mbar_wait_cluster(&sm.acc_full, 0) : mbar_wait(&sm.acc_full, 0);
     fence_after();
   }
   if (ks > 1) {
@@ -400,9 +507,13 @@ __global__ void __launch_bounds__(kThreadsT, ST == 2 ? 2 : 1)
   }
   fence_before();
   __syncthreads();
+  if constexpr (kPair) cluster_sync_all();  // neither CTA leaves while the pair still uses its memory
   if (warp == 1) {
     fence_after();
-    tmem_dealloc(tmem, kTmemColsT);
+    if constexpr (kPair)
+      tmem_dealloc_pair(tmem, kTmemColsT);
+    else
+      tmem_dealloc(tmem, kTmemColsT);
   }
 }
 
@@ -616,8 +727,9 @@ cudaError_t run_tgemm_tn(const uint8_t* w, int rows_total, int K, int mtiles, in
     return cudaErrorInvalidValue;
   a.ksplit = ksplit;
   CUtensorMap wmap, pmap;
+  if (C::kPair && ((mtiles & 1) || ksplit != 1 || K / kKBlock < C::kStages)) return cudaErrorInvalidValue;
   if (!make_map(&wmap, w, (uint64_t)rows_total, (uint64_t)K, (uint32_t)box_rows) ||
-      !make_map(&pmap, x.planes, (uint64_t)kPlanes * x.Spad, (uint64_t)K, TN))
+      !make_map(&pmap, x.planes, (uint64_t)kPlanes * x.Spad, (uint64_t)K, C::kPair ? 32u : (uint32_t)TN))
     return cudaErrorInvalidValue;
   a.nkb = K / kKBlock;
   a.box_rows = box_rows;
@@ -647,11 +759,11 @@ cudaError_t run_tgemm_tn(const uint8_t* w, int rows_total, int K, int mtiles, in
   cfg.stream = s;
   cudaLaunchAttribute at[1];
   at[0].id = cudaLaunchAttributeClusterDimension;
-  at[0].val.clusterDim.x = ksplit;
+  at[0].val.clusterDim.x = C::kPair ? 2 : ksplit;
   at[0].val.clusterDim.y = 1;
   at[0].val.clusterDim.z = 1;
   cfg.attrs = at;
-  cfg.numAttrs = ksplit > 1 ? 1 : 0;
+  cfg.numAttrs = (C::kPair || ksplit > 1) ? 1 : 0;
   return cudaLaunchKernelEx(&cfg, kern, wmap, pmap, a);
 }
 
@@ -671,6 +783,8 @@ cudaError_t run_tgemm(const uint8_t* w, int rows_total, int K, int mtiles, int b
   if (x.Spad >= 128) {  // many tokens: 64-token tiles, two CTAs per SM unless K is split
     const int ks = pick_ksplit(mtiles * (x.Spad / 64), nkb);
     if (ks > 1) return run_tgemm_tn<EPI, 64>(w, rows_total, K, mtiles, box_rows, second_row0, x, a, s, ks);
+    if ((mtiles & 1) == 0 && nkb >= TCfg<64, kPairST>::kStages)  // CTA pairs: 256-row tiles
+      return run_tgemm_tn<EPI, 64, kPairST>(w, rows_total, K, mtiles, box_rows, second_row0, x, a, s);
     return run_tgemm_tn<EPI, 64, 2>(w, rows_total, K, mtiles, box_rows, second_row0, x, a, s);
   }
   // few tokens: split the long-K projection (down), and q|k|v so that each CTA finishes one 16-token chunk
