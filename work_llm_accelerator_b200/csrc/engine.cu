@@ -126,6 +126,7 @@ struct qwen_engine {
   int pre_cap = 0;
   float *p_x = nullptr, *p_xn = nullptr, *p_q = nullptr, *p_ctx = nullptr, *p_a = nullptr, *p_h = nullptr,
         *p_k = nullptr, *p_v = nullptr;
+  float* p_qkv = nullptr;  // W8: biased q|k|v rows before RoPE [cap][2048]
   int* p_tokens = nullptr;
   int8_t* p_planes = nullptr;  // W8 prefill: digit planes [3][Spad][8960] and steps [Spad]
   float* p_steps = nullptr;
@@ -262,6 +263,8 @@ int ensure_prefill_buffers(qwen_engine* e, int n) {
   e->p_attn_bytes = prefill_attn_tc_scratch_bytes(cap);
   E_TRY(cudaMalloc(&e->p_attn, e->p_attn_bytes));
   if (e->wbits == 8) {
+    cudaFree(e->p_qkv);
+    E_TRY(dalloc(&e->p_qkv, (size_t)cap * kQkvRows));
     cudaFree(e->p_planes);
     cudaFree(e->p_steps);
     E_TRY(dalloc(&e->p_planes, tgemm_plane_bytes(cap, kInter)));
@@ -438,7 +441,7 @@ int enqueue_decode_batched(qwen_engine* e, int n, int max_len, bool advance) {
     E_TRY(mark(kBcDigits));
     E_TRY(tgemm_rmsnorm_digitize(e->p_x, L.input_ln, dp, s));
     E_TRY(mark(kBcQkv));
-    E_TRY(tgemm_qkv_decode(L, dp, e->d_pos, e->d_seq, kv, e->rope_dec_cos, e->rope_dec_sin, e->p_q, s));
+    E_TRY(tgemm_qkv_decode(L, dp, e->d_pos, e->d_seq, kv, e->rope_dec_cos, e->rope_dec_sin, e->p_q, e->p_qkv, s));
     E_TRY(mark(kBcAttn));
     E_TRY(launch_decode_attention(e->p_q, kv, tok, max_len, e->p_ctx, e->attn_part, e->attn_cnt, s, false));
     E_TRY(mark(kBcDigits));
@@ -537,7 +540,7 @@ int enqueue_prefill(qwen_engine* e, int slot, int n) {
     E_TRY(launch_prefill_rmsnorm(e->p_x, L.input_ln, n, e->p_xn, s));
     if (tc) {  // W8: projections on the int8 tensor cores
       E_TRY(tgemm_digitize(e->p_xn, dp, s));
-      E_TRY(tgemm_qkv(L, dp, e->rope_pre_cos, e->rope_pre_sin, e->p_q, e->p_k, e->p_v, s));
+      E_TRY(tgemm_qkv(L, dp, e->rope_pre_cos, e->rope_pre_sin, e->p_q, e->p_k, e->p_v, e->p_qkv, s));
     } else {
       E_TRY(launch_prefill_qkv(e->wbits, L, e->p_xn, n, e->rope_pre_cos, e->rope_pre_sin, e->p_q, e->p_k, e->p_v, s));
     }
@@ -721,6 +724,7 @@ void qwen_engine_destroy(qwen_engine* e) {
   cudaFree(e->p_planes);
   cudaFree(e->p_steps);
   cudaFree(e->p_attn);
+  cudaFree(e->p_qkv);
   for (cudaEvent_t ev : e->kev)
     if (ev) cudaEventDestroy(ev);
   for (cudaEvent_t ev : e->bev) cudaEventDestroy(ev);

@@ -63,7 +63,8 @@ struct Ctx {
   // int8 tensor-core projections (wbits 8): split-K scratch (decode), digit planes and steps (prefill)
   QgemmScratch qsc{nullptr, nullptr};
   Buf planes, psteps;
-  Buf attn;  // tensor-core prefill attention scratch
+  Buf attn;     // tensor-core prefill attention scratch
+  Buf qkv_raw;  // W8 prefill: biased q|k|v rows before RoPE
   // zero-weight layer for the stub entry points
   Buf zw, zs;
   LayerPtrs zero{};
@@ -354,8 +355,9 @@ int run_prefill(int wbits, const LayerPtrs& L, bool attention, bool mlp, const f
     QB_TRY(launch_prefill_rmsnorm((const float*)c.x.p, D.input_ln, S, (float*)c.out.p, c.stream));
     if (tc) {
       QB_TRY(tgemm_digitize((const float*)c.out.p, dp, c.stream));
+      QB_TRY(ensure(c.qkv_raw, (size_t)S * kQkvRows * 4));
       QB_TRY(tgemm_qkv(D, dp, (const float*)c.rope_pre_cos.p, (const float*)c.rope_pre_sin.p, (float*)c.q.p,
-                       (float*)c.kc.p, (float*)c.vc.p, c.stream));
+                       (float*)c.kc.p, (float*)c.vc.p, (float*)c.qkv_raw.p, c.stream));
     } else {
       QB_TRY(launch_prefill_qkv(wbits, D, (const float*)c.out.p, S, (const float*)c.rope_pre_cos.p,
                                 (const float*)c.rope_pre_sin.p, (float*)c.q.p, (float*)c.kc.p, (float*)c.vc.p,

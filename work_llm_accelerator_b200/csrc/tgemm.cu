@@ -78,20 +78,11 @@ struct TArgs {
   const float* steps;
   const float* scale;
   const float* bias;
-  const float* cosv;
-  const float* sinv;
   float* out;
-  float* k_cache;
-  float* v_cache;
   const float* resid;
   bool round_out;
   int* raw;
-  // decode (batched): RoPE row = pos[t], K/V rows written through the paged view at (seq[t], pos[t]),
-  // SiLU with expf (the decode reference) instead of approx_exp (the prefill reference)
-  bool decode;
-  const int* pos;
-  const int* seq;
-  KvView kv;
+  bool decode;  // gate|up SiLU with expf (the decode reference) instead of approx_exp (the prefill reference)
 };
 
 __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int c0, int c1, uint64_t* bar) {
@@ -331,30 +322,14 @@ __global__ void __launch_bounds__(kThreadsT, (ST == 2 || ST == kPairST) ? 2 : 1)
   const int tb = rank * tp, te = tb + tp;
   const int* inbox = reinterpret_cast<const int*>(stages);
   bool ok = true;
-  // Epilogue constants and the global loads of a chunk (RoPE table, K/V row addresses, residual) do not
-  // depend on the accumulators: the first chunk's are issued before the wait, behind the main loop.
+  // Epilogue constants and the global loads of a chunk (the residual) do not depend on the accumulators:
+  // the first chunk's are issued before the wait, behind the main loop.
   int row = 0;
   float sc = 0.f, bb = 0.f;
-  float cs[kChunkN], sn[kChunkN], res[kChunkN];
-  float* kvp[kChunkN];
+  float res[kChunkN];
   const int S_hi = min(a.S, n0 + te);  // tokens that exist and belong to this CTA
   auto chunk_loads = [&](int c0) {
-    if constexpr (EPI == kTQkv) {
-      const int h = mtile, p = r & 63;
-      const bool rope = h < kHeads + kKvHeads;
-#pragma unroll
-      for (int c = 0; c < kChunkN; ++c) {
-        const int n = min(n0 + c0 + c, a.S - 1);
-        const int pos = a.decode ? __ldg(a.pos + n) : n;
-        cs[c] = rope ? __ldg(a.cosv + (size_t)pos * 64 + p) : 1.f;
-        sn[c] = rope ? __ldg(a.sinv + (size_t)pos * 64 + p) : 0.f;
-        kvp[c] = nullptr;
-        if (a.decode && h >= kHeads) {
-          const int which = h < kHeads + kKvHeads ? 0 : 1;
-          kvp[c] = kv_row(a.kv, __ldg(a.seq + n), pos, which) + (row - kHidden - which * kKvWidth);
-        }
-      }
-    } else if constexpr (EPI == kTDown) {
+    if constexpr (EPI == kTDown) {
 #pragma unroll
       for (int c = 0; c < kChunkN; ++c) {
         const int n = n0 + c0 + c;
@@ -455,38 +430,12 @@ __global__ void __launch_bounds__(kThreadsT, (ST == 2 || ST == kPairST) ? 2 : 1)
             if (n < S_hi) a.out[(size_t)n * kHidden + row] = y;
           }
         } else if constexpr (EPI == kTQkv) {
-          // tile = head: rows r and r ^ 64 are RoPE partners (q and k heads); token index = position
-          const int h = mtile;
-          const bool rope = h < kHeads + kKvHeads;
-#pragma unroll
-          for (int c = 0; c < kChunkN; ++c) sm.ys[r][c] = __fmaf_rn(sc, yv[c], bb);
-          named_sync(kBarT, kEpiT);
-          float* dst;
-          size_t stride;
-          if (h < kHeads) {
-            dst = a.out + row;
-            stride = kHidden;
-          } else if (h < kHeads + kKvHeads) {
-            dst = a.k_cache + (row - kHidden);
-            stride = kKvWidth;
-          } else {
-            dst = a.v_cache + (row - kHidden - kKvWidth);
-            stride = kKvWidth;
-          }
+          // biased q|k|v rows [S][2048]; RoPE and the K/V row writes follow in qkv_rope_kernel
 #pragma unroll
           for (int c = 0; c < kChunkN; ++c) {
             const int n = n0 + c0 + c;
-            const float mine = sm.ys[r][c], other = sm.ys[r ^ 64][c];
-            float y = mine;
-            if (rope)
-              y = r < 64 ? __fsub_rn(__fmul_rn(mine, cs[c]), __fmul_rn(other, sn[c]))
-                         : __fadd_rn(__fmul_rn(mine, cs[c]), __fmul_rn(other, sn[c]));
-            if (n < S_hi) {
-              if (kvp[c] != nullptr) *kvp[c] = y;
-              else dst[(size_t)n * stride] = y;
-            }
+            if (n < S_hi) a.out[(size_t)n * kQkvRows + row] = __fmaf_rn(sc, yv[c], bb);
           }
-          named_sync(kBarT, kEpiT);
         } else {  // gate|up: tile rows 0..63 gate rows 64 j.., 64..127 the matching up rows
 #pragma unroll
           for (int c = 0; c < kChunkN; ++c) sm.ys[r][c] = sc * yv[c];
@@ -687,6 +636,46 @@ __global__ void __launch_bounds__(128) rmsnorm_digitize_kernel(const float* __re
   }
 }
 
+// RoPE of the biased q|k|v rows and their destinations, one CTA of 256 threads per token. A thread takes the
+// partner rows (d, d + 64) of a head: q and k heads rotate (d < 64: y_d = x_d cos - x_{d+64} sin,
+// y_{d+64} = x_{d+64} cos + x_d sin, the reference's operations and order), v rows pass through. Prefill:
+// position = token index, K/V rows into flat caches; decode: position pos[t], K/V rows through the paged view
+// at (seq[t], pos[t]).
+__global__ void __launch_bounds__(256) qkv_rope_kernel(const float* __restrict__ raw, const float* __restrict__ cosv,
+                                                       const float* __restrict__ sinv, bool decode,
+                                                       const int* __restrict__ posv, const int* __restrict__ seqv,
+                                                       KvView kv, float* __restrict__ k_cache, float* __restrict__ v_cache,
+                                                       float* __restrict__ q_out) {
+  const int t = blockIdx.x;
+  const int pos = decode ? posv[t] : t;
+  const float* x = raw + (size_t)t * kQkvRows;
+  float* kdst = decode ? kv_row(kv, seqv[t], pos, 0) : k_cache + (size_t)t * kKvWidth;
+  float* vdst = decode ? kv_row(kv, seqv[t], pos, 1) : v_cache + (size_t)t * kKvWidth;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int pr = threadIdx.x + 256 * i;  // pair index: head pr / 64, dims d and d + 64
+    const int head = pr >> 6, d = pr & 63;
+    const int r0 = head * kHeadDim + d, r1 = r0 + 64;
+    const float x0 = x[r0], x1 = x[r1];
+    float y0 = x0, y1 = x1;
+    if (head < kHeads + kKvHeads) {
+      const float c = cosv[(size_t)pos * 64 + d], sn = sinv[(size_t)pos * 64 + d];
+      y0 = __fsub_rn(__fmul_rn(x0, c), __fmul_rn(x1, sn));
+      y1 = __fadd_rn(__fmul_rn(x1, c), __fmul_rn(x0, sn));
+    }
+    if (head < kHeads) {
+      q_out[(size_t)t * kHidden + r0] = y0;
+      q_out[(size_t)t * kHidden + r1] = y1;
+    } else if (head < kHeads + kKvHeads) {
+      kdst[r0 - kHidden] = y0;
+      kdst[r1 - kHidden] = y1;
+    } else {
+      vdst[r0 - kHidden - kKvWidth] = y0;
+      vdst[r1 - kHidden - kKvWidth] = y1;
+    }
+  }
+}
+
 // ---------------------------------------------------------------------------------------------------
 // host side
 // ---------------------------------------------------------------------------------------------------
@@ -787,11 +776,8 @@ cudaError_t run_tgemm(const uint8_t* w, int rows_total, int K, int mtiles, int b
       return run_tgemm_tn<EPI, 64, kPairST>(w, rows_total, K, mtiles, box_rows, second_row0, x, a, s);
     return run_tgemm_tn<EPI, 64, 2>(w, rows_total, K, mtiles, box_rows, second_row0, x, a, s);
   }
-  // few tokens: split the long-K projection (down), and q|k|v so that each CTA finishes one 16-token chunk
-  // (its epilogue has dependent loads per chunk); measured slower for the short-K o_proj and gate|up
-  int ks = 1;
-  if (nkb >= 32) ks = pick_ksplit(mtiles, nkb);
-  else if (EPI == kTQkv) ks = std::min(pick_ksplit(mtiles, nkb), std::max(1, x.Spad / 16));
+  // few tokens: split the long-K projection (down); measured slower for the short-K ones
+  const int ks = nkb >= 32 ? pick_ksplit(mtiles, nkb) : 1;
   switch (x.Spad) {
     case 16: return run_tgemm_tn<EPI, 16>(w, rows_total, K, mtiles, box_rows, second_row0, x, a, s, ks);
     case 32: return run_tgemm_tn<EPI, 32>(w, rows_total, K, mtiles, box_rows, second_row0, x, a, s, ks);
@@ -815,16 +801,16 @@ cudaError_t tgemm_digitize(const float* x, DigitPlanes d, cudaStream_t s) {
 }
 
 cudaError_t tgemm_qkv(const LayerDev& L, const DigitPlanes& x, const float* rope_cos, const float* rope_sin, float* q_out,
-                      float* k_cache, float* v_cache, cudaStream_t s) {
+                      float* k_cache, float* v_cache, float* raw, cudaStream_t s) {
   TArgs a{};
   a.scale = L.qkv_s;
   a.bias = L.qkv_b;
-  a.cosv = rope_cos;
-  a.sinv = rope_sin;
-  a.out = q_out;
-  a.k_cache = k_cache;
-  a.v_cache = v_cache;
-  return run_tgemm<kTQkv>(L.qkv_w, kQkvRows, kHidden, kQkvRows / kTileM, kTileM, 0, x, a, s);
+  a.out = raw;
+  cudaError_t e = run_tgemm<kTQkv>(L.qkv_w, kQkvRows, kHidden, kQkvRows / kTileM, kTileM, 0, x, a, s);
+  if (e != cudaSuccess) return e;
+  qkv_rope_kernel<<<x.S, 256, 0, s>>>(raw, rope_cos, rope_sin, false, nullptr, nullptr, KvView{}, k_cache, v_cache,
+                                      q_out);
+  return cudaGetLastError();
 }
 
 cudaError_t tgemm_o(const LayerDev& L, const DigitPlanes& x, float* out, cudaStream_t s) {
@@ -852,18 +838,15 @@ cudaError_t tgemm_down(const LayerDev& L, const DigitPlanes& x, const float* res
 }
 
 cudaError_t tgemm_qkv_decode(const LayerDev& L, const DigitPlanes& x, const int* pos, const int* seq, KvView kv,
-                             const float* rope_cos, const float* rope_sin, float* q_out, cudaStream_t s) {
+                             const float* rope_cos, const float* rope_sin, float* q_out, float* raw, cudaStream_t s) {
   TArgs a{};
   a.scale = L.qkv_s;
   a.bias = L.qkv_b;
-  a.cosv = rope_cos;
-  a.sinv = rope_sin;
-  a.out = q_out;
-  a.decode = true;
-  a.pos = pos;
-  a.seq = seq;
-  a.kv = kv;
-  return run_tgemm<kTQkv>(L.qkv_w, kQkvRows, kHidden, kQkvRows / kTileM, kTileM, 0, x, a, s);
+  a.out = raw;
+  cudaError_t e = run_tgemm<kTQkv>(L.qkv_w, kQkvRows, kHidden, kQkvRows / kTileM, kTileM, 0, x, a, s);
+  if (e != cudaSuccess) return e;
+  qkv_rope_kernel<<<x.S, 256, 0, s>>>(raw, rope_cos, rope_sin, true, pos, seq, kv, nullptr, nullptr, q_out);
+  return cudaGetLastError();
 }
 
 cudaError_t tgemm_gateup_decode(const LayerDev& L, const DigitPlanes& x, float* h, cudaStream_t s) {

@@ -28,10 +28,11 @@ cudaError_t tgemm_digitize(const float* x, DigitPlanes d, cudaStream_t s);
 cudaError_t tgemm_rmsnorm_digitize(const float* x, const float* w, DigitPlanes d, cudaStream_t s);
 
 // Projections of all S tokens with the prefill epilogues (the same operations as the CUDA-core prefill
-// GEMMs in prefill_simt.cu): q|k|v + RoPE (table rows = token index) + K/V rows of a flat cache; o_proj;
-// gate|up + SiLU(approx_exp) * up; down + residual (optional bf16 rounding).
+// GEMMs in prefill_simt.cu): q|k|v + RoPE (table rows = token index) + K/V rows of a flat cache (raw:
+// [S][2048] fp32 scratch for the biased rows before RoPE); o_proj; gate|up + SiLU(approx_exp) * up;
+// down + residual (optional bf16 rounding).
 cudaError_t tgemm_qkv(const LayerDev& L, const DigitPlanes& x, const float* rope_cos, const float* rope_sin, float* q_out,
-                      float* k_cache, float* v_cache, cudaStream_t s);
+                      float* k_cache, float* v_cache, float* raw, cudaStream_t s);
 cudaError_t tgemm_o(const LayerDev& L, const DigitPlanes& x, float* out, cudaStream_t s);
 cudaError_t tgemm_gateup(const LayerDev& L, const DigitPlanes& x, float* h, cudaStream_t s);
 cudaError_t tgemm_down(const LayerDev& L, const DigitPlanes& x, const float* resid, float* out, bool round_out,
@@ -41,7 +42,7 @@ cudaError_t tgemm_down(const LayerDev& L, const DigitPlanes& x, const float* res
 // tables and the new K/V rows written through the paged view at (seq[t], pos[t]); gate|up with expf SiLU.
 // o_proj and down are the same as for prefill.
 cudaError_t tgemm_qkv_decode(const LayerDev& L, const DigitPlanes& x, const int* pos, const int* seq, KvView kv,
-                             const float* rope_cos, const float* rope_sin, float* q_out, cudaStream_t s);
+                             const float* rope_cos, const float* rope_sin, float* q_out, float* raw, cudaStream_t s);
 cudaError_t tgemm_gateup_decode(const LayerDev& L, const DigitPlanes& x, float* h, cudaStream_t s);
 // Decode RMSNorm (double accumulation) of n rows of 1536.
 cudaError_t decode_rmsnorm(const float* x, const float* w, int n, float* out, cudaStream_t s);
