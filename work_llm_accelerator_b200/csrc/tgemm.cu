@@ -467,6 +467,7 @@ __global__ void __launch_bounds__(kThreadsT, (ST == 2 || ST == kPairST) ? 2 : 1)
 }
 
 // One CTA per token row: per-token step and the three digit planes; padded rows become zero.
+constexpr int kDigitVec = 9;  // float4 per thread: rows up to 9216 floats
 __global__ void __launch_bounds__(256) digitize_kernel(const float* __restrict__ x, int S, int K, int Spad,
                                                        int8_t* __restrict__ planes, float* __restrict__ steps) {
   const int t = blockIdx.x;
@@ -483,11 +484,17 @@ __global__ void __launch_bounds__(256) digitize_kernel(const float* __restrict__
     if (threadIdx.x == 0) steps[t] = 1.0f;
     return;
   }
+  // the row is read once and held in registers (four values per float4, up to kDigitVec per thread)
   const float* row = x + (size_t)t * K;
+  float4 v[kDigitVec];
   float m = 0.f;
-  for (int k = threadIdx.x * 4; k < K; k += 1024) {
-    const float4 v = *reinterpret_cast<const float4*>(row + k);
-    m = fmaxf(m, fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
+#pragma unroll
+  for (int i = 0; i < kDigitVec; ++i) {
+    const int k = 4 * ((int)threadIdx.x + 256 * i);
+    if (k < K) {
+      v[i] = *reinterpret_cast<const float4*>(row + k);
+      m = fmaxf(m, fmaxf(fmaxf(fabsf(v[i].x), fabsf(v[i].y)), fmaxf(fabsf(v[i].z), fabsf(v[i].w))));
+    }
   }
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
@@ -497,9 +504,11 @@ __global__ void __launch_bounds__(256) digitize_kernel(const float* __restrict__
   for (int i = 0; i < 8; ++i) mx = fmaxf(mx, red[i]);
   const float st = mx > 0.0f ? mx / kDigitRange : 1.0f;
   if (threadIdx.x == 0) steps[t] = st;
-  for (int k = threadIdx.x * 4; k < K; k += 1024) {
-    const float4 v = *reinterpret_cast<const float4*>(row + k);
-    const float vv[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+  for (int i = 0; i < kDigitVec; ++i) {
+    const int k = 4 * ((int)threadIdx.x + 256 * i);
+    if (k >= K) break;
+    const float vv[4] = {v[i].x, v[i].y, v[i].z, v[i].w};
     uint32_t w0 = 0, w1 = 0, w2 = 0;
 #pragma unroll
     for (int e = 0; e < 4; ++e) {
@@ -795,7 +804,7 @@ cudaError_t tgemm_rmsnorm_digitize(const float* x, const float* w, DigitPlanes d
 }
 
 cudaError_t tgemm_digitize(const float* x, DigitPlanes d, cudaStream_t s) {
-  if (d.K % 4 || d.Spad != tgemm_pad(d.S) || d.S < 1) return cudaErrorInvalidValue;
+  if (d.K % 4 || d.K > 4 * 256 * kDigitVec || d.Spad != tgemm_pad(d.S) || d.S < 1) return cudaErrorInvalidValue;
   digitize_kernel<<<d.Spad, 256, 0, s>>>(x, d.S, d.K, d.Spad, d.planes, d.steps);
   return cudaGetLastError();
 }
