@@ -62,7 +62,8 @@ int qwen_engine_reset(qwen_engine* e, int slot);
  * of more than 4 sequences as one many-token tensor-core step, default 1; 0 = groups of 4), "lm_tc" (LM head
  * on the tensor cores, default 1; 0 = CUDA-core GEMV), "stack_ring" (weight stages in flight per SM in the
  * persistent kernel, 2..9, default 9), "prefill_attn_tc" (prefill attention on the tensor cores, default 1;
- * 0 = CUDA-core kernel). */
+ * 0 = CUDA-core kernel), "attn_ctas" (cap on the CTAs of the separate decode attention kernel, default 0 = one
+ * per SM; results do not depend on it). */
 int qwen_engine_set_option(qwen_engine* e, const char* name, long long value);
 /* Per-layer outputs of the last prefill/decode call: [28][rows][1536] floats (rows = tokens of that call). */
 int qwen_engine_read_hidden(qwen_engine* e, float* out, long long n_floats);

@@ -292,6 +292,40 @@ def test_batched_w8_decode_matches_single(host, n):
         eng.close()
 
 
+def test_decode_attention_grid_does_not_change_results(host):
+    """The separate decode attention kernel is persistent: its CTAs walk contiguous ranges of the
+    (token, KV head, 64-key chunk) items, so one CTA may finish one (token, head) and start the next; a
+    follow-up kernel merges each (token, head)'s chunks in order. Every grid size (option "attn_ctas", down
+    to one CTA doing everything) gives bit-identical layer outputs, equal to the persistent single-sequence
+    kernel's; the histories are ragged (1 to 5 chunks, a chunk holding only the new row)."""
+    rng = np.random.default_rng(77)
+    lens = (3, 64, 65, 200, 257, 130)
+    prompts = [[int(t) for t in rng.integers(0, qo.VOCAB, n)] for n in lens]
+    eng = host.Engine(0, 8, max_seqs=len(lens), max_len=512)
+    try:
+        eng.init_synthetic(23)
+        eng.set_option("dump_hidden", 1)
+        single_tok, single_hid = [], []
+        for i, p in enumerate(prompts):
+            first = eng.prefill(i, p)
+            single_tok.append(int(eng.decode([i], [first])[0]))
+            single_hid.append(eng.read_hidden(1)[:, 0].copy())
+            eng.reset(i)
+        for ctas in (0, 1, 5, 16):
+            eng.set_option("attn_ctas", ctas)
+            cur = [eng.prefill(i, p) for i, p in enumerate(prompts)]
+            out = [int(t) for t in eng.decode(list(range(len(lens))), cur)]
+            hid = eng.read_hidden(len(lens))
+            for i in range(len(lens)):
+                assert np.array_equal(hid[:, i], single_hid[i]), (ctas, i, rel_l2(hid[:, i], single_hid[i]))
+            assert out == single_tok, ctas
+            for i in range(len(lens)):
+                eng.reset(i)
+        assert host.kernel_error(reset=True) == 0
+    finally:
+        eng.close()
+
+
 def test_tensor_core_lm_head_matches_cuda_core_head(host):
     """The tensor-core LM head (fp16 table x two fp16 planes of the normalised activations, 22 significant
     bits; tensor-core fp32 accumulation) and the CUDA-core GEMV head give the same greedy tokens and logits

@@ -133,6 +133,7 @@ struct qwen_engine {
   void* p_attn = nullptr;      // tensor-core prefill attention scratch (fp16 operand planes)
   size_t p_attn_bytes = 0;
   bool use_attn_tc = true;
+  int attn_ctas = 0;  // option "attn_ctas": cap on the decode attention grid (0 = one CTA per SM)
   // options
   bool use_graphs = true, use_pdl = true, dump_hidden = false, keep_logits = false, prefetch = true;
   std::map<long long, cudaGraphExec_t> graphs;
@@ -210,6 +211,7 @@ KvView paged_view(qwen_engine* e, int layer) {
   kv.page_table = e->d_page_table;
   kv.layer = layer;
   kv.max_pages = e->max_pages;
+  kv.pool_pages = e->n_pages;
   return kv;
 }
 
@@ -368,7 +370,7 @@ int enqueue_decode(qwen_engine* e, int nt, int max_len, bool advance) {
       const QgemmLayerMaps& M = e->maps[l];
       E_TRY(qgemm_qkv(M, L, src, tok, e->rope_dec_cos, e->rope_dec_sin, e->q, kv, e->qsc, e->stream, pdl && l > 0));
       E_TRY(launch_decode_attention(e->q, kv, tok, max_len, e->ctx, e->attn_part, e->attn_cnt, e->stream, pdl,
-                                    e->prefetch ? L.gu_w : nullptr, gu_bytes));
+                                    e->prefetch ? L.gu_w : nullptr, gu_bytes, e->attn_ctas));
       E_TRY(qgemm_o(M, L, e->ctx, nt, e->a, e->qsc, e->stream, pdl));
       E_TRY(qgemm_gateup(M, L, e->a, nt, e->h, e->qsc, e->stream, pdl));
       E_TRY(qgemm_down(M, L, e->h, e->a, nt, yout, true, e->qsc, e->stream, pdl));
@@ -376,7 +378,7 @@ int enqueue_decode(qwen_engine* e, int nt, int max_len, bool advance) {
       E_TRY(launch_decode_qkv(e->wbits, L, src, tok, e->rope_dec_cos, e->rope_dec_sin, e->q, kv, e->stream,
                               pdl && l > 0, e->prefetch ? L.o_w : nullptr, o_bytes));
       E_TRY(launch_decode_attention(e->q, kv, tok, max_len, e->ctx, e->attn_part, e->attn_cnt, e->stream, pdl,
-                                    e->prefetch ? L.gu_w : nullptr, gu_bytes));
+                                    e->prefetch ? L.gu_w : nullptr, gu_bytes, e->attn_ctas));
       E_TRY(launch_decode_o(e->wbits, L, e->ctx, nt, e->a, e->stream, pdl, e->prefetch ? L.down_w : nullptr,
                             down_bytes));
       E_TRY(launch_decode_gateup(e->wbits, L, e->a, nt, e->h, e->stream, pdl, e->prefetch ? next_qkv : nullptr,
@@ -443,7 +445,8 @@ int enqueue_decode_batched(qwen_engine* e, int n, int max_len, bool advance) {
     E_TRY(mark(kBcQkv));
     E_TRY(tgemm_qkv_decode(L, dp, e->d_pos, e->d_seq, kv, e->rope_dec_cos, e->rope_dec_sin, e->p_q, e->p_qkv, s));
     E_TRY(mark(kBcAttn));
-    E_TRY(launch_decode_attention(e->p_q, kv, tok, max_len, e->p_ctx, e->attn_part, e->attn_cnt, s, false));
+    E_TRY(launch_decode_attention(e->p_q, kv, tok, max_len, e->p_ctx, e->attn_part, e->attn_cnt, s, false,
+                                  nullptr, 0, e->attn_ctas));
     E_TRY(mark(kBcDigits));
     E_TRY(tgemm_digitize(e->p_ctx, dp, s));
     E_TRY(mark(kBcO));
@@ -800,6 +803,11 @@ int qwen_engine_set_option(qwen_engine* e, const char* name, long long value) {
     e->graphs.clear();
   } else if (n == "prefill_attn_tc") {
     e->use_attn_tc = value != 0;
+  } else if (n == "attn_ctas") {
+    if (value < 0) return kStatusInvalid;
+    e->attn_ctas = value;
+    for (auto& kv : e->graphs) cudaGraphExecDestroy(kv.second);
+    e->graphs.clear();
   } else if (n == "batched") {
     e->use_batched = value != 0;
   } else if (n == "stack") {

@@ -129,6 +129,7 @@ struct KvView {
   const int* page_table;   // nullptr => flat
   int layer;               // paged only
   int max_pages;           // paged only: row length of the page table
+  int pool_pages = 0;      // paged only: pages in the pool (the extent of the decode attention's tensor maps)
 };
 
 // Floats per page: [layer][K|V][kPage][256].

@@ -52,13 +52,16 @@ int lm_head_partial_floats();  // size of the `partial` scratch in floats
 // Error flag of the streaming GEMV kernels (1 = a bounded mbarrier wait gave up); optionally cleared.
 unsigned gemv_kernel_error(bool reset);
 
-// --- decode attention (flash-decoding over 64-token chunks; combine by the last chunk CTA) -------
-// ctx [nt][1536]. scratch: attn_partial_floats(nt, max_len) floats; counters: nt * 2 uints (zeroed once).
+// --- decode attention (flash-decoding over 64-token chunks, then an in-order merge kernel) --------
+// ctx [nt][1536]. scratch: attn_partial_floats(nt, max_len) floats; counters: unused (kept for callers).
 // `prefetch`/`prefetch_bytes` optionally name weights of the following kernels to stream into L2 meanwhile.
+// `max_ctas` > 0 caps the persistent grid (default: one CTA per SM); results do not depend on it.
 cudaError_t launch_decode_attention(const float* q, KvView kv, DecodeTokens tok, int max_len, float* ctx,
                                     float* scratch, unsigned* counters, cudaStream_t s, bool pdl,
-                                    const void* prefetch = nullptr, size_t prefetch_bytes = 0);
+                                    const void* prefetch = nullptr, size_t prefetch_bytes = 0, int max_ctas = 0);
 size_t attn_partial_floats(int nt, int max_len);
+// Error flag of the decode attention kernel (1 = a bounded mbarrier wait gave up); optionally cleared.
+unsigned decode_attn_kernel_error(bool reset);
 
 // --- prefill -------------------------------------------------------------------------------------
 // xn [S][1536] = prefill RMSNorm (serial fp32 sum, approx_sqrt), bit-identical to the reference.

@@ -437,7 +437,8 @@ int qwen_b200_set_prefill_seq_capacity(int capacity) {
 unsigned qwen_b200_kernel_error(int reset) {
   return qb::gemv_kernel_error(reset != 0) | qb::qgemm_kernel_error(reset != 0) |
          qb::stack::decode_stack_kernel_error(reset != 0) | qb::tgemm_kernel_error(reset != 0) |
-         qb::lm_head_kernel_error(reset != 0) | qb::attn_tc_kernel_error(reset != 0);
+         qb::lm_head_kernel_error(reset != 0) | qb::attn_tc_kernel_error(reset != 0) |
+         qb::decode_attn_kernel_error(reset != 0);
 }
 
 int qwen_b200_device_count(void) {
