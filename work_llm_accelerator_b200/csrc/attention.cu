@@ -256,6 +256,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1) decode_attn_kernel(const __gr
       issue_v(i, it, 0);
     }
     griddep_wait();
+    griddep_launch();
     for (int i = 0; i < first; ++i) {
       const ItemSrc it = shfl_src(mine, i);
       issue_k(i, it, 1);

@@ -778,6 +778,15 @@ template <int EPI>
 cudaError_t run_tgemm(const uint8_t* w, int rows_total, int K, int mtiles, int box_rows, int second_row0,
                       const DigitPlanes& x, TArgs a, cudaStream_t s) {
   const int nkb = K / kKBlock;
+  // 33-64 tokens: every row tile re-reads the token digit planes, which already outweigh its weights, so
+  // the planes' traffic sets the time: CTA pairs (each CTA stages half of the planes) where the row tiles
+  // pair up; K split (long K only: measured slower for the short-K projections) for the down projection.
+  if (x.Spad == 64) {
+    const int ks = nkb >= 32 ? pick_ksplit(mtiles, nkb) : 1;
+    if (ks == 1 && (mtiles & 1) == 0 && nkb >= TCfg<64, kPairST>::kStages)
+      return run_tgemm_tn<EPI, 64, kPairST>(w, rows_total, K, mtiles, box_rows, second_row0, x, a, s);
+    return run_tgemm_tn<EPI, 64>(w, rows_total, K, mtiles, box_rows, second_row0, x, a, s, ks);
+  }
   if (x.Spad >= 128) {  // many tokens: 64-token tiles, two CTAs per SM unless K is split
     const int ks = pick_ksplit(mtiles * (x.Spad / 64), nkb);
     if (ks > 1) return run_tgemm_tn<EPI, 64>(w, rows_total, K, mtiles, box_rows, second_row0, x, a, s, ks);
@@ -790,7 +799,6 @@ cudaError_t run_tgemm(const uint8_t* w, int rows_total, int K, int mtiles, int b
   switch (x.Spad) {
     case 16: return run_tgemm_tn<EPI, 16>(w, rows_total, K, mtiles, box_rows, second_row0, x, a, s, ks);
     case 32: return run_tgemm_tn<EPI, 32>(w, rows_total, K, mtiles, box_rows, second_row0, x, a, s, ks);
-    case 64: return run_tgemm_tn<EPI, 64>(w, rows_total, K, mtiles, box_rows, second_row0, x, a, s, ks);
     default: return cudaErrorInvalidValue;
   }
 }
