@@ -445,7 +445,7 @@ int enqueue_decode_batched(qwen_engine* e, int n, int max_len, bool advance) {
     E_TRY(mark(kBcQkv));
     E_TRY(tgemm_qkv_decode(L, dp, e->d_pos, e->d_seq, kv, e->rope_dec_cos, e->rope_dec_sin, e->p_q, e->p_qkv, s));
     E_TRY(mark(kBcAttn));
-    E_TRY(launch_decode_attention(e->p_q, kv, tok, max_len, e->p_ctx, e->attn_part, e->attn_cnt, s, false,
+    E_TRY(launch_decode_attention(e->p_q, kv, tok, max_len, e->p_ctx, e->attn_part, e->attn_cnt, s, true,
                                   nullptr, 0, e->attn_ctas));
     E_TRY(mark(kBcDigits));
     E_TRY(tgemm_digitize(e->p_ctx, dp, s));

@@ -212,12 +212,15 @@ __global__ void __launch_bounds__(kThreadsT, (ST == 2 || ST == kPairST) ? 2 : 1)
     else
       tmem_alloc(&sm.tmem_base, kTmemColsT);
   }
-  for (int i = threadIdx.x; i < kTN; i += blockDim.x) sm.steps[i] = a.steps[n0 + i];
   fence_before();
   __syncthreads();
   if constexpr (kPair) cluster_sync_all();  // both CTAs' barriers initialised before any cross-CTA signal
   fence_after();
   const uint32_t tmem = sm.tmem_base;
+  // Programmatic dependent launch: everything above is local. The weights do not depend on the preceding
+  // kernel, so the producer issues the first stages' weight tiles before waiting for it; the digit planes,
+  // the token steps and every global write come after the wait.
+  griddep_launch();
 
   if (warp == 0) {
     if (lane == 0) {
@@ -229,33 +232,47 @@ __global__ void __launch_bounds__(kThreadsT, (ST == 2 || ST == kPairST) ? 2 : 1)
       bool ok = true;
       // pair form: every copy completes on the leader's full barrier
       const uint32_t full0 = kPair ? peer_addr(smem_u32(&sm.full[0]), 0) : 0u;
-      for (int kb = kb_lo; kb < kb_hi && ok; ++kb) {
-        if (!(ok = kPair ? mbar_wait_cluster(&sm.empty[s], ph ^ 1) : mbar_wait(&sm.empty[s], ph ^ 1))) break;
-        uint8_t* st = stages + (size_t)s * kStageBytes;
+      auto load_weights = [&](int kb, int st_i) {
+        uint8_t* st = stages + (size_t)st_i * kStageBytes;
         if constexpr (kPair) {
-          if (prank == 0) mbar_arrive_expect_tx(&sm.full[s], 2 * kStageBytes);
-          const uint32_t fb = full0 + 8u * s;
+          if (prank == 0) mbar_arrive_expect_tx(&sm.full[st_i], 2 * kStageBytes);
+          const uint32_t fb = full0 + 8u * st_i;
           tma_load_2d_pair(st, &wmap, kb * kKBlock, row0, fb);
           if (a.box_rows != kTileM) tma_load_2d_pair(st + a.box_rows * kKBlock, &wmap, kb * kKBlock, row0 + a.second_row0, fb);
+        } else {
+          mbar_arrive_expect_tx(&sm.full[st_i], kStageBytes);
+          tma_load_2d(st, &wmap, kb * kKBlock, row0, &sm.full[st_i]);
+          if (a.box_rows != kTileM)
+            tma_load_2d(st + a.box_rows * kKBlock, &wmap, kb * kKBlock, row0 + a.second_row0, &sm.full[st_i]);
+        }
+      };
+      auto load_planes = [&](int kb, int st_i) {
+        uint8_t* st = stages + (size_t)st_i * kStageBytes;
+        if constexpr (kPair) {
+          const uint32_t fb = full0 + 8u * st_i;
 #pragma unroll
           for (int i = 0; i < 3; ++i) {  // plane rows 96 prank + 32 i .. + 32 (row = 64 plane + token)
             const int pr = 96 * prank + 32 * i;
             tma_load_2d_pair(st + kUnitBytes + i * 32 * kKBlock, &pmap, kb * kKBlock, (pr / 64) * a.Spad + n0 + pr % 64,
                              fb);
           }
-          if (++s == kStagesT) {
-            s = 0;
-            ph ^= 1;
-          }
-          continue;
-        }
-        mbar_arrive_expect_tx(&sm.full[s], kStageBytes);
-        tma_load_2d(st, &wmap, kb * kKBlock, row0, &sm.full[s]);
-        if (a.box_rows != kTileM)
-          tma_load_2d(st + a.box_rows * kKBlock, &wmap, kb * kKBlock, row0 + a.second_row0, &sm.full[s]);
+        } else {
 #pragma unroll
-        for (int p = 0; p < kPlanes; ++p)
-          tma_load_2d(st + kUnitBytes + p * kPlaneTile, &pmap, kb * kKBlock, p * a.Spad + n0, &sm.full[s]);
+          for (int p = 0; p < kPlanes; ++p)
+            tma_load_2d(st + kUnitBytes + p * kPlaneTile, &pmap, kb * kKBlock, p * a.Spad + n0, &sm.full[st_i]);
+        }
+      };
+      // the first stages are free (fresh barriers): their weight tiles go out before the dependency wait
+      const int pre = min(kStagesT, kb_hi - kb_lo);
+      for (int i = 0; i < pre; ++i) load_weights(kb_lo + i, i);
+      griddep_wait();
+      for (int i = 0; i < pre; ++i) load_planes(kb_lo + i, i);
+      s = pre % kStagesT;
+      ph = pre == kStagesT ? 1u : 0u;
+      for (int kb = kb_lo + pre; kb < kb_hi && ok; ++kb) {
+        if (!(ok = kPair ? mbar_wait_cluster(&sm.empty[s], ph ^ 1) : mbar_wait(&sm.empty[s], ph ^ 1))) break;
+        load_weights(kb, s);
+        load_planes(kb, s);
         if (++s == kStagesT) {
           s = 0;
           ph ^= 1;
@@ -345,6 +362,9 @@ __global__ void __launch_bounds__(kThreadsT, (ST == 2 || ST == kPairST) ? 2 : 1)
     }
     if constexpr (EPI != kTRaw) sc = __ldg(a.scale + row);
     if constexpr (EPI == kTQkv) bb = __ldg(a.bias + row);
+    griddep_wait();  // the token steps (and the residual) come from earlier kernels
+    if (r < kTN) sm.steps[r] = a.steps[n0 + r];
+    named_sync(kBarT, kEpiT);
     if (tb < te && n0 + tb < a.S) chunk_loads(tb);
     ok = kPair ? mbar_wait_cluster(&sm.acc_full, 0) : mbar_wait(&sm.acc_full, 0);
     fence_after();
@@ -470,6 +490,8 @@ __global__ void __launch_bounds__(kThreadsT, (ST == 2 || ST == kPairST) ? 2 : 1)
 constexpr int kDigitVec = 9;  // float4 per thread: rows up to 9216 floats
 __global__ void __launch_bounds__(256) digitize_kernel(const float* __restrict__ x, int S, int K, int Spad,
                                                        int8_t* __restrict__ planes, float* __restrict__ steps) {
+  griddep_wait();  // inputs come from the preceding kernel (programmatic dependent launch)
+  griddep_launch();
   const int t = blockIdx.x;
   __shared__ float red[8];
   int8_t* p0 = planes + (size_t)t * K;
@@ -530,6 +552,8 @@ __global__ void __launch_bounds__(256) digitize_kernel(const float* __restrict__
 // 512 j + 4 tid + e, xor-shuffle within the warp, the four warps in order), so both give identical rows.
 __global__ void __launch_bounds__(128) decode_rmsnorm_kernel(const float* __restrict__ x, const float* __restrict__ w,
                                                              float* __restrict__ out) {
+  griddep_wait();  // inputs come from the preceding kernel (programmatic dependent launch)
+  griddep_launch();
   __shared__ double red[4];
   const int t = blockIdx.x, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const float* row = x + (size_t)t * kHidden;
@@ -571,6 +595,8 @@ __global__ void __launch_bounds__(128) decode_rmsnorm_kernel(const float* __rest
 __global__ void __launch_bounds__(128) rmsnorm_digitize_kernel(const float* __restrict__ x, const float* __restrict__ w,
                                                                int S, int Spad, int8_t* __restrict__ planes,
                                                                float* __restrict__ steps) {
+  griddep_wait();  // inputs come from the preceding kernel (programmatic dependent launch)
+  griddep_launch();
   __shared__ double red[4];
   __shared__ float redm[4];
   const int t = blockIdx.x, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -655,6 +681,8 @@ __global__ void __launch_bounds__(256) qkv_rope_kernel(const float* __restrict__
                                                        const int* __restrict__ posv, const int* __restrict__ seqv,
                                                        KvView kv, float* __restrict__ k_cache, float* __restrict__ v_cache,
                                                        float* __restrict__ q_out) {
+  griddep_wait();  // inputs come from the preceding kernel (programmatic dependent launch)
+  griddep_launch();
   const int t = blockIdx.x;
   const int pos = decode ? posv[t] : t;
   const float* x = raw + (size_t)t * kQkvRows;
@@ -755,13 +783,15 @@ cudaError_t run_tgemm_tn(const uint8_t* w, int rows_total, int K, int mtiles, in
   cfg.blockDim = dim3(kThreadsT);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = s;
-  cudaLaunchAttribute at[1];
-  at[0].id = cudaLaunchAttributeClusterDimension;
-  at[0].val.clusterDim.x = C::kPair ? 2 : ksplit;
-  at[0].val.clusterDim.y = 1;
-  at[0].val.clusterDim.z = 1;
+  cudaLaunchAttribute at[2];
+  at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[0].val.programmaticStreamSerializationAllowed = 1;
+  at[1].id = cudaLaunchAttributeClusterDimension;
+  at[1].val.clusterDim.x = C::kPair ? 2 : ksplit;
+  at[1].val.clusterDim.y = 1;
+  at[1].val.clusterDim.z = 1;
   cfg.attrs = at;
-  cfg.numAttrs = (C::kPair || ksplit > 1) ? 1 : 0;
+  cfg.numAttrs = (C::kPair || ksplit > 1) ? 2 : 1;
   return cudaLaunchKernelEx(&cfg, kern, wmap, pmap, a);
 }
 
@@ -807,14 +837,12 @@ cudaError_t run_tgemm(const uint8_t* w, int rows_total, int K, int mtiles, int b
 
 cudaError_t tgemm_rmsnorm_digitize(const float* x, const float* w, DigitPlanes d, cudaStream_t s) {
   if (d.K != kHidden || d.Spad != tgemm_pad(d.S) || d.S < 1) return cudaErrorInvalidValue;
-  rmsnorm_digitize_kernel<<<d.Spad, 128, 0, s>>>(x, w, d.S, d.Spad, d.planes, d.steps);
-  return cudaGetLastError();
+  return launch_k(rmsnorm_digitize_kernel, dim3(d.Spad), dim3(128), 0, s, true, x, w, d.S, d.Spad, d.planes, d.steps);
 }
 
 cudaError_t tgemm_digitize(const float* x, DigitPlanes d, cudaStream_t s) {
   if (d.K % 4 || d.K > 4 * 256 * kDigitVec || d.Spad != tgemm_pad(d.S) || d.S < 1) return cudaErrorInvalidValue;
-  digitize_kernel<<<d.Spad, 256, 0, s>>>(x, d.S, d.K, d.Spad, d.planes, d.steps);
-  return cudaGetLastError();
+  return launch_k(digitize_kernel, dim3(d.Spad), dim3(256), 0, s, true, x, d.S, d.K, d.Spad, d.planes, d.steps);
 }
 
 cudaError_t tgemm_qkv(const LayerDev& L, const DigitPlanes& x, const float* rope_cos, const float* rope_sin, float* q_out,
@@ -825,9 +853,9 @@ cudaError_t tgemm_qkv(const LayerDev& L, const DigitPlanes& x, const float* rope
   a.out = raw;
   cudaError_t e = run_tgemm<kTQkv>(L.qkv_w, kQkvRows, kHidden, kQkvRows / kTileM, kTileM, 0, x, a, s);
   if (e != cudaSuccess) return e;
-  qkv_rope_kernel<<<x.S, 256, 0, s>>>(raw, rope_cos, rope_sin, false, nullptr, nullptr, KvView{}, k_cache, v_cache,
-                                      q_out);
-  return cudaGetLastError();
+  return launch_k(qkv_rope_kernel, dim3(x.S), dim3(256), 0, s, true, static_cast<const float*>(raw), rope_cos, rope_sin,
+                  false, static_cast<const int*>(nullptr), static_cast<const int*>(nullptr), KvView{}, k_cache, v_cache,
+                  q_out);
 }
 
 cudaError_t tgemm_o(const LayerDev& L, const DigitPlanes& x, float* out, cudaStream_t s) {
@@ -862,8 +890,8 @@ cudaError_t tgemm_qkv_decode(const LayerDev& L, const DigitPlanes& x, const int*
   a.out = raw;
   cudaError_t e = run_tgemm<kTQkv>(L.qkv_w, kQkvRows, kHidden, kQkvRows / kTileM, kTileM, 0, x, a, s);
   if (e != cudaSuccess) return e;
-  qkv_rope_kernel<<<x.S, 256, 0, s>>>(raw, rope_cos, rope_sin, true, pos, seq, kv, nullptr, nullptr, q_out);
-  return cudaGetLastError();
+  return launch_k(qkv_rope_kernel, dim3(x.S), dim3(256), 0, s, true, static_cast<const float*>(raw), rope_cos, rope_sin,
+                  true, pos, seq, kv, static_cast<float*>(nullptr), static_cast<float*>(nullptr), q_out);
 }
 
 cudaError_t tgemm_gateup_decode(const LayerDev& L, const DigitPlanes& x, float* h, cudaStream_t s) {
@@ -884,8 +912,7 @@ cudaError_t tgemm_raw(const uint8_t* codes, int rows, const DigitPlanes& x, int*
 
 cudaError_t decode_rmsnorm(const float* x, const float* w, int n, float* out, cudaStream_t s) {
   if (n < 1) return cudaErrorInvalidValue;
-  decode_rmsnorm_kernel<<<n, 128, 0, s>>>(x, w, out);
-  return cudaGetLastError();
+  return launch_k(decode_rmsnorm_kernel, dim3(n), dim3(128), 0, s, true, x, w, out);
 }
 
 unsigned tgemm_kernel_error(bool reset) {
