@@ -455,34 +455,38 @@ __global__ void __launch_bounds__(kMergeThreads) decode_attn_merge_kernel(Decode
   float* sb = sa + kGroups * nc;
   float* inv = sb + kGroups * nc;
   const float* base = part + ((size_t)t * kKvHeads + g) * max_chunks * kGroups * kPartStride;
+  const int h = tid / kHeadDim, d = tid % kHeadDim;
+  const float* src = base + (size_t)h * kPartStride + 2 + d;
+  // the first chunks' values do not depend on the rescale factors: their loads go out first
+  float av[kMergeLoads];
+#pragma unroll
+  for (int k = 0; k < kMergeLoads; ++k) av[k] = __ldcg(src + (size_t)min(k, nc - 1) * kGroups * kPartStride);
   for (int i = tid; i < kGroups * nc; i += kMergeThreads) {
-    const int c = i / kGroups, h = i % kGroups;
-    mv[h * nc + c] = __ldcg(base + ((size_t)c * kGroups + h) * kPartStride);
-    lv[h * nc + c] = __ldcg(base + ((size_t)c * kGroups + h) * kPartStride + 1);
+    const int c = i / kGroups, hh = i % kGroups;
+    mv[hh * nc + c] = __ldcg(base + ((size_t)c * kGroups + hh) * kPartStride);
+    lv[hh * nc + c] = __ldcg(base + ((size_t)c * kGroups + hh) * kPartStride + 1);
   }
   __syncthreads();
   if (tid < kGroups) {
-    const int h = tid;
     float M = -INFINITY, Lsum = 0.f;
     for (int c = 0; c < nc; ++c) {
-      const float Mn = fmaxf(M, mv[h * nc + c]);
-      const float fa = expf(M - Mn), fb = expf(mv[h * nc + c] - Mn);
-      sa[h * nc + c] = fa;
-      sb[h * nc + c] = fb;
-      Lsum = __fadd_rn(__fmul_rn(Lsum, fa), __fmul_rn(lv[h * nc + c], fb));
+      const float Mn = fmaxf(M, mv[tid * nc + c]);
+      const float fa = expf(M - Mn), fb = expf(mv[tid * nc + c] - Mn);
+      sa[tid * nc + c] = fa;
+      sb[tid * nc + c] = fb;
+      Lsum = __fadd_rn(__fmul_rn(Lsum, fa), __fmul_rn(lv[tid * nc + c], fb));
       M = Mn;
     }
-    inv[h] = Lsum > 0.0f ? 1.0f / Lsum : 0.0f;
+    inv[tid] = Lsum > 0.0f ? 1.0f / Lsum : 0.0f;
   }
   __syncthreads();
-  const int h = tid / kHeadDim, d = tid % kHeadDim;
-  const float* src = base + (size_t)h * kPartStride + 2 + d;
   float o = 0.f;
   for (int c0 = 0; c0 < nc; c0 += kMergeLoads) {
-    float av[kMergeLoads];
+    if (c0 > 0) {
 #pragma unroll
-    for (int k = 0; k < kMergeLoads; ++k)
-      av[k] = __ldcg(src + (size_t)min(c0 + k, nc - 1) * kGroups * kPartStride);
+      for (int k = 0; k < kMergeLoads; ++k)
+        av[k] = __ldcg(src + (size_t)min(c0 + k, nc - 1) * kGroups * kPartStride);
+    }
 #pragma unroll
     for (int k = 0; k < kMergeLoads; ++k)
       if (c0 + k < nc) o = __fadd_rn(__fmul_rn(o, sa[h * nc + c0 + k]), __fmul_rn(av[k], sb[h * nc + c0 + k]));
