@@ -257,7 +257,7 @@ def test_persistent_step_kernel_matches_separate_kernels(host, prompt_len):
         assert np.array_equal(a, b), (step, rel_l2(a, b))
 
 
-@pytest.mark.parametrize("n", [5, 12])
+@pytest.mark.parametrize("n", [5, 12, 40])  # 40: 64-token padding (CTA-pair GEMM tiles)
 def test_batched_w8_decode_matches_single(host, n):
     """More than four sequences per step take the batched path (every projection of all tokens in one
     many-token tensor-core GEMM, paged attention over all tokens); it performs the same per-token

@@ -26,7 +26,7 @@ def torch_reference(q, k, v):
     return out.view(-1).float()
 
 
-@pytest.mark.parametrize("seq_len", [1, 63, 64, 65, 513, 2048])
+@pytest.mark.parametrize("seq_len", [1, 63, 64, 65, 513, 2048, 4096, 32768])  # 32768: the maximum (512 chunks)
 def test_decode_attention_op_matches_torch(built_libs, gpu_available, seq_len):
     import torch
 
