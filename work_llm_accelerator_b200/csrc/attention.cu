@@ -514,6 +514,8 @@ struct PrefillSmem {
 __global__ void __launch_bounds__(256) prefill_attn_kernel(const float* __restrict__ q, const float* __restrict__ kc,
                                                            const float* __restrict__ vc, int S,
                                                            float* __restrict__ ctx, const int* only_if) {
+  griddep_wait();  // inputs come from the preceding kernel (programmatic dependent launch)
+  griddep_launch();
   if (only_if != nullptr && *reinterpret_cast<const volatile int*>(only_if) == 0) return;
   extern __shared__ float4 smem4[];
   PrefillSmem& sm = *reinterpret_cast<PrefillSmem*>(smem4);
@@ -736,8 +738,8 @@ cudaError_t launch_prefill_attention(const float* q, const float* k_cache, const
   const size_t smem = sizeof(PrefillSmem);
   cudaError_t e = cudaFuncSetAttribute(prefill_attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
-  prefill_attn_kernel<<<dim3((S + kPQ - 1) / kPQ, kKvHeads), 256, smem, s>>>(q, k_cache, v_cache, S, ctx, nullptr);
-  return cudaGetLastError();
+  return launch_k(prefill_attn_kernel, dim3((S + kPQ - 1) / kPQ, kKvHeads), dim3(256), smem, s, true, q, k_cache,
+                  v_cache, S, ctx, static_cast<const int*>(nullptr));
 }
 
 cudaError_t launch_prefill_attention_gated(const float* q, const float* k_cache, const float* v_cache, int S,
@@ -745,8 +747,8 @@ cudaError_t launch_prefill_attention_gated(const float* q, const float* k_cache,
   const size_t smem = sizeof(PrefillSmem);
   cudaError_t e = cudaFuncSetAttribute(prefill_attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
-  prefill_attn_kernel<<<dim3((S + kPQ - 1) / kPQ, kKvHeads), 256, smem, s>>>(q, k_cache, v_cache, S, ctx, only_if);
-  return cudaGetLastError();
+  return launch_k(prefill_attn_kernel, dim3((S + kPQ - 1) / kPQ, kKvHeads), dim3(256), smem, s, true, q, k_cache,
+                  v_cache, S, ctx, only_if);
 }
 
 }  // namespace qb

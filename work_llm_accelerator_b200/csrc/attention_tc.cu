@@ -84,6 +84,8 @@ __global__ void __launch_bounds__(256) attn_split_kernel(const float* __restrict
                                                          const float* __restrict__ v, int S, int Spad, int nvt,
                                                          __half* __restrict__ qp, __half* __restrict__ kp,
                                                          __half* __restrict__ vt, int* __restrict__ flag) {
+  griddep_wait();  // inputs come from the preceding kernel (programmatic dependent launch)
+  griddep_launch();
   bool bad = false;
   if ((int)blockIdx.x < nvt) {
     __shared__ float tile[64][65];
@@ -176,6 +178,8 @@ __device__ __forceinline__ uint32_t half2_bits(float a, float b) {
 __global__ void __launch_bounds__(kThreadsA, 1)
     attn_tc_kernel(const __half* __restrict__ qp, const __grid_constant__ CUtensorMap kmap,
                    const __grid_constant__ CUtensorMap vmap, int S, const int* flag, float* __restrict__ ctx) {
+  griddep_wait();  // inputs come from the preceding kernel (programmatic dependent launch)
+  griddep_launch();
   if (*reinterpret_cast<const volatile int*>(flag) != 0) return;  // values outside the split: CUDA-core kernel
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* tiles = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -499,8 +503,9 @@ cudaError_t launch_prefill_attention_tc(const float* q, const float* k_cache, co
   const int nvt = (Spad / 64) * 4;
   const size_t elems4 = ((size_t)S * (kHidden + kKvWidth)) / 4;
   const int nqk = (int)std::min<size_t>((elems4 + 255) / 256, 148 * 8);
-  attn_split_kernel<<<nvt + nqk, 256, 0, s>>>(q, k_cache, v_cache, S, Spad, nvt, qp, kp, vt, flag);
-  if ((e = cudaGetLastError()) != cudaSuccess) return e;
+  if ((e = launch_k(attn_split_kernel, dim3(nvt + nqk), dim3(256), 0, s, true, q, k_cache, v_cache, S, Spad, nvt, qp,
+                    kp, vt, flag)) != cudaSuccess)
+    return e;
   static std::mutex mu;
   static unsigned long long attr_set = 0;
   int dev = 0;
@@ -514,8 +519,9 @@ cudaError_t launch_prefill_attention_tc(const float* q, const float* k_cache, co
       attr_set |= 1ull << dev;
     }
   }
-  attn_tc_kernel<<<dim3((S + kBQ - 1) / kBQ, kHeads), kThreadsA, kSmemA, s>>>(qp, kmap, vmap, S, flag, ctx);
-  if ((e = cudaGetLastError()) != cudaSuccess) return e;
+  if ((e = launch_k(attn_tc_kernel, dim3((S + kBQ - 1) / kBQ, kHeads), dim3(kThreadsA), kSmemA, s, true,
+                    static_cast<const __half*>(qp), kmap, vmap, S, static_cast<const int*>(flag), ctx)) != cudaSuccess)
+    return e;
   // values outside the fp16 split: the CUDA-core kernel computes the context (it returns at once otherwise)
   return launch_prefill_attention_gated(q, k_cache, v_cache, S, ctx, flag, s);
 }

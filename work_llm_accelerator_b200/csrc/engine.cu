@@ -39,6 +39,8 @@ __global__ void embed_gather_kernel(const uint16_t* __restrict__ embed, const in
 // flat [n][256] K and V of one layer <-> paged rows of one slot
 __global__ void kv_scatter_kernel(const float* __restrict__ kf, const float* __restrict__ vf, int n, KvView kv,
                                   int slot, int to_pages) {
+  griddep_wait();  // inputs come from the preceding kernel (programmatic dependent launch)
+  griddep_launch();
   const int t = blockIdx.x;
   if (t >= n) return;
   float* kd = kv_row(kv, slot, t, 0);
@@ -558,8 +560,8 @@ int enqueue_prefill(qwen_engine* e, int slot, int n) {
     } else {
       E_TRY(launch_prefill_o(e->wbits, L, e->p_ctx, n, e->p_a, s));
     }
-    kv_scatter_kernel<<<n, 256, 0, s>>>(e->p_k, e->p_v, n, paged_view(e, l), slot, 1);
-    E_TRY(cudaGetLastError());
+    E_TRY(launch_k(kv_scatter_kernel, dim3(n), dim3(256), 0, s, true, static_cast<const float*>(e->p_k),
+                   static_cast<const float*>(e->p_v), n, paged_view(e, l), slot, 1));
     E_TRY(launch_prefill_rmsnorm(e->p_a, L.post_ln, n, e->p_xn, s));
     if (tc) {
       E_TRY(tgemm_digitize(e->p_xn, dp, s));

@@ -24,6 +24,8 @@ constexpr size_t kNormSmem = (size_t)kNormTok * kNormPad * 4 + kNormTok * 4;
 
 __global__ void __launch_bounds__(128) prefill_rmsnorm_kernel(const float* __restrict__ x, const float* __restrict__ w,
                                                               int S, float* __restrict__ xn) {
+  griddep_wait();  // inputs come from the preceding kernel (programmatic dependent launch)
+  griddep_launch();
   extern __shared__ float nsm[];
   float* rows = nsm;                          // [kNormTok][kNormPad]
   float* inv_s = nsm + kNormTok * kNormPad;   // [kNormTok]
@@ -218,8 +220,8 @@ cudaError_t launch_prefill_rmsnorm(const float* x, const float* w, int S, float*
   const cudaError_t e =
       cudaFuncSetAttribute(prefill_rmsnorm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kNormSmem);
   if (e != cudaSuccess) return e;
-  prefill_rmsnorm_kernel<<<(S + kNormTok - 1) / kNormTok, 128, kNormSmem, s>>>(x, w, S, xn);
-  return cudaGetLastError();
+  return launch_k(prefill_rmsnorm_kernel, dim3((S + kNormTok - 1) / kNormTok), dim3(128), kNormSmem, s, true, x, w, S,
+                  xn);
 }
 
 cudaError_t launch_prefill_rope_table(int npos, float* cos_out, float* sin_out, cudaStream_t s) {
