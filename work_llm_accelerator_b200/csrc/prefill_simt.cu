@@ -16,10 +16,10 @@ namespace {
 
 // ---- RMSNorm -------------------------------------------------------------------------------------
 // CTA = 8 tokens. The reference's sum of squares is one serial fp32 chain per token (kept bit for bit):
-// all 128 threads stage the 8 rows in shared memory with every load in flight at once, lanes 0..7 of warp 0
-// run the 8 chains (rows padded by one float: the lanes read different banks), then all threads write the
-// normalised rows from shared memory.
-constexpr int kNormTok = 8, kNormPad = kHidden + 1;
+// all 128 threads stage the 8 rows in shared memory with asynchronous 16-byte copies, every one in flight
+// at once, lanes 0..7 of warp 0 run the 8 chains (rows padded by four floats: 16-byte aligned, and the
+// lanes read different banks), then all threads write the normalised rows from shared memory.
+constexpr int kNormTok = 8, kNormPad = kHidden + 4;
 constexpr size_t kNormSmem = (size_t)kNormTok * kNormPad * 4 + kNormTok * 4;
 
 __global__ void __launch_bounds__(128) prefill_rmsnorm_kernel(const float* __restrict__ x, const float* __restrict__ w,
@@ -33,13 +33,11 @@ __global__ void __launch_bounds__(128) prefill_rmsnorm_kernel(const float* __res
   const int n = min(kNormTok, S - t0);
   for (int i = tid; i < n * (kHidden / 4); i += 128) {
     const int r = i / (kHidden / 4), f = i % (kHidden / 4);
-    const float4 v = *reinterpret_cast<const float4*>(x + (size_t)(t0 + r) * kHidden + 4 * f);
-    float* d = rows + r * kNormPad + 4 * f;
-    d[0] = v.x;
-    d[1] = v.y;
-    d[2] = v.z;
-    d[3] = v.w;
+    const unsigned dst = (unsigned)__cvta_generic_to_shared(rows + r * kNormPad + 4 * f);
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(x + (size_t)(t0 + r) * kHidden + 4 * f)
+                 : "memory");
   }
+  asm volatile("cp.async.wait_all;" ::: "memory");
   __syncthreads();
   if (tid < n) {
     const float* row = rows + tid * kNormPad;
@@ -217,6 +215,7 @@ cudaError_t run_gemm(const GemmArgs& a, int n_tiles, cudaStream_t s) {
 }  // namespace
 
 cudaError_t launch_prefill_rmsnorm(const float* x, const float* w, int S, float* xn, cudaStream_t s) {
+  if (reinterpret_cast<uintptr_t>(x) & 15) return cudaErrorInvalidValue;  // 16-byte asynchronous row copies
   const cudaError_t e =
       cudaFuncSetAttribute(prefill_rmsnorm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kNormSmem);
   if (e != cudaSuccess) return e;
