@@ -817,8 +817,8 @@ cudaError_t run_tgemm(const uint8_t* w, int rows_total, int K, int mtiles, int b
       return run_tgemm_tn<EPI, 64, kPairST>(w, rows_total, K, mtiles, box_rows, second_row0, x, a, s);
     return run_tgemm_tn<EPI, 64>(w, rows_total, K, mtiles, box_rows, second_row0, x, a, s, ks);
   }
-  if (x.Spad >= 128) {  // many tokens: 64-token tiles, two CTAs per SM unless K is split
-    const int ks = pick_ksplit(mtiles * (x.Spad / 64), nkb);
+  if (x.Spad >= 128) {  // many tokens: 64-token tiles, two CTAs per SM unless K is split (long K only)
+    const int ks = nkb >= 32 ? pick_ksplit(mtiles * (x.Spad / 64), nkb) : 1;
     if (ks > 1) return run_tgemm_tn<EPI, 64>(w, rows_total, K, mtiles, box_rows, second_row0, x, a, s, ks);
     if ((mtiles & 1) == 0 && nkb >= TCfg<64, kPairST>::kStages)  // CTA pairs: 256-row tiles
       return run_tgemm_tn<EPI, 64, kPairST>(w, rows_total, K, mtiles, box_rows, second_row0, x, a, s);
