@@ -542,11 +542,11 @@ int enqueue_prefill(qwen_engine* e, int slot, int n) {
   const DigitPlanes dph{e->p_planes, e->p_steps, n, tgemm_pad(n), kInter};
   for (int l = 0; l < kLayers; ++l) {
     const LayerDev& L = e->layers[l];
-    E_TRY(launch_prefill_rmsnorm(e->p_x, L.input_ln, n, e->p_xn, s));
     if (tc) {  // W8: projections on the int8 tensor cores
-      E_TRY(tgemm_digitize(e->p_xn, dp, s));
+      E_TRY(tgemm_prefill_rmsnorm_digitize(e->p_x, L.input_ln, dp, s));
       E_TRY(tgemm_qkv(L, dp, e->rope_pre_cos, e->rope_pre_sin, e->p_q, e->p_k, e->p_v, e->p_qkv, s));
     } else {
+      E_TRY(launch_prefill_rmsnorm(e->p_x, L.input_ln, n, e->p_xn, s));
       E_TRY(launch_prefill_qkv(e->wbits, L, e->p_xn, n, e->rope_pre_cos, e->rope_pre_sin, e->p_q, e->p_k, e->p_v, s));
     }
     if (e->use_attn_tc) {
@@ -562,13 +562,13 @@ int enqueue_prefill(qwen_engine* e, int slot, int n) {
     }
     E_TRY(launch_k(kv_scatter_kernel, dim3(n), dim3(256), 0, s, true, static_cast<const float*>(e->p_k),
                    static_cast<const float*>(e->p_v), n, paged_view(e, l), slot, 1));
-    E_TRY(launch_prefill_rmsnorm(e->p_a, L.post_ln, n, e->p_xn, s));
     if (tc) {
-      E_TRY(tgemm_digitize(e->p_xn, dp, s));
+      E_TRY(tgemm_prefill_rmsnorm_digitize(e->p_a, L.post_ln, dp, s));
       E_TRY(tgemm_gateup(L, dp, e->p_h, s));
       E_TRY(tgemm_digitize(e->p_h, dph, s));
       E_TRY(tgemm_down(L, dph, e->p_a, e->p_x, true, s));
     } else {
+      E_TRY(launch_prefill_rmsnorm(e->p_a, L.post_ln, n, e->p_xn, s));
       E_TRY(launch_prefill_gateup(e->wbits, L, e->p_xn, n, e->p_h, s));
       E_TRY(launch_prefill_down(e->wbits, L, e->p_h, e->p_a, n, e->p_x, true, s));
     }

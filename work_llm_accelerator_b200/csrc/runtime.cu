@@ -351,14 +351,14 @@ int run_prefill(int wbits, const LayerPtrs& L, bool attention, bool mlp, const f
     QB_TRY(ensure(c.kc, kvb));
     QB_TRY(ensure(c.vc, kvb));
     QB_TRY(ensure(c.ctx, SH));
-    // xn reuses `out` as scratch
-    QB_TRY(launch_prefill_rmsnorm((const float*)c.x.p, D.input_ln, S, (float*)c.out.p, c.stream));
     if (tc) {
-      QB_TRY(tgemm_digitize((const float*)c.out.p, dp, c.stream));
+      QB_TRY(tgemm_prefill_rmsnorm_digitize((const float*)c.x.p, D.input_ln, dp, c.stream));
       QB_TRY(ensure(c.qkv_raw, (size_t)S * kQkvRows * 4));
       QB_TRY(tgemm_qkv(D, dp, (const float*)c.rope_pre_cos.p, (const float*)c.rope_pre_sin.p, (float*)c.q.p,
                        (float*)c.kc.p, (float*)c.vc.p, (float*)c.qkv_raw.p, c.stream));
     } else {
+      // xn reuses `out` as scratch
+      QB_TRY(launch_prefill_rmsnorm((const float*)c.x.p, D.input_ln, S, (float*)c.out.p, c.stream));
       QB_TRY(launch_prefill_qkv(wbits, D, (const float*)c.out.p, S, (const float*)c.rope_pre_cos.p,
                                 (const float*)c.rope_pre_sin.p, (float*)c.q.p, (float*)c.kc.p, (float*)c.vc.p,
                                 c.stream));
@@ -380,13 +380,13 @@ int run_prefill(int wbits, const LayerPtrs& L, bool attention, bool mlp, const f
   }
   if (mlp) {
     QB_TRY(ensure(c.h, (size_t)S * kInter * 4));
-    QB_TRY(launch_prefill_rmsnorm(a_dev, D.post_ln, S, (float*)c.q.p, c.stream));
     if (tc) {
-      QB_TRY(tgemm_digitize((const float*)c.q.p, dp, c.stream));
+      QB_TRY(tgemm_prefill_rmsnorm_digitize(a_dev, D.post_ln, dp, c.stream));
       QB_TRY(tgemm_gateup(D, dp, (float*)c.h.p, c.stream));
       QB_TRY(tgemm_digitize((const float*)c.h.p, dph, c.stream));
       QB_TRY(tgemm_down(D, dph, a_dev, (float*)c.out.p, false, c.stream));
     } else {
+      QB_TRY(launch_prefill_rmsnorm(a_dev, D.post_ln, S, (float*)c.q.p, c.stream));
       QB_TRY(launch_prefill_gateup(wbits, D, (const float*)c.q.p, S, (float*)c.h.p, c.stream));
       QB_TRY(launch_prefill_down(wbits, D, (const float*)c.h.p, a_dev, S, (float*)c.out.p, false, c.stream));
     }

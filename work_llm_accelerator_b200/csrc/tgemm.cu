@@ -546,6 +546,106 @@ __global__ void __launch_bounds__(256) digitize_kernel(const float* __restrict__
   }
 }
 
+// Prefill RMSNorm (hls/prefill_only/qwen_prefill_attention_kernel.cpp:47-57,112-126) followed by the digit
+// planes of the normalised rows, in one kernel: the same values as prefill_rmsnorm_kernel (prefill_simt.cu)
+// followed by digitize_kernel, without writing the normalised rows to global memory. CTA = 2 token rows
+// (so that short prompts still spread the digit divisions over many SMs), staged in shared memory by
+// asynchronous 16-byte copies; lanes 0..1 of warp 0 run the reference's serial fp32 sums of squares, the
+// rows are normalised in place, then every thread digitizes 12 values of each row.
+constexpr int kPNormTok = 2, kPNormPad = kHidden + 4;  // rows padded by four floats: aligned, conflict-free
+constexpr size_t kPNormSmem = (size_t)kPNormTok * kPNormPad * 4 + kPNormTok * 4 + 4 * kPNormTok * 4;
+
+__global__ void __launch_bounds__(128) prefill_rmsnorm_digitize_kernel(const float* __restrict__ x,
+                                                                       const float* __restrict__ w, int S, int Spad,
+                                                                       int8_t* __restrict__ planes,
+                                                                       float* __restrict__ steps) {
+  griddep_wait();  // inputs come from the preceding kernel (programmatic dependent launch)
+  griddep_launch();
+  extern __shared__ __align__(16) float psm[];
+  float* rows = psm;                            // [kPNormTok][kPNormPad]
+  float* inv_s = psm + kPNormTok * kPNormPad;   // [kPNormTok]
+  float* redm = inv_s + kPNormTok;              // [4 warps][kPNormTok]
+  const int t0 = blockIdx.x * kPNormTok, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int n = max(0, min(kPNormTok, S - t0));
+  for (int i = tid; i < n * (kHidden / 4); i += 128) {
+    const int r = i / (kHidden / 4), f = i % (kHidden / 4);
+    const unsigned dst = (unsigned)__cvta_generic_to_shared(rows + r * kPNormPad + 4 * f);
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(x + (size_t)(t0 + r) * kHidden + 4 * f)
+                 : "memory");
+  }
+  asm volatile("cp.async.wait_all;" ::: "memory");
+  __syncthreads();
+  if (tid < n) {
+    const float* row = rows + tid * kPNormPad;
+    float ms = 0.0f;
+#pragma unroll 16
+    for (int d = 0; d < kHidden; ++d) ms = __fadd_rn(ms, __fmul_rn(row[d], row[d]));
+    ms = __fdiv_rn(ms, (float)kHidden);
+    inv_s[tid] = __fdiv_rn(1.0f, approx_sqrt(__fadd_rn(ms, kEps)));
+  }
+  __syncthreads();
+  // thread = values 4 tid + 512 j (j < 3) of every row: normalise (in registers), row maxima
+  float v[kPNormTok][3][4];
+#pragma unroll
+  for (int r = 0; r < kPNormTok; ++r) {
+    float m = 0.f;
+#pragma unroll
+    for (int j = 0; j < 3; ++j) {
+      const int k = 4 * tid + 512 * j;
+      const float4 xv = *reinterpret_cast<const float4*>(rows + r * kPNormPad + k);
+      const float4 wv = __ldg(reinterpret_cast<const float4*>(w + k));
+      const float iv = r < n ? inv_s[r] : 0.f;
+      v[r][j][0] = __fmul_rn(__fmul_rn(xv.x, iv), wv.x);
+      v[r][j][1] = __fmul_rn(__fmul_rn(xv.y, iv), wv.y);
+      v[r][j][2] = __fmul_rn(__fmul_rn(xv.z, iv), wv.z);
+      v[r][j][3] = __fmul_rn(__fmul_rn(xv.w, iv), wv.w);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) m = fmaxf(m, fabsf(v[r][j][e]));
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    if (lane == 0) redm[warp * kPNormTok + r] = m;
+  }
+  __syncthreads();
+#pragma unroll
+  for (int r = 0; r < kPNormTok; ++r) {
+    const int t = t0 + r;
+    int8_t* p0 = planes + (size_t)t * kHidden;
+    int8_t* p1 = planes + ((size_t)Spad + t) * kHidden;
+    int8_t* p2 = planes + ((size_t)2 * Spad + t) * kHidden;
+    if (r >= n) {  // padded token rows: zero digits, step 1
+#pragma unroll
+      for (int j = 0; j < 3; ++j) {
+        const int k = 4 * tid + 512 * j;
+        *reinterpret_cast<uint32_t*>(p0 + k) = 0u;
+        *reinterpret_cast<uint32_t*>(p1 + k) = 0u;
+        *reinterpret_cast<uint32_t*>(p2 + k) = 0u;
+      }
+      if (tid == 0) steps[t] = 1.0f;
+      continue;
+    }
+    const float mx = fmaxf(fmaxf(redm[r], redm[kPNormTok + r]), fmaxf(redm[2 * kPNormTok + r], redm[3 * kPNormTok + r]));
+    const float st = mx > 0.0f ? mx / kDigitRange : 1.0f;
+    if (tid == 0) steps[t] = st;
+#pragma unroll
+    for (int j = 0; j < 3; ++j) {
+      const int k = 4 * tid + 512 * j;
+      uint32_t w0 = 0, w1 = 0, w2 = 0;
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        int d0, d1, d2;
+        split_digits((int)rintf(__fdiv_rn(v[r][j][e], st)), d0, d1, d2);
+        w0 |= (uint32_t)(d0 & 255) << (8 * e);
+        w1 |= (uint32_t)(d1 & 255) << (8 * e);
+        w2 |= (uint32_t)(d2 & 255) << (8 * e);
+      }
+      *reinterpret_cast<uint32_t*>(p0 + k) = w0;
+      *reinterpret_cast<uint32_t*>(p1 + k) = w1;
+      *reinterpret_cast<uint32_t*>(p2 + k) = w2;
+    }
+  }
+}
+
 // Decode RMSNorm of n token rows (hls/decode_only/qwen_decode_attention_kernel.cpp:13-27): double sum of
 // squares, inv = 1 / sqrt(ms + eps) in double, out = float(x * inv * w). 128 threads per token with the
 // element assignment and reduction order of the persistent decode kernel (thread tid sums elements
@@ -838,6 +938,16 @@ cudaError_t run_tgemm(const uint8_t* w, int rows_total, int K, int mtiles, int b
 cudaError_t tgemm_rmsnorm_digitize(const float* x, const float* w, DigitPlanes d, cudaStream_t s) {
   if (d.K != kHidden || d.Spad != tgemm_pad(d.S) || d.S < 1) return cudaErrorInvalidValue;
   return launch_k(rmsnorm_digitize_kernel, dim3(d.Spad), dim3(128), 0, s, true, x, w, d.S, d.Spad, d.planes, d.steps);
+}
+
+cudaError_t tgemm_prefill_rmsnorm_digitize(const float* x, const float* w, DigitPlanes d, cudaStream_t s) {
+  if (d.K != kHidden || d.Spad != tgemm_pad(d.S) || d.S < 1 || (reinterpret_cast<uintptr_t>(x) & 15))
+    return cudaErrorInvalidValue;
+  const cudaError_t attr = cudaFuncSetAttribute(prefill_rmsnorm_digitize_kernel,
+                                                cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kPNormSmem);
+  if (attr != cudaSuccess) return attr;
+  return launch_k(prefill_rmsnorm_digitize_kernel, dim3(d.Spad / kPNormTok), dim3(128), kPNormSmem, s, true, x, w,
+                  d.S, d.Spad, d.planes, d.steps);
 }
 
 cudaError_t tgemm_digitize(const float* x, DigitPlanes d, cudaStream_t s) {

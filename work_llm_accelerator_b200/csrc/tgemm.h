@@ -26,6 +26,9 @@ cudaError_t tgemm_digitize(const float* x, DigitPlanes d, cudaStream_t s);
 // Decode RMSNorm of x [S][1536] with weights w, then digit planes of the normalised rows: the same values
 // as decode_rmsnorm followed by tgemm_digitize, in one kernel.
 cudaError_t tgemm_rmsnorm_digitize(const float* x, const float* w, DigitPlanes d, cudaStream_t s);
+// Prefill RMSNorm (serial fp32 sums, approx_sqrt) of x [S][1536] with weights w, then the digit planes of the
+// normalised rows: the same values as launch_prefill_rmsnorm followed by tgemm_digitize, in one kernel.
+cudaError_t tgemm_prefill_rmsnorm_digitize(const float* x, const float* w, DigitPlanes d, cudaStream_t s);
 
 // Projections of all S tokens with the prefill epilogues (the same operations as the CUDA-core prefill
 // GEMMs in prefill_simt.cu): q|k|v + RoPE (table rows = token index) + K/V rows of a flat cache (raw:
