@@ -63,7 +63,10 @@ int qwen_engine_reset(qwen_engine* e, int slot);
  * on the tensor cores, default 1; 0 = CUDA-core GEMV), "stack_ring" (weight stages in flight per SM in the
  * persistent kernel, 2..9, default 9), "prefill_attn_tc" (prefill attention on the tensor cores, default 1;
  * 0 = CUDA-core kernel), "attn_ctas" (cap on the CTAs of the separate decode attention kernel, default 0 = one
- * per SM; results do not depend on it). */
+ * per SM; results do not depend on it), "exact" (every layer and the LM head in the reference host code's
+ * arithmetic order: serial fp32 sums per output without FMA, the double decode RMSNorm, the host C library's
+ * expf restated for the decode softmax and SiLU, the prefill approximations; greedy tokens and every layer's
+ * hidden state are then bit-identical to the reference host libraries. Default 0; slow: one thread per output). */
 int qwen_engine_set_option(qwen_engine* e, const char* name, long long value);
 /* Per-layer outputs of the last prefill/decode call: [28][rows][1536] floats (rows = tokens of that call). */
 int qwen_engine_read_hidden(qwen_engine* e, float* out, long long n_floats);

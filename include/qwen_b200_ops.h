@@ -77,6 +77,14 @@ int qwen_b200_prefill_attention(const float* q, const float* k_cache, const floa
  * x, y [n] fp32 device memory. */
 int qwen_b200_prefill_approx_exp(const float* x, float* y, long long n, void* stream);
 
+/* The decode softmax and SiLU exponential of the engine's "exact" option: y[i] = expf(x[i]) exactly as the
+ * reference host library's expf computes it (hls/decode_only/qwen_decode_attention_kernel.cpp:149 and
+ * qwen_decode_mlp_kernel.cpp:80 call std::exp on floats, which resolves to glibc's expf: a 32-entry 2^(i/32)
+ * table and a degree-3 polynomial in double, restated with the fused multiply-adds of glibc's x86-64 FMA
+ * build). Exposed so that its identity with the host C library can be checked.
+ * x, y [n] fp32 device memory. */
+int qwen_b200_exact_expf(const float* x, float* y, long long n, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

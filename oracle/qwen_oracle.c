@@ -469,6 +469,15 @@ int oracle_prefill_mlp(int wbits, const float* a, int seq_len, const float* ln_w
 /* caller-side helpers                                                                               */
 /* ------------------------------------------------------------------------------------------------ */
 
+/* The host C library's expf over an array: the function the reference host library calls for
+ * std::exp on floats (qwen_decode_attention_kernel.cpp:149, qwen_decode_mlp_kernel.cpp:80), so that
+ * tests can compare a GPU restatement with it on the same machine. */
+void oracle_expf_array(const float* x, float* y, uint64_t n) {
+  int64_t i;
+#pragma omp parallel for schedule(static)
+  for (i = 0; i < (int64_t)n; ++i) y[i] = expf(x[i]);
+}
+
 /* Round-to-nearest-even to bf16, kept in fp32 (reference_wrapper_backend.py:40-46). */
 void oracle_round_bf16(float* x, uint64_t n) {
   for (uint64_t i = 0; i < n; ++i) {

@@ -73,6 +73,7 @@ def port() -> ctypes.CDLL:
         lib.oracle_prefill_mlp.argtypes = [_c.c_int, _F, _c.c_int, _F, _B, _B, _B, _F, _F, _F, _F]
         for name in ("oracle_decode_attention", "oracle_decode_mlp", "oracle_prefill_attention", "oracle_prefill_mlp"):
             getattr(lib, name).restype = _c.c_int
+        lib.oracle_expf_array.argtypes = [_F, _F, _c.c_uint64]
         lib.oracle_approx_exp.argtypes = [_c.c_float]
         lib.oracle_approx_exp.restype = _c.c_float
         lib.oracle_approx_sqrt.argtypes = [_c.c_float]
@@ -296,6 +297,14 @@ def prefill_layer(p: LayerParams, x: np.ndarray, seq_len: int, k_cache: np.ndarr
 def round_bf16(x: np.ndarray) -> np.ndarray:
     y = np.ascontiguousarray(x, dtype=np.float32).copy()
     port().oracle_round_bf16(y.reshape(-1), y.size)
+    return y
+
+
+def host_expf(x: np.ndarray) -> np.ndarray:
+    """expf of every element by this machine's C library (the reference host library's std::exp on floats)."""
+    x = np.ascontiguousarray(x, np.float32)
+    y = np.empty_like(x)
+    port().oracle_expf_array(x, y, x.size)
     return y
 
 

@@ -105,8 +105,7 @@ def prefill_cases(ref: qo.RefLibs, ref_cap: qo.RefLibs | None) -> list[dict]:
     return cases
 
 
-def full_model_case() -> dict:
-    seed, S, steps = 31, 8, 4
+def full_model_case(seed: int = 31, S: int = 8, steps: int = 4, kind: str = "full_model_w4") -> dict:
     rng = np.random.default_rng(seed)
     prompt = rng.integers(0, qo.VOCAB, S).tolist()
     m_ref = qwen_full_model.OracleModel(seed, 4, use_reference_libs=True)
@@ -124,7 +123,7 @@ def full_model_case() -> dict:
         toks_ref.append(t_ref)
         toks_port.append(t_port)
     assert toks_ref == toks_port
-    return dict(kind="full_model_w4", seed=seed, prompt=prompt, tokens=toks_ref, hidden_sha=hid,
+    return dict(kind=kind, seed=seed, prompt=prompt, tokens=toks_ref, hidden_sha=hid,
                 final_hidden_head=head(m_ref.hidden_trace[-1]))
 
 
@@ -136,7 +135,11 @@ def main() -> None:
         "about": "reference host-library outputs on seeded synthetic inputs (oracle/qwen_oracle.py generators); "
                  "sha256 over the raw little-endian float32 bytes",
         "attention_scaling_f32": float(np.float32(1.0 / np.sqrt(np.float64(128.0)))),
-        "cases": decode_cases(ref) + prefill_cases(ref, ref_cap) + [full_model_case()],
+        "cases": decode_cases(ref) + prefill_cases(ref, ref_cap) + [
+            full_model_case(),
+            # a longer greedy run: 32-token prompt, 16 decode steps
+            full_model_case(seed=37, S=32, steps=16, kind="full_model_w4_long"),
+        ],
     }
     OUT.write_text(json.dumps(golden, indent=1) + "\n")
     print(f"wrote {OUT} ({len(golden['cases'])} cases) in {time.time() - t0:.1f}s")

@@ -25,6 +25,8 @@
 #include "qwen_kernels.cuh"
 #include "runtime.h"
 
+#include "exact.h"
+
 namespace qb {
 namespace {
 
@@ -168,6 +170,10 @@ struct qwen_engine {
   // tensor-core LM head
   bool use_lm_tc = true;
   LmScratch lm{nullptr, nullptr, nullptr};
+  // option "exact": every layer and the LM head in the reference's arithmetic order (exact.h)
+  bool exact = false;
+  int ex_cap = 0;                                              // token rows of the buffers below
+  float *ex_xn = nullptr, *ex_qkv = nullptr, *ex_gu = nullptr;  // [cap][1536], [cap][2048], [cap][17920]
 };
 
 namespace {
@@ -293,6 +299,99 @@ int ensure_tiles(qwen_engine* e) {
   return 0;
 }
 
+// Buffers of the reference-order path for up to n token rows (allocated on first use, outside capture).
+int ensure_exact(qwen_engine* e, int n) {
+  n = std::max(n, e->batch_cap);
+  if (n <= e->ex_cap) return 0;
+  int cap = std::max(128, e->ex_cap);
+  while (cap < n) cap *= 2;
+  cudaFree(e->ex_xn);
+  cudaFree(e->ex_qkv);
+  cudaFree(e->ex_gu);
+  e->ex_xn = e->ex_qkv = e->ex_gu = nullptr;
+  E_TRY(dalloc(&e->ex_xn, (size_t)cap * kHidden));
+  E_TRY(dalloc(&e->ex_qkv, (size_t)cap * kQkvRows));
+  E_TRY(dalloc(&e->ex_gu, (size_t)cap * 2 * kInter));
+  e->ex_cap = cap;
+  return 0;
+}
+
+// One decode step in the reference's arithmetic (qwen_decode_attention_kernel.cpp:168-218,
+// qwen_decode_mlp_kernel.cpp:87-122, the caller's bf16 rounding between layers and its final norm + LM head):
+// bit-identical to the reference host library's decode layers, token for token.
+int enqueue_decode_exact(qwen_engine* e, int nt, bool advance) {
+  cudaStream_t s = e->stream;
+  const int wb = e->wbits;
+  const float scaling = (float)(1.0 / std::sqrt((double)kHeadDim));  // qwen_decode_attention_kernel.cpp:118
+  embed_gather_kernel<<<nt, 256, 0, s>>>(e->embed, e->d_tokens, nt, e->x);
+  E_TRY(cudaGetLastError());
+  const float* xin = e->x;
+  for (int l = 0; l < kLayers; ++l) {
+    const LayerDev& L = e->layers[l];
+    const KvView kv = paged_view(e, l);
+    float* yout = (l & 1) ? e->y1 : e->y0;
+    E_TRY(exact::launch_rmsnorm_dec(xin, L.input_ln, nt, e->ex_xn, s));
+    E_TRY(exact::launch_project(wb, e->ex_xn, nt, kHidden, L.qkv_w, L.qkv_b, L.qkv_s, kQkvRows, e->ex_qkv, nullptr,
+                                false, s));
+    E_TRY(exact::launch_rope_store(e->ex_qkv, nt, e->d_pos, 0, e->rope_dec_cos, e->rope_dec_sin, e->q, kv, e->d_seq,
+                                   0, s));
+    E_TRY(exact::launch_attention_dec(e->q, kv, e->d_pos, e->d_seq, nt, scaling, e->ctx, s));
+    E_TRY(exact::launch_project(wb, e->ctx, nt, kHidden, L.o_w, nullptr, L.o_s, kHidden, e->a, nullptr, false, s));
+    E_TRY(exact::launch_rmsnorm_dec(e->a, L.post_ln, nt, e->ex_xn, s));
+    E_TRY(exact::launch_project(wb, e->ex_xn, nt, kHidden, L.gu_w, nullptr, L.gu_s, 2 * kInter, e->ex_gu, nullptr,
+                                false, s));
+    E_TRY(exact::launch_silu_mul(e->ex_gu, nt, false, e->h, s));
+    E_TRY(exact::launch_project(wb, e->h, nt, kInter, L.down_w, nullptr, L.down_s, kHidden, yout, e->a, true, s));
+    if (e->dump_hidden) {
+      E_TRY(cudaMemcpyAsync(e->dump + (size_t)l * nt * kHidden, yout, (size_t)nt * kHidden * 4,
+                            cudaMemcpyDeviceToDevice, s));
+    }
+    xin = yout;
+  }
+  E_TRY(exact::launch_lm_head(e->embed, e->final_norm, xin, nt, e->ex_xn, e->logits, e->d_next, s));
+  if (advance) {
+    E_TRY(launch_k(advance_kernel, dim3(1), dim3(32), 0, s, false, e->d_tokens, (const int*)e->d_next, e->d_pos, nt));
+  }
+  return 0;
+}
+
+// Prefill in the reference's arithmetic (qwen_prefill_attention_kernel.cpp:2232-2367,
+// qwen_prefill_mlp_kernel.cpp:264-337): K/V of every token first, then each query's causal context.
+int enqueue_prefill_exact(qwen_engine* e, int slot, int n) {
+  cudaStream_t s = e->stream;
+  const int wb = e->wbits;
+  embed_gather_kernel<<<n, 256, 0, s>>>(e->embed, e->p_tokens, n, e->p_x);
+  E_TRY(cudaGetLastError());
+  KvView flat{};
+  flat.k = e->p_k;
+  flat.v = e->p_v;
+  flat.page_table = nullptr;
+  for (int l = 0; l < kLayers; ++l) {
+    const LayerDev& L = e->layers[l];
+    E_TRY(launch_prefill_rmsnorm(e->p_x, L.input_ln, n, e->p_xn, s));
+    E_TRY(exact::launch_project(wb, e->p_xn, n, kHidden, L.qkv_w, L.qkv_b, L.qkv_s, kQkvRows, e->ex_qkv, nullptr,
+                                false, s));
+    E_TRY(exact::launch_rope_store(e->ex_qkv, n, nullptr, 0, e->rope_pre_cos, e->rope_pre_sin, e->p_q, flat, nullptr,
+                                   0, s));
+    E_TRY(exact::launch_attention_pre(e->p_q, e->p_k, e->p_v, n, e->p_ctx, s));
+    E_TRY(exact::launch_project(wb, e->p_ctx, n, kHidden, L.o_w, nullptr, L.o_s, kHidden, e->p_a, nullptr, false, s));
+    E_TRY(launch_k(kv_scatter_kernel, dim3(n), dim3(256), 0, s, false, static_cast<const float*>(e->p_k),
+                   static_cast<const float*>(e->p_v), n, paged_view(e, l), slot, 1));
+    E_TRY(launch_prefill_rmsnorm(e->p_a, L.post_ln, n, e->p_xn, s));
+    E_TRY(exact::launch_project(wb, e->p_xn, n, kHidden, L.gu_w, nullptr, L.gu_s, 2 * kInter, e->ex_gu, nullptr,
+                                false, s));
+    E_TRY(exact::launch_silu_mul(e->ex_gu, n, true, e->p_h, s));
+    E_TRY(exact::launch_project(wb, e->p_h, n, kInter, L.down_w, nullptr, L.down_s, kHidden, e->p_x, e->p_a, true, s));
+    if (e->dump_hidden) {
+      E_TRY(cudaMemcpyAsync(e->dump + (size_t)l * kHidden, e->p_x + (size_t)(n - 1) * kHidden, kHidden * 4,
+                            cudaMemcpyDeviceToDevice, s));
+    }
+  }
+  E_TRY(exact::launch_lm_head(e->embed, e->final_norm, e->p_x + (size_t)(n - 1) * kHidden, 1, e->ex_xn, e->logits,
+                              e->d_next, s));
+  return 0;
+}
+
 bool stack_enabled(const qwen_engine* e) { return e->wbits == 8 && e->use_stack && e->wtiles != nullptr; }
 
 // Final norm + LM head + argmax of n rows of x into d_next (logits kept when requested).
@@ -313,6 +412,7 @@ int enqueue_lm_head(qwen_engine* e, const float* x, int n, int* next, float* log
 // Enqueue one decode step for nt tokens whose ids/positions/slots are already in d_tokens/d_pos/d_seq.
 // max_len bounds the attention grid (positions + 1 of every token must be <= max_len).
 int enqueue_decode(qwen_engine* e, int nt, int max_len, bool advance) {
+  if (e->exact) return enqueue_decode_exact(e, nt, advance);
   const bool pdl = e->use_pdl;
   DecodeTokens tok{e->d_pos, e->d_seq, nt};
   float* xin = nullptr;
@@ -406,7 +506,7 @@ int enqueue_decode(qwen_engine* e, int nt, int max_len, bool advance) {
 }
 
 bool batched_ok(const qwen_engine* e, int n) {
-  return e->wbits == 8 && e->use_batched && n > kGemvMaxTokens && n <= e->batch_cap;
+  return e->wbits == 8 && e->use_batched && !e->exact && n > kGemvMaxTokens && n <= e->batch_cap;
 }
 
 // One greedy decode step of n > 4 tokens (W8): every projection of all tokens in one many-token tensor-core
@@ -534,6 +634,7 @@ int run_decode_step(qwen_engine* e, int nt, int max_len, bool advance) {
 // The device work of one prefill (tokens already in p_tokens): embedding gather, 28 layers, LM head of the
 // last token into d_next.
 int enqueue_prefill(qwen_engine* e, int slot, int n) {
+  if (e->exact) return enqueue_prefill_exact(e, slot, n);
   cudaStream_t s = e->stream;
   embed_gather_kernel<<<n, 256, 0, s>>>(e->embed, e->p_tokens, n, e->p_x);
   E_TRY(cudaGetLastError());
@@ -730,6 +831,9 @@ void qwen_engine_destroy(qwen_engine* e) {
   cudaFree(e->p_steps);
   cudaFree(e->p_attn);
   cudaFree(e->p_qkv);
+  cudaFree(e->ex_xn);
+  cudaFree(e->ex_qkv);
+  cudaFree(e->ex_gu);
   for (cudaEvent_t ev : e->kev)
     if (ev) cudaEventDestroy(ev);
   for (cudaEvent_t ev : e->bev) cudaEventDestroy(ev);
@@ -820,6 +924,14 @@ int qwen_engine_set_option(qwen_engine* e, const char* name, long long value) {
     e->use_qgemm = value != 0;
     for (auto& kv : e->graphs) cudaGraphExecDestroy(kv.second);
     e->graphs.clear();
+  } else if (n == "exact") {
+    e->exact = value != 0;
+    if (e->exact) {
+      E_TRY(cudaSetDevice(e->device));
+      if (int st = ensure_exact(e, e->pre_cap)) return st;
+    }
+    for (auto& kv : e->graphs) cudaGraphExecDestroy(kv.second);
+    e->graphs.clear();
   } else if (n == "dump_hidden") e->dump_hidden = value != 0;
   else if (n == "logits") e->keep_logits = value != 0;
   else return kStatusInvalid;
@@ -836,6 +948,9 @@ int qwen_engine_prefill(qwen_engine* e, int slot, const int32_t* tokens, int n, 
     if (tokens[i] < 0 || tokens[i] >= kVocab) return kStatusInvalid;
   E_TRY(cudaSetDevice(e->device));
   if (int st = ensure_prefill_buffers(e, n)) return st;
+  if (e->exact) {
+    if (int st = ensure_exact(e, n)) return st;
+  }
   if (int st = ensure_rope_pre(e, n)) return st;
   if (int st = ensure_pages(e, slot, n)) return st;
   cudaStream_t s = e->stream;

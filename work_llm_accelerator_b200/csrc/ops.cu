@@ -6,6 +6,7 @@
 
 #include "../../include/qwen_b200_ops.h"
 #include "attention_tc.h"
+#include "exact.h"
 #include "qgemm.h"
 #include "tgemm.h"
 #include "qwen_kernels.cuh"
@@ -245,6 +246,25 @@ extern "C" int qwen_b200_prefill_approx_exp(const float* x, float* y, long long 
   const cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) {
     set_error("qwen_b200_prefill_approx_exp: %s", cudaGetErrorString(e));
+    return kStatusCuda;
+  }
+  return 0;
+}
+
+extern "C" int qwen_b200_exact_expf(const float* x, float* y, long long n, void* stream) {
+  using namespace qb;
+  if (!x || !y || n < 0) {
+    set_error("qwen_b200_exact_expf: null buffer or negative n");
+    return kStatusInvalid;
+  }
+  if (!device_accessible(x) || !device_accessible(y)) {
+    set_error("qwen_b200_exact_expf: every buffer must be device (or managed) memory");
+    return kStatusInvalid;
+  }
+  if (n == 0) return 0;
+  const cudaError_t e = exact::launch_expf(x, y, n, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) {
+    set_error("qwen_b200_exact_expf: %s", cudaGetErrorString(e));
     return kStatusCuda;
   }
   return 0;

@@ -78,6 +78,8 @@ def core_lib() -> ctypes.CDLL:
         lib.qwen_b200_prefill_approx_exp.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_longlong,
                                                      ctypes.c_void_p]
         lib.qwen_b200_prefill_approx_exp.restype = ctypes.c_int
+        lib.qwen_b200_exact_expf.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_longlong, ctypes.c_void_p]
+        lib.qwen_b200_exact_expf.restype = ctypes.c_int
         lib.qwen_b200_kernel_error.argtypes = [ctypes.c_int]
         lib.qwen_b200_kernel_error.restype = ctypes.c_uint
         _core = lib
@@ -419,6 +421,13 @@ def prefill_approx_exp(x_ptr: int, y_ptr: int, n: int, stream: int = 0) -> None:
     st = core_lib().qwen_b200_prefill_approx_exp(x_ptr, y_ptr, n, stream or None)
     if st != 0:
         raise EngineError(f"qwen_b200_prefill_approx_exp failed with status {st}: {last_error()}")
+
+
+def exact_expf(x_ptr: int, y_ptr: int, n: int, stream: int = 0) -> None:
+    """y = expf(x) as the reference host library's C library computes it (device buffers; include/qwen_b200_ops.h)."""
+    st = core_lib().qwen_b200_exact_expf(x_ptr, y_ptr, n, stream or None)
+    if st != 0:
+        raise EngineError(f"qwen_b200_exact_expf failed with status {st}: {last_error()}")
 
 
 def w8_digit_planes(codes_ptr: int, rows: int, k: int, x_ptr: int, n_tokens: int, acc_ptr: int, step_ptr: int,
