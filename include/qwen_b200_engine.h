@@ -103,6 +103,19 @@ int qwen_engine_profile_decode(qwen_engine* e, int slot, int first_token, int st
  * GEMM, down GEMM, LM head}. */
 int qwen_engine_profile_batched(qwen_engine* e, const int32_t* slots, const int32_t* first_tokens, int n, int steps,
                                 float* ms_out);
+/* Token exchange of a multi-GPU run: one process and one engine per GPU, independent sequences on each, and
+ * the step's next-token ids all-gathered over NCCL (NVLink / NVSwitch) -- the only collective of the path.
+ * The reference has no counterpart (its host libraries run one layer of one sequence per call).
+ * NCCL is opened at run time (libnccl.so.2: the copy already loaded in the process, else the system one);
+ * failures return 30 with NCCL's message in qwen_b200_last_error().
+ *   qwen_engine_nccl_unique_id: a new communicator id (128 bytes), made on one rank and passed to the
+ *     others by the caller's own bootstrap (a TCP store, MPI, a file).
+ *   qwen_engine_nccl_init: join the communicator as `rank` of `nranks` (blocks until every rank joined).
+ *   qwen_engine_gather_tokens: enqueue on the engine's stream the all-gather of n int32 ids per rank,
+ *     d_local [n] -> d_all [nranks][n] (device memory), after the step that wrote them. */
+int qwen_engine_nccl_unique_id(uint8_t* id_out);
+int qwen_engine_nccl_init(qwen_engine* e, const uint8_t* id, int nranks, int rank);
+int qwen_engine_gather_tokens(qwen_engine* e, const int32_t* d_local, int n, int32_t* d_all);
 /* The engine's CUDA stream (cudaStream_t) for callers that record their own events. */
 void* qwen_engine_stream(qwen_engine* e);
 /* Number of kernels one decode step of `n` sequences launches. */

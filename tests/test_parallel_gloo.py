@@ -1,5 +1,7 @@
-"""World-size-2 gloo tests (CPU) of the multi-GPU host logic: sequence sharding, the per-step next-token
-all-gather and max-over-ranks timing, plus a rank that fails before joining a step."""
+"""World-size-2 gloo tests (CPU) of the multi-GPU host logic: sequence sharding, the bootstrap of the engines'
+NCCL token-exchange communicator (rank 0's id reaches every rank intact), max-over-ranks timing, and a rank
+that fails before joining a step. The all-gather itself is NCCL on the GPUs (qwen_engine_gather_tokens) and is
+exercised by bench.py --gpus N and the 2-GPU test in tests/test_gpu_multi.py."""
 from __future__ import annotations
 
 import os
@@ -10,7 +12,7 @@ import torch
 import torch.distributed as dist
 import torch.multiprocessing as mp
 
-from work_llm_accelerator_b200.parallel import gather_tokens, max_over_ranks, shard_range
+from work_llm_accelerator_b200.parallel import connect_engine, max_over_ranks, shard_range
 
 
 def _free_port() -> int:
@@ -30,17 +32,14 @@ def _worker(rank: int, world: int, port: int, mode: str, q) -> None:
     try:
         if mode == "gather":
             start, stop = shard_range(8, world, rank)
-            local = torch.arange(start, stop, dtype=torch.int32) * 10 + 1
-            steps = []
-            for step in range(3):
-                steps.append(gather_tokens(local + step, world).tolist())
+            uid = connect_engine(None, world, rank)  # the NCCL id made on rank 0, as every rank receives it
             slow = max_over_ranks([1.0 + rank, 5.0 - rank])
-            q.put((rank, steps, slow))
+            q.put((rank, (start, stop), uid, slow))
         elif mode == "fail":
             if rank == 1:
                 raise SystemExit(3)  # leaves before the step's collective
             try:
-                gather_tokens(torch.ones(2, dtype=torch.int32), world)
+                max_over_ranks([1.0])
                 q.put((rank, "no-error"))
             except Exception as exc:  # the peer's absence surfaces as an error, not a hang
                 q.put((rank, type(exc).__name__))
@@ -82,15 +81,14 @@ def test_shard_range_covers_everything():
         shard_range(4, 2, 2)
 
 
-def test_gather_and_max_world2():
+def test_id_exchange_and_max_world2():
     procs, results = _run("gather")
     assert all(p.exitcode == 0 for p in procs)
     results = dict((r[0], r[1:]) for r in results)
-    expected = [[1 + s, 11 + s, 21 + s, 31 + s, 41 + s, 51 + s, 61 + s, 71 + s] for s in range(3)]
+    assert results[0][0] == (0, 4) and results[1][0] == (4, 8)
+    assert len(results[0][1]) == 128 and results[0][1] == results[1][1]
     for rank in (0, 1):
-        steps, slow = results[rank]
-        assert steps == expected
-        assert slow == [2.0, 5.0]
+        assert results[rank][2] == [2.0, 5.0]
 
 
 def test_rank_failure_is_an_error_not_a_hang():

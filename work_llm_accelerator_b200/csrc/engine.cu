@@ -9,10 +9,14 @@
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
+#include <dlfcn.h>
+#include <nccl.h>  // types and the unique-id layout; the library itself is opened at run time
+
 #include <algorithm>
 #include <cmath>
 #include <cstring>
 #include <map>
+#include <mutex>
 #include <string>
 #include <vector>
 
@@ -60,7 +64,8 @@ __global__ void kv_scatter_kernel(const float* __restrict__ kf, const float* __r
 
 __global__ void advance_pos_kernel(int* __restrict__ pos, int n) {
   griddep_wait();
-  if ((int)threadIdx.x < n) pos[threadIdx.x] += 1;
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < n) pos[i] += 1;
 }
 
 // end of a device-resident decode step: next input token = argmax, position + 1
@@ -78,6 +83,48 @@ __global__ void advance_kernel(int* __restrict__ tokens, const int* __restrict__
     cudaError_t _e = (expr);                                                                        \
     if (_e != cudaSuccess) {                                                                        \
       set_error("%s failed: %s (%s:%d)", #expr, cudaGetErrorString(_e), __FILE__, __LINE__);        \
+      return kStatusCuda;                                                                           \
+    }                                                                                               \
+  } while (0)
+
+// NCCL entry points, resolved from libnccl.so.2 on first use: the process's already-loaded copy when one is
+// (e.g. PyTorch's), otherwise the system library. The core library keeps no link-time dependency on NCCL.
+struct NcclApi {
+  ncclResult_t (*get_unique_id)(ncclUniqueId*) = nullptr;
+  ncclResult_t (*comm_init_rank)(ncclComm_t*, int, ncclUniqueId, int) = nullptr;
+  ncclResult_t (*all_gather)(const void*, void*, size_t, ncclDataType_t, ncclComm_t, cudaStream_t) = nullptr;
+  ncclResult_t (*comm_destroy)(ncclComm_t) = nullptr;
+  const char* (*error_string)(ncclResult_t) = nullptr;
+  std::string load_error;
+};
+
+const NcclApi* nccl_api() {
+  static NcclApi api;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_GLOBAL);
+    if (!h) h = dlopen("libnccl.so", RTLD_NOW | RTLD_GLOBAL);
+    if (!h) {
+      const char* why = dlerror();
+      api.load_error = why ? why : "dlopen(libnccl.so.2) failed";
+      return;
+    }
+    api.get_unique_id = reinterpret_cast<decltype(api.get_unique_id)>(dlsym(h, "ncclGetUniqueId"));
+    api.comm_init_rank = reinterpret_cast<decltype(api.comm_init_rank)>(dlsym(h, "ncclCommInitRank"));
+    api.all_gather = reinterpret_cast<decltype(api.all_gather)>(dlsym(h, "ncclAllGather"));
+    api.comm_destroy = reinterpret_cast<decltype(api.comm_destroy)>(dlsym(h, "ncclCommDestroy"));
+    api.error_string = reinterpret_cast<decltype(api.error_string)>(dlsym(h, "ncclGetErrorString"));
+    if (!api.get_unique_id || !api.comm_init_rank || !api.all_gather || !api.comm_destroy || !api.error_string)
+      api.load_error = "libnccl.so.2 lacks an NCCL entry point";
+  });
+  return api.load_error.empty() ? &api : nullptr;
+}
+
+#define N_TRY(api, expr)                                                                              \
+  do {                                                                                              \
+    ncclResult_t _r = (expr);                                                                       \
+    if (_r != ncclSuccess) {                                                                        \
+      set_error("%s failed: %s", #expr, (api)->error_string(_r));                                   \
       return kStatusCuda;                                                                           \
     }                                                                                               \
   } while (0)
@@ -170,6 +217,9 @@ struct qwen_engine {
   // tensor-core LM head
   bool use_lm_tc = true;
   LmScratch lm{nullptr, nullptr, nullptr};
+  // token exchange of a multi-GPU run (qwen_engine_nccl_init)
+  ncclComm_t nccl = nullptr;
+  int nccl_ranks = 0, nccl_rank = 0;
   // option "exact": every layer and the LM head in the reference's arithmetic order (exact.h)
   bool exact = false;
   int ex_cap = 0;                                              // token rows of the buffers below
@@ -817,6 +867,11 @@ int qwen_engine_create(int device, int wbits, int max_seqs, int max_len, qwen_en
 void qwen_engine_destroy(qwen_engine* e) {
   if (!e) return;
   cudaSetDevice(e->device);
+  if (e->nccl) {
+    cudaStreamSynchronize(e->stream);
+    if (const NcclApi* api = nccl_api()) api->comm_destroy(e->nccl);
+    e->nccl = nullptr;
+  }
   for (auto& kv : e->graphs) cudaGraphExecDestroy(kv.second);
   void* ptrs[] = {e->wimg, e->simg, e->embed, e->final_norm, e->kv_pool, e->d_page_table, e->d_tokens, e->d_pos,
                   e->d_seq, e->d_next, e->x, e->q, e->ctx, e->a, e->y0, e->y1, e->h, e->attn_part, e->attn_cnt,
@@ -1273,34 +1328,47 @@ int qwen_engine_read_logits(qwen_engine* e, float* out, long long n_floats) {
 
 int qwen_engine_decode_device(qwen_engine* e, const int32_t* slots, const int32_t* d_tokens, int n,
                               int32_t* d_next) {
-  if (!e || !slots || !d_tokens || !d_next || n <= 0 || n > kGemvMaxTokens) return kStatusInvalid;
+  if (!e || !slots || !d_tokens || !d_next || n <= 0) return kStatusInvalid;
+  const bool batched = batched_ok(e, n);
+  if (n > kGemvMaxTokens && !batched) return kStatusInvalid;
   E_TRY(cudaSetDevice(e->device));
   int max_len = 0;
   const std::vector<int> want(slots, slots + n);
+  std::vector<char> seen(e->max_seqs, 0);
   for (int i = 0; i < n; ++i) {
     const int slot = slots[i];
-    if (slot < 0 || slot >= e->max_seqs) return kStatusInvalid;
+    if (slot < 0 || slot >= e->max_seqs || seen[slot]) return kStatusInvalid;
+    seen[slot] = 1;
     const int pos = e->seq_len[slot];
     if (int st = ensure_pages(e, slot, pos + 1)) return st;
     max_len = std::max(max_len, pos + 1);
   }
   if (int st = ensure_rope_dec(e, max_len)) return st;
+  if (batched) {
+    if (int st = ensure_prefill_buffers(e, n)) return st;
+  }
   if (want != e->dev_slots) {
     // (re)upload positions and slots; steady-state calls keep them on the device and advance them there
+    int* hio = batched ? e->hb_io : e->h_io;
+    const int cap = batched ? e->batch_cap : kGemvMaxTokens;
     E_TRY(cudaStreamSynchronize(e->stream));
     for (int i = 0; i < n; ++i) {
-      e->h_io[4 + i] = e->seq_len[slots[i]];
-      e->h_io[8 + i] = slots[i];
+      hio[cap + i] = e->seq_len[slots[i]];
+      hio[2 * cap + i] = slots[i];
     }
-    E_TRY(cudaMemcpyAsync(e->d_pos, e->h_io + 4, n * 4, cudaMemcpyHostToDevice, e->stream));
-    E_TRY(cudaMemcpyAsync(e->d_seq, e->h_io + 8, n * 4, cudaMemcpyHostToDevice, e->stream));
+    E_TRY(cudaMemcpyAsync(e->d_pos, hio + cap, n * 4, cudaMemcpyHostToDevice, e->stream));
+    E_TRY(cudaMemcpyAsync(e->d_seq, hio + 2 * cap, n * 4, cudaMemcpyHostToDevice, e->stream));
     E_TRY(cudaStreamSynchronize(e->stream));
     e->dev_slots = want;
   }
   E_TRY(cudaMemcpyAsync(e->d_tokens, d_tokens, n * 4, cudaMemcpyDeviceToDevice, e->stream));
-  if (int st = run_decode_step(e, n, max_len, false)) return st;
+  if (batched) {
+    if (int st = run_decode_step_batched(e, n, max_len, false)) return st;
+  } else {
+    if (int st = run_decode_step(e, n, max_len, false)) return st;
+  }
   E_TRY(cudaMemcpyAsync(d_next, e->d_next, n * 4, cudaMemcpyDeviceToDevice, e->stream));
-  advance_pos_kernel<<<1, 32, 0, e->stream>>>(e->d_pos, n);
+  advance_pos_kernel<<<(n + 255) / 256, 256, 0, e->stream>>>(e->d_pos, n);
   E_TRY(cudaGetLastError());
   for (int i = 0; i < n; ++i) e->seq_len[slots[i]] += 1;
   e->last_rows = n;
@@ -1377,6 +1445,46 @@ int qwen_engine_profile_kernels(qwen_engine* e, int n, int past, int iters, floa
   }
   cudaEventDestroy(t0);
   cudaEventDestroy(t1);
+  return 0;
+}
+
+int qwen_engine_nccl_unique_id(uint8_t* id_out) {
+  if (!id_out) return kStatusInvalid;
+  const NcclApi* api = nccl_api();
+  if (!api) {
+    set_error("NCCL unavailable: %s", "libnccl.so.2 could not be loaded");
+    return kStatusCuda;
+  }
+  ncclUniqueId id;
+  N_TRY(api, api->get_unique_id(&id));
+  std::memcpy(id_out, id.internal, NCCL_UNIQUE_ID_BYTES);
+  return 0;
+}
+
+int qwen_engine_nccl_init(qwen_engine* e, const uint8_t* id, int nranks, int rank) {
+  if (!e || !id || nranks <= 0 || rank < 0 || rank >= nranks || e->nccl) return kStatusInvalid;
+  const NcclApi* api = nccl_api();
+  if (!api) {
+    set_error("NCCL unavailable: %s", "libnccl.so.2 could not be loaded");
+    return kStatusCuda;
+  }
+  E_TRY(cudaSetDevice(e->device));
+  ncclUniqueId uid;
+  std::memcpy(uid.internal, id, NCCL_UNIQUE_ID_BYTES);
+  N_TRY(api, api->comm_init_rank(&e->nccl, nranks, uid, rank));
+  e->nccl_ranks = nranks;
+  e->nccl_rank = rank;
+  return 0;
+}
+
+int qwen_engine_gather_tokens(qwen_engine* e, const int32_t* d_local, int n, int32_t* d_all) {
+  if (!e || !d_local || !d_all || n <= 0) return kStatusInvalid;
+  if (!e->nccl) {
+    set_error("qwen_engine_gather_tokens: no communicator (call qwen_engine_nccl_init first)");
+    return kStatusInvalid;
+  }
+  const NcclApi* api = nccl_api();
+  N_TRY(api, api->all_gather(d_local, d_all, (size_t)n, ncclInt32, e->nccl, e->stream));
   return 0;
 }
 

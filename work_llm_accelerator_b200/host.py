@@ -185,13 +185,17 @@ def _configure_engine(lib: ctypes.CDLL) -> None:
     lib.qwen_engine_stream.argtypes = [vp]
     lib.qwen_engine_stream.restype = vp
     lib.qwen_engine_kernels_per_decode_step.argtypes = [vp, i]
+    lib.qwen_engine_nccl_unique_id.argtypes = [ctypes.c_char_p]
+    lib.qwen_engine_nccl_init.argtypes = [vp, ctypes.c_char_p, i, i]
+    lib.qwen_engine_gather_tokens.argtypes = [vp, vp, i, vp]
     for n in ("qwen_engine_create", "qwen_engine_init_synthetic", "qwen_engine_load_layer", "qwen_engine_load_embedding",
               "qwen_engine_prefill", "qwen_engine_decode", "qwen_engine_write_kv", "qwen_engine_read_kv",
               "qwen_engine_set_seq_len", "qwen_engine_seq_len", "qwen_engine_reset", "qwen_engine_set_option",
               "qwen_engine_read_hidden", "qwen_engine_read_logits", "qwen_engine_bench_decode",
               "qwen_engine_kernels_per_decode_step", "qwen_engine_decode_device", "qwen_engine_read_layer",
               "qwen_engine_profile_kernels", "qwen_engine_read_trace", "qwen_engine_profile_decode",
-              "qwen_engine_profile_batched"):
+              "qwen_engine_profile_batched", "qwen_engine_nccl_unique_id", "qwen_engine_nccl_init",
+              "qwen_engine_gather_tokens"):
         getattr(lib, n).restype = i
 
 
@@ -338,6 +342,16 @@ class Engine:
         names = ("rmsnorm", "digits", "qkv", "attention", "o", "gate_up", "down", "lm_head")
         return dict(zip(names, map(float, out)))
 
+    def nccl_init(self, unique_id: bytes, nranks: int, rank: int) -> None:
+        """Join the token-exchange communicator (include/qwen_b200_engine.h; blocks until all ranks joined)."""
+        if len(unique_id) != 128:
+            raise ValueError("an NCCL unique id is 128 bytes")
+        _check(self.lib.qwen_engine_nccl_init(self.handle, unique_id, nranks, rank), "nccl_init")
+
+    def gather_tokens(self, d_local_ptr: int, n: int, d_all_ptr: int) -> None:
+        """Enqueue the all-gather of n int32 ids per rank on the engine's stream (device pointers)."""
+        _check(self.lib.qwen_engine_gather_tokens(self.handle, d_local_ptr, n, d_all_ptr), "gather_tokens")
+
     def stream(self) -> int:
         return int(self.lib.qwen_engine_stream(self.handle) or 0)
 
@@ -421,6 +435,13 @@ def prefill_approx_exp(x_ptr: int, y_ptr: int, n: int, stream: int = 0) -> None:
     st = core_lib().qwen_b200_prefill_approx_exp(x_ptr, y_ptr, n, stream or None)
     if st != 0:
         raise EngineError(f"qwen_b200_prefill_approx_exp failed with status {st}: {last_error()}")
+
+
+def nccl_unique_id() -> bytes:
+    """A new 128-byte NCCL communicator id for Engine.nccl_init (made on one rank, passed to the others)."""
+    buf = ctypes.create_string_buffer(128)
+    _check(core_lib().qwen_engine_nccl_unique_id(buf), "nccl_unique_id")
+    return buf.raw
 
 
 def exact_expf(x_ptr: int, y_ptr: int, n: int, stream: int = 0) -> None:
