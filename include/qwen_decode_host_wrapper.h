@@ -75,6 +75,22 @@ int qwen_decode_layer_smoke_forward_w8(const float* input_token, int past_seq_le
                                        const float* up_scales, const float* down_scales, float* k_cache,
                                        float* v_cache, float* output_token);
 
+/* replaces hls/decode_only/qwen_decode_host_wrapper.h:89-113 (body: qwen_decode_layer0_reference_wrapper.cpp:75-209):
+ * the fp32-weight golden decoder layer (double accumulation, bf16 rounding after every linear and norm, the
+ * attention residual kept), one token at position past_seq_len. Weights are fp32 row-major [out][in]; biases
+ * may be null. Caches are head-major: past [2][past_seq_len][128], next [2][past_seq_len + 1][128]. Status 1
+ * when input, output or a next cache is null, past_seq_len < 0, a weight or norm vector is null, or a past
+ * cache is null while past_seq_len > 0 (the reference reads it). */
+int qwen_decode_layer0_reference_forward(const float* input_token, int past_seq_len, const float* past_k_cache,
+                                         const float* past_v_cache, const float* input_layernorm_weight,
+                                         const float* q_weight, const float* q_bias, const float* k_weight,
+                                         const float* k_bias, const float* v_weight, const float* v_bias,
+                                         const float* o_weight, const float* o_bias,
+                                         const float* post_attention_layernorm_weight, const float* gate_weight,
+                                         const float* gate_bias, const float* up_weight, const float* up_bias,
+                                         const float* down_weight, const float* down_bias, float rms_eps,
+                                         float* output_token, float* next_k_cache, float* next_v_cache);
+
 #ifdef __cplusplus
 }
 #endif

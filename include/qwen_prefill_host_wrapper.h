@@ -116,6 +116,29 @@ int qwen_prefill_layer_smoke_forward_w8(
     const float* o_scales, const float* gate_scales, const float* up_scales, const float* down_scales,
     float* k_cache, float* v_cache, float* output_sequence);
 
+/* replaces hls/prefill_only/qwen_prefill_host_wrapper.h:171-191 (body: qwen_prefill_layer0_reference_wrapper.cpp:
+ * 60-255, 257-300): the fp32-weight golden decoder layer over seq_len tokens from position 0 (fp32 RMSNorm,
+ * double accumulation, bf16 rounding after every linear and norm, bf16 RoPE factors, the attention residual
+ * kept). Status 1 when input or output is null, seq_len is outside 1..32768 or a weight or norm vector is null. */
+int qwen_prefill_layer0_reference_forward(const float* input_sequence, int seq_len,
+                                          const float* input_layernorm_weight, const float* q_weight,
+                                          const float* q_bias, const float* k_weight, const float* k_bias,
+                                          const float* v_weight, const float* v_bias, const float* o_weight,
+                                          const float* o_bias, const float* post_attention_layernorm_weight,
+                                          const float* gate_weight, const float* gate_bias, const float* up_weight,
+                                          const float* up_bias, const float* down_weight, const float* down_bias,
+                                          float rms_eps, float* output_sequence);
+/* replaces hls/prefill_only/qwen_prefill_host_wrapper.h:193-215 (body: :302-347): the same layer, also writing
+ * the bf16-rounded post-RoPE K and V head-major [2][seq_len][128] to k_cache / v_cache (both or neither:
+ * status 1 when exactly one is null). */
+int qwen_prefill_layer0_reference_forward_with_cache(
+    const float* input_sequence, int seq_len, const float* input_layernorm_weight, const float* q_weight,
+    const float* q_bias, const float* k_weight, const float* k_bias, const float* v_weight, const float* v_bias,
+    const float* o_weight, const float* o_bias, const float* post_attention_layernorm_weight,
+    const float* gate_weight, const float* gate_bias, const float* up_weight, const float* up_bias,
+    const float* down_weight, const float* down_bias, float rms_eps, float* output_sequence, float* k_cache,
+    float* v_cache);
+
 #ifdef __cplusplus
 }
 #endif

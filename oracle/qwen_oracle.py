@@ -377,6 +377,11 @@ def configure_abi(decode: ctypes.CDLL | None, prefill: ctypes.CDLL | None) -> No
         for n in ("qwen_decode_stub_forward", "qwen_decode_attention_smoke_forward", "qwen_decode_mlp_smoke_forward",
                   "qwen_decode_top_smoke_forward", "qwen_decode_layer_smoke_forward"):
             getattr(decode, n).restype = i
+        if hasattr(decode, "qwen_decode_layer0_reference_forward"):
+            # pointers as c_void_p: the biases may be null
+            vp = _c.c_void_p
+            decode.qwen_decode_layer0_reference_forward.argtypes = [vp, i] + [vp] * 18 + [_c.c_float, vp, vp, vp]
+            decode.qwen_decode_layer0_reference_forward.restype = i
     if prefill is not None:
         t11 = [i] * 11
         prefill.qwen_prefill_stub_forward.argtypes = [_F, i] + t11 + [_F]
@@ -390,6 +395,13 @@ def configure_abi(decode: ctypes.CDLL | None, prefill: ctypes.CDLL | None) -> No
                   "qwen_prefill_layer_smoke_forward", "qwen_prefill_glue_smoke_forward",
                   "qwen_prefill_top_smoke_forward"):
             getattr(prefill, n).restype = i
+        if hasattr(prefill, "qwen_prefill_layer0_reference_forward"):
+            vp = _c.c_void_p
+            prefill.qwen_prefill_layer0_reference_forward.argtypes = [vp, i] + [vp] * 16 + [_c.c_float, vp]
+            prefill.qwen_prefill_layer0_reference_forward.restype = i
+            prefill.qwen_prefill_layer0_reference_forward_with_cache.argtypes = ([vp, i] + [vp] * 16 +
+                                                                                 [_c.c_float, vp, vp, vp])
+            prefill.qwen_prefill_layer0_reference_forward_with_cache.restype = i
 
 
 def sram_ports() -> tuple:

@@ -52,8 +52,8 @@ def test_every_declared_symbol_is_exported(host):
 
 
 def test_reference_symbols_all_present(host, ref_libs):
-    """Every entry point of the reference's two libraries that the hot path uses is exported by the
-    drop-in library of the same name (layer0 goldens are out of scope)."""
+    """Every entry point of the reference's two libraries is exported by the drop-in library of the same
+    name (the layer0 fp32 golden layers included)."""
     import work_llm_accelerator_b200.build as b
 
     for ref_lib, ours in ((qo.REF_DECODE_LIB, b.LIB_DECODE), (qo.REF_PREFILL_LIB, b.LIB_PREFILL)):
@@ -63,8 +63,7 @@ def test_reference_symbols_all_present(host, ref_libs):
         our_syms = set(re.findall(r"\bT (qwen_\w+)\b",
                                   subprocess.run(["nm", "-D", "--defined-only", str(ours)], capture_output=True,
                                                  text=True).stdout))
-        needed = {s for s in ref_syms if "layer0_reference" not in s}
-        assert needed and needed <= our_syms, needed - our_syms
+        assert ref_syms and ref_syms <= our_syms, ref_syms - our_syms
 
 
 def _zero_ddr():

@@ -212,4 +212,30 @@ int qwen_decode_top_smoke_forward_w8(int layer_id, int past_seq_len, uint64_t in
                      control_sram);
 }
 
+int qwen_decode_layer0_reference_forward(const float* input_token, int past_seq_len, const float* past_k_cache,
+                                         const float* past_v_cache, const float* input_layernorm_weight,
+                                         const float* q_weight, const float* q_bias, const float* k_weight,
+                                         const float* k_bias, const float* v_weight, const float* v_bias,
+                                         const float* o_weight, const float* o_bias,
+                                         const float* post_attention_layernorm_weight, const float* gate_weight,
+                                         const float* gate_bias, const float* up_weight, const float* up_bias,
+                                         const float* down_weight, const float* down_bias, float rms_eps,
+                                         float* output_token, float* next_k_cache, float* next_v_cache) {
+  // the reference's own check (qwen_decode_layer0_reference_wrapper.cpp:101-103), then the pointers it
+  // dereferences without checking
+  if (input_token == nullptr || output_token == nullptr || next_k_cache == nullptr || next_v_cache == nullptr ||
+      past_seq_len < 0)
+    return 1;
+  if (input_layernorm_weight == nullptr || q_weight == nullptr || k_weight == nullptr || v_weight == nullptr ||
+      o_weight == nullptr || post_attention_layernorm_weight == nullptr || gate_weight == nullptr ||
+      up_weight == nullptr || down_weight == nullptr || (past_seq_len > 0 && (past_k_cache == nullptr ||
+                                                                              past_v_cache == nullptr)))
+    return 1;
+  const qb::Layer0Ptrs W{input_layernorm_weight, q_weight, q_bias, k_weight, k_bias, v_weight, v_bias, o_weight,
+                         o_bias, post_attention_layernorm_weight, gate_weight, gate_bias, up_weight, up_bias,
+                         down_weight, down_bias};
+  return qb::run_layer0_decode(W, input_token, past_seq_len, past_k_cache, past_v_cache, rms_eps, output_token,
+                               next_k_cache, next_v_cache);
+}
+
 }  // extern "C"

@@ -354,4 +354,38 @@ int qwen_prefill_layer_smoke_forward_w8(const float* input_sequence, int seq_len
                      k_cache, v_cache, output_sequence);
 }
 
+int qwen_prefill_layer0_reference_forward_with_cache(
+    const float* input_sequence, int seq_len, const float* input_layernorm_weight, const float* q_weight,
+    const float* q_bias, const float* k_weight, const float* k_bias, const float* v_weight, const float* v_bias,
+    const float* o_weight, const float* o_bias, const float* post_attention_layernorm_weight,
+    const float* gate_weight, const float* gate_bias, const float* up_weight, const float* up_bias,
+    const float* down_weight, const float* down_bias, float rms_eps, float* output_sequence, float* k_cache,
+    float* v_cache) {
+  // qwen_prefill_layer0_reference_wrapper.cpp:82-88, then the pointers the reference dereferences unchecked
+  if (input_sequence == nullptr || output_sequence == nullptr || seq_len <= 0 || seq_len > 32768) return 1;
+  if ((k_cache == nullptr) != (v_cache == nullptr)) return 1;
+  if (input_layernorm_weight == nullptr || q_weight == nullptr || k_weight == nullptr || v_weight == nullptr ||
+      o_weight == nullptr || post_attention_layernorm_weight == nullptr || gate_weight == nullptr ||
+      up_weight == nullptr || down_weight == nullptr)
+    return 1;
+  const qb::Layer0Ptrs W{input_layernorm_weight, q_weight, q_bias, k_weight, k_bias, v_weight, v_bias, o_weight,
+                         o_bias, post_attention_layernorm_weight, gate_weight, gate_bias, up_weight, up_bias,
+                         down_weight, down_bias};
+  return qb::run_layer0_prefill(W, input_sequence, seq_len, rms_eps, output_sequence, k_cache, v_cache);
+}
+
+int qwen_prefill_layer0_reference_forward(const float* input_sequence, int seq_len,
+                                          const float* input_layernorm_weight, const float* q_weight,
+                                          const float* q_bias, const float* k_weight, const float* k_bias,
+                                          const float* v_weight, const float* v_bias, const float* o_weight,
+                                          const float* o_bias, const float* post_attention_layernorm_weight,
+                                          const float* gate_weight, const float* gate_bias, const float* up_weight,
+                                          const float* up_bias, const float* down_weight, const float* down_bias,
+                                          float rms_eps, float* output_sequence) {
+  return qwen_prefill_layer0_reference_forward_with_cache(
+      input_sequence, seq_len, input_layernorm_weight, q_weight, q_bias, k_weight, k_bias, v_weight, v_bias,
+      o_weight, o_bias, post_attention_layernorm_weight, gate_weight, gate_bias, up_weight, up_bias, down_weight,
+      down_bias, rms_eps, output_sequence, nullptr, nullptr);
+}
+
 }  // extern "C"

@@ -672,20 +672,13 @@ cudaError_t launch_decode_attention(const float* q, KvView kv, DecodeTokens tok,
                                     float* scratch, unsigned* counters, cudaStream_t s, bool pdl,
                                     const void* prefetch, size_t prefetch_bytes, int max_ctas) {
   const int max_chunks = (max_len + kChunk - 1) / kChunk;
-  static int sms = 0;
-  if (sms == 0) {
-    int dev = 0;
-    cudaError_t e = cudaGetDevice(&dev);
-    if (e == cudaSuccess) e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const int sms = device_sm_count();
+  {
+    cudaError_t e = ensure_smem_attr((const void*)decode_attn_kernel, kDecodeAttnSmem);
     if (e == cudaSuccess)
-      e = cudaFuncSetAttribute(decode_attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kDecodeAttnSmem);
-    if (e == cudaSuccess)
-      e = cudaFuncSetAttribute(decode_attn_merge_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                               (int)((4 * kGroups * (kMaxSeq / kChunk) + kGroups) * sizeof(float)));
-    if (e != cudaSuccess) {
-      sms = 0;
-      return e;
-    }
+      e = ensure_smem_attr((const void*)decode_attn_merge_kernel,
+                           (4 * kGroups * (kMaxSeq / kChunk) + kGroups) * sizeof(float));
+    if (e != cudaSuccess) return e;
   }
   (void)counters;  // kept for the interface; the merge runs as its own kernel
   if (tok.nt <= 0 || max_chunks <= 0 || max_chunks > kMaxSeq / kChunk || (reinterpret_cast<uintptr_t>(q) & 15))

@@ -520,16 +520,7 @@ struct EpiLm {
   }
 };
 
-int num_sms() {
-  static int n = 0;
-  if (n == 0) {
-    int dev = 0;
-    cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
-    if (n <= 0) n = 148;
-  }
-  return n;
-}
+int num_sms() { return device_sm_count(); }
 
 // Stage geometry: a row is split into column blocks of at most 4 KB so that a stage (8 rows) stays small;
 // ring depth fills the shared-memory target (at least 2 stages).
@@ -552,12 +543,7 @@ cudaError_t run_gemv(GemvArgs a, const Epi& epi, cudaStream_t s, bool pdl) {
   plan_stages(a, WBITS, NT);
   const size_t smem = 256 + (size_t)NT * a.K * 4 + (size_t)a.nstages * kRows * a.kb_bytes + 2 * kRows * NT * 4;
   auto kern = gemv_kernel<WBITS, NT, MODE, Epi>;
-  static size_t attr_bytes = 0;  // per instantiation: raise the dynamic shared-memory limit when needed
-  if (smem > attr_bytes) {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    if (e != cudaSuccess) return e;
-    attr_bytes = smem;
-  }
+  if (cudaError_t e = ensure_smem_attr((const void*)kern, smem)) return e;
   const int grid = a.nunits < num_sms() ? a.nunits : num_sms();
   return launch_k(kern, dim3(grid), dim3(kThreads), smem, s, pdl, a, epi);
 }

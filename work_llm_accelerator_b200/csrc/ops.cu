@@ -28,6 +28,8 @@ struct OpScratch {
 std::mutex g_ops_mu;
 OpScratch g_ops[kMaxDevices];
 
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+
 bool device_accessible(const void* p) {
   cudaPointerAttributes a;
   if (cudaPointerGetAttributes(&a, p) != cudaSuccess) {
@@ -55,6 +57,11 @@ extern "C" int qwen_b200_decode_attention(const float* q, const float* k_cache, 
   if (!device_accessible(q) || !device_accessible(k_cache) || !device_accessible(v_cache) ||
       !device_accessible(context)) {
     set_error("qwen_b200_decode_attention: every buffer must be device (or managed) memory");
+    return kStatusInvalid;
+  }
+  if (!aligned16(q) || !aligned16(k_cache) || !aligned16(v_cache) || !aligned16(context)) {
+    set_error("qwen_b200_decode_attention: %s is not 16-byte aligned (the kernel moves 16-byte vectors)",
+              !aligned16(q) ? "q" : !aligned16(k_cache) ? "k_cache" : !aligned16(v_cache) ? "v_cache" : "context");
     return kStatusInvalid;
   }
   int dev = 0;

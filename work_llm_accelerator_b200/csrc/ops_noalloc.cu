@@ -76,6 +76,12 @@ extern "C" int qwen_b200_decode_attention_noalloc(const float* q, const float* k
     set_error("qwen_b200_decode_attention_noalloc: every buffer must be device (or managed) memory");
     return kStatusInvalid;
   }
+  auto aligned16 = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
+  if (!aligned16(q) || !aligned16(k_cache) || !aligned16(v_cache) || !aligned16(context)) {
+    set_error("qwen_b200_decode_attention_noalloc: %s is not 16-byte aligned (the kernel moves 16-byte vectors)",
+              !aligned16(q) ? "q" : !aligned16(k_cache) ? "k_cache" : !aligned16(v_cache) ? "v_cache" : "context");
+    return kStatusInvalid;
+  }
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) {
     set_error("qwen_b200_decode_attention_noalloc: no current CUDA device");

@@ -464,12 +464,7 @@ cudaError_t run_qgemm(const CUtensorMap& map, const QArgs& a, const Epi& e, cuda
   auto kern = qgemm_kernel<MODE, Epi>;
   const int kbs = (a.nkb + a.split - 1) / a.split;
   const size_t smem = sizeof(Smem) + 2048 + (size_t)kbs * 2048;
-  static size_t attr = 0;
-  if (smem > attr) {
-    cudaError_t err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    if (err != cudaSuccess) return err;
-    attr = smem;
-  }
+  if (cudaError_t err = ensure_smem_attr((const void*)kern, smem)) return err;
   return launch_k(kern, dim3(a.mtiles * a.split), dim3(kThreads), smem, s, pdl, map, a, e);
 }
 

@@ -4,6 +4,8 @@
 #include <cuda_runtime.h>
 
 #include <cstdint>
+#include <map>
+#include <mutex>
 #include <utility>
 
 #include "qwen_common.cuh"
@@ -90,6 +92,34 @@ cudaError_t launch_synth_fill(uint64_t seed, uint64_t stream, uint64_t count, fl
                               cudaStream_t s);
 cudaError_t launch_synth_embedding(uint64_t seed, uint16_t* embed, cudaStream_t s);
 cudaError_t launch_round_bf16(float* x, size_t n, cudaStream_t s);
+
+// Raise `func`'s dynamic shared-memory limit to `bytes` on the current device (function attributes belong to a
+// device's context, so a process that uses several GPUs needs them set on each), once per kernel and device.
+inline cudaError_t ensure_smem_attr(const void* func, size_t bytes) {
+  static std::mutex mu;
+  static std::map<std::pair<const void*, int>, size_t> done;
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  std::lock_guard<std::mutex> lock(mu);
+  size_t& have = done[std::make_pair(func, dev)];
+  if (bytes <= have) return cudaSuccess;
+  e = cudaFuncSetAttribute(func, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
+  if (e == cudaSuccess) have = bytes;
+  return e;
+}
+
+// Number of SMs of the current device (cached per device).
+inline int device_sm_count() {
+  static std::mutex mu;
+  static std::map<int, int> sms;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return 148;
+  std::lock_guard<std::mutex> lock(mu);
+  int& n = sms[dev];
+  if (n <= 0 && (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0)) n = 148;
+  return n;
+}
 
 // Launch helper: cudaLaunchKernelEx with optional programmatic stream serialization.
 template <typename... KArgs, typename... Args>

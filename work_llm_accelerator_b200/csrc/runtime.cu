@@ -19,6 +19,7 @@
 #include <vector>
 
 #include "attention_tc.h"
+#include "layer0_ref.h"
 #include "decode_stack.h"
 #include "qgemm.h"
 #include "lmhead.h"
@@ -65,6 +66,8 @@ struct Ctx {
   Buf planes, psteps;
   Buf attn;     // tensor-core prefill attention scratch
   Buf qkv_raw;  // W8 prefill: biased q|k|v rows before RoPE
+  // layer0 reference layers: fp32 weights and activations
+  Buf l0w, l0a;
   // zero-weight layer for the stub entry points
   Buf zw, zs;
   LayerPtrs zero{};
@@ -391,6 +394,155 @@ int run_prefill(int wbits, const LayerPtrs& L, bool attention, bool mlp, const f
       QB_TRY(launch_prefill_down(wbits, D, (const float*)c.h.p, a_dev, S, (float*)c.out.p, false, c.stream));
     }
     QB_TRY(cudaMemcpyAsync(out, c.out.p, SH, cudaMemcpyDefault, c.stream));
+  }
+  QB_TRY(cudaStreamSynchronize(c.stream));
+  return 0;
+}
+
+namespace {
+
+// Device copies of one layer0 layer's fp32 weights (offsets in floats; biases absent when null).
+struct L0Dev {
+  const float *in_ln, *q_w, *q_b, *k_w, *k_b, *v_w, *v_b, *o_w, *o_b;
+  const float *post_ln, *gate_w, *gate_b, *up_w, *up_b, *down_w, *down_b;
+};
+
+int stage_layer0(Ctx& c, const Layer0Ptrs& W, L0Dev* d) {
+  const size_t H = kHidden, KV = kKvWidth, I = kInter;
+  struct Part {
+    const float* src;
+    size_t n;
+    const float** dst;
+  } parts[] = {{W.input_ln, H, &d->in_ln},      {W.q_w, H * H, &d->q_w},       {W.q_b, H, &d->q_b},
+               {W.k_w, KV * H, &d->k_w},        {W.k_b, KV, &d->k_b},          {W.v_w, KV * H, &d->v_w},
+               {W.v_b, KV, &d->v_b},            {W.o_w, H * H, &d->o_w},       {W.o_b, H, &d->o_b},
+               {W.post_ln, H, &d->post_ln},     {W.gate_w, I * H, &d->gate_w}, {W.gate_b, I, &d->gate_b},
+               {W.up_w, I * H, &d->up_w},       {W.up_b, I, &d->up_b},         {W.down_w, H * I, &d->down_w},
+               {W.down_b, H, &d->down_b}};
+  size_t total = 0;
+  for (const Part& p : parts) total += (p.n + 3) / 4 * 4;  // every part 16-byte aligned
+  QB_TRY(ensure(c.l0w, total * 4));
+  float* base = (float*)c.l0w.p;
+  size_t off = 0;
+  for (const Part& p : parts) {
+    if (p.src) {
+      QB_TRY(cudaMemcpyAsync(base + off, p.src, p.n * 4, cudaMemcpyDefault, c.stream));
+      *p.dst = base + off;
+    } else {
+      *p.dst = nullptr;
+    }
+    off += (p.n + 3) / 4 * 4;
+  }
+  return 0;
+}
+
+// Activation buffers of n tokens (decode: n = 1 plus the assembled head-major caches of `total` rows).
+struct L0Act {
+  float *x, *xn, *q, *k, *v, *ctx, *o, *resid, *post, *gate, *up, *h, *down, *out, *kc, *vc;
+};
+
+int stage_act0(Ctx& c, int n, int cache_rows, L0Act* a) {
+  const size_t H = (size_t)n * kHidden, KV = (size_t)n * kKvWidth, I = (size_t)n * kInter;
+  const size_t C = (size_t)kKvHeads * cache_rows * kHeadDim;
+  const size_t sizes[] = {H, H, H, KV, KV, H, H, H, H, I, I, I, H, H, C, C};
+  float** dst[] = {&a->x, &a->xn, &a->q, &a->k, &a->v, &a->ctx, &a->o, &a->resid, &a->post, &a->gate, &a->up,
+                   &a->h, &a->down, &a->out, &a->kc, &a->vc};
+  size_t total = 0;
+  for (size_t z : sizes) total += (z + 3) / 4 * 4;
+  QB_TRY(ensure(c.l0a, total * 4));
+  float* base = (float*)c.l0a.p;
+  size_t off = 0;
+  for (int i = 0; i < 16; ++i) {
+    *dst[i] = base + off;
+    off += (sizes[i] + 3) / 4 * 4;
+  }
+  return 0;
+}
+
+// Attention output -> residual -> post-attention norm -> SwiGLU MLP -> output, for n tokens.
+int layer0_tail(Ctx& c, const L0Dev& d, const L0Act& a, int n, float eps, bool decode_form) {
+  const long long H = (long long)n * kHidden, I = (long long)n * kInter;
+  QB_TRY(l0::linear(a.ctx, n, kHidden, d.o_w, d.o_b, kHidden, a.o, c.stream));
+  QB_TRY(l0::add(a.x, a.o, H, a.resid, c.stream));
+  QB_TRY(l0::rmsnorm(a.resid, d.post_ln, n, eps, decode_form, a.post, c.stream));
+  QB_TRY(l0::linear(a.post, n, kHidden, d.gate_w, d.gate_b, kInter, a.gate, c.stream));
+  QB_TRY(l0::linear(a.post, n, kHidden, d.up_w, d.up_b, kInter, a.up, c.stream));
+  QB_TRY(l0::silu_mul(a.gate, a.up, I, a.h, c.stream));
+  QB_TRY(l0::linear(a.h, n, kInter, d.down_w, d.down_b, kHidden, a.down, c.stream));
+  QB_TRY(l0::add(a.resid, a.down, H, a.out, c.stream));
+  return 0;
+}
+
+}  // namespace
+
+int run_layer0_decode(const Layer0Ptrs& W, const float* x, int past, const float* past_k, const float* past_v,
+                      float eps, float* out, float* next_k, float* next_v) {
+  std::lock_guard<std::mutex> lock(g_mu);
+  Ctx& c = g_ctx;
+  if (int st = init_ctx(c)) return st;
+  const int total = past + 1;
+  if (int st = ensure_decode_rope(c, total)) return st;
+  L0Dev d;
+  L0Act a;
+  if (int st = stage_layer0(c, W, &d)) return st;
+  if (int st = stage_act0(c, 1, total, &a)) return st;
+  QB_TRY(cudaMemcpyAsync(a.x, x, (size_t)kHidden * 4, cudaMemcpyDefault, c.stream));
+  QB_TRY(l0::rmsnorm(a.x, d.in_ln, 1, eps, true, a.xn, c.stream));
+  QB_TRY(l0::linear(a.xn, 1, kHidden, d.q_w, d.q_b, kHidden, a.q, c.stream));
+  QB_TRY(l0::linear(a.xn, 1, kHidden, d.k_w, d.k_b, kKvWidth, a.k, c.stream));
+  QB_TRY(l0::linear(a.xn, 1, kHidden, d.v_w, d.v_b, kKvWidth, a.v, c.stream));
+  QB_TRY(l0::rope(a.q, a.k, 1, past, (const float*)c.rope_dec_cos.p, (const float*)c.rope_dec_sin.p, false, c.stream));
+  // next caches [2][total][128]: the caller's history rows, then this token's K (post-RoPE) and V
+  const size_t row = (size_t)kHeadDim * 4;
+  for (int h = 0; h < kKvHeads; ++h) {
+    if (past > 0) {
+      QB_TRY(cudaMemcpyAsync(a.kc + (size_t)h * total * kHeadDim, past_k + (size_t)h * past * kHeadDim, past * row,
+                             cudaMemcpyDefault, c.stream));
+      QB_TRY(cudaMemcpyAsync(a.vc + (size_t)h * total * kHeadDim, past_v + (size_t)h * past * kHeadDim, past * row,
+                             cudaMemcpyDefault, c.stream));
+    }
+    QB_TRY(cudaMemcpyAsync(a.kc + ((size_t)h * total + past) * kHeadDim, a.k + (size_t)h * kHeadDim, row,
+                           cudaMemcpyDeviceToDevice, c.stream));
+    QB_TRY(cudaMemcpyAsync(a.vc + ((size_t)h * total + past) * kHeadDim, a.v + (size_t)h * kHeadDim, row,
+                           cudaMemcpyDeviceToDevice, c.stream));
+  }
+  QB_TRY(l0::attention(a.q, 1, past, a.kc, a.vc, (long long)total * kHeadDim, kHeadDim, a.ctx, c.stream));
+  if (int st = layer0_tail(c, d, a, 1, eps, true)) return st;
+  QB_TRY(cudaMemcpyAsync(out, a.out, (size_t)kHidden * 4, cudaMemcpyDefault, c.stream));
+  QB_TRY(cudaMemcpyAsync(next_k, a.kc, (size_t)kKvHeads * total * row, cudaMemcpyDefault, c.stream));
+  QB_TRY(cudaMemcpyAsync(next_v, a.vc, (size_t)kKvHeads * total * row, cudaMemcpyDefault, c.stream));
+  QB_TRY(cudaStreamSynchronize(c.stream));
+  return 0;
+}
+
+int run_layer0_prefill(const Layer0Ptrs& W, const float* x, int S, float eps, float* out, float* k_cache,
+                       float* v_cache) {
+  std::lock_guard<std::mutex> lock(g_mu);
+  Ctx& c = g_ctx;
+  if (int st = init_ctx(c)) return st;
+  if (int st = ensure_decode_rope(c, S)) return st;  // same float(cos(double angle)) table, bf16-rounded in use
+  L0Dev d;
+  L0Act a;
+  if (int st = stage_layer0(c, W, &d)) return st;
+  if (int st = stage_act0(c, S, S, &a)) return st;
+  QB_TRY(cudaMemcpyAsync(a.x, x, (size_t)S * kHidden * 4, cudaMemcpyDefault, c.stream));
+  QB_TRY(l0::rmsnorm(a.x, d.in_ln, S, eps, false, a.xn, c.stream));
+  QB_TRY(l0::linear(a.xn, S, kHidden, d.q_w, d.q_b, kHidden, a.q, c.stream));
+  QB_TRY(l0::linear(a.xn, S, kHidden, d.k_w, d.k_b, kKvWidth, a.k, c.stream));
+  QB_TRY(l0::linear(a.xn, S, kHidden, d.v_w, d.v_b, kKvWidth, a.v, c.stream));
+  QB_TRY(l0::rope(a.q, a.k, S, 0, (const float*)c.rope_dec_cos.p, (const float*)c.rope_dec_sin.p, true, c.stream));
+  if (k_cache != nullptr) {
+    QB_TRY(l0::to_head_major(a.k, S, true, a.kc, c.stream));
+    QB_TRY(l0::to_head_major(a.v, S, true, a.vc, c.stream));
+  }
+  // attention reads the token-major rows [S][256] (unrounded, as the reference's k_proj_out / v_proj_out)
+  QB_TRY(l0::attention(a.q, S, 0, a.k, a.v, kHeadDim, kKvWidth, a.ctx, c.stream));
+  if (int st = layer0_tail(c, d, a, S, eps, false)) return st;
+  QB_TRY(cudaMemcpyAsync(out, a.out, (size_t)S * kHidden * 4, cudaMemcpyDefault, c.stream));
+  if (k_cache != nullptr) {
+    const size_t bytes = (size_t)kKvHeads * S * kHeadDim * 4;
+    QB_TRY(cudaMemcpyAsync(k_cache, a.kc, bytes, cudaMemcpyDefault, c.stream));
+    QB_TRY(cudaMemcpyAsync(v_cache, a.vc, bytes, cudaMemcpyDefault, c.stream));
   }
   QB_TRY(cudaStreamSynchronize(c.stream));
   return 0;

@@ -35,6 +35,22 @@ int run_decode(int wbits, const LayerPtrs& L, bool attention, bool mlp, const fl
 int run_prefill(int wbits, const LayerPtrs& L, bool attention, bool mlp, const float* x, int seq_len, float* k_cache,
                 float* v_cache, float* attn_out, float* out);
 
+// fp32 weights of one "layer0 reference" layer (unquantised, row-major [out][in]); biases may be null.
+struct Layer0Ptrs {
+  const float *input_ln, *q_w, *q_b, *k_w, *k_b, *v_w, *v_b, *o_w, *o_b;
+  const float *post_ln, *gate_w, *gate_b, *up_w, *up_b, *down_w, *down_b;
+};
+
+// The reference's fp32 golden decoder layer on the GPU, same arithmetic and roundings
+// (hls/decode_only/qwen_decode_layer0_reference_wrapper.cpp:75-209): one decode token at position `past`,
+// caches head-major ([2][past][128] in, [2][past + 1][128] out). Returns 0 or 30 / 31.
+int run_layer0_decode(const Layer0Ptrs& W, const float* x, int past, const float* past_k, const float* past_v,
+                      float eps, float* out, float* next_k, float* next_v);
+// Prefill form (hls/prefill_only/qwen_prefill_layer0_reference_wrapper.cpp:60-255): S tokens from position 0;
+// k_cache / v_cache (both or neither) receive the bf16-rounded post-RoPE K and V head-major [2][S][128].
+int run_layer0_prefill(const Layer0Ptrs& W, const float* x, int S, float eps, float* out, float* k_cache,
+                       float* v_cache);
+
 // Zero-weight layer (all codes 0, scales 1, norm weights 1, biases 0) on the device, used by the
 // reference's `*_stub_forward` entry points (hls/decode_only/qwen_decode_host_wrapper.cpp:12-71).
 const LayerPtrs& zero_layer_device();

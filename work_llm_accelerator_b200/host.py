@@ -105,6 +105,10 @@ def configure_decode_abi(lib: ctypes.CDLL) -> ctypes.CDLL:
         lib.qwen_decode_top_smoke_forward_w8.argtypes = top
         lib.qwen_decode_layer_smoke_forward_w8.argtypes = layer
         names += ["qwen_decode_top_smoke_forward_w8", "qwen_decode_layer_smoke_forward_w8"]
+    # layer0 golden layer: every pointer as c_void_p (biases may be null), rms_eps as float
+    vp = ctypes.c_void_p
+    lib.qwen_decode_layer0_reference_forward.argtypes = [vp, i] + [vp] * 18 + [ctypes.c_float, vp, vp, vp]
+    names.append("qwen_decode_layer0_reference_forward")
     for n in names:
         getattr(lib, n).restype = i
     return lib
@@ -127,6 +131,10 @@ def configure_prefill_abi(lib: ctypes.CDLL) -> ctypes.CDLL:
         lib.qwen_prefill_top_smoke_forward_w8.argtypes = top
         lib.qwen_prefill_layer_smoke_forward_w8.argtypes = layer
         names += ["qwen_prefill_top_smoke_forward_w8", "qwen_prefill_layer_smoke_forward_w8"]
+    vp = ctypes.c_void_p
+    lib.qwen_prefill_layer0_reference_forward.argtypes = [vp, i] + [vp] * 16 + [ctypes.c_float, vp]
+    lib.qwen_prefill_layer0_reference_forward_with_cache.argtypes = [vp, i] + [vp] * 16 + [ctypes.c_float, vp, vp, vp]
+    names += ["qwen_prefill_layer0_reference_forward", "qwen_prefill_layer0_reference_forward_with_cache"]
     for n in names:
         getattr(lib, n).restype = i
     return lib
