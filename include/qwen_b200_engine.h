@@ -49,6 +49,11 @@ int qwen_engine_decode(qwen_engine* e, const int32_t* slots, const int32_t* toke
  * ([t][kv_head][128] fp32). write_kv also sets the slot length to n_tokens when layer == 27. */
 int qwen_engine_write_kv(qwen_engine* e, int slot, int layer, const float* k, const float* v, int n_tokens);
 int qwen_engine_read_kv(qwen_engine* e, int slot, int layer, float* k, float* v, int n_tokens);
+/* The same rows in the Hugging Face cache layout the reference caller hands to and takes from its layers
+ * (verification/real_host_top_backend.py:199-206): head-major [kv_head 2][t][128] fp32 for K and for V.
+ * write_kv_hf also sets the slot length to n_tokens when layer == 27. */
+int qwen_engine_read_kv_hf(qwen_engine* e, int slot, int layer, float* k, float* v, int n_tokens);
+int qwen_engine_write_kv_hf(qwen_engine* e, int slot, int layer, const float* k, const float* v, int n_tokens);
 int qwen_engine_set_seq_len(qwen_engine* e, int slot, int len);
 int qwen_engine_seq_len(qwen_engine* e, int slot);
 int qwen_engine_reset(qwen_engine* e, int slot);

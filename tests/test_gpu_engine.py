@@ -352,3 +352,38 @@ def test_tensor_core_lm_head_matches_cuda_core_head(host):
         assert host.kernel_error(reset=True) == 0
     finally:
         eng.close()
+
+
+def test_hf_cache_export_and_import(host):
+    """The engine's KV rows in the Hugging Face per-layer layout the reference caller converts to and from
+    (verification/real_host_top_backend.py:199-206): read_kv_hf is the head-major transpose of read_kv,
+    write_kv_hf stores what read_kv_hf returns, and EngineBackend.hf_cache gives 28 (k, v) pairs of
+    [1][2][seq][128]."""
+    prompt = [int(t) for t in np.random.default_rng(8).integers(0, qo.VOCAB, 70)]
+    eng = host.Engine(0, 8, max_seqs=2, max_len=128)
+    try:
+        eng.init_synthetic(6)
+        be = host.EngineBackend(eng, slot=0)
+        res = be.prefill(prompt)
+        be.decode_step([int(np.argmax(res.logits[0]))], res.cache)
+        n = eng.seq_len(0)
+        assert n == 71
+        cache = be.hf_cache(res.cache)
+        assert len(cache) == qo.LAYERS and cache[0][0].shape == (1, 2, n, 128)
+        for layer in (0, 13, 27):
+            k, v = eng.read_kv(0, layer, n)
+            assert np.array_equal(cache[layer][0][0], k.reshape(n, 2, 128).transpose(1, 0, 2))
+            assert np.array_equal(cache[layer][1][0], v.reshape(n, 2, 128).transpose(1, 0, 2))
+        # import into the other slot, every layer, then read back token-major
+        for layer in range(qo.LAYERS):
+            eng.write_kv_hf(1, layer, cache[layer][0], cache[layer][1])
+        assert eng.seq_len(1) == n
+        for layer in (0, 27):
+            k0, v0 = eng.read_kv(0, layer, n)
+            k1, v1 = eng.read_kv(1, layer, n)
+            assert np.array_equal(k0, k1) and np.array_equal(v0, v1)
+        # both slots continue identically from the same cache
+        t = int(np.argmax(eng.read_logits(1)[0]))
+        assert int(eng.decode([0], [t])[0]) == int(eng.decode([1], [t])[0])
+    finally:
+        eng.close()

@@ -62,6 +62,25 @@ __global__ void kv_scatter_kernel(const float* __restrict__ kf, const float* __r
   }
 }
 
+// Paged rows of one layer of a slot <-> the Hugging Face cache layout [kv_head][token][128] (head-major), the
+// layout the reference caller converts to and from (verification/real_host_top_backend.py:199-206).
+__global__ void kv_hf_kernel(KvView kv, int slot, int n, float* __restrict__ kh, float* __restrict__ vh, int to_pages) {
+  const int t = blockIdx.x;
+  if (t >= n) return;
+  float* kr = kv_row(kv, slot, t, 0);
+  float* vr = kv_row(kv, slot, t, 1);
+  for (int i = threadIdx.x; i < kKvWidth; i += blockDim.x) {
+    const size_t o = ((size_t)(i >> 7) * n + t) * kHeadDim + (i & 127);
+    if (to_pages) {
+      kr[i] = kh[o];
+      vr[i] = vh[o];
+    } else {
+      kh[o] = kr[i];
+      vh[o] = vr[i];
+    }
+  }
+}
+
 __global__ void advance_pos_kernel(int* __restrict__ pos, int n) {
   griddep_wait();
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
@@ -1269,6 +1288,37 @@ int qwen_engine_read_kv(qwen_engine* e, int slot, int layer, float* k, float* v,
   E_TRY(cudaMemcpyAsync(k, e->p_k, (size_t)n_tokens * kKvWidth * 4, cudaMemcpyDefault, e->stream));
   E_TRY(cudaMemcpyAsync(v, e->p_v, (size_t)n_tokens * kKvWidth * 4, cudaMemcpyDefault, e->stream));
   E_TRY(cudaStreamSynchronize(e->stream));
+  return 0;
+}
+
+int qwen_engine_read_kv_hf(qwen_engine* e, int slot, int layer, float* k, float* v, int n_tokens) {
+  if (!e || slot < 0 || slot >= e->max_seqs || layer < 0 || layer >= kLayers || !k || !v || n_tokens <= 0 ||
+      n_tokens > e->seq_len[slot])
+    return kStatusInvalid;
+  E_TRY(cudaSetDevice(e->device));
+  if (int st = ensure_prefill_buffers(e, n_tokens)) return st;
+  kv_hf_kernel<<<n_tokens, 256, 0, e->stream>>>(paged_view(e, layer), slot, n_tokens, e->p_k, e->p_v, 0);
+  E_TRY(cudaGetLastError());
+  E_TRY(cudaMemcpyAsync(k, e->p_k, (size_t)n_tokens * kKvWidth * 4, cudaMemcpyDefault, e->stream));
+  E_TRY(cudaMemcpyAsync(v, e->p_v, (size_t)n_tokens * kKvWidth * 4, cudaMemcpyDefault, e->stream));
+  E_TRY(cudaStreamSynchronize(e->stream));
+  return 0;
+}
+
+int qwen_engine_write_kv_hf(qwen_engine* e, int slot, int layer, const float* k, const float* v, int n_tokens) {
+  if (!e || slot < 0 || slot >= e->max_seqs || layer < 0 || layer >= kLayers || !k || !v || n_tokens <= 0 ||
+      n_tokens > e->max_len)
+    return kStatusInvalid;
+  E_TRY(cudaSetDevice(e->device));
+  if (int st = ensure_prefill_buffers(e, n_tokens)) return st;
+  if (int st = ensure_pages(e, slot, n_tokens)) return st;
+  E_TRY(cudaMemcpyAsync(e->p_k, k, (size_t)n_tokens * kKvWidth * 4, cudaMemcpyDefault, e->stream));
+  E_TRY(cudaMemcpyAsync(e->p_v, v, (size_t)n_tokens * kKvWidth * 4, cudaMemcpyDefault, e->stream));
+  kv_hf_kernel<<<n_tokens, 256, 0, e->stream>>>(paged_view(e, layer), slot, n_tokens, e->p_k, e->p_v, 1);
+  E_TRY(cudaGetLastError());
+  E_TRY(cudaStreamSynchronize(e->stream));
+  if (layer == kLayers - 1) e->seq_len[slot] = n_tokens;
+  e->dev_slots.clear();
   return 0;
 }
 

@@ -175,6 +175,8 @@ def _configure_engine(lib: ctypes.CDLL) -> None:
     lib.qwen_engine_decode.argtypes = [vp, _I32, _I32, i, _I32]
     lib.qwen_engine_write_kv.argtypes = [vp, i, i, _F, _F, i]
     lib.qwen_engine_read_kv.argtypes = [vp, i, i, _F, _F, i]
+    lib.qwen_engine_read_kv_hf.argtypes = [vp, i, i, _F, _F, i]
+    lib.qwen_engine_write_kv_hf.argtypes = [vp, i, i, _F, _F, i]
     lib.qwen_engine_set_seq_len.argtypes = [vp, i, i]
     lib.qwen_engine_seq_len.argtypes = [vp, i]
     lib.qwen_engine_reset.argtypes = [vp, i]
@@ -203,7 +205,7 @@ def _configure_engine(lib: ctypes.CDLL) -> None:
               "qwen_engine_kernels_per_decode_step", "qwen_engine_decode_device", "qwen_engine_read_layer",
               "qwen_engine_profile_kernels", "qwen_engine_read_trace", "qwen_engine_profile_decode",
               "qwen_engine_profile_batched", "qwen_engine_nccl_unique_id", "qwen_engine_nccl_init",
-              "qwen_engine_gather_tokens"):
+              "qwen_engine_gather_tokens", "qwen_engine_read_kv_hf", "qwen_engine_write_kv_hf"):
         getattr(lib, n).restype = i
 
 
@@ -282,6 +284,18 @@ class Engine:
         v = np.zeros(n_tokens * KV_WIDTH, np.float32)
         _check(self.lib.qwen_engine_read_kv(self.handle, slot, layer, k, v, n_tokens), "read_kv")
         return k, v
+
+    def read_kv_hf(self, slot: int, layer: int, n_tokens: int) -> tuple[np.ndarray, np.ndarray]:
+        """K and V of one layer in the Hugging Face cache layout [2 kv heads][n_tokens][128] (head-major)."""
+        k = np.zeros(KV_WIDTH * n_tokens, np.float32)
+        v = np.zeros(KV_WIDTH * n_tokens, np.float32)
+        _check(self.lib.qwen_engine_read_kv_hf(self.handle, slot, layer, k, v, n_tokens), "read_kv_hf")
+        return k.reshape(2, n_tokens, 128), v.reshape(2, n_tokens, 128)
+
+    def write_kv_hf(self, slot: int, layer: int, k: np.ndarray, v: np.ndarray) -> None:
+        k = np.ascontiguousarray(k, np.float32).reshape(-1)
+        v = np.ascontiguousarray(v, np.float32).reshape(-1)
+        _check(self.lib.qwen_engine_write_kv_hf(self.handle, slot, layer, k, v, k.size // KV_WIDTH), "write_kv_hf")
 
     def set_seq_len(self, slot: int, n: int) -> None:
         _check(self.lib.qwen_engine_set_seq_len(self.handle, slot, n), "set_seq_len")
@@ -385,8 +399,8 @@ class DecodeResult:
 class EngineBackend:
     """prefill / decode_step over the device-resident engine, shaped like the reference's
     RealHostTopBackend (verification/real_host_top_backend.py:208-351): input ids in, logits and a cache
-    handle out. The cache handle is the engine slot; KV stays in HBM (read it back with
-    `engine.read_kv`)."""
+    handle out. The cache handle is the engine slot; KV stays in HBM. `hf_cache` exports it in the Hugging
+    Face per-layer layout the reference returns ((k, v) per layer, each [1][2][seq][128])."""
 
     def __init__(self, engine: Engine, slot: int = 0):
         self.engine = engine
@@ -405,6 +419,15 @@ class EngineBackend:
         ids = np.asarray(input_ids, dtype=np.int64).reshape(-1)
         self.engine.decode([cache], ids[-1:].astype(np.int32))
         return DecodeResult(logits=self.engine.read_logits(1), cache=cache)
+
+    def hf_cache(self, cache) -> tuple:
+        """The slot's KV cache as the reference's cache tuple: 28 x (k, v), each float32 [1][2][seq][128]."""
+        n = self.engine.seq_len(cache)
+        layers = []
+        for layer in range(LAYERS):
+            k, v = self.engine.read_kv_hf(cache, layer, n)
+            layers.append((k[None], v[None]))
+        return tuple(layers)
 
 
 def decode_attention(q_ptr: int, k_ptr: int, v_ptr: int, seq_len: int, ctx_ptr: int, stream: int = 0) -> None:
