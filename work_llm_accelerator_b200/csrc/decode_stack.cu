@@ -15,9 +15,10 @@
 // the ring keeps filling (9 x 16 KB per SM, 21 MB over the GPU), so HBM stays busy across step
 // boundaries and layer boundaries.
 //
-// Roles (192 threads):
+// Roles (224 threads):
 //   warp 0      producer: cp.async.bulk of pre-swizzled 16 KB weight units into the ring
-//   warp 1      TMEM owner (32 columns = two 16-column accumulators) and MMA issuer (one lane)
+//   warps 1, 6  MMA issuers (one lane each), alternate 16 KB units of an item into their own accumulators;
+//               warp 1 also owns the TMEM allocation (64 columns: two items in flight x two 16-column parts)
 //   warps 2-5   workers: wait for a step's inputs (global completion counters), build the activation
 //               digits for the CTA's K blocks, read accumulators from TMEM, split-K reduction with
 //               integer atomics (exact, order-free), the step's epilogue; attention chunks

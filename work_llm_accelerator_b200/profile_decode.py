@@ -13,7 +13,10 @@
         prefills `batch` sequences, then times device-resident greedy decode steps of all of them
         together (the batched W8 path) and prints tokens/s.
 
-Both hold about 2.2 GB (W8) of weights on the device plus a 1024-position KV pool.
+The modes hold about 2.2 GB (W8) of weights on the device plus the KV pool of their sequences.
+--profile-range brackets the timed part with cudaProfilerStart/Stop, so that
+`ncu --profile-from-start off ...` captures only those launches (not the weight synthesis or the history
+prefills before them).
 """
 from __future__ import annotations
 
@@ -38,7 +41,15 @@ def main(argv=None) -> int:
     ap.add_argument("--graphs", type=int, default=1, help="steps: 1 = CUDA graphs, 0 = eager launches")
     ap.add_argument("--option", action="append", default=[], metavar="NAME=VALUE",
                     help="engine option (e.g. qgemm=0, prefetch=0, pdl=0)")
+    ap.add_argument("--profile-range", action="store_true",
+                    help="bracket the timed part with cudaProfilerStart/Stop (ncu --profile-from-start off)")
     a = ap.parse_args(argv)
+
+    def profiler(on: bool) -> None:
+        if a.profile_range:
+            import torch
+
+            (torch.cuda.cudart().cudaProfilerStart if on else torch.cuda.cudart().cudaProfilerStop)()
 
     max_seqs = a.batch if a.mode == "batched" else 1
     eng = host.Engine(0, a.wbits, max_seqs=max_seqs, max_len=max(1024, a.prompt + 2 * a.steps + 16))
@@ -54,6 +65,7 @@ def main(argv=None) -> int:
             stream = torch.cuda.ExternalStream(eng.stream())
             eng.prefill(0, prompt)  # warm-up (allocations, first launches)
             times = []
+            profiler(True)
             for _ in range(a.steps):
                 eng.reset(0)
                 e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -62,6 +74,7 @@ def main(argv=None) -> int:
                 e1.record(stream)
                 e1.synchronize()
                 times.append(e0.elapsed_time(e1))
+            profiler(False)
             ms = min(times)
             print(json.dumps({"prompt": a.prompt, "ms": ms, "tok_per_s": a.prompt / (ms * 1e-3)}))
         elif a.mode == "batched":
@@ -69,7 +82,9 @@ def main(argv=None) -> int:
             first = []
             for i in range(a.batch):
                 first.append(eng.prefill(i, rng.integers(0, 151936, a.prompt).astype(np.int32)))
+            profiler(True)
             ms = eng.bench_decode(list(range(a.batch)), first, a.steps, 2)
+            profiler(False)
             cats = eng.profile_batched(list(range(a.batch)), first, 2)
             print(json.dumps({"batch": a.batch, "history": a.prompt, "ms_per_step": ms,
                               "tok_per_s": a.batch / (ms * 1e-3), "ms_by_group": cats}))
@@ -80,7 +95,9 @@ def main(argv=None) -> int:
             eng.set_option("graphs", a.graphs)
             prompt = np.random.default_rng(1).integers(0, 151936, a.prompt).astype(np.int32)
             tok = eng.prefill(0, prompt)
+            profiler(True)
             ms = eng.bench_decode([0], [tok], a.steps, 1)
+            profiler(False)
             print(json.dumps({"ms_per_step": ms}))
     finally:
         eng.close()
