@@ -41,6 +41,11 @@ int qwen_engine_load_embedding(qwen_engine* e, const uint16_t* embed_f16, const 
 
 /* Prefill `n` tokens into sequence slot `slot` (which must be empty); writes the greedy next token. */
 int qwen_engine_prefill(qwen_engine* e, int slot, const int32_t* tokens, int n, int32_t* next_token);
+/* Chunked prefill: `n` more prompt tokens into `slot` after the tokens it already holds (an empty slot: the same
+ * as qwen_engine_prefill). The chunk's tokens take the following positions and attend to the cached rows and to
+ * each other causally; the result equals prefilling the whole prompt at once (the reference only prefills from
+ * position 0, hls/prefill_only/qwen_prefill_attention_kernel.cpp:2232-2367). Writes the greedy next token. */
+int qwen_engine_prefill_chunk(qwen_engine* e, int slot, const int32_t* tokens, int n, int32_t* next_token);
 /* One greedy decode step for `n` sequences: tokens[i] is appended to slots[i]; next_tokens[i] receives
  * the argmax. Host buffers; the call returns after the next tokens are on the host. */
 int qwen_engine_decode(qwen_engine* e, const int32_t* slots, const int32_t* tokens, int n, int32_t* next_tokens);

@@ -511,8 +511,10 @@ struct PrefillSmem {
   float den[kPairs];
 };
 
+// Queries q0 + qi (local rows of q and ctx) sit at positions qoff + q0 + qi and see keys 0 .. that position
+// (qoff > 0: a prefill chunk after qoff cached tokens; kc / vc then hold qoff + S rows).
 __global__ void __launch_bounds__(256) prefill_attn_kernel(const float* __restrict__ q, const float* __restrict__ kc,
-                                                           const float* __restrict__ vc, int S,
+                                                           const float* __restrict__ vc, int S, int qoff,
                                                            float* __restrict__ ctx, const int* only_if) {
   griddep_wait();  // inputs come from the preceding kernel (programmatic dependent launch)
   griddep_launch();
@@ -533,7 +535,7 @@ __global__ void __launch_bounds__(256) prefill_attn_kernel(const float* __restri
     sm.mx[tid] = -1.0e30f;
     sm.den[tid] = 0.0f;
   }
-  const int kend = q0 + nq;  // keys [0, kend)
+  const int kend = qoff + q0 + nq;  // keys [0, kend)
   const int ntiles = (kend + kPK - 1) / kPK;
 
   // pass 1: causal max of the scaled scores
@@ -551,7 +553,7 @@ __global__ void __launch_bounds__(256) prefill_attn_kernel(const float* __restri
       float s = 0.0f;
       for (int d = 0; d < kHeadDim; ++d) s = __fadd_rn(s, __fmul_rn(sm.qs[p][d], sm.ks[lane][d]));
       const float ss = __fmul_rn(s, kAttentionScaling);
-      float m = (qi < nq && key <= q0 + qi) ? ss : -INFINITY;
+      float m = (qi < nq && key <= qoff + q0 + qi) ? ss : -INFINITY;
 #pragma unroll
       for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
       if (lane == 0) sm.mx[p] = m > sm.mx[p] ? m : sm.mx[p];
@@ -581,7 +583,7 @@ __global__ void __launch_bounds__(256) prefill_attn_kernel(const float* __restri
       float s = 0.0f;
       for (int dd = 0; dd < kHeadDim; ++dd) s = __fadd_rn(s, __fmul_rn(sm.qs[p][dd], sm.ks[lane][dd]));
       const float ss = __fmul_rn(s, kAttentionScaling);
-      const bool valid = qi < nq && key <= q0 + qi;
+      const bool valid = qi < nq && key <= qoff + q0 + qi;
       const float e = valid ? approx_exp(__fsub_rn(ss, sm.mx[p])) : 0.0f;
       sm.es[p][lane] = e;
       float l = e;
@@ -727,21 +729,19 @@ unsigned decode_attn_kernel_error(bool reset) {
 }
 
 cudaError_t launch_prefill_attention(const float* q, const float* k_cache, const float* v_cache, int S, float* ctx,
-                                     cudaStream_t s) {
+                                     cudaStream_t s, int qoff) {
   const size_t smem = sizeof(PrefillSmem);
-  cudaError_t e = cudaFuncSetAttribute(prefill_attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-  if (e != cudaSuccess) return e;
+  if (cudaError_t e = ensure_smem_attr((const void*)prefill_attn_kernel, smem)) return e;
   return launch_k(prefill_attn_kernel, dim3((S + kPQ - 1) / kPQ, kKvHeads), dim3(256), smem, s, true, q, k_cache,
-                  v_cache, S, ctx, static_cast<const int*>(nullptr));
+                  v_cache, S, qoff, ctx, static_cast<const int*>(nullptr));
 }
 
 cudaError_t launch_prefill_attention_gated(const float* q, const float* k_cache, const float* v_cache, int S,
-                                           float* ctx, const int* only_if, cudaStream_t s) {
+                                           float* ctx, const int* only_if, cudaStream_t s, int qoff) {
   const size_t smem = sizeof(PrefillSmem);
-  cudaError_t e = cudaFuncSetAttribute(prefill_attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-  if (e != cudaSuccess) return e;
+  if (cudaError_t e = ensure_smem_attr((const void*)prefill_attn_kernel, smem)) return e;
   return launch_k(prefill_attn_kernel, dim3((S + kPQ - 1) / kPQ, kKvHeads), dim3(256), smem, s, true, q, k_cache,
-                  v_cache, S, ctx, only_if);
+                  v_cache, S, qoff, ctx, only_if);
 }
 
 }  // namespace qb

@@ -78,10 +78,11 @@ __device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, i
 }
 
 // fp32 -> (hi, lo) fp16 planes. Blocks [0, nvt): V tiles of 64 tokens x 64 features, transposed into
-// vt [2][256][Spad]; the rest: Q [S][1536] -> qp [2][S][1536] and K [S][256] -> kp [2][S][256], four
-// values per thread. A value the split cannot hold (|x| >= 32768, inf, nan) sets *flag.
+// vt [2][256][Spad]; the rest: Q [Sq][1536] -> qp [2][Sq][1536] and K [S][256] -> kp [2][S][256], four
+// values per thread (Sq = S, or the Sq queries of a prefill chunk after S - Sq cached keys). A value the
+// split cannot hold (|x| >= 32768, inf, nan) sets *flag.
 __global__ void __launch_bounds__(256) attn_split_kernel(const float* __restrict__ q, const float* __restrict__ k,
-                                                         const float* __restrict__ v, int S, int Spad, int nvt,
+                                                         const float* __restrict__ v, int Sq, int S, int Spad, int nvt,
                                                          __half* __restrict__ qp, __half* __restrict__ kp,
                                                          __half* __restrict__ vt, int* __restrict__ flag) {
   griddep_wait();  // inputs come from the preceding kernel (programmatic dependent launch)
@@ -107,7 +108,7 @@ __global__ void __launch_bounds__(256) attn_split_kernel(const float* __restrict
       vt[(size_t)kKvWidth * Spad + o] = l;
     }
   } else {
-    const size_t nq4 = (size_t)S * kHidden / 4, nk4 = (size_t)S * kKvWidth / 4;
+    const size_t nq4 = (size_t)Sq * kHidden / 4, nk4 = (size_t)S * kKvWidth / 4;
     const size_t stride = (size_t)(gridDim.x - nvt) * blockDim.x;
     for (size_t i = (size_t)(blockIdx.x - nvt) * blockDim.x + threadIdx.x; i < nq4 + nk4; i += stride) {
       const bool isq = i < nq4;
@@ -122,7 +123,7 @@ __global__ void __launch_bounds__(256) attn_split_kernel(const float* __restrict
         ls[e] = __float2half_rn(__fsub_rn(xs[e], __half2float(hs[e])));
       }
       __half* dst = isq ? qp : kp;
-      const size_t plane = isq ? (size_t)S * kHidden : (size_t)S * kKvWidth;
+      const size_t plane = isq ? (size_t)Sq * kHidden : (size_t)S * kKvWidth;
       uint2 hv, lv;
       hv.x = (uint32_t)__half_as_ushort(hs[0]) | ((uint32_t)__half_as_ushort(hs[1]) << 16);
       hv.y = (uint32_t)__half_as_ushort(hs[2]) | ((uint32_t)__half_as_ushort(hs[3]) << 16);
@@ -177,7 +178,8 @@ __device__ __forceinline__ uint32_t half2_bits(float a, float b) {
 
 __global__ void __launch_bounds__(kThreadsA, 1)
     attn_tc_kernel(const __half* __restrict__ qp, const __grid_constant__ CUtensorMap kmap,
-                   const __grid_constant__ CUtensorMap vmap, int S, const int* flag, float* __restrict__ ctx) {
+                   const __grid_constant__ CUtensorMap vmap, int Sq, int qoff, const int* flag,
+                   float* __restrict__ ctx) {
   griddep_wait();  // inputs come from the preceding kernel (programmatic dependent launch)
   griddep_launch();
   if (*reinterpret_cast<const volatile int*>(flag) != 0) return;  // values outside the split: CUDA-core kernel
@@ -187,8 +189,9 @@ __global__ void __launch_bounds__(kThreadsA, 1)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int qt = gridDim.x - 1 - blockIdx.x;  // heaviest query tiles first
   const int h = blockIdx.y, g = h / kGroups;
-  const int q0 = qt * kBQ;
-  const int T = (min(q0 + kBQ, S) + kBK - 1) / kBK;  // key tiles of the causal prefix
+  const int q0 = qt * kBQ;  // local query rows q0 .. q0 + 127 sit at positions qoff + q0 ..
+  const int S = qoff + Sq;  // keys
+  const int T = (min(qoff + q0 + kBQ, S) + kBK - 1) / kBK;  // key tiles of the causal prefix
   const int G = 2 * T;                                // pass 1 tiles, then pass 2 tiles
 
   if (threadIdx.x == 0) {
@@ -313,7 +316,8 @@ __global__ void __launch_bounds__(kThreadsA, 1)
     const int quarter = warp & 3;      // the TMEM lanes this warp may access
     const int kg = (warp - 2) >> 2;    // key group of each tile
     const int r = quarter * 32 + lane;
-    const int qrow = q0 + r;
+    const int qrow = q0 + r;       // local query row (row of qp and ctx)
+    const int qpos = qoff + qrow;  // its position: keys 0 .. qpos are visible
     const uint32_t lane_addr = tmem + ((uint32_t)(quarter * 32) << 16);
     // per-row exchange between the key groups, in the weight tile's space while no weight tile is live
     float* xch = reinterpret_cast<float*>(tiles + kOffP);
@@ -323,10 +327,10 @@ __global__ void __launch_bounds__(kThreadsA, 1)
       uint32_t qv[16];
 #pragma unroll
       for (int pl = 0; pl < 2; ++pl) {
-        const uint4* src = reinterpret_cast<const uint4*>(qp + ((size_t)pl * S + qrow) * kHidden + h * kHeadDim + 32 * kg);
+        const uint4* src = reinterpret_cast<const uint4*>(qp + ((size_t)pl * Sq + qrow) * kHidden + h * kHeadDim + 32 * kg);
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
-          const uint4 u = qrow < S ? src[i] : make_uint4(0u, 0u, 0u, 0u);
+          const uint4 u = qrow < Sq ? src[i] : make_uint4(0u, 0u, 0u, 0u);
           qv[4 * i] = u.x;
           qv[4 * i + 1] = u.y;
           qv[4 * i + 2] = u.z;
@@ -352,7 +356,7 @@ __global__ void __launch_bounds__(kThreadsA, 1)
 #pragma unroll
       for (int i = 0; i < kKeysPer; ++i) {
         const float ss = __fmul_rn(__uint_as_float(v[i]), kAttentionScaling);
-        if (kb + i <= qrow && ss > m) m = ss;
+        if (kb + i <= qpos && ss > m) m = ss;
       }
     }
     xch[kg * kBQ + r] = m;
@@ -388,8 +392,8 @@ __global__ void __launch_bounds__(kThreadsA, 1)
         const F2 a = add2(mul2(f2(__uint_as_float(v[i]), __uint_as_float(v[i + 1])), sc2, nz), m2);
         float x0, x1;
         approx_exp_fast2(f2_lo(a), f2_hi(a), x0, x1, nz);
-        e[i] = select_f32(kb + i <= qrow, x0, 0.0f);
-        e[i + 1] = select_f32(kb + i + 1 <= qrow, x1, 0.0f);
+        e[i] = select_f32(kb + i <= qpos, x0, 0.0f);
+        e[i + 1] = select_f32(kb + i + 1 <= qpos, x1, 0.0f);
         den2 = add2(den2, f2(e[i], e[i + 1]));  // even and odd keys in two running sums
       }
 #pragma unroll
@@ -427,7 +431,7 @@ __global__ void __launch_bounds__(kThreadsA, 1)
     constexpr int kCols = kHeadDim / kKeyGroups;  // context columns of this thread
     uint32_t o[kCols];
     if (ok) tmem_ld_cols<kCols>(lane_addr + kCols * kg, o);
-    if (ok && qrow < S) {
+    if (ok && qrow < Sq) {
       float4* dst = reinterpret_cast<float4*>(ctx + (size_t)qrow * kHidden + h * kHeadDim + kCols * kg);
 #pragma unroll
       for (int i = 0; i < kCols / 4; ++i)
@@ -477,14 +481,17 @@ int pad64(int S) { return (S + 63) / 64 * 64; }
 
 }  // namespace
 
-size_t prefill_attn_tc_scratch_bytes(int S) {
-  return 256 + round256((size_t)2 * S * kHidden * 2) + round256((size_t)2 * S * kKvWidth * 2) +
+size_t prefill_attn_tc_scratch_bytes(int S) { return prefill_attn_tc_scratch_bytes(S, S); }
+
+size_t prefill_attn_tc_scratch_bytes(int Sq, int S) {
+  return 256 + round256((size_t)2 * Sq * kHidden * 2) + round256((size_t)2 * S * kKvWidth * 2) +
          round256((size_t)2 * kKvWidth * pad64(S) * 2);
 }
 
-cudaError_t launch_prefill_attention_tc(const float* q, const float* k_cache, const float* v_cache, int S, float* ctx,
-                                        void* scratch, size_t scratch_bytes, cudaStream_t s) {
-  if (S < 1 || !scratch || scratch_bytes < prefill_attn_tc_scratch_bytes(S) ||
+cudaError_t launch_prefill_attention_tc(const float* q, const float* k_cache, const float* v_cache, int Sq, float* ctx,
+                                        void* scratch, size_t scratch_bytes, cudaStream_t s, int qoff) {
+  const int S = qoff + Sq;  // keys
+  if (Sq < 1 || qoff < 0 || !scratch || scratch_bytes < prefill_attn_tc_scratch_bytes(Sq, S) ||
       (reinterpret_cast<uintptr_t>(scratch) & 255) || (reinterpret_cast<uintptr_t>(q) & 15) ||
       (reinterpret_cast<uintptr_t>(k_cache) & 15))
     return cudaErrorInvalidValue;
@@ -492,7 +499,7 @@ cudaError_t launch_prefill_attention_tc(const float* q, const float* k_cache, co
   uint8_t* base = static_cast<uint8_t*>(scratch);
   int* flag = reinterpret_cast<int*>(base);
   __half* qp = reinterpret_cast<__half*>(base + 256);
-  __half* kp = reinterpret_cast<__half*>(base + 256 + round256((size_t)2 * S * kHidden * 2));
+  __half* kp = reinterpret_cast<__half*>(base + 256 + round256((size_t)2 * Sq * kHidden * 2));
   __half* vt = reinterpret_cast<__half*>(reinterpret_cast<uint8_t*>(kp) + round256((size_t)2 * S * kKvWidth * 2));
   CUtensorMap kmap, vmap;
   if (!make_map3(&kmap, kp, kKvWidth, (uint64_t)S, kKvWidth * 2, (uint64_t)S * kKvWidth * 2, 64, kBK) ||
@@ -501,29 +508,18 @@ cudaError_t launch_prefill_attention_tc(const float* q, const float* k_cache, co
   cudaError_t e = cudaMemsetAsync(flag, 0, sizeof(int), s);
   if (e != cudaSuccess) return e;
   const int nvt = (Spad / 64) * 4;
-  const size_t elems4 = ((size_t)S * (kHidden + kKvWidth)) / 4;
+  const size_t elems4 = ((size_t)Sq * kHidden + (size_t)S * kKvWidth) / 4;
   const int nqk = (int)std::min<size_t>((elems4 + 255) / 256, 148 * 8);
-  if ((e = launch_k(attn_split_kernel, dim3(nvt + nqk), dim3(256), 0, s, true, q, k_cache, v_cache, S, Spad, nvt, qp,
-                    kp, vt, flag)) != cudaSuccess)
+  if ((e = launch_k(attn_split_kernel, dim3(nvt + nqk), dim3(256), 0, s, true, q, k_cache, v_cache, Sq, S, Spad, nvt,
+                    qp, kp, vt, flag)) != cudaSuccess)
     return e;
-  static std::mutex mu;
-  static unsigned long long attr_set = 0;
-  int dev = 0;
-  if ((e = cudaGetDevice(&dev)) != cudaSuccess) return e;
-  {
-    std::lock_guard<std::mutex> lock(mu);
-    if (dev < 64 && !((attr_set >> dev) & 1ull)) {
-      if ((e = cudaFuncSetAttribute(attn_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemA)) !=
-          cudaSuccess)
-        return e;
-      attr_set |= 1ull << dev;
-    }
-  }
-  if ((e = launch_k(attn_tc_kernel, dim3((S + kBQ - 1) / kBQ, kHeads), dim3(kThreadsA), kSmemA, s, true,
-                    static_cast<const __half*>(qp), kmap, vmap, S, static_cast<const int*>(flag), ctx)) != cudaSuccess)
+  if ((e = ensure_smem_attr((const void*)attn_tc_kernel, kSmemA)) != cudaSuccess) return e;
+  if ((e = launch_k(attn_tc_kernel, dim3((Sq + kBQ - 1) / kBQ, kHeads), dim3(kThreadsA), kSmemA, s, true,
+                    static_cast<const __half*>(qp), kmap, vmap, Sq, qoff, static_cast<const int*>(flag), ctx)) !=
+      cudaSuccess)
     return e;
   // values outside the fp16 split: the CUDA-core kernel computes the context (it returns at once otherwise)
-  return launch_prefill_attention_gated(q, k_cache, v_cache, S, ctx, flag, s);
+  return launch_prefill_attention_gated(q, k_cache, v_cache, Sq, ctx, flag, s, qoff);
 }
 
 unsigned attn_tc_kernel_error(bool reset) {

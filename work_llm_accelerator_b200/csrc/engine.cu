@@ -42,15 +42,15 @@ __global__ void embed_gather_kernel(const uint16_t* __restrict__ embed, const in
   for (int d = threadIdx.x; d < kHidden; d += blockDim.x) x[(size_t)t * kHidden + d] = __half2float(row[d]);
 }
 
-// flat [n][256] K and V of one layer <-> paged rows of one slot
+// flat [n][256] K and V of one layer <-> paged rows pos0 .. pos0 + n - 1 of one slot
 __global__ void kv_scatter_kernel(const float* __restrict__ kf, const float* __restrict__ vf, int n, KvView kv,
-                                  int slot, int to_pages) {
+                                  int slot, int to_pages, int pos0) {
   griddep_wait();  // inputs come from the preceding kernel (programmatic dependent launch)
   griddep_launch();
   const int t = blockIdx.x;
   if (t >= n) return;
-  float* kd = kv_row(kv, slot, t, 0);
-  float* vd = kv_row(kv, slot, t, 1);
+  float* kd = kv_row(kv, slot, pos0 + t, 0);
+  float* vd = kv_row(kv, slot, pos0 + t, 1);
   for (int d = threadIdx.x; d < kKvWidth; d += blockDim.x) {
     if (to_pages) {
       kd[d] = kf[(size_t)t * kKvWidth + d];
@@ -424,9 +424,19 @@ int enqueue_decode_exact(qwen_engine* e, int nt, bool advance) {
   return 0;
 }
 
+// A prefill chunk after `past` cached tokens: the slot's K/V rows [0, past) of layer l into the flat rows
+// [0, past) that the chunk's attention reads (its own rows follow at [past, past + n)).
+int gather_history(qwen_engine* e, int slot, int l, int past, bool pdl) {
+  if (past <= 0) return 0;
+  E_TRY(launch_k(kv_scatter_kernel, dim3(past), dim3(256), 0, e->stream, pdl, static_cast<const float*>(e->p_k),
+                 static_cast<const float*>(e->p_v), past, paged_view(e, l), slot, 0, 0));
+  return 0;
+}
+
 // Prefill in the reference's arithmetic (qwen_prefill_attention_kernel.cpp:2232-2367,
-// qwen_prefill_mlp_kernel.cpp:264-337): K/V of every token first, then each query's causal context.
-int enqueue_prefill_exact(qwen_engine* e, int slot, int n) {
+// qwen_prefill_mlp_kernel.cpp:264-337): K/V of every token first, then each query's causal context. With
+// past > 0 the n tokens continue a slot that holds `past` tokens (positions past .. past + n - 1).
+int enqueue_prefill_exact(qwen_engine* e, int slot, int n, int past) {
   cudaStream_t s = e->stream;
   const int wb = e->wbits;
   embed_gather_kernel<<<n, 256, 0, s>>>(e->embed, e->p_tokens, n, e->p_x);
@@ -440,12 +450,14 @@ int enqueue_prefill_exact(qwen_engine* e, int slot, int n) {
     E_TRY(launch_prefill_rmsnorm(e->p_x, L.input_ln, n, e->p_xn, s));
     E_TRY(exact::launch_project(wb, e->p_xn, n, kHidden, L.qkv_w, L.qkv_b, L.qkv_s, kQkvRows, e->ex_qkv, nullptr,
                                 false, s));
-    E_TRY(exact::launch_rope_store(e->ex_qkv, n, nullptr, 0, e->rope_pre_cos, e->rope_pre_sin, e->p_q, flat, nullptr,
-                                   0, s));
-    E_TRY(exact::launch_attention_pre(e->p_q, e->p_k, e->p_v, n, e->p_ctx, s));
+    if (int st = gather_history(e, slot, l, past, false)) return st;
+    E_TRY(exact::launch_rope_store(e->ex_qkv, n, nullptr, past, e->rope_pre_cos, e->rope_pre_sin, e->p_q, flat,
+                                   nullptr, 0, s));
+    E_TRY(exact::launch_attention_pre(e->p_q, e->p_k, e->p_v, n, e->p_ctx, s, past));
     E_TRY(exact::launch_project(wb, e->p_ctx, n, kHidden, L.o_w, nullptr, L.o_s, kHidden, e->p_a, nullptr, false, s));
-    E_TRY(launch_k(kv_scatter_kernel, dim3(n), dim3(256), 0, s, false, static_cast<const float*>(e->p_k),
-                   static_cast<const float*>(e->p_v), n, paged_view(e, l), slot, 1));
+    E_TRY(launch_k(kv_scatter_kernel, dim3(n), dim3(256), 0, s, false,
+                   static_cast<const float*>(e->p_k + (size_t)past * kKvWidth),
+                   static_cast<const float*>(e->p_v + (size_t)past * kKvWidth), n, paged_view(e, l), slot, 1, past));
     E_TRY(launch_prefill_rmsnorm(e->p_a, L.post_ln, n, e->p_xn, s));
     E_TRY(exact::launch_project(wb, e->p_xn, n, kHidden, L.gu_w, nullptr, L.gu_s, 2 * kInter, e->ex_gu, nullptr,
                                 false, s));
@@ -701,10 +713,16 @@ int run_decode_step(qwen_engine* e, int nt, int max_len, bool advance) {
 }
 
 // The device work of one prefill (tokens already in p_tokens): embedding gather, 28 layers, LM head of the
-// last token into d_next.
-int enqueue_prefill(qwen_engine* e, int slot, int n) {
-  if (e->exact) return enqueue_prefill_exact(e, slot, n);
+// last token into d_next. past > 0: a chunk continuing a slot that holds `past` tokens (chunked prefill):
+// the chunk's rows take positions past .. past + n - 1 (RoPE rows and flat K/V rows offset by past), the
+// slot's cached rows are gathered in front of them, and the attention runs with that query offset.
+int enqueue_prefill(qwen_engine* e, int slot, int n, int past) {
+  if (e->exact) return enqueue_prefill_exact(e, slot, n, past);
   cudaStream_t s = e->stream;
+  float* kf = e->p_k + (size_t)past * kKvWidth;  // this chunk's K / V rows in the flat buffers
+  float* vf = e->p_v + (size_t)past * kKvWidth;
+  const float* rc = e->rope_pre_cos + (size_t)past * 64;
+  const float* rs = e->rope_pre_sin + (size_t)past * 64;
   embed_gather_kernel<<<n, 256, 0, s>>>(e->embed, e->p_tokens, n, e->p_x);
   E_TRY(cudaGetLastError());
   const bool tc = e->wbits == 8;
@@ -714,15 +732,16 @@ int enqueue_prefill(qwen_engine* e, int slot, int n) {
     const LayerDev& L = e->layers[l];
     if (tc) {  // W8: projections on the int8 tensor cores
       E_TRY(tgemm_prefill_rmsnorm_digitize(e->p_x, L.input_ln, dp, s));
-      E_TRY(tgemm_qkv(L, dp, e->rope_pre_cos, e->rope_pre_sin, e->p_q, e->p_k, e->p_v, e->p_qkv, s));
+      E_TRY(tgemm_qkv(L, dp, rc, rs, e->p_q, kf, vf, e->p_qkv, s));
     } else {
       E_TRY(launch_prefill_rmsnorm(e->p_x, L.input_ln, n, e->p_xn, s));
-      E_TRY(launch_prefill_qkv(e->wbits, L, e->p_xn, n, e->rope_pre_cos, e->rope_pre_sin, e->p_q, e->p_k, e->p_v, s));
+      E_TRY(launch_prefill_qkv(e->wbits, L, e->p_xn, n, rc, rs, e->p_q, kf, vf, s));
     }
+    if (int st = gather_history(e, slot, l, past, true)) return st;
     if (e->use_attn_tc) {
-      E_TRY(launch_prefill_attention_tc(e->p_q, e->p_k, e->p_v, n, e->p_ctx, e->p_attn, e->p_attn_bytes, s));
+      E_TRY(launch_prefill_attention_tc(e->p_q, e->p_k, e->p_v, n, e->p_ctx, e->p_attn, e->p_attn_bytes, s, past));
     } else {
-      E_TRY(launch_prefill_attention(e->p_q, e->p_k, e->p_v, n, e->p_ctx, s));
+      E_TRY(launch_prefill_attention(e->p_q, e->p_k, e->p_v, n, e->p_ctx, s, past));
     }
     if (tc) {
       E_TRY(tgemm_digitize(e->p_ctx, dp, s));
@@ -730,8 +749,8 @@ int enqueue_prefill(qwen_engine* e, int slot, int n) {
     } else {
       E_TRY(launch_prefill_o(e->wbits, L, e->p_ctx, n, e->p_a, s));
     }
-    E_TRY(launch_k(kv_scatter_kernel, dim3(n), dim3(256), 0, s, true, static_cast<const float*>(e->p_k),
-                   static_cast<const float*>(e->p_v), n, paged_view(e, l), slot, 1));
+    E_TRY(launch_k(kv_scatter_kernel, dim3(n), dim3(256), 0, s, true, static_cast<const float*>(kf),
+                   static_cast<const float*>(vf), n, paged_view(e, l), slot, 1, past));
     if (tc) {
       E_TRY(tgemm_prefill_rmsnorm_digitize(e->p_a, L.post_ln, dp, s));
       E_TRY(tgemm_gateup(L, dp, e->p_h, s));
@@ -756,15 +775,15 @@ int enqueue_prefill(qwen_engine* e, int slot, int n) {
 
 // Prefill through a CUDA graph per (token count, slot) once one eager pass has run (kernel set-up outside
 // capture): the ~12 launches per layer of a short prompt otherwise cost host time comparable to the work.
-int run_prefill(qwen_engine* e, int slot, int n) {
-  if (!e->use_graphs || e->dump_hidden || e->keep_logits) return enqueue_prefill(e, slot, n);
-  const long long key = (2ll << 61) | ((long long)n << 20) | slot;
+int run_prefill(qwen_engine* e, int slot, int n, int past) {
+  if (!e->use_graphs || e->dump_hidden || e->keep_logits) return enqueue_prefill(e, slot, n, past);
+  const long long key = (2ll << 61) | ((long long)past << 36) | ((long long)n << 20) | slot;
   auto it = e->graphs.find(key);
   if (it == e->graphs.end()) {
-    if (int st = enqueue_prefill(e, slot, n)) return st;
+    if (int st = enqueue_prefill(e, slot, n, past)) return st;
     cudaGraph_t g;
     E_TRY(cudaStreamBeginCapture(e->stream, cudaStreamCaptureModeThreadLocal));
-    const int st = enqueue_prefill(e, slot, n);
+    const int st = enqueue_prefill(e, slot, n, past);
     cudaError_t ce = cudaStreamEndCapture(e->stream, &g);
     if (st) return st;
     E_TRY(ce);
@@ -1012,30 +1031,50 @@ int qwen_engine_set_option(qwen_engine* e, const char* name, long long value) {
   return 0;
 }
 
-int qwen_engine_prefill(qwen_engine* e, int slot, const int32_t* tokens, int n, int32_t* next_token) {
-  if (!e || slot < 0 || slot >= e->max_seqs || !tokens || n <= 0 || n > e->max_len) return kStatusInvalid;
-  if (e->seq_len[slot] != 0) {
-    set_error("prefill into a non-empty slot %d (reset it first)", slot);
+namespace {
+
+// n prompt tokens into `slot` after the `past` tokens it holds (0: a fresh prompt).
+int prefill_at(qwen_engine* e, int slot, const int32_t* tokens, int n, int past, int32_t* next_token) {
+  if (n <= 0 || past < 0 || past + n > e->max_len) {
+    set_error("prefill of %d tokens after %d exceeds the engine's max_len %d", n, past, e->max_len);
     return kStatusInvalid;
   }
   for (int i = 0; i < n; ++i)
     if (tokens[i] < 0 || tokens[i] >= kVocab) return kStatusInvalid;
   E_TRY(cudaSetDevice(e->device));
-  if (int st = ensure_prefill_buffers(e, n)) return st;
+  if (int st = ensure_prefill_buffers(e, past + n)) return st;  // flat K/V rows: history + chunk
   if (e->exact) {
     if (int st = ensure_exact(e, n)) return st;
   }
-  if (int st = ensure_rope_pre(e, n)) return st;
-  if (int st = ensure_pages(e, slot, n)) return st;
+  if (int st = ensure_rope_pre(e, past + n)) return st;
+  if (int st = ensure_pages(e, slot, past + n)) return st;
   cudaStream_t s = e->stream;
   E_TRY(cudaMemcpyAsync(e->p_tokens, tokens, (size_t)n * 4, cudaMemcpyHostToDevice, s));
-  if (int st = run_prefill(e, slot, n)) return st;
+  if (int st = run_prefill(e, slot, n, past)) return st;
   E_TRY(cudaMemcpyAsync(e->h_io + 12, e->d_next, 4, cudaMemcpyDeviceToHost, s));
   E_TRY(cudaStreamSynchronize(s));
-  e->seq_len[slot] = n;
+  e->seq_len[slot] = past + n;
   e->last_rows = 1;
+  e->dev_slots.clear();
   if (next_token) *next_token = e->h_io[12];
   return 0;
+}
+
+}  // namespace
+
+int qwen_engine_prefill(qwen_engine* e, int slot, const int32_t* tokens, int n, int32_t* next_token) {
+  if (!e || slot < 0 || slot >= e->max_seqs || !tokens || n <= 0 || n > e->max_len) return kStatusInvalid;
+  if (e->seq_len[slot] != 0) {
+    set_error("prefill into a non-empty slot %d (reset it first, or continue it with qwen_engine_prefill_chunk)",
+              slot);
+    return kStatusInvalid;
+  }
+  return prefill_at(e, slot, tokens, n, 0, next_token);
+}
+
+int qwen_engine_prefill_chunk(qwen_engine* e, int slot, const int32_t* tokens, int n, int32_t* next_token) {
+  if (!e || slot < 0 || slot >= e->max_seqs || !tokens || n <= 0) return kStatusInvalid;
+  return prefill_at(e, slot, tokens, n, e->seq_len[slot], next_token);
 }
 
 int qwen_engine_decode(qwen_engine* e, const int32_t* slots, const int32_t* tokens, int n, int32_t* next_tokens) {
@@ -1269,7 +1308,7 @@ int qwen_engine_write_kv(qwen_engine* e, int slot, int layer, const float* k, co
   if (int st = ensure_pages(e, slot, n_tokens)) return st;
   E_TRY(cudaMemcpyAsync(e->p_k, k, (size_t)n_tokens * kKvWidth * 4, cudaMemcpyDefault, e->stream));
   E_TRY(cudaMemcpyAsync(e->p_v, v, (size_t)n_tokens * kKvWidth * 4, cudaMemcpyDefault, e->stream));
-  kv_scatter_kernel<<<n_tokens, 256, 0, e->stream>>>(e->p_k, e->p_v, n_tokens, paged_view(e, layer), slot, 1);
+  kv_scatter_kernel<<<n_tokens, 256, 0, e->stream>>>(e->p_k, e->p_v, n_tokens, paged_view(e, layer), slot, 1, 0);
   E_TRY(cudaGetLastError());
   E_TRY(cudaStreamSynchronize(e->stream));
   if (layer == kLayers - 1) e->seq_len[slot] = n_tokens;
@@ -1283,7 +1322,7 @@ int qwen_engine_read_kv(qwen_engine* e, int slot, int layer, float* k, float* v,
     return kStatusInvalid;
   E_TRY(cudaSetDevice(e->device));
   if (int st = ensure_prefill_buffers(e, n_tokens)) return st;
-  kv_scatter_kernel<<<n_tokens, 256, 0, e->stream>>>(e->p_k, e->p_v, n_tokens, paged_view(e, layer), slot, 0);
+  kv_scatter_kernel<<<n_tokens, 256, 0, e->stream>>>(e->p_k, e->p_v, n_tokens, paged_view(e, layer), slot, 0, 0);
   E_TRY(cudaGetLastError());
   E_TRY(cudaMemcpyAsync(k, e->p_k, (size_t)n_tokens * kKvWidth * 4, cudaMemcpyDefault, e->stream));
   E_TRY(cudaMemcpyAsync(v, e->p_v, (size_t)n_tokens * kKvWidth * 4, cudaMemcpyDefault, e->stream));

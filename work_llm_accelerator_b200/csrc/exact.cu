@@ -172,11 +172,11 @@ __global__ void __launch_bounds__(kAttnThreads) attn_dec_kernel(const float* __r
                        ctx + (size_t)t * kHidden + h * kHeadDim, h / kGroups);
 }
 
-// grid (S, 12)
-__global__ void __launch_bounds__(kAttnThreads) attn_pre_kernel(const float* __restrict__ q, KvView kv,
+// grid (S, 12): query t at position q0 + t over keys 0 .. q0 + t
+__global__ void __launch_bounds__(kAttnThreads) attn_pre_kernel(const float* __restrict__ q, KvView kv, int q0,
                                                                 float* __restrict__ ctx) {
   const int t = blockIdx.x, h = blockIdx.y;
-  attention_one<true>(q + (size_t)t * kHidden + h * kHeadDim, kv, 0, t + 1, kAttentionScaling,
+  attention_one<true>(q + (size_t)t * kHidden + h * kHeadDim, kv, 0, q0 + t + 1, kAttentionScaling,
                       ctx + (size_t)t * kHidden + h * kHeadDim, h / kGroups);
 }
 
@@ -291,12 +291,12 @@ cudaError_t launch_attention_dec(const float* q, KvView kv, const int* pos, cons
 }
 
 cudaError_t launch_attention_pre(const float* q, const float* k, const float* v, int S, float* ctx,
-                                 cudaStream_t s) {
+                                 cudaStream_t s, int q0) {
   KvView kv{};
   kv.k = const_cast<float*>(k);
   kv.v = const_cast<float*>(v);
   kv.page_table = nullptr;
-  attn_pre_kernel<<<dim3(S, kHeads), kAttnThreads, 0, s>>>(q, kv, ctx);
+  attn_pre_kernel<<<dim3(S, kHeads), kAttnThreads, 0, s>>>(q, kv, q0, ctx);
   return cudaGetLastError();
 }
 

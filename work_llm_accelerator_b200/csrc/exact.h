@@ -42,10 +42,10 @@ cudaError_t launch_rope_store(const float* qkv, int n, const int* pos, int pos_b
 cudaError_t launch_attention_dec(const float* q, KvView kv, const int* pos, const int* seq, int n, float scaling,
                                  float* ctx, cudaStream_t s);
 
-// Causal prefill attention context (qwen_prefill_attention_kernel.cpp:204-289) of S queries over the flat
-// K/V rows [S][256]: the same two passes with approx_exp. q, ctx [S][1536].
+// Causal prefill attention context (qwen_prefill_attention_kernel.cpp:204-289) of S queries at positions
+// q0 .. q0 + S - 1 over the flat K/V rows [q0 + S][256]: the same two passes with approx_exp. q, ctx [S][1536].
 cudaError_t launch_attention_pre(const float* q, const float* k, const float* v, int S, float* ctx,
-                                 cudaStream_t s);
+                                 cudaStream_t s, int q0 = 0);
 
 // h[t][i] = silu(g) * u with g = gu[t][i], u = gu[t][8960 + i], silu(v) = v / (1 + exp(-v)): exact_expf
 // (decode, qwen_decode_mlp_kernel.cpp:79-81) or approx_exp (prefill, qwen_prefill_mlp_kernel.cpp:256-258).

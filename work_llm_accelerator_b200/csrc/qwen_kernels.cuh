@@ -77,12 +77,13 @@ cudaError_t launch_prefill_o(int wbits, const LayerDev& L, const float* ctx, int
 cudaError_t launch_prefill_gateup(int wbits, const LayerDev& L, const float* xn, int S, float* h, cudaStream_t s);
 cudaError_t launch_prefill_down(int wbits, const LayerDev& L, const float* h, const float* a, int S, float* out,
                                 bool round_out, cudaStream_t s);
-// Causal two-pass GQA attention with approx_exp (scores and max bit-identical to the reference).
+// Causal two-pass GQA attention with approx_exp (scores and max bit-identical to the reference): S queries
+// (rows of q and ctx) at positions qoff .. qoff + S - 1 over k_cache / v_cache rows 0 .. qoff + S - 1.
 cudaError_t launch_prefill_attention(const float* q, const float* k_cache, const float* v_cache, int S, float* ctx,
-                                     cudaStream_t s);
+                                     cudaStream_t s, int qoff = 0);
 // Same kernel, run only when *only_if != 0 (read on the device; the CTAs return at once otherwise).
 cudaError_t launch_prefill_attention_gated(const float* q, const float* k_cache, const float* v_cache, int S,
-                                           float* ctx, const int* only_if, cudaStream_t s);
+                                           float* ctx, const int* only_if, cudaStream_t s, int qoff = 0);
 
 // --- misc ----------------------------------------------------------------------------------------
 // Deterministic synthetic layer parameters written straight into a device DDR image of `wbits` layout.

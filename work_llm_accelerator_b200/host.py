@@ -172,6 +172,7 @@ def _configure_engine(lib: ctypes.CDLL) -> None:
     lib.qwen_engine_load_layer.argtypes = [vp, i, _B, _F]
     lib.qwen_engine_load_embedding.argtypes = [vp, _U16, _F]
     lib.qwen_engine_prefill.argtypes = [vp, i, _I32, i, _I32]
+    lib.qwen_engine_prefill_chunk.argtypes = [vp, i, _I32, i, _I32]
     lib.qwen_engine_decode.argtypes = [vp, _I32, _I32, i, _I32]
     lib.qwen_engine_write_kv.argtypes = [vp, i, i, _F, _F, i]
     lib.qwen_engine_read_kv.argtypes = [vp, i, i, _F, _F, i]
@@ -205,7 +206,8 @@ def _configure_engine(lib: ctypes.CDLL) -> None:
               "qwen_engine_kernels_per_decode_step", "qwen_engine_decode_device", "qwen_engine_read_layer",
               "qwen_engine_profile_kernels", "qwen_engine_read_trace", "qwen_engine_profile_decode",
               "qwen_engine_profile_batched", "qwen_engine_nccl_unique_id", "qwen_engine_nccl_init",
-              "qwen_engine_gather_tokens", "qwen_engine_read_kv_hf", "qwen_engine_write_kv_hf"):
+              "qwen_engine_gather_tokens", "qwen_engine_read_kv_hf", "qwen_engine_write_kv_hf",
+              "qwen_engine_prefill_chunk"):
         getattr(lib, n).restype = i
 
 
@@ -265,6 +267,13 @@ class Engine:
         toks = np.ascontiguousarray(tokens, np.int32)
         out = np.zeros(1, np.int32)
         _check(self.lib.qwen_engine_prefill(self.handle, slot, toks, toks.size, out), "prefill")
+        return int(out[0])
+
+    def prefill_chunk(self, slot: int, tokens: Sequence[int]) -> int:
+        """Continue the slot's prompt with more tokens (chunked prefill); returns the greedy next token."""
+        toks = np.ascontiguousarray(tokens, np.int32)
+        out = np.zeros(1, np.int32)
+        _check(self.lib.qwen_engine_prefill_chunk(self.handle, slot, toks, toks.size, out), "prefill_chunk")
         return int(out[0])
 
     def decode(self, slots: Sequence[int], tokens: Sequence[int]) -> np.ndarray:
