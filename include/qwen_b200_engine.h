@@ -67,7 +67,8 @@ int qwen_engine_reset(qwen_engine* e, int slot);
  * launch, default 1), "dump_hidden" (keep every layer's output of the last call, default 0),
  * "logits" (keep the last call's logits, default 0), "prefetch" (stream the next kernels' weights into L2,
  * default 1), "stack" (W8: the whole decode step as one persistent kernel, default 1; 0 = five tensor-core
- * kernels per layer), "qgemm" (W8 separate-kernel path on the int8 tensor cores, default 1; 0 = CUDA-core
+ * kernels per layer), "bs1" (W8, one sequence per step: the persistent kernel on the CUDA cores with
+ * self-validating cross-CTA words, default 1; 0 = the tensor-core persistent kernel; same results), "qgemm" (W8 separate-kernel path on the int8 tensor cores, default 1; 0 = CUDA-core
  * GEMV), "trace" (record a per-CTA, per-layer timeline of the persistent kernel, default 0), "batched" (W8: steps
  * of more than 4 sequences as one many-token tensor-core step, default 1; 0 = groups of 4), "lm_tc" (LM head
  * on the tensor cores, default 1; 0 = CUDA-core GEMV), "stack_ring" (weight stages in flight per SM in the

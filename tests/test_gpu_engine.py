@@ -240,20 +240,38 @@ def _decode_trace(host, seed, prompt, steps, max_len=256, **options):
         eng.close()
 
 
-@pytest.mark.parametrize("prompt_len", [5, 130])
-def test_persistent_step_kernel_matches_separate_kernels(host, prompt_len):
-    """The single-launch decode step (decode_stack.cu: all 28 layers in one persistent kernel) and the
-    five-launches-per-layer tensor-core path do the same arithmetic in the same order: every layer's
-    hidden state and every token are bit-identical. 130 prompt tokens give three 64-key attention chunks
-    (cross-CTA chunk merge); 5 give one."""
+@pytest.mark.parametrize("prompt_len", [5, 130, 600])
+def test_persistent_step_kernels_match_separate_kernels(host, prompt_len):
+    """The single-launch decode steps (decode_bs1.cu: batch 1 on the CUDA cores with self-validating
+    cross-CTA words; decode_stack.cu: the tensor-core persistent kernel) and the five-launches-per-layer
+    tensor-core path do the same arithmetic in the same order: every layer's hidden state and every token
+    are bit-identical. 130 prompt tokens give three 64-key attention chunks (cross-CTA chunk merge), 5 give
+    one, 600 give ten (more chunks than one merge batch)."""
     rng = np.random.default_rng(prompt_len)
     prompt = [int(t) for t in rng.integers(0, qo.VOCAB, prompt_len)]
     host.kernel_error(reset=True)
-    toks_s, hid_s = _decode_trace(host, 21, prompt, 4, max_len=512, stack=1)
+    toks_1, hid_1 = _decode_trace(host, 21, prompt, 4, max_len=1024, stack=1, bs1=1)
     assert host.kernel_error(reset=True) == 0
-    toks_k, hid_k = _decode_trace(host, 21, prompt, 4, max_len=512, stack=0)
-    assert toks_s == toks_k
-    for step, (a, b) in enumerate(zip(hid_s, hid_k)):
+    toks_s, hid_s = _decode_trace(host, 21, prompt, 4, max_len=1024, stack=1, bs1=0)
+    assert host.kernel_error(reset=True) == 0
+    toks_k, hid_k = _decode_trace(host, 21, prompt, 4, max_len=1024, stack=0)
+    assert toks_1 == toks_s == toks_k
+    for step, (a, b, c) in enumerate(zip(hid_1, hid_s, hid_k)):
+        assert np.array_equal(a, c), ("bs1", step, rel_l2(a, c))
+        assert np.array_equal(b, c), ("stack", step, rel_l2(b, c))
+
+
+def test_batch1_kernel_over_many_launches(host):
+    """The batch-1 persistent kernel keeps launch-parity words (zeroed by the following launch) and tagged
+    words (launch epoch and layer in the tag): 40 consecutive steps with the trace option on, each equal
+    to the separate kernels' step from the same state."""
+    rng = np.random.default_rng(77)
+    prompt = [int(t) for t in rng.integers(0, qo.VOCAB, 70)]
+    toks_1, hid_1 = _decode_trace(host, 5, prompt, 40, max_len=256, stack=1, bs1=1, trace=1)
+    assert host.kernel_error(reset=True) == 0
+    toks_k, hid_k = _decode_trace(host, 5, prompt, 40, max_len=256, stack=0)
+    assert toks_1 == toks_k
+    for step, (a, b) in enumerate(zip(hid_1, hid_k)):
         assert np.array_equal(a, b), (step, rel_l2(a, b))
 
 

@@ -25,7 +25,7 @@ NVCC = str(CUDA_HOME / "bin" / "nvcc")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVCC_FLAGS = ARCH + ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC", "--expt-relaxed-constexpr",
                      "-Xptxas", "-warn-spills"]
-CU_SOURCES = ["decode_gemv.cu", "attention.cu", "prefill_simt.cu", "misc.cu", "runtime.cu", "engine.cu", "ops.cu", "ops_noalloc.cu", "qgemm.cu", "decode_stack.cu", "tgemm.cu", "lmhead.cu", "attention_tc.cu", "exact.cu", "layer0_ref.cu"]
+CU_SOURCES = ["decode_gemv.cu", "attention.cu", "prefill_simt.cu", "misc.cu", "runtime.cu", "engine.cu", "ops.cu", "ops_noalloc.cu", "qgemm.cu", "decode_stack.cu", "decode_bs1.cu", "tgemm.cu", "lmhead.cu", "attention_tc.cu", "exact.cu", "layer0_ref.cu"]
 CXX = os.environ.get("QWEN_B200_CXX", "g++")
 
 LIB_CORE = LIB / "libqwen_b200.so"

@@ -22,6 +22,7 @@
 
 #include "../../include/qwen_b200_engine.h"
 #include "attention_tc.h"
+#include "decode_bs1.h"
 #include "decode_stack.h"
 #include "qgemm.h"
 #include "lmhead.h"
@@ -226,6 +227,12 @@ struct qwen_engine {
   int attn_max_chunks = 0;
   unsigned long long* trace = nullptr;  // optional timeline of the persistent kernel
   int stack_ring = 9;                   // weight stages in flight per CTA
+  // persistent batch-1 step on the CUDA cores (wbits == 8, one sequence per step): its schedule and words
+  bool use_bs1 = true;
+  bs1::Sync* bs1_sync = nullptr;
+  bs1::Buffers bs1_buf{nullptr, nullptr, nullptr, nullptr, nullptr, nullptr, nullptr};
+  uint32_t* d_item_off1 = nullptr;
+  stack::Item* d_items1 = nullptr;
   cudaEvent_t kev[3] = {nullptr, nullptr, nullptr};  // per-kernel timing (profile_decode)
   bool time_kernels = false;
   // per-category timing of the batched step (profile_batched): events around each kernel group
@@ -474,6 +481,7 @@ int enqueue_prefill_exact(qwen_engine* e, int slot, int n, int past) {
 }
 
 bool stack_enabled(const qwen_engine* e) { return e->wbits == 8 && e->use_stack && e->wtiles != nullptr; }
+bool bs1_enabled(const qwen_engine* e, int nt) { return nt == 1 && e->use_bs1 && e->d_items1 != nullptr; }
 
 // Final norm + LM head + argmax of n rows of x into d_next (logits kept when requested).
 int enqueue_lm_head(qwen_engine* e, const float* x, int n, int* next, float* logits, bool pdl) {
@@ -504,7 +512,33 @@ int enqueue_decode(qwen_engine* e, int nt, int max_len, bool advance) {
   const size_t qkv_bytes = (size_t)kQkvRows * kHidden * wb / 8;
   const size_t lm_head_prefetch = (size_t)32 << 20;
   if (e->time_kernels) E_TRY(cudaEventRecord(e->kev[0], e->stream));
-  if (stack_enabled(e)) {
+  if (stack_enabled(e) && bs1_enabled(e, nt)) {
+    if (int st = ensure_tiles(e)) return st;
+    bs1::Args a{};
+    a.wtiles = e->wtiles;
+    a.layers = e->d_layers;
+    a.embed = e->embed;
+    a.tokens = e->d_tokens;
+    a.pos = e->d_pos;
+    a.seq = e->d_seq;
+    a.rope_cos = e->rope_dec_cos;
+    a.rope_sin = e->rope_dec_sin;
+    a.kv_pool = e->kv_pool;
+    a.page_table = e->d_page_table;
+    a.max_pages = e->max_pages;
+    a.y0 = e->y0;
+    a.y1 = e->y1;
+    a.dump = e->dump_hidden ? e->dump : nullptr;
+    a.buf = e->bs1_buf;
+    a.max_chunks = e->attn_max_chunks;
+    a.sync = e->bs1_sync;
+    a.item_off = e->d_item_off1;
+    a.items = e->d_items1;
+    a.trace = e->trace;
+    a.ring = e->stack_ring;
+    E_TRY(bs1::launch_decode_bs1(a, e->stack_ctas, e->stream));
+    xin = ((kLayers - 1) & 1) ? e->y1 : e->y0;
+  } else if (stack_enabled(e)) {
     if (int st = ensure_tiles(e)) return st;
     stack::Args a{};
     a.wtiles = e->wtiles;
@@ -882,6 +916,25 @@ int qwen_engine_create(int device, int wbits, int max_seqs, int max_len, qwen_en
   e->attn_max_chunks = (max_len + 512 + 64 + 63) / 64;
   E_TRY(dalloc(&e->attn_part, std::max(attn_partial_floats(T, max_len + 512 + 64),
                                        stack::attn_part_floats(T, e->attn_max_chunks))));
+  if (e->stack_ctas > 0 && bs1::decode_bs1_smem() <= (size_t)227 * 1024) {
+    const stack::Schedule s1 = bs1::build_schedule(e->stack_ctas);
+    if (!s1.off.empty()) {
+      bs1::Buffers& b = e->bs1_buf;
+      const size_t words[7] = {bs1::acc_words(), bs1::part_words(e->attn_max_chunks), bs1::ctx_words(),
+                               bs1::cmax_words(), bs1::h_words(), bs1::hmax_words(), bs1::step_words()};
+      unsigned long long** ptrs[7] = {&b.acc, &b.part, &b.ctx, &b.cmax, &b.h, &b.hmax, &b.steps};
+      for (int i = 0; i < 7; ++i) {
+        E_TRY(dalloc(ptrs[i], words[i]));
+        E_TRY(cudaMemset(*ptrs[i], 0, words[i] * 8));
+      }
+      E_TRY(cudaMalloc(&e->bs1_sync, sizeof(bs1::Sync)));
+      E_TRY(cudaMemset(e->bs1_sync, 0, sizeof(bs1::Sync)));
+      E_TRY(dalloc(&e->d_item_off1, s1.off.size()));
+      E_TRY(cudaMemcpy(e->d_item_off1, s1.off.data(), s1.off.size() * 4, cudaMemcpyHostToDevice));
+      E_TRY(dalloc(&e->d_items1, s1.items.size()));
+      E_TRY(cudaMemcpy(e->d_items1, s1.items.data(), s1.items.size() * sizeof(stack::Item), cudaMemcpyHostToDevice));
+    }
+  }
   E_TRY(dalloc(&e->attn_cnt, (size_t)T * kKvHeads));
   E_TRY(cudaMemset(e->attn_cnt, 0, (size_t)T * kKvHeads * 4));
   {
@@ -916,7 +969,8 @@ void qwen_engine_destroy(qwen_engine* e) {
                   e->lm_part, e->lm_cnt, e->dump, e->logits, e->rope_dec_cos, e->rope_dec_sin, e->rope_pre_cos,
                   e->rope_pre_sin, e->p_x, e->p_xn, e->p_q, e->p_ctx, e->p_a, e->p_h, e->p_k, e->p_v, e->p_tokens,
                   e->qsc.acc, e->qsc.cnt, e->wtiles, e->d_layers, e->sync, e->stack_acc, e->stack_steps,
-                  e->d_item_off, e->d_items};
+                  e->d_item_off, e->d_items, e->bs1_buf.acc, e->bs1_buf.part, e->bs1_buf.ctx, e->bs1_buf.cmax,
+                  e->bs1_buf.h, e->bs1_buf.hmax, e->bs1_buf.steps, e->bs1_sync, e->d_item_off1, e->d_items1};
   for (void* p : ptrs) cudaFree(p);
   cudaFree(e->trace);
   cudaFree(e->lm.planes);
@@ -1011,6 +1065,10 @@ int qwen_engine_set_option(qwen_engine* e, const char* name, long long value) {
     e->use_batched = value != 0;
   } else if (n == "stack") {
     e->use_stack = value != 0;
+    for (auto& kv : e->graphs) cudaGraphExecDestroy(kv.second);
+    e->graphs.clear();
+  } else if (n == "bs1") {
+    e->use_bs1 = value != 0;
     for (auto& kv : e->graphs) cudaGraphExecDestroy(kv.second);
     e->graphs.clear();
   } else if (n == "qgemm") {

@@ -20,6 +20,7 @@
 
 #include "attention_tc.h"
 #include "layer0_ref.h"
+#include "decode_bs1.h"
 #include "decode_stack.h"
 #include "qgemm.h"
 #include "lmhead.h"
@@ -588,7 +589,8 @@ int qwen_b200_set_prefill_seq_capacity(int capacity) {
 
 unsigned qwen_b200_kernel_error(int reset) {
   return qb::gemv_kernel_error(reset != 0) | qb::qgemm_kernel_error(reset != 0) |
-         qb::stack::decode_stack_kernel_error(reset != 0) | qb::tgemm_kernel_error(reset != 0) |
+         qb::stack::decode_stack_kernel_error(reset != 0) | qb::bs1::decode_bs1_kernel_error(reset != 0) |
+         qb::tgemm_kernel_error(reset != 0) |
          qb::lm_head_kernel_error(reset != 0) | qb::attn_tc_kernel_error(reset != 0) |
          qb::decode_attn_kernel_error(reset != 0);
 }
