@@ -25,15 +25,16 @@
 // older copy of a word another SM rewrote), so a consumer sees either the old or the new word. Every data
 // word a stage reads was produced by work that precedes it in the layer's dependency chain, and every
 // buffer that is reused (layer parity) is rewritten only by work that depends on all of its readers.
-// While a stage's inputs are still on their way, one warp per CTA polls one sentinel word per producer
-// tile; the workers then read their own words once (re-reading any that are not complete yet).
+// Every worker reads its own input words until they are all current (one L2 round trip once the data has
+// landed; a separate completion signal would add one).
 //
 // Roles (160 threads):
 //   warp 0      lane 0: producer, cp.async.bulk of pre-swizzled 16 KB weight units into a ring of shared
 //               memory stages, never waiting for activations; lanes 1-31 zero the other launch parity of
 //               the packed words at the start
 //   warps 1-4   workers: read a stage's inputs, build the digits of their K blocks, dp4a over the ring
-//               units, publish the results; attention chunks (the last chunk of a merge group merges it)
+//               units, publish the results; attention chunks (the item of a merge group's last chunk also
+//               merges the group)
 // Every wait gives up after ~1 s, raising an abort flag that ends all other waits quickly, and records the
 // failure in the kernel error flag.
 #include <cuda_fp16.h>
@@ -125,12 +126,6 @@ __device__ __forceinline__ void st_word(unsigned long long* p, unsigned long lon
 
 __device__ __forceinline__ void red_word(unsigned long long* p, unsigned long long v) {
   asm volatile("red.relaxed.gpu.global.add.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
-}
-
-__device__ __forceinline__ unsigned long long atom_word(unsigned long long* p, unsigned long long v) {
-  unsigned long long old;
-  asm volatile("atom.relaxed.gpu.global.add.u64 %0, [%1], %2;" : "=l"(old) : "l"(p), "l"(v) : "memory");
-  return old;
 }
 
 __device__ __forceinline__ unsigned tag_of(unsigned epoch, int l) { return ((epoch + 1u) << 5) | (unsigned)l; }
@@ -424,29 +419,6 @@ __device__ long long gemv_units(Worker& w, Ctrl& cs, const Args& a, uint8_t* rin
   return (long long)r0 + 256ll * (long long)r1 + 65536ll * (long long)r2;
 }
 
-// Warp 0 waits for one sentinel word per tile (its last row) of the o_proj and, with `down`, the down
-// projection of layer l, and for their digit-step words; the other workers wait at the barrier.
-__device__ void wait_sentinels(const Args& a, const Worker& w, int l, bool down) {
-  if (w.warp == 0) {
-    const unsigned long long* acc = acc_layer(a, w.par, l);
-    const unsigned long long* sw = a.buf.steps + (size_t)l * 4;
-    const unsigned tag = tag_of(w.epoch, l);
-    const int ln = w.lane;
-    Spin sp;
-    while (true) {
-      bool ok = true;
-      if (ln < 12) ok = count_ok(ld_word(acc + acc_row(kO) + ln * 128 + 127), nseg(kO));
-      else if (ln < 24 && down) ok = count_ok(ld_word(acc + acc_row(kDown) + (ln - 12) * 128 + 127), nseg(kDown));
-      else if (ln == 24) ok = tag_ok(ld_word(sw + kO), tag);
-      else if (ln == 25 && down) ok = tag_ok(ld_word(sw + kDown), tag);
-      if (__all_sync(0xffffffffu, ok)) break;
-      const bool go = sp.keep_going(w.abort_flag);
-      if (!__shfl_sync(0xffffffffu, go, 0)) break;
-    }
-  }
-  named_sync(kBarW, kWorkers);
-}
-
 // Layer lp's output y = bf16(a + down_s * (step_d * down_total)) with a = o_s * (step_o * o_total), this
 // thread's elements, from the packed words (the expressions of the tensor-core kernels' epilogues).
 __device__ void load_y(const Args& a, const Worker& w, int lp, const float4 (&os)[3], const float4 (&ds)[3],
@@ -455,7 +427,6 @@ __device__ void load_y(const Args& a, const Worker& w, int lp, const float4 (&os
   const unsigned long long* sw = a.buf.steps + (size_t)lp * 4;
   const unsigned tag = tag_of(w.epoch, lp);
   unsigned long long wo[3][4], wd[3][4], so, sd;
-  wait_sentinels(a, w, lp, true);
   Spin sp;
   while (true) {
 #pragma unroll
@@ -495,7 +466,6 @@ __device__ void load_a(const Args& a, const Worker& w, int l, const float4 (&os)
   const unsigned long long* sw = a.buf.steps + (size_t)l * 4;
   const unsigned tag = tag_of(w.epoch, l);
   unsigned long long wo[3][4], so;
-  wait_sentinels(a, w, l, false);
   Spin sp;
   while (true) {
 #pragma unroll
@@ -523,8 +493,9 @@ __device__ void load_a(const Args& a, const Worker& w, int l, const float4 (&os)
 
 // ---------------------------------------------------------------------------------------------------
 // attention (hls/decode_only/qwen_decode_attention_kernel.cpp:113-162): one 64-key chunk x one KV group x
-// three of its six query heads per item; each item stores its chunk partial (m, l, acc) as tagged words and
-// the last chunk of its merge group to finish merges the group's chunks.
+// three of its six query heads per item; each item stores its chunk partial (m, l, acc) as tagged words, and
+// the item of the group's last chunk merges the group's chunks (a merging item waits only for items of lower
+// index, which every CTA runs first: no wait can go round in a circle).
 // ---------------------------------------------------------------------------------------------------
 struct AttnItem {
   int g, hp, c, n, nhist;
@@ -748,15 +719,12 @@ __device__ void attn_item(const Args& a, AttnSmem& sm, Ctrl& cs, const Worker& w
     const int j = tid >> 1;
     st_word(part_ptr(a, l, q_head(it, j), it.c) + (tid & 1), tagged(tag, (tid & 1) ? sm.ls[j] : sm.ms[j]));
   }
-  // count the chunk; the last of the merge group merges (the other partials are read as tagged words)
-  named_sync(kBarW, kWorkers);
+  if (tid == 0) stamp(a, l, stack::kTraceAttnPart);
+  // the item of the group's last chunk merges the group: it reads the other chunks' partials as tagged
+  // words, waiting on the data itself
+  if (it.c != nch - 1) return;
   const int group = it.g * 2 + it.hp;
-  if (tid == 0) {
-    cs.flag = atom_word(acc_l + kAttnCounter + group, 1ull) == (unsigned long long)(nch - 1);
-    stamp(a, l, stack::kTraceAttnPart);
-  }
-  named_sync(kBarW, kWorkers);
-  if (!cs.flag) return;
+  named_sync(kBarW, kWorkers);  // this item's own partial is written
   // thread = 4 dims of one of the three heads (96 threads); the context and the group's max |ctx| as tagged
   // words
   float m = 0.0f;
@@ -905,16 +873,6 @@ __device__ void workers(const Args& a, uint8_t* ring, uint8_t* attn, uint8_t* di
       const Item it = a.items[si[kO]];
       if (tr) stamp(a, l, stack::kTraceWait + 2);
       const unsigned long long* cm = a.buf.cmax + (size_t)(l & 1) * kMergeGroups;
-      if (w.warp == 0) {  // sentinels: the group maxima, written after each group's context
-        Spin sp;
-        while (true) {
-          const bool ok = w.lane >= kMergeGroups || tag_ok(ld_word(cm + w.lane), tag);
-          if (__all_sync(0xffffffffu, ok)) break;
-          const bool go = sp.keep_going(abort_flag);
-          if (!__shfl_sync(0xffffffffu, go, 0)) break;
-        }
-      }
-      named_sync(kBarW, kWorkers);
       const int nel = (it.kb1 - it.kb0) * kKBlock;  // this item's context elements, 4 per thread
       const unsigned long long* cw = a.buf.ctx + (size_t)(l & 1) * kHidden + it.kb0 * kKBlock + 4 * w.tid;
       unsigned long long x[4] = {0, 0, 0, 0}, mw[kMergeGroups];
@@ -982,47 +940,42 @@ __device__ void workers(const Args& a, uint8_t* ring, uint8_t* attn, uint8_t* di
     if (si[kDown] >= 0) {
       const Item it = a.items[si[kDown]];
       const unsigned long long* hm = a.buf.hmax + (size_t)(l & 1) * kGuItems;
-      if (w.warp == 0) {  // sentinels: every gate|up item's max, written after its h values
-        Spin sp;
-        while (true) {
-          bool ok = true;
-          for (int i = w.lane; i < kGuItems; i += 32) ok = ok && tag_ok(ld_word(hm + i), tag);
-          if (__all_sync(0xffffffffu, ok)) break;
-          const bool go = sp.keep_going(abort_flag);
-          if (!__shfl_sync(0xffffffffu, go, 0)) break;
-        }
-      }
-      named_sync(kBarW, kWorkers);
-      float m = 0.0f;
+      // every gate|up item's max |h| (for the step) and this thread's h values (at most 2 x 4 per thread),
+      // read together until all are current
+      const int n4 = (it.kb1 - it.kb0) * (kKBlock / 4);
+      static_assert(seg_len(stack::kDown) * (kKBlock / 4) <= 2 * kWorkers, "two h quads per thread");
+      const unsigned long long* hp = a.buf.h + (size_t)(l & 1) * kInter + it.kb0 * kKBlock;
+      const bool has1 = w.tid + kWorkers < kGuItems, f0 = w.tid < n4, f1 = w.tid + kWorkers < n4;
+      unsigned long long x0 = 0, x1 = 0, hx[2][4] = {{0, 0, 0, 0}, {0, 0, 0, 0}};
       {
-        unsigned long long x0 = 0, x1 = 0;
-        const bool has1 = w.tid + kWorkers < kGuItems;
         Spin sp;
         while (true) {
           x0 = ld_word(hm + w.tid);
           if (has1) x1 = ld_word(hm + w.tid + kWorkers);
-          if ((tag_ok(x0, tag) && (!has1 || tag_ok(x1, tag))) || !sp.keep_going(abort_flag)) break;
+          if (f0) {
+            ld_word2(hp + 4 * w.tid, hx[0][0], hx[0][1]);
+            ld_word2(hp + 4 * w.tid + 2, hx[0][2], hx[0][3]);
+          }
+          if (f1) {
+            ld_word2(hp + 4 * (w.tid + kWorkers), hx[1][0], hx[1][1]);
+            ld_word2(hp + 4 * (w.tid + kWorkers) + 2, hx[1][2], hx[1][3]);
+          }
+          bool ok = tag_ok(x0, tag) && (!has1 || tag_ok(x1, tag));
+#pragma unroll
+          for (int e = 0; e < 4; ++e) ok = ok && (!f0 || tag_ok(hx[0][e], tag)) && (!f1 || tag_ok(hx[1][e], tag));
+          if (ok || !sp.keep_going(abort_flag)) break;
         }
-        m = fmaxf(word_value(x0), has1 ? word_value(x1) : 0.0f);
       }
       if (tr) stamp(a, l, stack::kTraceWait + 4);
-      const float mx = block_max(cs, m, w);
+      const float mx = block_max(cs, fmaxf(word_value(x0), has1 ? word_value(x1) : 0.0f), w);
       const float step = mx > 0.0f ? mx / umma::kDigitRange : 1.0f;
       if (w.tid == 0) st_word(a.buf.steps + (size_t)l * 4 + kDown, tagged(tag, step));
-      const int n4 = (it.kb1 - it.kb0) * (kKBlock / 4);
-      const unsigned long long* hp = a.buf.h + (size_t)(l & 1) * kInter + it.kb0 * kKBlock;
-      for (int f = w.tid; f < n4; f += kWorkers) {
-        unsigned long long x[4];
-        Spin sp;
-        while (true) {
-          ld_word2(hp + 4 * f, x[0], x[1]);
-          ld_word2(hp + 4 * f + 2, x[2], x[3]);
-          if ((tag_ok(x[0], tag) && tag_ok(x[1], tag) && tag_ok(x[2], tag) && tag_ok(x[3], tag)) ||
-              !sp.keep_going(abort_flag))
-            break;
+#pragma unroll
+      for (int b = 0; b < 2; ++b) {
+        if (b == 0 ? f0 : f1) {
+          const float hv[4] = {word_value(hx[b][0]), word_value(hx[b][1]), word_value(hx[b][2]), word_value(hx[b][3])};
+          put_digits(dig, 4 * (w.tid + b * kWorkers), hv, step);
         }
-        const float hv[4] = {word_value(x[0]), word_value(x[1]), word_value(x[2]), word_value(x[3])};
-        put_digits(dig, 4 * f, hv, step);
       }
       named_sync(kBarW, kWorkers);
       if (tr) stamp(a, l, stack::kTraceBuilt + 4);

@@ -19,12 +19,10 @@ __host__ __device__ constexpr int nseg(int s) {
 }
 __host__ __device__ constexpr int seg_len(int s) { return (stack::nkb(s) + nseg(s) - 1) / nseg(s); }
 
-// Words per layer of the packed split-K block: q|k|v rows at 0, o at 2048, down at 3584, then one attention
-// chunk counter per merge group (KV group x half of its query heads) at 5120.
-constexpr int kAccRows = 2048 + 1536 + 1536 + 8;
+// Words per layer of the packed split-K block: q|k|v rows at 0, o at 2048, down at 3584.
+constexpr int kAccRows = 2048 + 1536 + 1536;
 __host__ __device__ constexpr int acc_row(int s) { return s == stack::kQkv ? 0 : s == stack::kO ? 2048 : 3584; }
-constexpr int kAttnCounter = 5120;
-constexpr int kMergeGroups = kKvHeads * 2;
+constexpr int kMergeGroups = kKvHeads * 2;  // attention merge groups: KV group x half of its query heads
 constexpr int kGuItems = 140;
 constexpr int kPartWords = 4 + kHeadDim;  // one attention chunk partial of one head: m, l, -, -, acc[128]
 
@@ -39,8 +37,7 @@ struct Sync {
 // Cross-CTA data of one launch. Two kinds of self-validating 64-bit words:
 //   packed split-K words (acc): bits 48..63 count the K segments added so far, bits 0..47 hold the sum of
 //     (segment total + 2^43); a consumer reads the word until the count is complete. Launch parity
-//     (epoch & 1) selects the half; each launch zeroes the other half for the next one. The attention chunk
-//     counters of the block are plain counts.
+//     (epoch & 1) selects the half; each launch zeroes the other half for the next one.
 //   tagged words (part, ctx, cmax, h, hmax, steps): bits 32..63 = ((epoch + 1) << 5 | layer), bits 0..31 =
 //     an fp32 value; a consumer reads the word until its tag is the current one. Layer parity selects the
 //     half.
