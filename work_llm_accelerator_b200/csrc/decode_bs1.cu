@@ -70,6 +70,8 @@ constexpr int kChunk = 64;         // attention keys per work item (one KV page)
 constexpr int kRow = kHeadDim + 4;
 constexpr int kHalf = 3;           // query heads per attention item
 constexpr int kMergeBatch = 8;     // chunk partials read per round trip by the merge
+// the merge's rescale factors (3 heads x chunks x 3 floats) reuse the attention chunk rows
+static_assert(kChunk * kRow >= kHalf * 3 * ((kMaxSeq + 1024) / kChunk), "rescale factors of every chunk");
 constexpr long long kSpinLimit = 2000000000ll;  // clock cycles, ~1 s
 constexpr unsigned long long kBias = 1ull << 43;
 constexpr unsigned long long kLow48 = (1ull << 48) - 1;
@@ -557,49 +559,87 @@ __device__ __forceinline__ float rope(float mine, float other, int d, float c, f
   return d < 64 ? __fsub_rn(__fmul_rn(mine, c), __fmul_rn(other, sn)) : __fadd_rn(__fmul_rn(mine, c), __fmul_rn(other, sn));
 }
 
-// Context of head h, dims d0..d0+3: the chunk partials merged in chunk order, online: M' = max(M, m_c),
-// o = o e^(M - M') + acc_c e^(m_c - M'), L likewise; out = o / L (the other decode kernels' formula). The
-// partials are read kMergeBatch chunks per round trip; a word that is not current yet is read again.
-__device__ void merge_head(const Args& a, const Worker& w, int l, int h, int nch, int d0, float (&out)[4]) {
+// The merge of one group's chunk partials (three heads), in two phases.
+//   1. warp j (< 3) = head j, lane = chunk: each lane reads its chunk's (m, l) words, a warp prefix-max scan
+//      gives the running maxima M_c = max(M_(c-1), m_c) (M_(-1) = -inf), and each lane forms its chunk's
+//      rescale factors sa_c = e^(M_(c-1) - M_c), sb_c = e^(m_c - M_c) (shared memory, with l_c);
+//   2. thread = head tid / 32, dims 4 lane .. +3: o = o sa_c + acc_c sb_c and L = L sa_c + l_c sb_c over the
+//      chunks in order; out = o / L.
+// The values and their order are those of merging chunk by chunk with the running max (the formula of the
+// other decode kernels); phase 1 only computes every exponential at once. Partials are read as tagged words,
+// waiting on the data.
+__device__ void merge_group(const Args& a, float* sab, const Worker& w, int l, int h0, int nch, float (&out)[4]) {
   const unsigned tag = tag_of(w.epoch, l);
-  float M = -INFINITY, L = 0.f, o[4] = {0.f, 0.f, 0.f, 0.f};
+  const int j = w.warp, lane = w.lane;
+  if (j < kHalf) {
+    float carry = -INFINITY;
+    for (int c0 = 0; c0 < nch; c0 += 32) {
+      const int c = c0 + lane;
+      unsigned long long mw = 0, lw = 0;
+      if (c < nch) {
+        const unsigned long long* pc = part_ptr(a, l, h0 + j, c);
+        Spin sp;
+        while (true) {
+          ld_word2(pc, mw, lw);
+          if ((tag_ok(mw, tag) && tag_ok(lw, tag)) || !sp.keep_going(w.abort_flag)) break;
+        }
+      }
+      const float mc = c < nch ? word_value(mw) : -INFINITY;
+      float x = mc;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const float y = __shfl_up_sync(0xffffffffu, x, o);
+        if (lane >= o) x = fmaxf(x, y);
+      }
+      const float Mc = fmaxf(carry, x);
+      float Mp = __shfl_up_sync(0xffffffffu, Mc, 1);
+      if (lane == 0) Mp = carry;
+      if (c < nch) {
+        float* e = sab + ((size_t)j * a.max_chunks + c) * 3;
+        e[0] = expf(Mp - Mc);
+        e[1] = expf(mc - Mc);
+        e[2] = word_value(lw);
+      }
+      carry = __shfl_sync(0xffffffffu, Mc, 31);
+    }
+  }
+  named_sync(kBarW, kWorkers);
+  if (j >= kHalf) return;
+  const int d0 = 4 * lane;
+  float L = 0.f, o[4] = {0.f, 0.f, 0.f, 0.f};
   for (int c0 = 0; c0 < nch; c0 += kMergeBatch) {
-    unsigned long long hw[kMergeBatch][2], dw[kMergeBatch][4];
+    unsigned long long dw[kMergeBatch][4];
     Spin sp;
     while (true) {
 #pragma unroll
-      for (int j = 0; j < kMergeBatch; ++j) {
-        if (c0 + j < nch) {
-          const unsigned long long* pc = part_ptr(a, l, h, c0 + j);
-          ld_word2(pc, hw[j][0], hw[j][1]);
-          ld_word2(pc + 4 + d0, dw[j][0], dw[j][1]);
-          ld_word2(pc + 6 + d0, dw[j][2], dw[j][3]);
+      for (int k = 0; k < kMergeBatch; ++k) {
+        if (c0 + k < nch) {
+          const unsigned long long* pc = part_ptr(a, l, h0 + j, c0 + k);
+          ld_word2(pc + 4 + d0, dw[k][0], dw[k][1]);
+          ld_word2(pc + 6 + d0, dw[k][2], dw[k][3]);
         }
       }
       bool ok = true;
 #pragma unroll
-      for (int j = 0; j < kMergeBatch; ++j)
-        if (c0 + j < nch)
-          ok = ok && tag_ok(hw[j][0], tag) && tag_ok(hw[j][1], tag) && tag_ok(dw[j][0], tag) &&
-               tag_ok(dw[j][1], tag) && tag_ok(dw[j][2], tag) && tag_ok(dw[j][3], tag);
+      for (int k = 0; k < kMergeBatch; ++k)
+        if (c0 + k < nch)
+          ok = ok && tag_ok(dw[k][0], tag) && tag_ok(dw[k][1], tag) && tag_ok(dw[k][2], tag) && tag_ok(dw[k][3], tag);
       if (ok || !sp.keep_going(w.abort_flag)) break;
     }
 #pragma unroll
-    for (int j = 0; j < kMergeBatch; ++j) {
-      if (c0 + j < nch) {
-        const float mc = word_value(hw[j][0]), lc = word_value(hw[j][1]);
-        const float Mn = fmaxf(M, mc);
-        const float sa = expf(M - Mn), sb = expf(mc - Mn);
+    for (int k = 0; k < kMergeBatch; ++k) {
+      if (c0 + k < nch) {
+        const float* e = sab + ((size_t)j * a.max_chunks + c0 + k) * 3;
+        const float sa = e[0], sb = e[1];
 #pragma unroll
-        for (int e = 0; e < 4; ++e) o[e] = __fadd_rn(__fmul_rn(o[e], sa), __fmul_rn(word_value(dw[j][e]), sb));
-        L = __fadd_rn(__fmul_rn(L, sa), __fmul_rn(lc, sb));
-        M = Mn;
+        for (int q = 0; q < 4; ++q) o[q] = __fadd_rn(__fmul_rn(o[q], sa), __fmul_rn(word_value(dw[k][q]), sb));
+        L = __fadd_rn(__fmul_rn(L, sa), __fmul_rn(e[2], sb));
       }
     }
   }
   const float inv = L > 0.0f ? 1.0f / L : 0.0f;
 #pragma unroll
-  for (int e = 0; e < 4; ++e) out[e] = o[e] * inv;
+  for (int q = 0; q < 4; ++q) out[q] = o[q] * inv;
 }
 
 __device__ void attn_item(const Args& a, AttnSmem& sm, Ctrl& cs, const Worker& w, int l, int nch,
@@ -726,12 +766,12 @@ __device__ void attn_item(const Args& a, AttnSmem& sm, Ctrl& cs, const Worker& w
   const int group = it.g * 2 + it.hp;
   named_sync(kBarW, kWorkers);  // this item's own partial is written
   // thread = 4 dims of one of the three heads (96 threads); the context and the group's max |ctx| as tagged
-  // words
+  // words. The chunk rows in shared memory are free now: they hold the rescale factors.
   float m = 0.0f;
+  float out[4];
+  merge_group(a, &sm.ks[0][0], w, l, q_head(it, 0), nch, out);
   if (tid < kHalf * 32) {
     const int j = tid >> 5, d0 = 4 * lane, h = q_head(it, j);
-    float out[4];
-    merge_head(a, w, l, h, nch, d0, out);
     unsigned long long* cw = a.buf.ctx + (size_t)(l & 1) * kHidden + h * kHeadDim + d0;
 #pragma unroll
     for (int e = 0; e < 4; ++e) {
@@ -754,8 +794,6 @@ __device__ void attn_item(const Args& a, AttnSmem& sm, Ctrl& cs, const Worker& w
 struct AttnPlan {
   bool active;
   int nch, total;
-  AttnItem it;
-  QkvConst qc;
 };
 
 __device__ void attention_prefetch(const Args& a, AttnSmem& sm, const Worker& w, int l, AttnPlan& p) {
@@ -764,15 +802,15 @@ __device__ void attention_prefetch(const Args& a, AttnSmem& sm, const Worker& w,
   p.active = (int)blockIdx.x < p.total;
   if (!p.active) return;
   named_sync(kBarW, kWorkers);  // the attention buffers are free (the previous layer's items are done)
-  p.it = attn_decode(a, w, l, blockIdx.x, p.nch);
-  attn_load_rows(sm, p.it, 0, p.it.nhist, w.tid);
-  qkv_const(a, w, l, p.it, p.qc);
+  const AttnItem it = attn_decode(a, w, l, blockIdx.x, p.nch);
+  attn_load_rows(sm, it, 0, it.nhist, w.tid);
 }
 
 __device__ void attention_stage(const Args& a, AttnSmem& sm, Ctrl& cs, const Worker& w, int l, const AttnPlan& p) {
   if (!p.active) return;
-  AttnItem it = p.it;
-  QkvConst qc = p.qc;
+  AttnItem it = attn_decode(a, w, l, blockIdx.x, p.nch);
+  QkvConst qc;
+  qkv_const(a, w, l, it, qc);
   if (w.tid == 0) stamp(a, l, stack::kTraceWait + 1);
   for (int i = blockIdx.x;;) {
     attn_item(a, sm, cs, w, l, p.nch, it, qc);
