@@ -516,7 +516,7 @@ def run_b200(args, world: int, rank: int, local: int) -> dict | None:
     sb = step_bytes(wbits, history_mid)
     step_achieved = sb / (ms * 1e-3) / 1e9
     traffic = None
-    tr = ROOT / "profiles" / "decode_stack_w8_bs1_dram.json"
+    tr = ROOT / "profiles" / "decode_bs1_w8_bs1_dram.json"
     if tr.exists() and wbits == 8:
         d = json.loads(tr.read_text())
         traffic = d.get("dram_bytes_per_launch")
@@ -582,7 +582,7 @@ def run_b200(args, world: int, rank: int, local: int) -> dict | None:
         "config": bench_config(world, args.warmup, args.steps, wbits),
         "e2e": {"value": world / (ms_e2e * 1e-3), "unit": "tok/s", "h2d_bytes_per_step": 12, "d2h_bytes_per_step": 4},
         "roofline": {"bound": "hbm",
-                     "kernel": ("decode_stack_kernel: persistent 28-layer W8 decode step (1 launch per step)"
+                     "kernel": ("decode_bs1_kernel: persistent 28-layer W8 batch-1 decode step (1 launch per step)"
                                 if wbits == 8 else "28 layers x 5 CUDA-core kernels (W4)"),
                      "achieved": layers_achieved, "peak": peak, "unit": "GB/s", "frac": layers_achieved / peak,
                      "traffic": traffic, "peak_source": peak_kind, "algorithmic_bytes_per_launch": lb,

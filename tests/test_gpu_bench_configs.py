@@ -1,7 +1,8 @@
 """The benchmarked GPU paths compared directly with the oracle at the benchmark configurations' shapes.
 
-- Config 2: every layer of the persistent 28-layer decode kernel (`decode_stack_kernel`, the bench line's
-  kernel) at history 517 after a 512-token prompt. Each layer's input (the engine's own previous-layer output)
+- Config 2: every layer of the persistent 28-layer decode kernel (`decode_bs1_kernel`, the bench line's
+  kernel; the tensor-core `decode_stack_kernel` gives bit-identical layers) at history 517 after a 512-token
+  prompt. Each layer's input (the engine's own previous-layer output)
   and K/V history go to the oracle's decode layer (W8). The oracle's bf16-rounded output must match the
   engine's per element within one bf16 unit in the last place plus 1e-5 of the row's RMS, every layer within
   north_star's 1e-3 relative L2, and the new K/V rows within 1e-5.
