@@ -261,6 +261,21 @@ def test_persistent_step_kernels_match_separate_kernels(host, prompt_len):
         assert np.array_equal(b, c), ("stack", step, rel_l2(b, c))
 
 
+def test_batch1_kernel_long_history(host):
+    """A 2500-token history gives 40 attention chunks: 160 chunk items for 148 CTAs, so some CTAs run two
+    items (a merging item waits only on items of lower index) and the merge's running-max scan spans two
+    32-chunk windows. Every layer's output equals the separate kernels' over three steps."""
+    rng = np.random.default_rng(2500)
+    prompt = [int(t) for t in rng.integers(0, qo.VOCAB, 2500)]
+    host.kernel_error(reset=True)
+    toks_1, hid_1 = _decode_trace(host, 9, prompt, 3, max_len=2600, stack=1, bs1=1)
+    assert host.kernel_error(reset=True) == 0
+    toks_k, hid_k = _decode_trace(host, 9, prompt, 3, max_len=2600, stack=0)
+    assert toks_1 == toks_k
+    for step, (a, b) in enumerate(zip(hid_1, hid_k)):
+        assert np.array_equal(a, b), (step, rel_l2(a, b))
+
+
 def test_batch1_kernel_over_many_launches(host):
     """The batch-1 persistent kernel keeps launch-parity words (zeroed by the following launch) and tagged
     words (launch epoch and layer in the tag): 40 consecutive steps with the trace option on, each equal
