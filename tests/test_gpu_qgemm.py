@@ -108,7 +108,8 @@ def test_digit_products_rejects_bad_shapes(built_libs, gpu_available):
     (256, 1536, 130),   # two token tiles, the second ragged
     (2048, 1536, 300),  # q|k|v rows, three token tiles
     (2048, 1536, 64),   # one 64-token tile, few row tiles: K split over 8-CTA clusters
-    (9728, 1536, 33),   # one 64-token tile, many row tiles: the CTA-pair form
+    (9728, 1536, 33),   # one 64-token tile, many row tiles: the CTA-pair form, one wave (two MMA issuers)
+    (9728, 1536, 200),  # four token tiles: CTA pairs beyond one wave (one issuer, two CTAs per SM)
     (128, 8960, 129),   # down_proj K, ragged tokens
     (256, 8960, 2433),  # many token tiles: the CTA-pair form (256-row tiles), ragged tokens
 ])

@@ -43,19 +43,29 @@ constexpr int kMaxStages = 8;
 // tcgen05.mma.cta_group::2 (M = 256, N = 192); each holds its 128 weight rows and half of the 192 digit-plane
 // rows, so a stage moves 16 + 12 KB per CTA instead of 16 + 24 KB; three stages, two CTAs per SM.
 constexpr int kPairST = 3;
+// ST = kPairDualST: the CTA-pair form with one CTA per SM (grids of one wave): a second MMA-issuing warp
+// takes every other K block into a second accumulator (the epilogue adds the two exact int32 sums), so two
+// issue streams run per tile, with six stages. Each issuing thread completes about one MMA per 147 ns
+// whatever N is, so a tile's main loop is bound by its MMA count per issuer when the grid is one wave.
+constexpr int kPairDualST = 4;
 template <int TN, int ST = 0>
 struct TCfg {
-  static constexpr bool kPair = ST == kPairST;
+  static constexpr bool kPair = ST == kPairST || ST == kPairDualST;
+  static constexpr bool kDual = ST == kPairDualST;
+  static constexpr int kThreads = kDual ? kThreadsT + 32 : kThreadsT;
+  static constexpr int kAccStride = 256;  // TMEM columns between the two accumulators (kDual)
   static constexpr int kPlaneTile = TN * kKBlock;
   static constexpr int kStage = kUnitBytes + (kPair ? kPlanes * kPlaneTile / 2 : kPlanes * kPlaneTile);
   static constexpr int kAutoStages = (200 * 1024) / kStage > kMaxStages ? kMaxStages : (200 * 1024) / kStage;
-  static constexpr int kStages = ST > 0 ? ST : kAutoStages;
+  static constexpr int kStages = kDual ? 6 : ST > 0 ? ST : kAutoStages;
   // The three plane tiles sit back to back in a stage, which is the layout of one 3 TN-row tile: up to
   // N = 256 one MMA covers all three planes (accumulator column p TN + n = plane p, token n).
   static constexpr bool kFused = kPlanes * TN <= 256;
   static constexpr uint32_t kIdesc = idesc_i8(kPair ? 2 * kTileM : kTileM, kFused ? kPlanes * TN : TN);
-  static constexpr int kTmemCols = kPlanes * TN <= 32 ? 32 : kPlanes * TN <= 64 ? 64 : kPlanes * TN <= 128 ? 128
+  static constexpr int kTmemCols = kDual ? 512
+                                   : kPlanes * TN <= 32 ? 32 : kPlanes * TN <= 64 ? 64 : kPlanes * TN <= 128 ? 128
                                    : kPlanes * TN <= 256 ? 256 : 512;
+  static_assert(!kDual || kPlanes * TN <= kAccStride, "two accumulators side by side");
   static_assert(TN % 16 == 0 && TN <= 128, "token tile");
   static_assert(!kPair || TN == 64, "the pair form splits 3 x 64 plane rows into two halves of 96");
 };
@@ -177,7 +187,7 @@ __device__ __forceinline__ void mma_t(uint32_t d, uint64_t a, uint64_t b, uint32
 }
 
 template <int EPI, int TN, int ST>
-__global__ void __launch_bounds__(kThreadsT, (ST == 2 || ST == kPairST) ? 2 : 1)
+__global__ void __launch_bounds__(TCfg<TN, ST>::kThreads, (ST == 2 || ST == kPairST) ? 2 : 1)
     tgemm_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ CUtensorMap pmap, TArgs a) {
   using C = TCfg<TN, ST>;
   constexpr int kTN = TN;
@@ -203,7 +213,7 @@ __global__ void __launch_bounds__(kThreadsT, (ST == 2 || ST == kPairST) ? 2 : 1)
       mbar_init(&sm.full[s], 1);
       mbar_init(&sm.empty[s], 1);
     }
-    mbar_init(&sm.acc_full, 1);
+    mbar_init(&sm.acc_full, C::kDual ? 2 : 1);
     mbar_fence_init();
   }
   if (warp == 1) {
@@ -287,34 +297,41 @@ __global__ void __launch_bounds__(kThreadsT, (ST == 2 || ST == kPairST) ? 2 : 1)
         }
       }
     }
-  } else if (warp == 1) {
+  } else if (warp == 1 || (C::kDual && warp == 6)) {
+    // issuer 0 (warp 1) takes every K block, or with kDual the even ones (K block index from kb_lo) into the
+    // first accumulator and issuer 1 (warp 6) the odd ones into the second
+    const int iss = warp == 1 ? 0 : 1;
     if (lane == 0 && (!kPair || prank == 0)) {
       int s = 0;
       unsigned ph = 0;
-      bool ok = true;
+      bool ok = true, first = true;
+      const uint32_t dacc = tmem + (uint32_t)(iss * C::kAccStride);
       for (int kb = kb_lo; kb < kb_hi; ++kb) {
-        ok = ok && mbar_wait(&sm.full[s], ph);
-        fence_after();
-        if (ok) {
-          const uint32_t sb = smem_u32(stages + (size_t)s * kStageBytes);
-          const uint64_t ad = sw128_desc(sb);
+        if (!C::kDual || ((kb - kb_lo) & 1) == iss) {
+          ok = ok && mbar_wait(&sm.full[s], ph);
+          fence_after();
+          if (ok) {
+            const uint32_t sb = smem_u32(stages + (size_t)s * kStageBytes);
+            const uint64_t ad = sw128_desc(sb);
 #pragma unroll
-          for (int p = 0; p < (C::kFused ? 1 : kPlanes); ++p) {
-            const uint64_t bd = sw128_desc(sb + kUnitBytes + p * kPlaneTile);
+            for (int p = 0; p < (C::kFused ? 1 : kPlanes); ++p) {
+              const uint64_t bd = sw128_desc(sb + kUnitBytes + p * kPlaneTile);
 #pragma unroll
-            for (int j = 0; j < kKBlock / 32; ++j) {
-              if constexpr (kPair)
-                mma_pair<C::kIdesc>(tmem + p * kTN, ad + 2 * j, bd + 2 * j, (kb > kb_lo || j > 0) ? 1u : 0u);
-              else
-                mma_t<C::kIdesc>(tmem + p * kTN, ad + 2 * j, bd + 2 * j, (kb > kb_lo || j > 0) ? 1u : 0u);
+              for (int j = 0; j < kKBlock / 32; ++j) {
+                if constexpr (kPair)
+                  mma_pair<C::kIdesc>(dacc + p * kTN, ad + 2 * j, bd + 2 * j, (!first || j > 0) ? 1u : 0u);
+                else
+                  mma_t<C::kIdesc>(dacc + p * kTN, ad + 2 * j, bd + 2 * j, (!first || j > 0) ? 1u : 0u);
+              }
             }
           }
-        }
-        if constexpr (kPair) {  // both CTAs' stage s is free once the pair MMAs finished
-          mma_commit_pair(smem_u32(&sm.empty[s]));
-          mma_commit_pair(peer_addr(smem_u32(&sm.empty[s]), 1));
-        } else {
-          mma_commit(&sm.empty[s]);
+          first = false;
+          if constexpr (kPair) {  // both CTAs' stage s is free once the pair MMAs finished
+            mma_commit_pair(smem_u32(&sm.empty[s]));
+            mma_commit_pair(peer_addr(smem_u32(&sm.empty[s]), 1));
+          } else {
+            mma_commit(&sm.empty[s]);
+          }
         }
         if (++s == kStagesT) {
           s = 0;
@@ -354,7 +371,7 @@ __global__ void __launch_bounds__(kThreadsT, (ST == 2 || ST == kPairST) ? 2 : 1)
       }
     }
   };
-  if (warp >= 2) {
+  if (warp >= 2 && warp < 6) {
     if constexpr (EPI == kTGateUp) {
       row = r < 64 ? mtile * 64 + r : a.second_row0 + mtile * 64 + (r - 64);
     } else {
@@ -371,7 +388,7 @@ __global__ void __launch_bounds__(kThreadsT, (ST == 2 || ST == kPairST) ? 2 : 1)
   }
   if (ks > 1) {
     cluster_sync_all();  // every CTA's main loop done: the cluster's stage memory is free
-    if (warp >= 2) {
+    if (warp >= 2 && warp < 6) {
       const uint32_t lane_base = tmem + ((uint32_t)(q * 32) << 16);
       const uint32_t ib = smem_u32(stages);
       for (int c0 = 0; c0 < kPlanes * kTN; c0 += kChunkN) {
@@ -392,7 +409,7 @@ __global__ void __launch_bounds__(kThreadsT, (ST == 2 || ST == kPairST) ? 2 : 1)
     }
     cluster_sync_all();  // every partial delivered
   }
-  if (warp >= 2) {
+  if (warp >= 2 && warp < 6) {
     const uint32_t lane_base = tmem + ((uint32_t)(q * 32) << 16);
     for (int c0 = tb; c0 < te && n0 + c0 < a.S; c0 += kChunkN) {  // chunks holding real tokens only
       if (c0 != tb) chunk_loads(c0);
@@ -415,6 +432,18 @@ __global__ void __launch_bounds__(kThreadsT, (ST == 2 || ST == kPairST) ? 2 : 1)
         tmem_ld16(lane_base + c0, v0);
         tmem_ld16(lane_base + kTN + c0, v1);
         tmem_ld16(lane_base + 2 * kTN + c0, v2);
+        if constexpr (C::kDual) {  // the second issuer's K blocks (every issuer has at least one)
+          int u[16];
+          tmem_ld16(lane_base + C::kAccStride + c0, u);
+#pragma unroll
+          for (int c = 0; c < 16; ++c) v0[c] += u[c];
+          tmem_ld16(lane_base + C::kAccStride + kTN + c0, u);
+#pragma unroll
+          for (int c = 0; c < 16; ++c) v1[c] += u[c];
+          tmem_ld16(lane_base + C::kAccStride + 2 * kTN + c0, u);
+#pragma unroll
+          for (int c = 0; c < 16; ++c) v2[c] += u[c];
+        }
       } else {
 #pragma unroll
         for (int c = 0; c < 16; ++c) v0[c] = v1[c] = v2[c] = 0;
@@ -854,6 +883,7 @@ cudaError_t run_tgemm_tn(const uint8_t* w, int rows_total, int K, int mtiles, in
   a.ksplit = ksplit;
   CUtensorMap wmap, pmap;
   if (C::kPair && ((mtiles & 1) || ksplit != 1 || K / kKBlock < C::kStages)) return cudaErrorInvalidValue;
+  if (C::kDual && K / kKBlock < 2) return cudaErrorInvalidValue;  // each issuer needs a K block
   if (!make_map(&wmap, w, (uint64_t)rows_total, (uint64_t)K, (uint32_t)box_rows) ||
       !make_map(&pmap, x.planes, (uint64_t)kPlanes * x.Spad, (uint64_t)K, C::kPair ? 32u : (uint32_t)TN))
     return cudaErrorInvalidValue;
@@ -880,7 +910,7 @@ cudaError_t run_tgemm_tn(const uint8_t* w, int rows_total, int K, int mtiles, in
   }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(mtiles * ksplit, x.Spad / TN);
-  cfg.blockDim = dim3(kThreadsT);
+  cfg.blockDim = dim3(C::kThreads);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = s;
   cudaLaunchAttribute at[2];
@@ -911,8 +941,12 @@ cudaError_t run_tgemm(const uint8_t* w, int rows_total, int K, int mtiles, int b
   // 33-64 tokens: every row tile re-reads the token digit planes, which already outweigh its weights, so
   // the planes' traffic sets the time: CTA pairs (each CTA stages half of the planes) where the row tiles
   // pair up; K split (long K only: measured slower for the short-K projections) for the down projection.
+  // A grid of CTA pairs that fits one wave of the 148 SMs takes the two-issuer form (one CTA per SM).
+  const bool one_wave = mtiles * (x.Spad / 64) <= 148;
   if (x.Spad == 64) {
     const int ks = nkb >= 32 ? pick_ksplit(mtiles, nkb) : 1;
+    if (ks == 1 && (mtiles & 1) == 0 && one_wave && nkb >= TCfg<64, kPairDualST>::kStages)
+      return run_tgemm_tn<EPI, 64, kPairDualST>(w, rows_total, K, mtiles, box_rows, second_row0, x, a, s);
     if (ks == 1 && (mtiles & 1) == 0 && nkb >= TCfg<64, kPairST>::kStages)
       return run_tgemm_tn<EPI, 64, kPairST>(w, rows_total, K, mtiles, box_rows, second_row0, x, a, s);
     return run_tgemm_tn<EPI, 64>(w, rows_total, K, mtiles, box_rows, second_row0, x, a, s, ks);
@@ -920,6 +954,8 @@ cudaError_t run_tgemm(const uint8_t* w, int rows_total, int K, int mtiles, int b
   if (x.Spad >= 128) {  // many tokens: 64-token tiles, two CTAs per SM unless K is split (long K only)
     const int ks = nkb >= 32 ? pick_ksplit(mtiles * (x.Spad / 64), nkb) : 1;
     if (ks > 1) return run_tgemm_tn<EPI, 64>(w, rows_total, K, mtiles, box_rows, second_row0, x, a, s, ks);
+    if ((mtiles & 1) == 0 && one_wave && nkb >= TCfg<64, kPairDualST>::kStages)
+      return run_tgemm_tn<EPI, 64, kPairDualST>(w, rows_total, K, mtiles, box_rows, second_row0, x, a, s);
     if ((mtiles & 1) == 0 && nkb >= TCfg<64, kPairST>::kStages)  // CTA pairs: 256-row tiles
       return run_tgemm_tn<EPI, 64, kPairST>(w, rows_total, K, mtiles, box_rows, second_row0, x, a, s);
     return run_tgemm_tn<EPI, 64, 2>(w, rows_total, K, mtiles, box_rows, second_row0, x, a, s);
