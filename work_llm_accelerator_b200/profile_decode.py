@@ -12,6 +12,11 @@
     python -m work_llm_accelerator_b200.profile_decode batched --batch 64 --prompt 2048 --steps 8
         prefills `batch` sequences, then times device-resident greedy decode steps of all of them
         together (the batched W8 path) and prints tokens/s.
+    python -m work_llm_accelerator_b200.profile_decode trace --wbits 8 --prompt 512 --steps 6
+        runs W8 batch-1 decode steps with the engine's "trace" option and prints the persistent kernel's
+        per-layer timeline of the last step: for each stage the time (us, latest CTA) at which its inputs
+        were held, its digits built and its results published, median over layers 1-26, from the moment the
+        last q|k|v CTA held its inputs.
 
 The modes hold about 2.2 GB (W8) of weights on the device plus the KV pool of their sequences.
 --profile-range brackets the timed part with cudaProfilerStart/Stop, so that
@@ -28,9 +33,40 @@ import numpy as np
 from . import host
 
 
+# Trace slots of the persistent kernels (decode_stack.h kTrace*): per stage i (0 q|k|v, 1 attention, 2 o_proj,
+# 3 gate|up, 4 down) inputs held (0 + i), digits built (5 + i) and done (10 + i); attention: q ready (34),
+# chunk partial stored (35), group merged (36).
+_TRACE_EVENTS = {"qkv_inputs": 0, "qkv_built": 5, "qkv_done": 10, "attn_q": 34, "attn_chunk": 35,
+                 "attn_merged": 36, "o_built": 7, "o_done": 12, "gate_up_inputs": 3, "gate_up_built": 8,
+                 "gate_up_done": 13, "down_inputs": 4, "down_built": 9, "down_done": 14}
+
+
+def trace_timeline(eng, prompt_len: int, steps: int) -> dict:
+    """Per-layer stage timeline of one traced W8 batch-1 decode step (the last of `steps`)."""
+    eng.set_option("trace", 1)
+    prompt = np.random.default_rng(1).integers(0, 151936, prompt_len).astype(np.int32)
+    tok = eng.prefill(0, prompt)
+    for _ in range(steps):
+        tok = int(eng.decode([0], [tok])[0])
+    tr = eng.read_trace(148).astype(np.int64)  # [ctas][28][slots], global-timer ns, 0 = not stamped
+    layers = []
+    for l in range(tr.shape[1]):
+        t = tr[:, l, :]
+        latest = {k: int(t[:, slot].max()) for k, slot in _TRACE_EVENTS.items()}
+        layers.append(latest)
+    out = {}
+    for k in _TRACE_EVENTS:
+        vals = [(layers[l][k] - layers[l]["qkv_inputs"]) / 1e3 for l in range(1, tr.shape[1] - 1) if layers[l][k] > 0]
+        if vals:
+            out[k] = round(float(np.median(vals)), 2)
+    per_layer = [(layers[l + 1]["qkv_inputs"] - layers[l]["qkv_inputs"]) / 1e3 for l in range(1, tr.shape[1] - 2)]
+    out["layer_us"] = round(float(np.median(per_layer)), 2)
+    return {"prompt": prompt_len, "steps": steps, "median_us_from_qkv_inputs": out}
+
+
 def main(argv=None) -> int:
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
-    ap.add_argument("mode", choices=["kernels", "steps", "prefill", "batched"])
+    ap.add_argument("mode", choices=["kernels", "steps", "prefill", "batched", "trace"])
     ap.add_argument("--batch", type=int, default=64, help="batched: sequences decoded together")
     ap.add_argument("--wbits", type=int, default=8, choices=[4, 8])
     ap.add_argument("--seed", type=int, default=7)
@@ -91,6 +127,8 @@ def main(argv=None) -> int:
         elif a.mode == "kernels":
             us = eng.profile_kernels(1, a.past, iters=a.iters)
             print(json.dumps({k: round(v * 1000.0, 3) for k, v in us.items()}))
+        elif a.mode == "trace":
+            print(json.dumps(trace_timeline(eng, a.prompt, a.steps)))
         else:
             eng.set_option("graphs", a.graphs)
             prompt = np.random.default_rng(1).integers(0, 151936, a.prompt).astype(np.int32)
