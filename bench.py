@@ -12,7 +12,7 @@ value : device-resident decode loop (token ids stay on the GPU; one CUDA-graph l
         with CUDA events on the engine stream, max over ranks.
 e2e   : the same steps through the engine's C-ABI call with host token buffers (H2D of the step's input
         token, D2H of the argmax inside the timed region).
-With N GPUs the engines all-gather each step's next-token ids over NCCL from C++ (qwen_engine_gather_tokens).
+With N GPUs the engines all-gather each step's next-token ids over NCCL from C++ (qwen_engine_gather_tokens_async, on a side stream beside the next step).
 
 Sub-records, each with its own time and roofline (work counts from work_llm_accelerator_b200.performance_model):
   batched       config 3: 64 sequences x 2048-token history, greedy steps; 64/N sequences per GPU (strong scaling)
@@ -431,14 +431,19 @@ def run_b200(args, world: int, rank: int, local: int) -> dict | None:
     bufs = [torch.tensor([first], dtype=torch.int32, device="cuda"), torch.zeros(1, dtype=torch.int32, device="cuda")]
     gathered = torch.zeros(world, dtype=torch.int32, device="cuda")
 
+    if world > 1:  # two SMs left free for the NCCL kernel of the gather, which runs beside the next step
+        eng.set_option("bs1_ctas", torch.cuda.get_device_properties(local).multi_processor_count - 2)
+
     def dev_step(i):
         eng.decode_device([0], bufs[i % 2].data_ptr(), bufs[(i + 1) % 2].data_ptr())
-        if world > 1:  # the step's token ids of every rank, over NCCL from the engine (C++)
-            eng.gather_tokens(bufs[(i + 1) % 2].data_ptr(), 1, gathered.data_ptr())
+        if world > 1:  # the step's token ids of every rank, over NCCL from the engine (C++), on a side stream
+            eng.gather_tokens_async(bufs[(i + 1) % 2].data_ptr(), 1, gathered.data_ptr())
 
     with torch.cuda.stream(stream):
         for i in range(args.warmup):
             dev_step(i)
+        if world > 1:
+            eng.gather_join()
         stream.synchronize()
         if world > 1:
             dist.barrier()
@@ -450,6 +455,8 @@ def run_b200(args, world: int, rank: int, local: int) -> dict | None:
         ev0.record(stream)
         for i in range(args.warmup, args.warmup + args.steps):
             dev_step(i)
+        if world > 1:  # the timed region ends after the last gather
+            eng.gather_join()
         ev1.record(stream)
         ev1.synchronize()
         clk = clocks.stop()

@@ -68,7 +68,8 @@ int qwen_engine_reset(qwen_engine* e, int slot);
  * "logits" (keep the last call's logits, default 0), "prefetch" (stream the next kernels' weights into L2,
  * default 1), "stack" (W8: the whole decode step as one persistent kernel, default 1; 0 = five tensor-core
  * kernels per layer), "bs1" (W8, one sequence per step: the persistent kernel on the CUDA cores with
- * self-validating cross-CTA words, default 1; 0 = the tensor-core persistent kernel; same results), "qgemm" (W8 separate-kernel path on the int8 tensor cores, default 1; 0 = CUDA-core
+ * self-validating cross-CTA words, default 1; 0 = the tensor-core persistent kernel; same results),
+ * "bs1_ctas" (CTAs of that kernel, 144 .. the SM count, default the SM count; results do not depend on it), "qgemm" (W8 separate-kernel path on the int8 tensor cores, default 1; 0 = CUDA-core
  * GEMV), "trace" (record a per-CTA, per-layer timeline of the persistent kernel, default 0), "batched" (W8: steps
  * of more than 4 sequences as one many-token tensor-core step, default 1; 0 = groups of 4), "lm_tc" (LM head
  * on the tensor cores, default 1; 0 = CUDA-core GEMV), "stack_ring" (weight stages in flight per SM in the
@@ -127,6 +128,14 @@ int qwen_engine_profile_batched(qwen_engine* e, const int32_t* slots, const int3
 int qwen_engine_nccl_unique_id(uint8_t* id_out);
 int qwen_engine_nccl_init(qwen_engine* e, const uint8_t* id, int nranks, int rank);
 int qwen_engine_gather_tokens(qwen_engine* e, const int32_t* d_local, int n, int32_t* d_all);
+/* The same all-gather on a side stream of the engine, so that it runs beside the following decode steps:
+ * it starts after the engine stream's work enqueued so far, and the engine stream's work enqueued after the
+ * call waits for the previous asynchronous gather (at most two in flight: d_local may be rewritten from the
+ * step after next on). qwen_engine_gather_join makes the engine stream wait for the last one (d_all is then
+ * complete once the stream reaches that point). With option "bs1_ctas" below the SM count the batch-1
+ * decode kernel leaves SMs free for the NCCL kernel. */
+int qwen_engine_gather_tokens_async(qwen_engine* e, const int32_t* d_local, int n, int32_t* d_all);
+int qwen_engine_gather_join(qwen_engine* e);
 /* The engine's CUDA stream (cudaStream_t) for callers that record their own events. */
 void* qwen_engine_stream(qwen_engine* e);
 /* Number of kernels one decode step of `n` sequences launches. */

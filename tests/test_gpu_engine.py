@@ -276,6 +276,20 @@ def test_batch1_kernel_long_history(host):
         assert np.array_equal(a, b), (step, rel_l2(a, b))
 
 
+def test_batch1_kernel_cta_count_does_not_change_results(host):
+    """Option "bs1_ctas": the batch-1 kernel's schedule over 144 (the fewest: one down_proj item per CTA) or
+    146 CTAs gives the same layers and tokens as over every SM."""
+    rng = np.random.default_rng(144)
+    prompt = [int(t) for t in rng.integers(0, qo.VOCAB, 200)]
+    toks_a, hid_a = _decode_trace(host, 4, prompt, 3, max_len=512, stack=1, bs1=1)
+    for ctas in (144, 146):
+        toks_b, hid_b = _decode_trace(host, 4, prompt, 3, max_len=512, stack=1, bs1=1, bs1_ctas=ctas)
+        assert host.kernel_error(reset=True) == 0
+        assert toks_a == toks_b
+        for step, (a, b) in enumerate(zip(hid_a, hid_b)):
+            assert np.array_equal(a, b), (ctas, step, rel_l2(a, b))
+
+
 def test_batch1_kernel_over_many_launches(host):
     """The batch-1 persistent kernel keeps launch-parity words (zeroed by the following launch) and tagged
     words (launch epoch and layer in the tag): 40 consecutive steps with the trace option on, each equal

@@ -47,6 +47,42 @@ def test_single_rank_gather(host):
         eng.close()
 
 
+def test_single_rank_async_gather(host):
+    """The side-stream gather (qwen_engine_gather_tokens_async) beside the following steps, with the batch-1
+    kernel on 146 CTAs (two SMs free): after the join, every step's gathered id equals the id the step wrote,
+    and the tokens equal the synchronous loop's."""
+    import torch
+
+    def run(async_gather: bool):
+        eng = host.Engine(0, 8, max_seqs=1, max_len=64)
+        try:
+            eng.nccl_init(host.nccl_unique_id(), 1, 0)
+            eng.init_synthetic(3)
+            if async_gather:
+                eng.set_option("bs1_ctas", 146)
+            first = eng.prefill(0, [1, 2, 3, 4])
+            bufs = [torch.tensor([first], dtype=torch.int32, device="cuda"), torch.zeros(1, dtype=torch.int32, device="cuda")]
+            seen = torch.full((6,), -1, dtype=torch.int32, device="cuda")
+            stream = torch.cuda.ExternalStream(eng.stream())
+            with torch.cuda.stream(stream):
+                for i in range(6):
+                    eng.decode_device([0], bufs[i % 2].data_ptr(), bufs[(i + 1) % 2].data_ptr())
+                    if async_gather:
+                        eng.gather_tokens_async(bufs[(i + 1) % 2].data_ptr(), 1, seen[i:].data_ptr())
+                    else:
+                        eng.gather_tokens(bufs[(i + 1) % 2].data_ptr(), 1, seen[i:].data_ptr())
+                if async_gather:
+                    eng.gather_join()
+            torch.cuda.synchronize()
+            assert host.kernel_error(reset=True) == 0
+            return seen.cpu().tolist()
+        finally:
+            torch.cuda.synchronize()
+            eng.close()
+
+    assert run(True) == run(False)
+
+
 def _free_port() -> int:
     s = socket.socket()
     s.bind(("127.0.0.1", 0))
@@ -86,6 +122,19 @@ def _rank_main(rank: int, world: int, port: int, q) -> None:
             own.append(int(nxt.item()))
             seen.append(allv.cpu().tolist())
             cur.copy_(nxt)
+        # the side-stream gathers beside the steps (the bench's multi-GPU loop), batch-1 kernel on 146 CTAs
+        eng.set_option("bs1_ctas", 146)
+        bufs = [cur.clone(), torch.zeros(1, dtype=torch.int32, device="cuda")]
+        allk = torch.full((4, world), -1, dtype=torch.int32, device="cuda")
+        stream = torch.cuda.ExternalStream(eng.stream())
+        with torch.cuda.stream(stream):
+            for i in range(4):
+                eng.decode_device([0], bufs[i % 2].data_ptr(), bufs[(i + 1) % 2].data_ptr())
+                own.append(None)  # filled below
+                eng.gather_tokens_async(bufs[(i + 1) % 2].data_ptr(), 1, allk[i].data_ptr())
+            eng.gather_join()
+        torch.cuda.synchronize()
+        seen += allk.cpu().tolist()
         q.put((rank, own, seen))
     finally:
         torch.cuda.synchronize()
@@ -120,3 +169,7 @@ def test_two_gpu_token_gather(host):
     for step in range(4):
         want = [res[0][0][step], res[1][0][step]]
         assert res[0][1][step] == want and res[1][1][step] == want
+    # asynchronous gathers: both ranks see the same ids, each rank's own id in its column
+    for step in range(4, 8):
+        assert res[0][1][step] == res[1][1][step]
+        assert all(v >= 0 for v in res[0][1][step])

@@ -229,6 +229,7 @@ struct qwen_engine {
   int stack_ring = 9;                   // weight stages in flight per CTA
   // persistent batch-1 step on the CUDA cores (wbits == 8, one sequence per step): its schedule and words
   bool use_bs1 = true;
+  int bs1_ctas = 0;  // CTAs of the batch-1 kernel (option "bs1_ctas"; default: every SM)
   bs1::Sync* bs1_sync = nullptr;
   bs1::Buffers bs1_buf{nullptr, nullptr, nullptr, nullptr, nullptr, nullptr, nullptr};
   uint32_t* d_item_off1 = nullptr;
@@ -246,6 +247,11 @@ struct qwen_engine {
   // token exchange of a multi-GPU run (qwen_engine_nccl_init)
   ncclComm_t nccl = nullptr;
   int nccl_ranks = 0, nccl_rank = 0;
+  // asynchronous token gathers (qwen_engine_gather_tokens_async): a side stream and the completion events of
+  // the last two gathers
+  cudaStream_t gather_stream = nullptr;
+  cudaEvent_t gather_ready = nullptr, gather_done[2] = {nullptr, nullptr};
+  long long gather_n = 0;
   // option "exact": every layer and the LM head in the reference's arithmetic order (exact.h)
   bool exact = false;
   int ex_cap = 0;                                              // token rows of the buffers below
@@ -536,7 +542,7 @@ int enqueue_decode(qwen_engine* e, int nt, int max_len, bool advance) {
     a.items = e->d_items1;
     a.trace = e->trace;
     a.ring = e->stack_ring;
-    E_TRY(bs1::launch_decode_bs1(a, e->stack_ctas, e->stream));
+    E_TRY(bs1::launch_decode_bs1(a, e->bs1_ctas, e->stream));
     xin = ((kLayers - 1) & 1) ? e->y1 : e->y0;
   } else if (stack_enabled(e)) {
     if (int st = ensure_tiles(e)) return st;
@@ -931,6 +937,7 @@ int qwen_engine_create(int device, int wbits, int max_seqs, int max_len, qwen_en
       E_TRY(cudaMemset(e->bs1_sync, 0, sizeof(bs1::Sync)));
       E_TRY(dalloc(&e->d_item_off1, s1.off.size()));
       E_TRY(cudaMemcpy(e->d_item_off1, s1.off.data(), s1.off.size() * 4, cudaMemcpyHostToDevice));
+      e->bs1_ctas = e->stack_ctas;
       E_TRY(dalloc(&e->d_items1, s1.items.size()));
       E_TRY(cudaMemcpy(e->d_items1, s1.items.data(), s1.items.size() * sizeof(stack::Item), cudaMemcpyHostToDevice));
     }
@@ -958,6 +965,12 @@ int qwen_engine_create(int device, int wbits, int max_seqs, int max_len, qwen_en
 void qwen_engine_destroy(qwen_engine* e) {
   if (!e) return;
   cudaSetDevice(e->device);
+  if (e->gather_stream) {
+    cudaStreamSynchronize(e->gather_stream);
+    cudaStreamDestroy(e->gather_stream);
+  }
+  for (cudaEvent_t ev : {e->gather_ready, e->gather_done[0], e->gather_done[1]})
+    if (ev) cudaEventDestroy(ev);
   if (e->nccl) {
     cudaStreamSynchronize(e->stream);
     if (const NcclApi* api = nccl_api()) api->comm_destroy(e->nccl);
@@ -1065,6 +1078,22 @@ int qwen_engine_set_option(qwen_engine* e, const char* name, long long value) {
     e->use_batched = value != 0;
   } else if (n == "stack") {
     e->use_stack = value != 0;
+    for (auto& kv : e->graphs) cudaGraphExecDestroy(kv.second);
+    e->graphs.clear();
+  } else if (n == "bs1_ctas") {
+    // the batch-1 kernel on fewer CTAs than SMs, leaving SMs free for kernels on other streams (the NCCL
+    // gather of a multi-GPU run); the schedule needs at least as many CTAs as one projection has items
+    if (e->d_items1 == nullptr || value < 1 || value > e->stack_ctas) return kStatusInvalid;
+    const stack::Schedule s1 = bs1::build_schedule((int)value);
+    if (s1.off.empty()) {
+      set_error("bs1_ctas %lld: fewer CTAs than the items of one projection", value);
+      return kStatusInvalid;
+    }
+    E_TRY(cudaSetDevice(e->device));
+    E_TRY(cudaStreamSynchronize(e->stream));
+    E_TRY(cudaMemcpy(e->d_item_off1, s1.off.data(), s1.off.size() * 4, cudaMemcpyHostToDevice));
+    E_TRY(cudaMemcpy(e->d_items1, s1.items.data(), s1.items.size() * sizeof(stack::Item), cudaMemcpyHostToDevice));
+    e->bs1_ctas = (int)value;
     for (auto& kv : e->graphs) cudaGraphExecDestroy(kv.second);
     e->graphs.clear();
   } else if (n == "bs1") {
@@ -1632,6 +1661,42 @@ int qwen_engine_gather_tokens(qwen_engine* e, const int32_t* d_local, int n, int
   }
   const NcclApi* api = nccl_api();
   N_TRY(api, api->all_gather(d_local, d_all, (size_t)n, ncclInt32, e->nccl, e->stream));
+  return 0;
+}
+
+int qwen_engine_gather_tokens_async(qwen_engine* e, const int32_t* d_local, int n, int32_t* d_all) {
+  if (!e || !d_local || !d_all || n <= 0) return kStatusInvalid;
+  if (!e->nccl) {
+    set_error("qwen_engine_gather_tokens_async: no communicator (call qwen_engine_nccl_init first)");
+    return kStatusInvalid;
+  }
+  E_TRY(cudaSetDevice(e->device));
+  if (!e->gather_stream) {
+    E_TRY(cudaStreamCreateWithFlags(&e->gather_stream, cudaStreamNonBlocking));
+    E_TRY(cudaEventCreateWithFlags(&e->gather_ready, cudaEventDisableTiming));
+    for (cudaEvent_t& ev : e->gather_done) E_TRY(cudaEventCreateWithFlags(&ev, cudaEventDisableTiming));
+  }
+  const NcclApi* api = nccl_api();
+  // the gather starts after the engine stream's work so far (the step that wrote d_local) and runs beside
+  // the following steps
+  E_TRY(cudaEventRecord(e->gather_ready, e->stream));
+  E_TRY(cudaStreamWaitEvent(e->gather_stream, e->gather_ready, 0));
+  N_TRY(api, api->all_gather(d_local, d_all, (size_t)n, ncclInt32, e->nccl, e->gather_stream));
+  const int k = (int)(e->gather_n & 1);
+  E_TRY(cudaEventRecord(e->gather_done[k], e->gather_stream));
+  // at most two gathers in flight: the engine stream's work after this call waits for the previous gather,
+  // so a buffer that gather read may be rewritten from the step after next on
+  if (e->gather_n > 0) E_TRY(cudaStreamWaitEvent(e->stream, e->gather_done[k ^ 1], 0));
+  ++e->gather_n;
+  return 0;
+}
+
+int qwen_engine_gather_join(qwen_engine* e) {
+  if (!e) return kStatusInvalid;
+  if (e->gather_n > 0) {
+    E_TRY(cudaSetDevice(e->device));
+    E_TRY(cudaStreamWaitEvent(e->stream, e->gather_done[(e->gather_n - 1) & 1], 0));
+  }
   return 0;
 }
 

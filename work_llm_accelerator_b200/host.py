@@ -199,6 +199,8 @@ def _configure_engine(lib: ctypes.CDLL) -> None:
     lib.qwen_engine_nccl_unique_id.argtypes = [ctypes.c_char_p]
     lib.qwen_engine_nccl_init.argtypes = [vp, ctypes.c_char_p, i, i]
     lib.qwen_engine_gather_tokens.argtypes = [vp, vp, i, vp]
+    lib.qwen_engine_gather_tokens_async.argtypes = [vp, vp, i, vp]
+    lib.qwen_engine_gather_join.argtypes = [vp]
     for n in ("qwen_engine_create", "qwen_engine_init_synthetic", "qwen_engine_load_layer", "qwen_engine_load_embedding",
               "qwen_engine_prefill", "qwen_engine_decode", "qwen_engine_write_kv", "qwen_engine_read_kv",
               "qwen_engine_set_seq_len", "qwen_engine_seq_len", "qwen_engine_reset", "qwen_engine_set_option",
@@ -206,7 +208,8 @@ def _configure_engine(lib: ctypes.CDLL) -> None:
               "qwen_engine_kernels_per_decode_step", "qwen_engine_decode_device", "qwen_engine_read_layer",
               "qwen_engine_profile_kernels", "qwen_engine_read_trace", "qwen_engine_profile_decode",
               "qwen_engine_profile_batched", "qwen_engine_nccl_unique_id", "qwen_engine_nccl_init",
-              "qwen_engine_gather_tokens", "qwen_engine_read_kv_hf", "qwen_engine_write_kv_hf",
+              "qwen_engine_gather_tokens", "qwen_engine_gather_tokens_async", "qwen_engine_gather_join",
+              "qwen_engine_read_kv_hf", "qwen_engine_write_kv_hf",
               "qwen_engine_prefill_chunk"):
         getattr(lib, n).restype = i
 
@@ -382,6 +385,14 @@ class Engine:
     def gather_tokens(self, d_local_ptr: int, n: int, d_all_ptr: int) -> None:
         """Enqueue the all-gather of n int32 ids per rank on the engine's stream (device pointers)."""
         _check(self.lib.qwen_engine_gather_tokens(self.handle, d_local_ptr, n, d_all_ptr), "gather_tokens")
+
+    def gather_tokens_async(self, d_local_ptr: int, n: int, d_all_ptr: int) -> None:
+        """The same all-gather on a side stream, beside the engine's following steps (see the C header)."""
+        _check(self.lib.qwen_engine_gather_tokens_async(self.handle, d_local_ptr, n, d_all_ptr), "gather_tokens_async")
+
+    def gather_join(self) -> None:
+        """Make the engine's stream wait for the last asynchronous gather."""
+        _check(self.lib.qwen_engine_gather_join(self.handle), "gather_join")
 
     def stream(self) -> int:
         return int(self.lib.qwen_engine_stream(self.handle) or 0)
