@@ -69,7 +69,10 @@ int qwen_engine_reset(qwen_engine* e, int slot);
  * default 1), "stack" (W8: the whole decode step as one persistent kernel, default 1; 0 = five tensor-core
  * kernels per layer), "bs1" (W8, one sequence per step: the persistent kernel on the CUDA cores with
  * self-validating cross-CTA words, default 1; 0 = the tensor-core persistent kernel; same results),
- * "bs1_ctas" (CTAs of that kernel, 144 .. the SM count, default the SM count; results do not depend on it), "qgemm" (W8 separate-kernel path on the int8 tensor cores, default 1; 0 = CUDA-core
+ * "bs1_ctas" (CTAs of that kernel, 144 .. the SM count, default the SM count; results do not depend on it),
+ * "bs1_poison" (test hook of the failure path: the next batch-1 launch finds its cross-CTA counts
+ * impossible, gives up after its bounded waits (~1 s) and sets the kernel error flag; the launch after it is
+ * clean), "qgemm" (W8 separate-kernel path on the int8 tensor cores, default 1; 0 = CUDA-core
  * GEMV), "trace" (record a per-CTA, per-layer timeline of the persistent kernel, default 0), "batched" (W8: steps
  * of more than 4 sequences as one many-token tensor-core step, default 1; 0 = groups of 4), "lm_tc" (LM head
  * on the tensor cores, default 1; 0 = CUDA-core GEMV), "stack_ring" (weight stages in flight per SM in the

@@ -290,6 +290,45 @@ def test_batch1_kernel_cta_count_does_not_change_results(host):
             assert np.array_equal(a, b), (ctas, step, rel_l2(a, b))
 
 
+def test_batch1_kernel_bounded_waits_end_a_broken_step(host):
+    """Failure path of the batch-1 kernel without a GPU fault: option "bs1_poison" fills the launch's packed
+    split-K words with counts no producer can complete, so its consumers wait out their bounded waits (~1 s),
+    raise the abort flag (every other wait then ends at once) and set the kernel error flag. The step returns
+    within seconds, the next launch (the other launch parity, zeroed by the broken one) completes without an
+    error, and after a fresh prefill the kernel again equals the separate kernels."""
+    import time
+
+    rng = np.random.default_rng(31)
+    prompt = [int(t) for t in rng.integers(0, qo.VOCAB, 40)]
+    eng = host.Engine(0, 8, max_seqs=1, max_len=256)
+    try:
+        eng.init_synthetic(31)
+        host.kernel_error(reset=True)
+        tok = eng.prefill(0, prompt)
+        tok = int(eng.decode([0], [tok])[0])
+        assert host.kernel_error(reset=True) == 0
+        eng.set_option("bs1_poison", 1)
+        t0 = time.time()
+        eng.decode([0], [tok])
+        assert time.time() - t0 < 30.0
+        assert host.kernel_error(reset=True) == 1  # a bounded wait gave up
+        eng.decode([0], [tok])
+        assert host.kernel_error(reset=True) == 0
+        eng.reset(0)
+        eng.set_option("dump_hidden", 1)
+        toks, hid = [eng.prefill(0, prompt)], []
+        for _ in range(3):
+            toks.append(int(eng.decode([0], [toks[-1]])[0]))
+            hid.append(eng.read_hidden(1).copy())
+        assert host.kernel_error(reset=True) == 0
+    finally:
+        eng.close()
+    toks_k, hid_k = _decode_trace(host, 31, prompt, 3, max_len=256, stack=0)
+    assert toks == toks_k
+    for step, (a, b) in enumerate(zip(hid, hid_k)):
+        assert np.array_equal(a, b), (step, rel_l2(a, b))
+
+
 def test_batch1_kernel_over_many_launches(host):
     """The batch-1 persistent kernel keeps launch-parity words (zeroed by the following launch) and tagged
     words (launch epoch and layer in the tag): 40 consecutive steps with the trace option on, each equal

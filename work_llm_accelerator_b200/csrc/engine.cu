@@ -230,6 +230,7 @@ struct qwen_engine {
   // persistent batch-1 step on the CUDA cores (wbits == 8, one sequence per step): its schedule and words
   bool use_bs1 = true;
   int bs1_ctas = 0;  // CTAs of the batch-1 kernel (option "bs1_ctas"; default: every SM)
+  bool bs1_poison = false;  // test hook (option "bs1_poison"): the next batch-1 launch finds impossible counts
   bs1::Sync* bs1_sync = nullptr;
   bs1::Buffers bs1_buf{nullptr, nullptr, nullptr, nullptr, nullptr, nullptr, nullptr};
   uint32_t* d_item_off1 = nullptr;
@@ -542,6 +543,14 @@ int enqueue_decode(qwen_engine* e, int nt, int max_len, bool advance) {
     a.items = e->d_items1;
     a.trace = e->trace;
     a.ring = e->stack_ring;
+    if (e->bs1_poison) {
+      // both launch halves of the packed split-K words get counts no producer can complete (bytes 0x40: count
+      // field 0x4040, value field far below a carry into it): the launch's consumers wait out their bounded
+      // waits (~1 s), raise the abort flag and set the kernel error flag; the launch zeroes the other half as
+      // usual, so the launch after it is clean
+      E_TRY(cudaMemsetAsync(e->bs1_buf.acc, 0x40, bs1::acc_words() * 8, e->stream));
+      e->bs1_poison = false;
+    }
     E_TRY(bs1::launch_decode_bs1(a, e->bs1_ctas, e->stream));
     xin = ((kLayers - 1) & 1) ? e->y1 : e->y0;
   } else if (stack_enabled(e)) {
@@ -1094,6 +1103,10 @@ int qwen_engine_set_option(qwen_engine* e, const char* name, long long value) {
     E_TRY(cudaMemcpy(e->d_item_off1, s1.off.data(), s1.off.size() * 4, cudaMemcpyHostToDevice));
     E_TRY(cudaMemcpy(e->d_items1, s1.items.data(), s1.items.size() * sizeof(stack::Item), cudaMemcpyHostToDevice));
     e->bs1_ctas = (int)value;
+    for (auto& kv : e->graphs) cudaGraphExecDestroy(kv.second);
+    e->graphs.clear();
+  } else if (n == "bs1_poison") {
+    e->bs1_poison = value != 0;
     for (auto& kv : e->graphs) cudaGraphExecDestroy(kv.second);
     e->graphs.clear();
   } else if (n == "bs1") {
