@@ -96,7 +96,6 @@ struct Ctrl {
   double red[4];
   float redf[4];
   float ys[128];
-  int flag;
 };
 
 constexpr size_t kSmemBytes = 1024 + (size_t)kRing * kUnitBytes + kAttnBytes + kDigitBytes + sizeof(Ctrl);

@@ -78,7 +78,10 @@ struct Args {
   Sync* sync;
   const uint32_t* item_off;  // [ctas + 1]
   const stack::Item* items;
-  unsigned long long* trace;  // optional [ctas][28][stack::kTraceSlots] global-timer stamps (ns)
+  // optional [ctas][28][stack::kTraceSlots] stamps: the stage slots of decode_stack.h (global timer, ns), and
+  // for the gate|up dot products kTraceUnit + 0/1/2 = global timer at units 0, 8 and the last, + 3/4/5 = SM
+  // clock at the same units, + 6 + w = SM clock of worker warp w at the loop's end
+  unsigned long long* trace;
   int ring;                  // weight stages in flight per CTA (2..9)
 };
 
