@@ -184,7 +184,7 @@ __global__ void __launch_bounds__(kThreadsA, 1)
   griddep_launch();
   if (*reinterpret_cast<const volatile int*>(flag) != 0) return;  // values outside the split: CUDA-core kernel
   extern __shared__ __align__(1024) uint8_t smem_raw[];
-  uint8_t* tiles = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* tiles = align_smem_1024(smem_raw);
   ACtl& c = *reinterpret_cast<ACtl*>(tiles + kTileBytes);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int qt = gridDim.x - 1 - blockIdx.x;  // heaviest query tiles first

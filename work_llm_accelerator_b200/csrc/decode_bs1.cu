@@ -1042,7 +1042,7 @@ __device__ void workers(const Args& a, uint8_t* ring, uint8_t* attn, uint8_t* di
 
 __global__ void __launch_bounds__(kThreads, 1) decode_bs1_kernel(const __grid_constant__ Args a) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
-  uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* base = align_smem_1024(smem_raw);
   uint8_t* ring = base;
   uint8_t* attn = base + (size_t)kRing * kUnitBytes;
   uint8_t* dig = attn + kAttnBytes;

@@ -992,7 +992,7 @@ __device__ void workers(const Args& a, uint8_t* uni, Ctrl& cs, uint32_t tmem, ui
 
 __global__ void __launch_bounds__(kThreads, 1) decode_stack_kernel(const __grid_constant__ Args a) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
-  uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* base = align_smem_1024(smem_raw);
   uint8_t* ring = base;
   uint8_t* uni = base + (size_t)kRing * kUnitBytes;
   Ctrl& cs = *reinterpret_cast<Ctrl*>(uni + kUnionBytes);

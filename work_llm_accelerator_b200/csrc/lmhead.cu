@@ -80,7 +80,7 @@ __global__ void __launch_bounds__(kLmThreads, 1)
     lm_head_kernel(const __grid_constant__ CUtensorMap emap, const __grid_constant__ CUtensorMap pmap, LmArgs a) {
   using C = LmCfg<NP>;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
-  uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* base = align_smem_1024(smem_raw);
   uint8_t* bres = base;                              // resident B blocks (small token counts)
   uint8_t* ring = base + C::kResBytes;               // stages
   LmCtrl& cs = *reinterpret_cast<LmCtrl*>(ring + (size_t)C::kStages * C::kStage);

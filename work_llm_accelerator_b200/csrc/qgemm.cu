@@ -183,10 +183,10 @@ template <int MODE, class Epi>
 __global__ void __launch_bounds__(kThreads, 1) qgemm_kernel(const __grid_constant__ CUtensorMap tmap, QArgs a, Epi epi) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   // 128-byte-swizzled tiles need 1024-byte-aligned shared addresses: align both regions explicitly
-  uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* base = align_smem_1024(smem_raw);
   Smem& sm = *reinterpret_cast<Smem*>(base);
   uint8_t* bsm = base + sizeof(Smem);
-  bsm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(bsm) + 1023) & ~uintptr_t(1023));
+  bsm = align_smem_1024(bsm);
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   const int mtile = blockIdx.x / a.split, ks = blockIdx.x % a.split;
   const int kper = (a.nkb + a.split - 1) / a.split;

@@ -196,7 +196,7 @@ __global__ void __launch_bounds__(TCfg<TN, ST>::kThreads, (ST == 2 || ST == kPai
   constexpr int kPlaneTile = C::kPlaneTile;
   constexpr int kTmemColsT = C::kTmemCols;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
-  uint8_t* stages = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* stages = align_smem_1024(smem_raw);
   TSmem& sm = *reinterpret_cast<TSmem*>(stages + (size_t)kStagesT * kStageBytes);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   // split K: the ksplit CTAs of a cluster share one output tile, CTA `rank` sums K blocks [kb_lo, kb_hi)
