@@ -267,12 +267,12 @@ struct Worker {
   unsigned* abort_flag;
 };
 
-// Digits of 4 consecutive elements at byte k of each plane (plane stride kDigitStride).
-__device__ __forceinline__ void put_digits(uint8_t* dig, int k, const float (&v)[4], float step) {
+// Digits of 4 consecutive elements at byte k of each plane (plane stride kDigitStride); r = digit_recip(step).
+__device__ __forceinline__ void put_digits(uint8_t* dig, int k, const float (&v)[4], double r) {
   uint32_t w0 = 0, w1 = 0, w2 = 0;
 #pragma unroll
   for (int e = 0; e < 4; ++e) {
-    const int X = (int)rintf(__fdiv_rn(v[e], step));
+    const int X = umma::digit_quotient(v[e], r);
     int d0, d1, d2;
     umma::split_digits(X, d0, d1, d2);
     w0 |= (uint32_t)(d0 & 255) << (8 * e);
@@ -334,12 +334,12 @@ __device__ float norm_and_step(Ctrl& cs, float (&v)[3][4], bool norm, const floa
 }
 
 // Digits of this thread's elements of a 1536-wide row that fall into K blocks [kb0, kb1).
-__device__ __forceinline__ void row_digits(uint8_t* dig, const float (&v)[3][4], float step, int kb0, int kb1,
+__device__ __forceinline__ void row_digits(uint8_t* dig, const float (&v)[3][4], double r, int kb0, int kb1,
                                            int tid) {
 #pragma unroll
   for (int j = 0; j < 3; ++j) {
     const int k = 512 * j + 4 * tid;
-    if (k >= kb0 * kKBlock && k < kb1 * kKBlock) put_digits(dig, k - kb0 * kKBlock, v[j], step);
+    if (k >= kb0 * kKBlock && k < kb1 * kKBlock) put_digits(dig, k - kb0 * kKBlock, v[j], r);
   }
 }
 
@@ -896,7 +896,7 @@ __device__ void workers(const Args& a, uint8_t* ring, uint8_t* attn, uint8_t* di
       if (tr) stamp(a, l, stack::kTraceWait + 0);
       const float step = norm_and_step(cs, v, true, wv, w);
       if (w.tid == 0) st_word(a.buf.steps + (size_t)l * 4 + kQkv, tagged(tag, step));
-      row_digits(dig, v, step, it.kb0, it.kb1, w.tid);
+      row_digits(dig, v, umma::digit_recip(step), it.kb0, it.kb1, w.tid);
       named_sync(kBarW, kWorkers);
       if (tr) stamp(a, l, stack::kTraceBuilt + 0);
       const long long tot = gemv_units(w, cs, a, ring, dig, it.kb1 - it.kb0);
@@ -934,7 +934,7 @@ __device__ void workers(const Args& a, uint8_t* ring, uint8_t* attn, uint8_t* di
       if (w.tid == 0) st_word(a.buf.steps + (size_t)l * 4 + kO, tagged(tag, step));
       if (4 * w.tid < nel) {
         const float v[4] = {word_value(x[0]), word_value(x[1]), word_value(x[2]), word_value(x[3])};
-        put_digits(dig, 4 * w.tid, v, step);
+        put_digits(dig, 4 * w.tid, v, umma::digit_recip(step));
       }
       named_sync(kBarW, kWorkers);
       if (tr) stamp(a, l, stack::kTraceBuilt + 2);
@@ -954,7 +954,7 @@ __device__ void workers(const Args& a, uint8_t* ring, uint8_t* attn, uint8_t* di
       load_a(a, w, l, os, v);
       if (tr) stamp(a, l, stack::kTraceWait + 3);
       const float step = norm_and_step(cs, v, true, wv, w);
-      row_digits(dig, v, step, 0, nkb(kGu), w.tid);
+      row_digits(dig, v, umma::digit_recip(step), 0, nkb(kGu), w.tid);
       named_sync(kBarW, kWorkers);
       if (tr) stamp(a, l, stack::kTraceBuilt + 3);
       const long long tot = gemv_units(w, cs, a, ring, dig, it.kb1 - it.kb0, l);
@@ -1007,11 +1007,12 @@ __device__ void workers(const Args& a, uint8_t* ring, uint8_t* attn, uint8_t* di
       const float mx = block_max(cs, fmaxf(word_value(x0), has1 ? word_value(x1) : 0.0f), w);
       const float step = mx > 0.0f ? mx / umma::kDigitRange : 1.0f;
       if (w.tid == 0) st_word(a.buf.steps + (size_t)l * 4 + kDown, tagged(tag, step));
+      const double rstep = umma::digit_recip(step);
 #pragma unroll
       for (int b = 0; b < 2; ++b) {
         if (b == 0 ? f0 : f1) {
           const float hv[4] = {word_value(hx[b][0]), word_value(hx[b][1]), word_value(hx[b][2]), word_value(hx[b][3])};
-          put_digits(dig, 4 * (w.tid + b * kWorkers), hv, step);
+          put_digits(dig, 4 * (w.tid + b * kWorkers), hv, rstep);
         }
       }
       named_sync(kBarW, kWorkers);

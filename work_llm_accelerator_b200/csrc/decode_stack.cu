@@ -278,11 +278,11 @@ __device__ void mma_issuer(const Args& a, uint8_t* ring_smem, uint8_t* digits, C
 // ---------------------------------------------------------------------------------------------------
 // workers: activation digits
 // ---------------------------------------------------------------------------------------------------
-__device__ __forceinline__ void put_digits(uint8_t* blk, int t, int kk, const float (&v)[4], float step) {
+__device__ __forceinline__ void put_digits(uint8_t* blk, int t, int kk, const float (&v)[4], double r) {
   uint32_t w0 = 0, w1 = 0, w2 = 0;
 #pragma unroll
   for (int e = 0; e < 4; ++e) {
-    const int X = (int)rintf(__fdiv_rn(v[e], step));
+    const int X = umma::digit_quotient(v[e], r);
     int d0, d1, d2;
     split_digits(X, d0, d1, d2);
     w0 |= (uint32_t)(d0 & 255) << (8 * e);
@@ -488,10 +488,11 @@ __device__ void build_full(const Args& a, Ctrl& cs, uint8_t* dbuf, const InSrc& 
     const float st = mx > 0.0f ? mx / kDigitRange : 1.0f;
     step[t] = st;
     if (step_out != nullptr && tid == 0) step_out[t] = st;
+    const double r = umma::digit_recip(st);
 #pragma unroll
     for (int j = 0; j < 3; ++j) {
       const int k = 512 * j + 4 * tid;
-      put_digits(dbuf + (size_t)(k >> 7) * kDigitBlockBytes, t, k & 127, v[j], st);
+      put_digits(dbuf + (size_t)(k >> 7) * kDigitBlockBytes, t, k & 127, v[j], r);
     }
   }
 }
@@ -505,6 +506,7 @@ __device__ void build_down(const Args& a, uint8_t* dbuf, int l, uint32_t b0, uin
     const float st = mx > 0.0f ? mx / kDigitRange : 1.0f;
     step[t] = st;
     if (step_out != nullptr && tid == 0) step_out[t] = st;
+    const double r = umma::digit_recip(st);
     for (uint32_t i = b0; i < b1; ++i) {
       const Item it = a.items[i];
       const int n4 = (it.kb1 - it.kb0) * 32;
@@ -512,7 +514,7 @@ __device__ void build_down(const Args& a, uint8_t* dbuf, int l, uint32_t b0, uin
         const int k = it.kb0 * kKBlock + 4 * f;
         const float4 x = __ldcg(reinterpret_cast<const float4*>(a.h + (size_t)t * kInter + k));
         const float v[4] = {x.x, x.y, x.z, x.w};
-        put_digits(dbuf + (size_t)(it.dslot + (f >> 5)) * kDigitBlockBytes, t, 4 * (f & 31), v, st);
+        put_digits(dbuf + (size_t)(it.dslot + (f >> 5)) * kDigitBlockBytes, t, 4 * (f & 31), v, r);
       }
     }
   }

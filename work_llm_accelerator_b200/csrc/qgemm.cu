@@ -135,6 +135,7 @@ __device__ void build_digits(const QArgs& a, Smem& sm, uint8_t* bsm, int kb0, in
     if (tid == 0) sm.sx[t] = step;
     named_sync(kBarEpi, kEpiThreads);
     // digits of this CTA's K range: one 16-byte chunk per thread iteration
+    const double rstep = umma::digit_recip(step);
     const int nchunks = (kb1 - kb0) * 8;
     for (int c = tid; c < nchunks; c += kEpiThreads) {
       const int j = c >> 3, c16 = c & 7;
@@ -150,7 +151,7 @@ __device__ void build_digits(const QArgs& a, Smem& sm, uint8_t* bsm, int kb0, in
           v = load_x(a, MODE, t, k);
           if (MODE != kQPlain) v = (float)((double)v * inv * (double)a.norm_w[k]);
         }
-        const int X = (int)rintf(__fdiv_rn(v, step));
+        const int X = umma::digit_quotient(v, rstep);
         int d0, d1, d2;
         umma::split_digits(X, d0, d1, d2);
         w0[e >> 2] |= (uint32_t)(d0 & 255) << (8 * (e & 3));

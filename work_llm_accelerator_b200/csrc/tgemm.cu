@@ -555,6 +555,7 @@ __global__ void __launch_bounds__(256) digitize_kernel(const float* __restrict__
   for (int i = 0; i < 8; ++i) mx = fmaxf(mx, red[i]);
   const float st = mx > 0.0f ? mx / kDigitRange : 1.0f;
   if (threadIdx.x == 0) steps[t] = st;
+  const double rst = digit_recip(st);
 #pragma unroll
   for (int i = 0; i < kDigitVec; ++i) {
     const int k = 4 * ((int)threadIdx.x + 256 * i);
@@ -564,7 +565,7 @@ __global__ void __launch_bounds__(256) digitize_kernel(const float* __restrict__
 #pragma unroll
     for (int e = 0; e < 4; ++e) {
       int d0, d1, d2;
-      split_digits((int)rintf(__fdiv_rn(vv[e], st)), d0, d1, d2);
+      split_digits(digit_quotient(vv[e], rst), d0, d1, d2);
       w0 |= (uint32_t)(d0 & 255) << (8 * e);
       w1 |= (uint32_t)(d1 & 255) << (8 * e);
       w2 |= (uint32_t)(d2 & 255) << (8 * e);
@@ -656,6 +657,7 @@ __global__ void __launch_bounds__(128) prefill_rmsnorm_digitize_kernel(const flo
     const float mx = fmaxf(fmaxf(redm[r], redm[kPNormTok + r]), fmaxf(redm[2 * kPNormTok + r], redm[3 * kPNormTok + r]));
     const float st = mx > 0.0f ? mx / kDigitRange : 1.0f;
     if (tid == 0) steps[t] = st;
+    const double rst = digit_recip(st);
 #pragma unroll
     for (int j = 0; j < 3; ++j) {
       const int k = 4 * tid + 512 * j;
@@ -663,7 +665,7 @@ __global__ void __launch_bounds__(128) prefill_rmsnorm_digitize_kernel(const flo
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
         int d0, d1, d2;
-        split_digits((int)rintf(__fdiv_rn(v[r][j][e], st)), d0, d1, d2);
+        split_digits(digit_quotient(v[r][j][e], rst), d0, d1, d2);
         w0 |= (uint32_t)(d0 & 255) << (8 * e);
         w1 |= (uint32_t)(d1 & 255) << (8 * e);
         w2 |= (uint32_t)(d2 & 255) << (8 * e);
@@ -782,13 +784,14 @@ __global__ void __launch_bounds__(128) rmsnorm_digitize_kernel(const float* __re
   const float mx = fmaxf(fmaxf(redm[0], redm[1]), fmaxf(redm[2], redm[3]));
   const float st = mx > 0.0f ? mx / kDigitRange : 1.0f;
   if (tid == 0) steps[t] = st;
+  const double rst = digit_recip(st);
 #pragma unroll
   for (int j = 0; j < 3; ++j) {
     uint32_t w0 = 0, w1 = 0, w2 = 0;
 #pragma unroll
     for (int e = 0; e < 4; ++e) {
       int d0, d1, d2;
-      split_digits((int)rintf(__fdiv_rn(v[j][e], st)), d0, d1, d2);
+      split_digits(digit_quotient(v[j][e], rst), d0, d1, d2);
       w0 |= (uint32_t)(d0 & 255) << (8 * e);
       w1 |= (uint32_t)(d1 & 255) << (8 * e);
       w2 |= (uint32_t)(d2 & 255) << (8 * e);

@@ -127,5 +127,22 @@ __device__ __forceinline__ void split_digits(int X, int& d0, int& d1, int& d2) {
 // Largest |X| the digit split represents, as the step divisor: step = max|x| / kDigitRange.
 constexpr float kDigitRange = 8355710.0f;
 
+// The digit integer X = rint(v / step) of the reference, whose quotient is the correctly rounded binary32
+// division, computed as rint(RN32(RN64(v * r))) with r = RN64(1 / step): one double multiply per element
+// instead of a float division (r is formed once per row). Both give the same X for all finite v, step > 0:
+// - |q| < 2^-126 (q = v / step exactly): both quotients are below 1/2 in magnitude, X = 0 either way.
+// - otherwise q lies in a normal binade [2^(e+23), 2^(e+24)) with binary32 spacing 2^e; RN32 of two values
+//   differs only if a rounding midpoint M = m 2^(e-1) (m odd, m > 2^24) lies between them. Write v = V 2^a,
+//   step = S 2^b (V, S odd integers below 2^24). q is not a midpoint (m S is odd and above 2^24, so
+//   M step = m S 2^(b+e-1) cannot equal V 2^a), and |q - M| = |v - M step| / step is a nonzero multiple of
+//   2^min(a, b+e-1) over step: >= 2^(e-25) > 2^-49 |q|, or >= |q| / V > 2^-24 |q|.
+//   RN64(v r) = q (1 + d1)(1 + d2), |d1|, |d2| <= 2^-53, is within 2^-51 |q| of q: on the same side of
+//   every midpoint, so it rounds to RN32(q).
+// v and step are binary32, so their conversions to double are exact, and |v r| stays near kDigitRange.
+__device__ __forceinline__ double digit_recip(float step) { return __ddiv_rn(1.0, (double)step); }
+__device__ __forceinline__ int digit_quotient(float v, double r) {
+  return (int)rintf(__double2float_rn(__dmul_rn((double)v, r)));
+}
+
 }  // namespace umma
 }  // namespace qb
