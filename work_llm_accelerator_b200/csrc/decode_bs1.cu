@@ -96,6 +96,7 @@ struct Ctrl {
   double red[4];
   float redf[4];
   float ys[128];
+  float av[kHidden];  // this layer's attention output a (o_proj + residual), kept by the gate|up item's load
 };
 
 constexpr size_t kSmemBytes = 1024 + (size_t)kRing * kUnitBytes + kAttnBytes + kDigitBytes + sizeof(Ctrl);
@@ -422,29 +423,34 @@ __device__ long long gemv_units(Worker& w, Ctrl& cs, const Args& a, uint8_t* rin
 
 // Layer lp's output y = bf16(a + down_s * (step_d * down_total)) with a = o_s * (step_o * o_total), this
 // thread's elements, from the packed words (the expressions of the tensor-core kernels' epilogues).
+// av: the layer's a = o_proj output (as load_a forms it), when this CTA already read it for its gate|up item;
+// then only the down words are polled.
 __device__ void load_y(const Args& a, const Worker& w, int lp, const float4 (&os)[3], const float4 (&ds)[3],
-                       float (&v)[3][4]) {
+                       const float* av, float (&v)[3][4]) {
   const unsigned long long* acc = acc_layer(a, w.par, lp);
   const unsigned long long* sw = a.buf.steps + (size_t)lp * 4;
   const unsigned tag = tag_of(w.epoch, lp);
-  unsigned long long wo[3][4], wd[3][4], so, sd;
+  const bool need_o = av == nullptr;
+  unsigned long long wo[3][4] = {{0, 0, 0, 0}, {0, 0, 0, 0}, {0, 0, 0, 0}}, wd[3][4], so = 0, sd;
   Spin sp;
   while (true) {
 #pragma unroll
     for (int j = 0; j < 3; ++j) {
       const int k = 512 * j + 4 * w.tid;
-      ld_word2(acc + acc_row(kO) + k, wo[j][0], wo[j][1]);
-      ld_word2(acc + acc_row(kO) + k + 2, wo[j][2], wo[j][3]);
+      if (need_o) {
+        ld_word2(acc + acc_row(kO) + k, wo[j][0], wo[j][1]);
+        ld_word2(acc + acc_row(kO) + k + 2, wo[j][2], wo[j][3]);
+      }
       ld_word2(acc + acc_row(kDown) + k, wd[j][0], wd[j][1]);
       ld_word2(acc + acc_row(kDown) + k + 2, wd[j][2], wd[j][3]);
     }
-    so = ld_word(sw + kO);
+    if (need_o) so = ld_word(sw + kO);
     sd = ld_word(sw + kDown);
-    bool ok = tag_ok(so, tag) && tag_ok(sd, tag);
+    bool ok = tag_ok(sd, tag) && (!need_o || tag_ok(so, tag));
 #pragma unroll
     for (int j = 0; j < 3; ++j)
 #pragma unroll
-      for (int e = 0; e < 4; ++e) ok = ok && count_ok(wo[j][e], nseg(kO)) && count_ok(wd[j][e], nseg(kDown));
+      for (int e = 0; e < 4; ++e) ok = ok && count_ok(wd[j][e], nseg(kDown)) && (!need_o || count_ok(wo[j][e], nseg(kO)));
     if (ok || !sp.keep_going(w.abort_flag)) break;
   }
   const float st_o = word_value(so), st_d = word_value(sd);
@@ -452,16 +458,18 @@ __device__ void load_y(const Args& a, const Worker& w, int lp, const float4 (&os
   for (int j = 0; j < 3; ++j) {
     const float osc[4] = {os[j].x, os[j].y, os[j].z, os[j].w};
     const float dsc[4] = {ds[j].x, ds[j].y, ds[j].z, ds[j].w};
+    float4 a4 = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (!need_o) a4 = *reinterpret_cast<const float4*>(av + 512 * j + 4 * w.tid);
+    const float ak[4] = {a4.x, a4.y, a4.z, a4.w};
 #pragma unroll
     for (int e = 0; e < 4; ++e) {
-      const long long to = packed_total(wo[j][e], nseg(kO)), td = packed_total(wd[j][e], nseg(kDown));
-      const float av = osc[e] * (float)((double)to * (double)st_o);
-      v[j][e] = round_bf16(__fadd_rn(av, dsc[e] * (float)((double)td * (double)st_d)));
+      const long long td = packed_total(wd[j][e], nseg(kDown));
+      const float avv = need_o ? osc[e] * (float)((double)packed_total(wo[j][e], nseg(kO)) * (double)st_o) : ak[e];
+      v[j][e] = round_bf16(__fadd_rn(avv, dsc[e] * (float)((double)td * (double)st_d)));
     }
   }
 }
 
-// The attention output a = o_s * (step_o * o_total) of layer l, this thread's elements.
 __device__ void load_a(const Args& a, const Worker& w, int l, const float4 (&os)[3], float (&v)[3][4]) {
   const unsigned long long* acc = acc_layer(a, w.par, l);
   const unsigned long long* sw = a.buf.steps + (size_t)l * 4;
@@ -881,7 +889,7 @@ __device__ void workers(const Args& a, uint8_t* ring, uint8_t* attn, uint8_t* di
         float4 os[3], ds[3];
         load_vec(P.o_s, w.tid, os);
         load_vec(P.down_s, w.tid, ds);
-        load_y(a, w, l - 1, os, ds, v);
+        load_y(a, w, l - 1, os, ds, si[kGu] >= 0 ? cs.av : nullptr, v);
         if (y_writer) {
           float* yw = ((l - 1) & 1) ? a.y1 : a.y0;
           float* dw = a.dump ? a.dump + (size_t)(l - 1) * kHidden : nullptr;
@@ -952,6 +960,9 @@ __device__ void workers(const Args& a, uint8_t* ring, uint8_t* attn, uint8_t* di
       const float gsc = __ldg(L.gu_s + row);
       float v[3][4];
       load_a(a, w, l, os, v);
+#pragma unroll
+      for (int j = 0; j < 3; ++j)  // a, for this CTA's load of the layer output y (same thread, same elements)
+        *reinterpret_cast<float4*>(cs.av + 512 * j + 4 * w.tid) = make_float4(v[j][0], v[j][1], v[j][2], v[j][3]);
       if (tr) stamp(a, l, stack::kTraceWait + 3);
       const float step = norm_and_step(cs, v, true, wv, w);
       row_digits(dig, v, umma::digit_recip(step), 0, nkb(kGu), w.tid);
@@ -1029,7 +1040,7 @@ __device__ void workers(const Args& a, uint8_t* ring, uint8_t* attn, uint8_t* di
     load_vec(a.layers[l].o_s, w.tid, os);
     load_vec(a.layers[l].down_s, w.tid, ds);
     float v[3][4];
-    load_y(a, w, l, os, ds, v);
+    load_y(a, w, l, os, ds, si[kGu] >= 0 ? cs.av : nullptr, v);
     float* yw = (l & 1) ? a.y1 : a.y0;
     float* dw = a.dump ? a.dump + (size_t)l * kHidden : nullptr;
 #pragma unroll
