@@ -67,7 +67,11 @@ constexpr int kThreads = 32 + kWorkers;
 constexpr int kBarW = 1;           // named barrier of the worker warps
 constexpr int kDigitStride = kHidden;  // bytes per digit plane (the widest K range of one item)
 constexpr int kChunk = 64;         // attention keys per work item (one KV page)
-constexpr int kRow = kHeadDim + 4;
+// K and q rows in shared memory: dims 64..127 start 68 floats into a 136-float row, so that the QK loop's
+// 16-byte reads (thread = key x half of the dims) of four keys and both halves fall into eight different
+// 16-byte bank groups, and the two halves of a q row into two
+constexpr int kRow = 136;
+constexpr int kHalfCol = 68;
 constexpr int kHalf = 3;           // query heads per attention item
 constexpr int kMergeBatch = 8;     // chunk partials read per round trip by the merge
 // the merge's rescale factors (3 heads x chunks x 3 floats) reuse the attention chunk rows
@@ -77,6 +81,8 @@ constexpr unsigned long long kBias = 1ull << 43;
 constexpr unsigned long long kLow48 = (1ull << 48) - 1;
 static_assert(kChunk == kPage, "an attention chunk must map onto one KV page");
 static_assert(seg_len(stack::kO) == kHalf, "an o_proj K segment is one attention merge group");
+
+__device__ __forceinline__ int kcol(int d) { return d < 64 ? d : d - 64 + kHalfCol; }
 
 struct AttnSmem {
   float ks[kChunk][kRow];
@@ -529,7 +535,7 @@ __device__ __forceinline__ AttnItem attn_decode(const Args& a, const Worker& w, 
 __device__ __forceinline__ void attn_load_rows(AttnSmem& sm, const AttnItem& it, int r0, int r1, int tid) {
   for (int i = r0 * 32 + tid; i < r1 * 32; i += kWorkers) {
     const int rr = i >> 5, f = i & 31;
-    cp_async16(&sm.ks[rr][4 * f], it.kbase + (size_t)rr * kKvWidth + 4 * f);
+    cp_async16(&sm.ks[rr][kcol(4 * f)], it.kbase + (size_t)rr * kKvWidth + 4 * f);
     cp_async16(&sm.vs[rr][4 * f], it.vbase + (size_t)rr * kKvWidth + 4 * f);
   }
 }
@@ -684,18 +690,18 @@ __device__ void attn_item(const Args& a, AttnSmem& sm, Ctrl& cs, const Worker& w
       vv = __fmaf_rn(qc.vs, (float)((double)packed_total(wv, nseg(kQkv)) * (double)st), qc.vb);
     }
 #pragma unroll
-    for (int j = 0; j < kHalf; ++j) sm.qs[j][d] = qv[j];
-    if (has_new) sm.ks[it.nhist][d] = kv;
+    for (int j = 0; j < kHalf; ++j) sm.qs[j][kcol(d)] = qv[j];
+    if (has_new) sm.ks[it.nhist][kcol(d)] = kv;
     named_sync(kBarW, kWorkers);
     float qr[kHalf], kr = 0.f;
 #pragma unroll
-    for (int j = 0; j < kHalf; ++j) qr[j] = rope(qv[j], sm.qs[j][d ^ 64], d, qc.rc, qc.rs);
-    if (has_new) kr = rope(kv, sm.ks[it.nhist][d ^ 64], d, qc.rc, qc.rs);
+    for (int j = 0; j < kHalf; ++j) qr[j] = rope(qv[j], sm.qs[j][kcol(d ^ 64)], d, qc.rc, qc.rs);
+    if (has_new) kr = rope(kv, sm.ks[it.nhist][kcol(d ^ 64)], d, qc.rc, qc.rs);
     named_sync(kBarW, kWorkers);
 #pragma unroll
-    for (int j = 0; j < kHalf; ++j) sm.qs[j][d] = qr[j];
+    for (int j = 0; j < kHalf; ++j) sm.qs[j][kcol(d)] = qr[j];
     if (has_new) {
-      sm.ks[it.nhist][d] = kr;
+      sm.ks[it.nhist][kcol(d)] = kr;
       sm.vs[it.nhist][d] = vv;
       if (it.hp == 0) {  // the cache row of this step, for later steps
         float* krow = w.kvrow + ((size_t)l * 2) * kPage * kKvWidth + it.g * kHeadDim + d;
@@ -710,14 +716,14 @@ __device__ void attn_item(const Args& a, AttnSmem& sm, Ctrl& cs, const Worker& w
   const float scaling = kAttentionScaling;
   {
     // thread = (key, half of the head dims): three heads over 64 dims, the two halves added
-    const int key = tid >> 1, f0 = (tid & 1) * 16;
+    const int key = tid >> 1, c0 = (tid & 1) * kHalfCol;
     float s0 = 0.f, s1 = 0.f, s2 = 0.f;
 #pragma unroll
-    for (int f = f0; f < f0 + 16; ++f) {
-      const float4 kk = *reinterpret_cast<const float4*>(&sm.ks[key][4 * f]);
-      const float4 x0 = *reinterpret_cast<const float4*>(&sm.qs[0][4 * f]);
-      const float4 x1 = *reinterpret_cast<const float4*>(&sm.qs[1][4 * f]);
-      const float4 x2 = *reinterpret_cast<const float4*>(&sm.qs[2][4 * f]);
+    for (int f = 0; f < 16; ++f) {
+      const float4 kk = *reinterpret_cast<const float4*>(&sm.ks[key][c0 + 4 * f]);
+      const float4 x0 = *reinterpret_cast<const float4*>(&sm.qs[0][c0 + 4 * f]);
+      const float4 x1 = *reinterpret_cast<const float4*>(&sm.qs[1][c0 + 4 * f]);
+      const float4 x2 = *reinterpret_cast<const float4*>(&sm.qs[2][c0 + 4 * f]);
       s0 = fmaf(x0.x, kk.x, fmaf(x0.y, kk.y, fmaf(x0.z, kk.z, fmaf(x0.w, kk.w, s0))));
       s1 = fmaf(x1.x, kk.x, fmaf(x1.y, kk.y, fmaf(x1.z, kk.z, fmaf(x1.w, kk.w, s1))));
       s2 = fmaf(x2.x, kk.x, fmaf(x2.y, kk.y, fmaf(x2.z, kk.z, fmaf(x2.w, kk.w, s2))));
@@ -752,7 +758,7 @@ __device__ void attn_item(const Args& a, AttnSmem& sm, Ctrl& cs, const Worker& w
   }
   named_sync(kBarW, kWorkers);
   float acc[kHalf] = {0.f, 0.f, 0.f};
-#pragma unroll 4
+#pragma unroll 8
   for (int key = 0; key < n; ++key) {
     const float vv = sm.vs[key][tid];
     const float4 e = *reinterpret_cast<const float4*>(&sm.es[key][0]);
