@@ -246,7 +246,7 @@ def test_persistent_step_kernels_match_separate_kernels(host, prompt_len):
     cross-CTA words; decode_stack.cu: the tensor-core persistent kernel) and the five-launches-per-layer
     tensor-core path do the same arithmetic in the same order: every layer's hidden state and every token
     are bit-identical. 130 prompt tokens give three 64-key attention chunks (cross-CTA chunk merge), 5 give
-    one, 600 give ten (more chunks than one merge batch)."""
+    one, 600 give ten (one merge batch of the batch-1 kernel; the 2500-token test below needs four)."""
     rng = np.random.default_rng(prompt_len)
     prompt = [int(t) for t in rng.integers(0, qo.VOCAB, prompt_len)]
     host.kernel_error(reset=True)

@@ -73,7 +73,7 @@ constexpr int kChunk = 64;         // attention keys per work item (one KV page)
 constexpr int kRow = 136;
 constexpr int kHalfCol = 68;
 constexpr int kHalf = 3;           // query heads per attention item
-constexpr int kMergeBatch = 8;     // chunk partials read per round trip by the merge
+constexpr int kMergeBatch = 12;    // chunk partials read per round trip by the merge
 // the merge's rescale factors (3 heads x chunks x 3 floats) reuse the attention chunk rows
 static_assert(kChunk * kRow >= kHalf * 3 * ((kMaxSeq + 1024) / kChunk), "rescale factors of every chunk");
 constexpr long long kSpinLimit = 2000000000ll;  // clock cycles, ~1 s
