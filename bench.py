@@ -431,8 +431,6 @@ def run_b200(args, world: int, rank: int, local: int) -> dict | None:
     bufs = [torch.tensor([first], dtype=torch.int32, device="cuda"), torch.zeros(1, dtype=torch.int32, device="cuda")]
     gathered = torch.zeros(world, dtype=torch.int32, device="cuda")
 
-    if world > 1:  # two SMs left free for the NCCL kernel of the gather, which runs beside the next step
-        eng.set_option("bs1_ctas", torch.cuda.get_device_properties(local).multi_processor_count - 2)
 
     def dev_step(i):
         eng.decode_device([0], bufs[i % 2].data_ptr(), bufs[(i + 1) % 2].data_ptr())

@@ -69,7 +69,8 @@ int qwen_engine_reset(qwen_engine* e, int slot);
  * default 1), "stack" (W8: the whole decode step as one persistent kernel, default 1; 0 = five tensor-core
  * kernels per layer), "bs1" (W8, one sequence per step: the persistent kernel on the CUDA cores with
  * self-validating cross-CTA words, default 1; 0 = the tensor-core persistent kernel; same results),
- * "bs1_ctas" (CTAs of that kernel, 144 .. the SM count, default the SM count; results do not depend on it),
+ * "bs1_ctas" (CTAs of that kernel, 144 .. the SM count, default 144, which leaves SMs free for kernels on
+ * other streams and measured fastest; results do not depend on it),
  * "bs1_poison" (test hook of the failure path: the next batch-1 launch finds its cross-CTA counts
  * impossible, gives up after its bounded waits (~1 s) and sets the kernel error flag; the launch after it is
  * clean), "qgemm" (W8 separate-kernel path on the int8 tensor cores, default 1; 0 = CUDA-core
@@ -135,8 +136,8 @@ int qwen_engine_gather_tokens(qwen_engine* e, const int32_t* d_local, int n, int
  * it starts after the engine stream's work enqueued so far, and the engine stream's work enqueued after the
  * call waits for the previous asynchronous gather (at most two in flight: d_local may be rewritten from the
  * step after next on). qwen_engine_gather_join makes the engine stream wait for the last one (d_all is then
- * complete once the stream reaches that point). With option "bs1_ctas" below the SM count the batch-1
- * decode kernel leaves SMs free for the NCCL kernel. */
+ * complete once the stream reaches that point). With option "bs1_ctas" below the SM count (the default) the
+ * batch-1 decode kernel leaves SMs free for the NCCL kernel. */
 int qwen_engine_gather_tokens_async(qwen_engine* e, const int32_t* d_local, int n, int32_t* d_all);
 int qwen_engine_gather_join(qwen_engine* e);
 /* The engine's CUDA stream (cudaStream_t) for callers that record their own events. */

@@ -277,12 +277,12 @@ def test_batch1_kernel_long_history(host):
 
 
 def test_batch1_kernel_cta_count_does_not_change_results(host):
-    """Option "bs1_ctas": the batch-1 kernel's schedule over 144 (the fewest: one down_proj item per CTA) or
-    146 CTAs gives the same layers and tokens as over every SM."""
+    """Option "bs1_ctas": the batch-1 kernel's default schedule over 144 CTAs (the fewest: one down_proj item
+    per CTA) gives the same layers and tokens as over 146 CTAs and over every SM of a B200 (148)."""
     rng = np.random.default_rng(144)
     prompt = [int(t) for t in rng.integers(0, qo.VOCAB, 200)]
     toks_a, hid_a = _decode_trace(host, 4, prompt, 3, max_len=512, stack=1, bs1=1)
-    for ctas in (144, 146):
+    for ctas in (146, 148):
         toks_b, hid_b = _decode_trace(host, 4, prompt, 3, max_len=512, stack=1, bs1=1, bs1_ctas=ctas)
         assert host.kernel_error(reset=True) == 0
         assert toks_a == toks_b

@@ -229,7 +229,7 @@ struct qwen_engine {
   int stack_ring = 9;                   // weight stages in flight per CTA
   // persistent batch-1 step on the CUDA cores (wbits == 8, one sequence per step): its schedule and words
   bool use_bs1 = true;
-  int bs1_ctas = 0;  // CTAs of the batch-1 kernel (option "bs1_ctas"; default: every SM)
+  int bs1_ctas = 0;  // CTAs of the batch-1 kernel (option "bs1_ctas"; default: bs1::kMinCtas)
   bool bs1_poison = false;  // test hook (option "bs1_poison"): the next batch-1 launch finds impossible counts
   bs1::Sync* bs1_sync = nullptr;
   bs1::Buffers bs1_buf{nullptr, nullptr, nullptr, nullptr, nullptr, nullptr, nullptr};
@@ -932,7 +932,8 @@ int qwen_engine_create(int device, int wbits, int max_seqs, int max_len, qwen_en
   E_TRY(dalloc(&e->attn_part, std::max(attn_partial_floats(T, max_len + 512 + 64),
                                        stack::attn_part_floats(T, e->attn_max_chunks))));
   if (e->stack_ctas > 0 && bs1::decode_bs1_smem() <= (size_t)227 * 1024) {
-    const stack::Schedule s1 = bs1::build_schedule(e->stack_ctas);
+    const int ctas1 = std::min(e->stack_ctas, bs1::kMinCtas);
+    const stack::Schedule s1 = bs1::build_schedule(ctas1);
     if (!s1.off.empty()) {
       bs1::Buffers& b = e->bs1_buf;
       const size_t words[7] = {bs1::acc_words(), bs1::part_words(e->attn_max_chunks), bs1::ctx_words(),
@@ -944,9 +945,9 @@ int qwen_engine_create(int device, int wbits, int max_seqs, int max_len, qwen_en
       }
       E_TRY(cudaMalloc(&e->bs1_sync, sizeof(bs1::Sync)));
       E_TRY(cudaMemset(e->bs1_sync, 0, sizeof(bs1::Sync)));
-      E_TRY(dalloc(&e->d_item_off1, s1.off.size()));
+      E_TRY(dalloc(&e->d_item_off1, (size_t)e->stack_ctas + 1));  // option "bs1_ctas" goes up to every SM
       E_TRY(cudaMemcpy(e->d_item_off1, s1.off.data(), s1.off.size() * 4, cudaMemcpyHostToDevice));
-      e->bs1_ctas = e->stack_ctas;
+      e->bs1_ctas = ctas1;
       E_TRY(dalloc(&e->d_items1, s1.items.size()));
       E_TRY(cudaMemcpy(e->d_items1, s1.items.data(), s1.items.size() * sizeof(stack::Item), cudaMemcpyHostToDevice));
     }
