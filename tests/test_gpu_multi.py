@@ -147,7 +147,7 @@ def test_two_gpu_token_gather(host):
     import torch.multiprocessing as mp
 
     if torch.cuda.device_count() < 2:
-        pytest.skip("needs two GPUs (gpurun --gpus 2)")
+        pytest.skip("needs two GPUs")
     world = 2
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
